@@ -1,0 +1,163 @@
+"""ctypes binding of libgsplat_cuda.so (include/gsplat_cuda.h).
+
+This is the same binding a Crystal `lib GSCuda ... end` block declares; the
+Python side exists for tests, the benchmark and Python users. There is no
+fallback: if the library is missing or fails to load, importing the
+rasterizer raises.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgsplat_cuda.so")
+
+GSC_OK = 0
+GSC_ERR_INVALID = -1
+GSC_ERR_CUDA = -2
+GSC_ERR_CAPACITY = -3
+GSC_ERR_TIMEOUT = -4
+GSC_ERR_NOMEM = -5
+GSC_ERR_NODEVICE = -6
+GSC_ERR_UNSUPPORTED = -7
+
+GSC_MODE_FULL = 0
+GSC_MODE_REF = 1
+
+GSC_FRAME_SPLATS = 0
+GSC_FRAME_KEYS = 1
+GSC_FRAME_VALUES = 2
+GSC_FRAME_RANGES = 3
+GSC_FRAME_IMAGE = 4
+GSC_FRAME_FINAL_T = 5
+GSC_FRAME_LAST = 6
+GSC_FRAME_N_CONTRIB = 7
+GSC_FRAME_GRAD2D = 8
+
+P = C.c_void_p
+
+
+class Camera(C.Structure):
+    """gsc_camera == the reference's packed CameraParamsGPU (176 bytes)."""
+    _fields_ = [("view", C.c_float * 16), ("proj", C.c_float * 16),
+                ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float), ("cy", C.c_float),
+                ("width", C.c_int32), ("height", C.c_int32),
+                ("tan_fov_x", C.c_float), ("tan_fov_y", C.c_float),
+                ("campos", C.c_float * 3), ("_pad", C.c_float)]
+
+
+class RasterConfig(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("sh_degree", C.c_int32), ("t_stop", C.c_float),
+                ("alpha_min", C.c_float), ("alpha_max", C.c_float), ("lowpass", C.c_float),
+                ("fov_cull", C.c_float), ("near_z", C.c_float), ("far_z", C.c_float),
+                ("background", C.c_float * 3)]
+
+
+class Gaussians(C.Structure):
+    _fields_ = [("position", P), ("log_scale", P), ("rotation", P), ("logit_opacity", P),
+                ("sh", P), ("count", C.c_int64)]
+
+
+class GaussianGrads(C.Structure):
+    _fields_ = [("position", P), ("log_scale", P), ("rotation", P), ("logit_opacity", P),
+                ("sh", P)]
+
+
+class Projected(C.Structure):
+    _fields_ = [(name, P) for name in ("splats", "mean2d", "cov2d", "conic", "depth", "radius",
+                                       "colors", "opacity", "tiles_touched", "cov3d")]
+
+
+class Grads2D(C.Structure):
+    _fields_ = [("mean2d", P), ("cov2d", P), ("opacity", P), ("colors", P)]
+
+
+class AdamGroup(C.Structure):
+    _fields_ = [("param", P), ("grad", P), ("m", P), ("v", P), ("numel", C.c_int64),
+                ("lr", C.c_float), ("weight_decay", C.c_float)]
+
+
+assert C.sizeof(Camera) == 176, C.sizeof(Camera)
+
+_SIGS = {
+    "gsc_version": (C.c_int, []),
+    "gsc_last_error": (C.c_char_p, []),
+    "gsc_raster_config_default": (None, [C.POINTER(RasterConfig)]),
+    "gsc_init": (C.c_int, [C.c_int, C.POINTER(P)]),
+    "gsc_destroy": (C.c_int, [P]),
+    "gsc_set_stream": (C.c_int, [P, P]),
+    "gsc_sync": (C.c_int, [P]),
+    "gsc_alloc": (C.c_int, [P, C.c_size_t, C.POINTER(P)]),
+    "gsc_free": (C.c_int, [P, P]),
+    "gsc_memcpy_h2d": (C.c_int, [P, P, P, C.c_size_t]),
+    "gsc_memcpy_d2h": (C.c_int, [P, P, P, C.c_size_t]),
+    "gsc_memset": (C.c_int, [P, P, C.c_int, C.c_size_t]),
+    "gsc_preprocess": (C.c_int, [P, C.POINTER(Gaussians), C.POINTER(Camera), C.POINTER(RasterConfig),
+                                 C.POINTER(Projected)]),
+    "gsc_bin": (C.c_int, [P, C.c_int64, P, C.c_int32, C.c_int32, P, P, C.c_int64,
+                          C.POINTER(C.c_int64)]),
+    "gsc_sort_pairs_u64": (C.c_int, [P, P, P, C.c_int64, C.c_int, C.c_int]),
+    "gsc_tile_ranges": (C.c_int, [P, P, C.c_int64, C.c_int32, P]),
+    "gsc_composite_forward": (C.c_int, [P, P, P, P, C.c_int32, C.c_int32, C.POINTER(RasterConfig),
+                                        P, P, P, P]),
+    "gsc_composite_backward": (C.c_int, [P, P, P, P, C.c_int32, C.c_int32, C.POINTER(RasterConfig),
+                                         P, P, P, C.c_float, P, P, P, P]),
+    "gsc_preprocess_backward": (C.c_int, [P, C.POINTER(Gaussians), C.POINTER(Camera),
+                                          C.POINTER(RasterConfig), P, C.POINTER(GaussianGrads),
+                                          C.POINTER(Grads2D)]),
+    "gsc_l1_loss_grad": (C.c_int, [P, P, P, C.c_int64, C.c_float, P, P]),
+    "gsc_adam_step": (C.c_int, [P, C.POINTER(AdamGroup), C.c_int32, C.c_float, C.c_float,
+                                C.c_float, C.c_int32, C.c_float]),
+    "gsc_frame_create": (C.c_int, [P, C.POINTER(P)]),
+    "gsc_frame_destroy": (C.c_int, [P]),
+    "gsc_rasterize_forward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),
+                                        C.POINTER(RasterConfig), P, P, P, C.POINTER(C.c_int64)]),
+    "gsc_rasterize_backward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),
+                                         C.POINTER(RasterConfig), P, P, C.c_float, P,
+                                         C.POINTER(GaussianGrads), C.POINTER(Grads2D)]),
+    "gsc_frame_get": (C.c_int, [P, C.c_int, C.POINTER(P), C.POINTER(C.c_int64)]),
+}
+
+EXPORTED = tuple(_SIGS)
+
+_lib = None
+
+
+class GscError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"{msg} (status {code})")
+        self.code = code
+
+
+def lib():
+    """Load libgsplat_cuda.so once; raise if it is missing (no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run __graft_entry__.build() "
+                              "or python crystal-gausplat_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc, what=""):
+    if rc != GSC_OK:
+        msg = lib().gsc_last_error().decode(errors="replace")
+        raise GscError(rc, f"{what}: {msg}" if what else msg)
+    return rc
+
+
+def default_config(mode=GSC_MODE_FULL, sh_degree=3, background=(0.0, 0.0, 0.0), t_stop=None):
+    cfg = RasterConfig()
+    lib().gsc_raster_config_default(C.byref(cfg))
+    cfg.mode = mode
+    cfg.sh_degree = sh_degree
+    for i in range(3):
+        cfg.background[i] = background[i]
+    if t_stop is not None:
+        cfg.t_stop = t_stop
+    return cfg

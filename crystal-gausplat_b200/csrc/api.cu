@@ -1,0 +1,591 @@
+// api.cu — the extern "C" boundary of libgsplat_cuda.so (include/gsplat_cuda.h):
+// context, memory, stage entry points, and whole-view orchestration mirroring
+// Rasterizer.forward / Rasterizer.backward (src/gaussian_splatting/rasterizer.cr:48-104).
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace gs {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  if (e == cudaErrorMemoryAllocation) return GSC_ERR_NOMEM;
+  return GSC_ERR_CUDA;
+}
+
+int ensure(gsc_ctx* ctx, GsBuf* b, size_t bytes) {
+  if (bytes <= b->bytes && b->ptr) return GSC_OK;
+  if (b->ptr) {
+    // The old buffer may still be read by queued work on this stream.
+    GS_CK(cudaStreamSynchronize(ctx->stream));
+    GS_CK(cudaFree(b->ptr));
+    b->ptr = nullptr;
+    b->bytes = 0;
+  }
+  size_t want = bytes + bytes / 4 + 256;
+  cudaError_t e = cudaMalloc(&b->ptr, want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    b->ptr = nullptr;
+    e = cudaMalloc(&b->ptr, bytes ? bytes : 256);
+    if (e != cudaSuccess) {
+      b->ptr = nullptr;
+      return cuda_fail(e, "cudaMalloc");
+    }
+    want = bytes ? bytes : 256;
+  }
+  b->bytes = want;
+  return GSC_OK;
+}
+
+int scratch_reserve(gsc_ctx* ctx, size_t bytes) { return ensure(ctx, &ctx->scratch, bytes); }
+
+static float power_cut_of(float alpha_min) {
+  if (!(alpha_min > 0.0f)) return -INFINITY;
+  return (float)(std::log((double)alpha_min) - 1e-3);
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+static int read_u64(gsc_ctx* ctx, const uint64_t* dptr, uint64_t* out) {
+  GS_CK(cudaMemcpyAsync(ctx->pinned, dptr, 8, cudaMemcpyDeviceToHost, ctx->stream));
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  std::memcpy(out, ctx->pinned, 8);
+  return GSC_OK;
+}
+
+static int tile_bits_of(int num_tiles) {
+  int b = 0;
+  while ((1ll << b) < (long long)num_tiles) b++;
+  return b;
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+struct gsc_frame {
+  gsc_ctx* ctx = nullptr;
+  GsBuf splats, block_sums, offsets, total, keys, vals, ranges, image, final_T, last, n_contrib, grad2d;
+  int64_t n = 0, num_keys = 0;
+  int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
+  float* image_ptr = nullptr;  // image the last forward wrote (caller's or frame's)
+  bool has_forward = false;
+};
+
+extern "C" {
+
+GSC_API int gsc_version(void) { return GSC_VERSION; }
+
+GSC_API const char* gsc_last_error(void) { return g_last_error.c_str(); }
+
+GSC_API void gsc_raster_config_default(gsc_raster_config* cfg) {
+  if (!cfg) return;
+  cfg->mode = GSC_MODE_FULL;
+  cfg->sh_degree = 3;
+  cfg->t_stop = 1e-3f;
+  cfg->alpha_min = 1.0f / 255.0f;
+  cfg->alpha_max = 0.99f;
+  cfg->lowpass = 0.3f;
+  cfg->fov_cull = 1.3f;
+  cfg->near_z = 0.01f;
+  cfg->far_z = 1000.0f;
+  cfg->background[0] = cfg->background[1] = cfg->background[2] = 0.0f;
+}
+
+GSC_API int gsc_init(int device, gsc_ctx** out) {
+  GS_REQUIRE(out, "gsc_init: out is null");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    set_error("gsc_init: no CUDA device");
+    return GSC_ERR_NODEVICE;
+  }
+  if (device < 0 || device >= count) {
+    set_error("gsc_init: device index out of range");
+    return GSC_ERR_NODEVICE;
+  }
+  GS_CK(cudaSetDevice(device));
+  gsc_ctx* ctx = new gsc_ctx();
+  ctx->device = device;
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  e = cudaMalloc(&ctx->err, 16);
+  if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, 16);
+  if (e == cudaSuccess) e = cudaMallocHost(&ctx->pinned, 4096);
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(e, "gsc_init");
+    if (ctx->err) cudaFree(ctx->err);
+    delete ctx;
+    return rc;
+  }
+  *out = ctx;
+  return GSC_OK;
+}
+
+GSC_API int gsc_destroy(gsc_ctx* ctx) {
+  if (!ctx) return GSC_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->scratch.ptr) cudaFree(ctx->scratch.ptr);
+  if (ctx->err) cudaFree(ctx->err);
+  if (ctx->pinned) cudaFreeHost(ctx->pinned);
+  delete ctx;
+  return GSC_OK;
+}
+
+GSC_API int gsc_set_stream(gsc_ctx* ctx, void* stream) {
+  GS_REQUIRE(ctx, "gsc_set_stream: null context");
+  ctx->stream = (cudaStream_t)stream;
+  return GSC_OK;
+}
+
+GSC_API int gsc_sync(gsc_ctx* ctx) {
+  GS_REQUIRE(ctx, "gsc_sync: null context");
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  GS_CK(cudaMemcpyAsync(ctx->pinned, ctx->err, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  uint32_t flags;
+  std::memcpy(&flags, ctx->pinned, 4);
+  if (flags) {
+    GS_CK(cudaMemsetAsync(ctx->err, 0, 4, ctx->stream));
+    GS_CK(cudaStreamSynchronize(ctx->stream));
+    if (flags & GS_DEVERR_TIMEOUT) {
+      set_error("a bounded device-side wait gave up (look-back timeout)");
+      return GSC_ERR_TIMEOUT;
+    }
+    set_error("a device-side bounds check failed");
+    return GSC_ERR_CUDA;
+  }
+  return GSC_OK;
+}
+
+GSC_API int gsc_alloc(gsc_ctx* ctx, size_t bytes, void** out) {
+  GS_REQUIRE(ctx && out, "gsc_alloc: null argument");
+  *out = nullptr;
+  cudaError_t e = cudaMalloc(out, bytes ? bytes : 1);
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return cuda_fail(e, "gsc_alloc");
+  }
+  return GSC_OK;
+}
+
+GSC_API int gsc_free(gsc_ctx* ctx, void* ptr) {
+  GS_REQUIRE(ctx, "gsc_free: null context");
+  if (ptr) GS_CK(cudaFree(ptr));
+  return GSC_OK;
+}
+
+GSC_API int gsc_memcpy_h2d(gsc_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  GS_REQUIRE(ctx && (bytes == 0 || (dst && src)), "gsc_memcpy_h2d: null argument");
+  GS_CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  return GSC_OK;
+}
+
+GSC_API int gsc_memcpy_d2h(gsc_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  GS_REQUIRE(ctx && (bytes == 0 || (dst && src)), "gsc_memcpy_d2h: null argument");
+  GS_CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  return GSC_OK;
+}
+
+GSC_API int gsc_memset(gsc_ctx* ctx, void* dst, int value, size_t bytes) {
+  GS_REQUIRE(ctx && (bytes == 0 || dst), "gsc_memset: null argument");
+  GS_CK(cudaMemsetAsync(dst, value, bytes, ctx->stream));
+  return GSC_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Stages
+// ---------------------------------------------------------------------------
+namespace gs {
+
+static int check_gaussians(const gsc_gaussians* g) {
+  GS_REQUIRE(g, "null gaussians");
+  GS_REQUIRE(g->count >= 0 && g->count < (1ll << 31), "gaussian count out of range [0, 2^31)");
+  if (g->count == 0) return GSC_OK;
+  GS_REQUIRE(g->position && g->log_scale && g->rotation && g->logit_opacity && g->sh,
+             "null gaussian parameter pointer");
+  GS_REQUIRE(aligned16(g->rotation) && aligned16(g->sh), "rotation and sh must be 16-byte aligned");
+  return GSC_OK;
+}
+
+static int check_view(const gsc_camera* cam, const gsc_raster_config* cfg) {
+  GS_REQUIRE(cam && cfg, "null camera or config");
+  GS_REQUIRE(cam->width > 0 && cam->height > 0 && cam->width <= 65536 && cam->height <= 65536,
+             "camera width/height out of range");
+  GS_REQUIRE(cfg->mode == GSC_MODE_FULL || cfg->mode == GSC_MODE_REF, "unknown mode");
+  GS_REQUIRE(cfg->sh_degree >= 0 && cfg->sh_degree <= 3, "sh_degree must be 0..3");
+  return GSC_OK;
+}
+
+static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
+                         const gsc_raster_config* cfg, const gsc_projected* o, uint32_t* block_sums) {
+  PreprocessArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.n = g->count;
+  a.pos = g->position; a.log_scale = g->log_scale; a.rot = g->rotation;
+  a.logit_opacity = g->logit_opacity; a.sh = g->sh;
+  a.cam = *cam; a.cfg = *cfg;
+  a.tiles_x = (cam->width + GS_TILE - 1) / GS_TILE;
+  a.tiles_y = (cam->height + GS_TILE - 1) / GS_TILE;
+  a.splats = o->splats; a.block_sums = block_sums;
+  a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
+  a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
+  a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
+  return launch_preprocess(a, ctx->stream);
+}
+
+// Scan the per-block tile counts into offsets and read the total back.
+static int do_scan(gsc_ctx* ctx, int64_t n, const uint32_t* sums, uint64_t* offsets, uint64_t* total,
+                   uint64_t* host_total) {
+  *host_total = 0;
+  if (n == 0) return GSC_OK;
+  int rc = launch_scan_block_sums(sums, (n + 255) / 256, offsets, total, ctx->stream);
+  if (rc) return rc;
+  return read_u64(ctx, total, host_total);
+}
+
+static void fill_fwd(CompositeFwdArgs* a, const float* splats, const uint32_t* vals, const uint32_t* ranges,
+                     int W, int H, const gsc_raster_config* cfg) {
+  std::memset(a, 0, sizeof *a);
+  a->splats = splats; a->vals = vals; a->ranges = ranges;
+  a->width = W; a->height = H;
+  a->tiles_x = (W + GS_TILE - 1) / GS_TILE; a->tiles_y = (H + GS_TILE - 1) / GS_TILE;
+  a->t_stop = cfg->t_stop; a->alpha_min = cfg->alpha_min; a->alpha_max = cfg->alpha_max;
+  a->power_cut = power_cut_of(cfg->alpha_min);
+  for (int c = 0; c < 3; c++) a->bg[c] = cfg->background[c];
+}
+
+static void fill_bwd(CompositeBwdArgs* a, const float* splats, const uint32_t* vals, const uint32_t* ranges,
+                     int W, int H, const gsc_raster_config* cfg) {
+  std::memset(a, 0, sizeof *a);
+  a->splats = splats; a->vals = vals; a->ranges = ranges;
+  a->width = W; a->height = H;
+  a->tiles_x = (W + GS_TILE - 1) / GS_TILE; a->tiles_y = (H + GS_TILE - 1) / GS_TILE;
+  a->alpha_min = cfg->alpha_min; a->alpha_max = cfg->alpha_max;
+  a->power_cut = power_cut_of(cfg->alpha_min);
+  for (int c = 0; c < 3; c++) a->bg[c] = cfg->background[c];
+}
+
+static int do_preprocess_bwd(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
+                             const gsc_raster_config* cfg, const float* grad2d,
+                             const gsc_gaussian_grads* gr, const gsc_grads2d* g2d) {
+  PreprocessBwdArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.n = g->count;
+  a.pos = g->position; a.log_scale = g->log_scale; a.rot = g->rotation;
+  a.logit_opacity = g->logit_opacity; a.sh = g->sh;
+  a.cam = *cam; a.cfg = *cfg;
+  a.grad2d = grad2d;
+  a.g_pos = gr->position; a.g_log_scale = gr->log_scale; a.g_rot = gr->rotation;
+  a.g_logit_opacity = gr->logit_opacity; a.g_sh = gr->sh;
+  if (g2d) {
+    a.d_mean2d = g2d->mean2d; a.d_cov2d = g2d->cov2d; a.d_opacity = g2d->opacity; a.d_colors = g2d->colors;
+  }
+  return launch_preprocess_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream);
+}
+
+static int check_grads(const gsc_gaussian_grads* gr) {
+  GS_REQUIRE(gr && gr->position && gr->log_scale && gr->rotation && gr->logit_opacity && gr->sh,
+             "null gradient pointer");
+  return GSC_OK;
+}
+
+}  // namespace gs
+
+#define GS_TRY(expr)          \
+  do {                        \
+    int _rc = (expr);         \
+    if (_rc != GSC_OK) return _rc; \
+  } while (0)
+
+extern "C" {
+
+GSC_API int gsc_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
+                           const gsc_raster_config* cfg, const gsc_projected* out) {
+  GS_REQUIRE(ctx && out, "gsc_preprocess: null argument");
+  GS_TRY(check_gaussians(g));
+  GS_TRY(check_view(cam, cfg));
+  GS_REQUIRE(g->count == 0 || (out->splats && aligned16(out->splats)),
+             "gsc_preprocess: splats must be non-null and 16-byte aligned");
+  return do_preprocess(ctx, g, cam, cfg, out, nullptr);
+}
+
+GSC_API int gsc_bin(gsc_ctx* ctx, int64_t n, const float* splats, int32_t tiles_x, int32_t tiles_y,
+                    uint64_t* keys, uint32_t* values, int64_t capacity, int64_t* num_keys) {
+  GS_REQUIRE(ctx && num_keys, "gsc_bin: null argument");
+  GS_REQUIRE(n >= 0 && n < (1ll << 31), "gsc_bin: n out of range");
+  GS_REQUIRE(tiles_x > 0 && tiles_y > 0, "gsc_bin: bad tile grid");
+  *num_keys = 0;
+  if (n == 0) return GSC_OK;
+  GS_REQUIRE(splats && aligned16(splats), "gsc_bin: splats must be non-null and 16-byte aligned");
+  const int64_t nb = (n + 255) / 256;
+  GS_TRY(scratch_reserve(ctx, align256(nb * 4) + align256(nb * 8) + 256));
+  uint32_t* sums = (uint32_t*)scratch_base(ctx);
+  uint64_t* offsets = (uint64_t*)(scratch_base(ctx) + align256(nb * 4));
+  uint64_t* total = (uint64_t*)(scratch_base(ctx) + align256(nb * 4) + align256(nb * 8));
+  GS_TRY(launch_block_sums(splats, n, sums, ctx->stream));
+  uint64_t m = 0;
+  GS_TRY(do_scan(ctx, n, sums, offsets, total, &m));
+  *num_keys = (int64_t)m;
+  if ((int64_t)m > capacity) {
+    set_error("gsc_bin: key count " + std::to_string(m) + " exceeds capacity " + std::to_string(capacity));
+    return GSC_ERR_CAPACITY;
+  }
+  if (m == 0) return GSC_OK;
+  GS_REQUIRE(keys && values, "gsc_bin: null keys/values");
+  return launch_emit_keys(splats, n, offsets, tiles_x, tiles_y, keys, values, ctx->stream);
+}
+
+GSC_API int gsc_sort_pairs_u64(gsc_ctx* ctx, uint64_t* keys, uint32_t* values, int64_t n,
+                               int begin_bit, int end_bit) {
+  GS_REQUIRE(ctx, "gsc_sort_pairs_u64: null context");
+  GS_REQUIRE(n >= 0 && n < (1ll << 30), "gsc_sort_pairs_u64: n must be in [0, 2^30)");
+  GS_REQUIRE(begin_bit >= 0 && end_bit <= 64 && begin_bit <= end_bit, "gsc_sort_pairs_u64: bad bit range");
+  if (n <= 1 || begin_bit == end_bit) return GSC_OK;
+  GS_REQUIRE(keys && values, "gsc_sort_pairs_u64: null keys/values");
+  GS_TRY(scratch_reserve(ctx, sort_scratch_bytes(n, begin_bit, end_bit)));
+  return launch_sort_pairs(ctx, keys, values, n, begin_bit, end_bit, scratch_base(ctx));
+}
+
+GSC_API int gsc_tile_ranges(gsc_ctx* ctx, const uint64_t* sorted_keys, int64_t n, int32_t num_tiles,
+                            uint32_t* ranges) {
+  GS_REQUIRE(ctx && ranges && num_tiles > 0, "gsc_tile_ranges: bad argument");
+  GS_REQUIRE(n >= 0 && (n == 0 || sorted_keys), "gsc_tile_ranges: bad keys");
+  return launch_tile_ranges(sorted_keys, n, num_tiles, ranges, ctx->stream);
+}
+
+GSC_API int gsc_composite_forward(gsc_ctx* ctx, const float* splats, const uint32_t* values,
+                                  const uint32_t* ranges, int32_t width, int32_t height,
+                                  const gsc_raster_config* cfg, float* image, uint32_t* n_contrib,
+                                  float* final_T, uint32_t* last) {
+  GS_REQUIRE(ctx && cfg && ranges && image && width > 0 && height > 0, "gsc_composite_forward: bad argument");
+  GS_REQUIRE(!splats || aligned16(splats), "gsc_composite_forward: splats must be 16-byte aligned");
+  CompositeFwdArgs a;
+  fill_fwd(&a, splats, values, ranges, width, height, cfg);
+  a.image = image; a.n_contrib = n_contrib; a.final_T = final_T; a.last = last;
+  return launch_composite_fwd(a, ctx->stream);
+}
+
+GSC_API int gsc_composite_backward(gsc_ctx* ctx, const float* splats, const uint32_t* values,
+                                   const uint32_t* ranges, int32_t width, int32_t height,
+                                   const gsc_raster_config* cfg, const float* dL_dimage,
+                                   const float* image, const float* target, float l1_scale,
+                                   const float* final_T, const uint32_t* last, float* grad2d,
+                                   float* loss_sum) {
+  GS_REQUIRE(ctx && cfg && ranges && final_T && grad2d && width > 0 && height > 0,
+             "gsc_composite_backward: bad argument");
+  GS_REQUIRE(target ? (image != nullptr) : (dL_dimage != nullptr),
+             "gsc_composite_backward: need dL_dimage, or image and target");
+  GS_REQUIRE(cfg->mode != GSC_MODE_FULL || last, "gsc_composite_backward: FULL mode needs `last`");
+  CompositeBwdArgs a;
+  fill_bwd(&a, splats, values, ranges, width, height, cfg);
+  a.dL_dimage = dL_dimage; a.image = image; a.target = target; a.l1_scale = l1_scale;
+  a.final_T = final_T; a.last = last; a.grad2d = grad2d; a.loss_sum = loss_sum;
+  return launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream);
+}
+
+GSC_API int gsc_preprocess_backward(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
+                                    const gsc_raster_config* cfg, const float* grad2d,
+                                    const gsc_gaussian_grads* grads, const gsc_grads2d* g2d) {
+  GS_REQUIRE(ctx, "gsc_preprocess_backward: null context");
+  GS_TRY(check_gaussians(g));
+  GS_TRY(check_view(cam, cfg));
+  GS_TRY(check_grads(grads));
+  GS_REQUIRE(g->count == 0 || grad2d, "gsc_preprocess_backward: null grad2d");
+  return do_preprocess_bwd(ctx, g, cam, cfg, grad2d, grads, g2d);
+}
+
+GSC_API int gsc_l1_loss_grad(gsc_ctx* ctx, const float* pred, const float* target, int64_t numel,
+                             float scale, float* grad, float* loss_sum) {
+  GS_REQUIRE(ctx && numel >= 0 && (numel == 0 || (pred && target && grad)), "gsc_l1_loss_grad: bad argument");
+  return launch_l1(pred, target, numel, scale, grad, loss_sum, ctx->num_sms, ctx->stream);
+}
+
+GSC_API int gsc_adam_step(gsc_ctx* ctx, const gsc_adam_group* groups, int32_t ngroups, float beta1,
+                          float beta2, float eps, int32_t step, float grad_scale) {
+  GS_REQUIRE(ctx && groups && ngroups > 0 && ngroups <= kMaxAdamGroups, "gsc_adam_step: 1..8 groups");
+  GS_REQUIRE(step >= 1, "gsc_adam_step: step must be >= 1");
+  AdamArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.ngroups = ngroups;
+  a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.grad_scale = grad_scale;
+  // 1 - beta^t evaluated in double and rounded once.
+  a.bc1 = (float)(1.0 - std::pow((double)beta1, (double)step));
+  a.bc2 = (float)(1.0 - std::pow((double)beta2, (double)step));
+  int64_t run = 0;
+  for (int i = 0; i < ngroups; i++) {
+    const gsc_adam_group& G = groups[i];
+    GS_REQUIRE(G.numel >= 0 && (G.numel == 0 || (G.param && G.grad && G.m && G.v)), "gsc_adam_step: bad group");
+    AdamGroupDev& d = a.g[i];
+    d.param = G.param; d.grad = G.grad; d.m = G.m; d.v = G.v; d.numel = G.numel;
+    d.lr = G.lr; d.weight_decay = G.weight_decay;
+    d.decay = 1.0f - G.lr * G.weight_decay;
+    d.vec = aligned16(G.param) && aligned16(G.grad) && aligned16(G.m) && aligned16(G.v);
+    run += (G.numel + 3) / 4;
+    a.chunk_end[i] = run;
+  }
+  return launch_adam(a, ctx->stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Whole-view orchestration
+// ---------------------------------------------------------------------------
+extern "C" {
+
+GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out) {
+  GS_REQUIRE(ctx && out, "gsc_frame_create: null argument");
+  gsc_frame* f = new gsc_frame();
+  f->ctx = ctx;
+  *out = f;
+  return GSC_OK;
+}
+
+GSC_API int gsc_frame_destroy(gsc_frame* f) {
+  if (!f) return GSC_OK;
+  cudaStreamSynchronize(f->ctx->stream);
+  GsBuf* bufs[] = {&f->splats, &f->block_sums, &f->offsets, &f->total, &f->keys, &f->vals, &f->ranges,
+                   &f->image, &f->final_T, &f->last, &f->n_contrib, &f->grad2d};
+  for (GsBuf* b : bufs)
+    if (b->ptr) cudaFree(b->ptr);
+  delete f;
+  return GSC_OK;
+}
+
+GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g,
+                                  const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
+                                  uint32_t* n_contrib, float* final_T, int64_t* num_rendered) {
+  GS_REQUIRE(ctx && f && f->ctx == ctx, "gsc_rasterize_forward: bad context/frame");
+  GS_TRY(check_gaussians(g));
+  GS_TRY(check_view(cam, cfg));
+  const int64_t n = g->count;
+  const int W = cam->width, H = cam->height;
+  const int tx = (W + GS_TILE - 1) / GS_TILE, ty = (H + GS_TILE - 1) / GS_TILE;
+  const int64_t nb = (n + 255) / 256;
+  const size_t npix = (size_t)W * H;
+  f->has_forward = false;
+  f->n = n; f->width = W; f->height = H; f->tiles_x = tx; f->tiles_y = ty;
+  GS_TRY(ensure(ctx, &f->splats, (size_t)n * 48));
+  GS_TRY(ensure(ctx, &f->block_sums, (size_t)nb * 4));
+  GS_TRY(ensure(ctx, &f->offsets, (size_t)nb * 8));
+  GS_TRY(ensure(ctx, &f->total, 8));
+  GS_TRY(ensure(ctx, &f->ranges, (size_t)tx * ty * 8));
+  GS_TRY(ensure(ctx, &f->final_T, npix * 4));
+  GS_TRY(ensure(ctx, &f->last, npix * 4));
+  GS_TRY(ensure(ctx, &f->n_contrib, npix * 4));
+  if (!image) {
+    GS_TRY(ensure(ctx, &f->image, npix * 12));
+    image = (float*)f->image.ptr;
+  }
+  f->image_ptr = image;
+  float* splats = (float*)f->splats.ptr;
+
+  gsc_projected proj;
+  std::memset(&proj, 0, sizeof proj);
+  proj.splats = splats;
+  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, (uint32_t*)f->block_sums.ptr));
+  uint64_t m = 0;
+  GS_TRY(do_scan(ctx, n, (uint32_t*)f->block_sums.ptr, (uint64_t*)f->offsets.ptr, (uint64_t*)f->total.ptr, &m));
+  if (m >= (1ull << 30)) {
+    set_error("gsc_rasterize_forward: " + std::to_string(m) + " keys exceed the 2^30 limit");
+    return GSC_ERR_CAPACITY;
+  }
+  f->num_keys = (int64_t)m;
+  if (num_rendered) *num_rendered = (int64_t)m;
+  GS_TRY(ensure(ctx, &f->keys, (size_t)m * 8 + 8));
+  GS_TRY(ensure(ctx, &f->vals, (size_t)m * 4 + 4));
+  uint64_t* keys = (uint64_t*)f->keys.ptr;
+  uint32_t* vals = (uint32_t*)f->vals.ptr;
+  if (m) {
+    GS_TRY(launch_emit_keys(splats, n, (const uint64_t*)f->offsets.ptr, tx, ty, keys, vals, ctx->stream));
+    const int end_bit = 32 + tile_bits_of(tx * ty);
+    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes((int64_t)m, 0, end_bit)));
+    GS_TRY(launch_sort_pairs(ctx, keys, vals, (int64_t)m, 0, end_bit, scratch_base(ctx)));
+  }
+  GS_TRY(launch_tile_ranges(keys, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
+  CompositeFwdArgs a;
+  fill_fwd(&a, splats, vals, (const uint32_t*)f->ranges.ptr, W, H, cfg);
+  a.image = image;
+  a.final_T = (float*)f->final_T.ptr;
+  a.last = (uint32_t*)f->last.ptr;
+  a.n_contrib = (uint32_t*)f->n_contrib.ptr;
+  GS_TRY(launch_composite_fwd(a, ctx->stream));
+  if (n_contrib)
+    GS_CK(cudaMemcpyAsync(n_contrib, f->n_contrib.ptr, npix * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  if (final_T)
+    GS_CK(cudaMemcpyAsync(final_T, f->final_T.ptr, npix * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  f->has_forward = true;
+  return GSC_OK;
+}
+
+GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g,
+                                   const gsc_camera* cam, const gsc_raster_config* cfg,
+                                   const float* dL_dimage, const float* target, float l1_scale,
+                                   float* loss_sum, const gsc_gaussian_grads* grads,
+                                   const gsc_grads2d* g2d) {
+  GS_REQUIRE(ctx && f && f->ctx == ctx, "gsc_rasterize_backward: bad context/frame");
+  GS_REQUIRE(f->has_forward, "gsc_rasterize_backward: no forward on this frame");
+  GS_TRY(check_gaussians(g));
+  GS_TRY(check_view(cam, cfg));
+  GS_TRY(check_grads(grads));
+  GS_REQUIRE(g->count == f->n && cam->width == f->width && cam->height == f->height,
+             "gsc_rasterize_backward: gaussians/camera differ from the frame's forward");
+  GS_REQUIRE((dL_dimage != nullptr) != (target != nullptr),
+             "gsc_rasterize_backward: exactly one of dL_dimage / target");
+  const int64_t n = f->n;
+  GS_TRY(ensure(ctx, &f->grad2d, (size_t)n * 36 + 4));
+  float* grad2d = (float*)f->grad2d.ptr;
+  GS_CK(cudaMemsetAsync(grad2d, 0, (size_t)n * 36, ctx->stream));
+  CompositeBwdArgs a;
+  fill_bwd(&a, (const float*)f->splats.ptr, (const uint32_t*)f->vals.ptr, (const uint32_t*)f->ranges.ptr,
+           f->width, f->height, cfg);
+  a.dL_dimage = dL_dimage;
+  a.image = f->image_ptr;
+  a.target = target;
+  a.l1_scale = l1_scale;
+  a.final_T = (const float*)f->final_T.ptr;
+  a.last = (const uint32_t*)f->last.ptr;
+  a.grad2d = grad2d;
+  a.loss_sum = loss_sum;
+  GS_TRY(launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream));
+  return do_preprocess_bwd(ctx, g, cam, cfg, grad2d, grads, g2d);
+}
+
+GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {
+  GS_REQUIRE(f && ptr, "gsc_frame_get: null argument");
+  const int64_t npix = (int64_t)f->width * f->height;
+  void* p = nullptr;
+  int64_t c = 0;
+  switch (which) {
+    case GSC_FRAME_SPLATS: p = f->splats.ptr; c = f->n * 12; break;
+    case GSC_FRAME_KEYS: p = f->keys.ptr; c = f->num_keys; break;
+    case GSC_FRAME_VALUES: p = f->vals.ptr; c = f->num_keys; break;
+    case GSC_FRAME_RANGES: p = f->ranges.ptr; c = (int64_t)f->tiles_x * f->tiles_y * 2; break;
+    case GSC_FRAME_IMAGE: p = f->image_ptr; c = npix * 3; break;
+    case GSC_FRAME_FINAL_T: p = f->final_T.ptr; c = npix; break;
+    case GSC_FRAME_LAST: p = f->last.ptr; c = npix; break;
+    case GSC_FRAME_N_CONTRIB: p = f->n_contrib.ptr; c = npix; break;
+    case GSC_FRAME_GRAD2D: p = f->grad2d.ptr; c = f->n * 9; break;
+    default: set_error("gsc_frame_get: unknown item"); return GSC_ERR_INVALID;
+  }
+  *ptr = p;
+  if (count) *count = c;
+  return GSC_OK;
+}
+
+}  // extern "C"

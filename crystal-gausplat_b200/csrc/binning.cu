@@ -1,0 +1,167 @@
+// binning.cu — tile binning: exact key allocation and canonical key emission
+// (replacing create_tile_keys, src/metal/kernels/gaussian.metal:315-357, whose
+// atomic slot counter gives a nondeterministic order and has no bound check),
+// and tile ranges (init_tile_ranges + compute_tile_ranges,
+// src/metal/kernels/radix_sort.metal:288-324).
+//
+// Allocation: preprocess leaves one tiles_touched sum per 256-Gaussian block;
+// scan_block_sums_kernel turns them into 64-bit exclusive offsets and the
+// total. Emission: each block owns the contiguous key range
+// [offset[b], offset[b] + sum[b]) and fills it with coalesced stores, every
+// thread locating the Gaussian of its output slot by binary search over the
+// block's inclusive scan. Canonical order: Gaussian id, then ty, then tx.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace gs {
+
+// Inclusive scan of one u32 per thread over a 256-thread block.
+__device__ __forceinline__ uint32_t block_incl_scan_256(uint32_t v, uint32_t* s_warp) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t t = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += t;
+  }
+  if (lane == 31) s_warp[w] = v;
+  __syncthreads();
+  uint32_t add = 0;
+  for (int k = 0; k < w; k++) add += s_warp[k];
+  __syncthreads();
+  return v + add;
+}
+
+__global__ void __launch_bounds__(1024) scan_block_sums_kernel(const uint32_t* sums, int64_t nb,
+                                                                uint64_t* offsets, uint64_t* total) {
+  __shared__ uint64_t s_warp[32];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int64_t chunk = (nb + 1023) / 1024;
+  const int64_t lo = min(nb, (int64_t)tid * chunk), hi = min(nb, lo + chunk);
+  uint64_t mine = 0;
+  for (int64_t k = lo; k < hi; k++) mine += sums[k];
+  uint64_t v = mine;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint64_t t = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += t;
+  }
+  if (lane == 31) s_warp[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    uint64_t x = s_warp[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      uint64_t t = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += t;
+    }
+    s_warp[lane] = x;
+  }
+  __syncthreads();
+  uint64_t run = (v - mine) + (w > 0 ? s_warp[w - 1] : 0);
+  for (int64_t k = lo; k < hi; k++) {
+    offsets[k] = run;
+    run += sums[k];
+  }
+  if (tid == 1023) *total = s_warp[31];
+}
+
+__global__ void __launch_bounds__(256) emit_keys_kernel(const float4* __restrict__ splats, int64_t n,
+                                                        const uint64_t* __restrict__ offsets,
+                                                        int tiles_x, int tiles_y,
+                                                        uint64_t* __restrict__ keys,
+                                                        uint32_t* __restrict__ vals) {
+  __shared__ uint32_t s_incl[256];
+  __shared__ int s_x0[256], s_y0[256], s_wx[256];
+  __shared__ uint32_t s_depth[256];
+  __shared__ uint32_t s_warp[8];
+  const int64_t base = (int64_t)blockIdx.x * 256;
+  const int64_t i = base + threadIdx.x;
+  uint32_t t = 0;
+  if (i < n) {
+    const float4 s0 = splats[i * 3], s2 = splats[i * 3 + 2];
+    t = __float_as_uint(s2.w);
+    if (t) {
+      int x0, x1, y0, y1;
+      tile_bounds(s0.x, s0.y, s2.z, tiles_x, tiles_y, &x0, &x1, &y0, &y1);
+      s_x0[threadIdx.x] = x0;
+      s_y0[threadIdx.x] = y0;
+      s_wx[threadIdx.x] = x1 - x0 + 1;
+      s_depth[threadIdx.x] = __float_as_uint(s2.y);
+    }
+  }
+  uint32_t incl = block_incl_scan_256(t, s_warp);
+  s_incl[threadIdx.x] = incl;
+  __syncthreads();
+  const uint32_t total = s_incl[255];
+  const uint64_t out = offsets[blockIdx.x];
+  for (uint32_t k = threadIdx.x; k < total; k += 256) {
+    int lo = 0, hi = 255;  // smallest j with s_incl[j] > k
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if (s_incl[mid] > k) hi = mid; else lo = mid + 1;
+    }
+    const uint32_t excl = lo ? s_incl[lo - 1] : 0u;
+    const uint32_t local = k - excl;
+    const int wx = s_wx[lo];
+    const int ty = s_y0[lo] + (int)(local / (uint32_t)wx);
+    const int tx = s_x0[lo] + (int)(local % (uint32_t)wx);
+    const uint64_t tile = (uint64_t)(uint32_t)(ty * tiles_x + tx);
+    keys[out + k] = (tile << 32) | (uint64_t)s_depth[lo];
+    vals[out + k] = (uint32_t)(base + lo);
+  }
+}
+
+__global__ void __launch_bounds__(256) tile_ranges_kernel(const uint64_t* __restrict__ keys, int64_t n,
+                                                          uint32_t num_tiles, uint32_t* __restrict__ ranges) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t t = (uint32_t)(keys[i] >> 32);
+  const uint32_t prev = i > 0 ? (uint32_t)(keys[i - 1] >> 32) : 0xFFFFFFFFu;
+  const uint32_t next = i < n - 1 ? (uint32_t)(keys[i + 1] >> 32) : 0xFFFFFFFFu;
+  if (t != prev && t < num_tiles) ranges[(size_t)t * 2] = (uint32_t)i;
+  if (t != next && t < num_tiles) ranges[(size_t)t * 2 + 1] = (uint32_t)(i + 1);
+}
+
+__global__ void __launch_bounds__(256) block_sums_kernel(const float4* __restrict__ splats, int64_t n,
+                                                         uint32_t* __restrict__ sums) {
+  __shared__ uint32_t s_warp[8];
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  uint32_t t = i < n ? __float_as_uint(splats[i * 3 + 2].w) : 0u;
+  uint32_t incl = block_incl_scan_256(t, s_warp);
+  if (threadIdx.x == 255) sums[blockIdx.x] = incl;
+}
+
+int launch_block_sums(const float* splats, int64_t n, uint32_t* sums, cudaStream_t stream) {
+  if (n == 0) return GSC_OK;
+  block_sums_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(splats), n, sums);
+  GS_CK_LAUNCH("block_sums_kernel");
+  return GSC_OK;
+}
+
+int launch_scan_block_sums(const uint32_t* sums, int64_t nb, uint64_t* offsets, uint64_t* total,
+                           cudaStream_t stream) {
+  scan_block_sums_kernel<<<1, 1024, 0, stream>>>(sums, nb, offsets, total);
+  GS_CK_LAUNCH("scan_block_sums_kernel");
+  return GSC_OK;
+}
+
+int launch_emit_keys(const float* splats, int64_t n, const uint64_t* offsets, int tiles_x,
+                     int tiles_y, uint64_t* keys, uint32_t* vals, cudaStream_t stream) {
+  if (n == 0) return GSC_OK;
+  emit_keys_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(splats), n, offsets, tiles_x, tiles_y, keys, vals);
+  GS_CK_LAUNCH("emit_keys_kernel");
+  return GSC_OK;
+}
+
+int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint32_t* ranges,
+                       cudaStream_t stream) {
+  GS_CK(cudaMemsetAsync(ranges, 0, sizeof(uint32_t) * 2 * (size_t)num_tiles, stream));
+  if (n == 0) return GSC_OK;
+  tile_ranges_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(keys, n, (uint32_t)num_tiles, ranges);
+  GS_CK_LAUNCH("tile_ranges_kernel");
+  return GSC_OK;
+}
+
+}  // namespace gs

@@ -1,0 +1,146 @@
+// common.cuh — shared device helpers and the context layout of libgsplat_cuda.so.
+//
+// Floating-point contract (all kernels): built with --fmad=false,
+// -prec-div=true, -prec-sqrt=true, -ftz=false, so every fp32 expression is
+// evaluated as written with IEEE rounding; the only fused operations are
+// explicit __fmaf_rn calls. The exponential is gs_expf below, not expf, so
+// the results of preprocess, binning and forward compositing are a pure
+// function of the documented operation order.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/gsplat_cuda.h"
+
+#define GS_TILE 16
+#define GS_TILE_PIXELS 256
+
+// Device error word bits (gsc_ctx::err), read back by gsc_sync.
+#define GS_DEVERR_TIMEOUT 1u
+#define GS_DEVERR_BOUNDS 2u
+
+namespace gs {
+
+constexpr float kShC0 = 0.28209479177387814f;
+constexpr float kShC1 = 0.4886025119029199f;
+
+struct ShConsts {
+  float c2[5];
+  float c3[7];
+};
+
+// Spherical-harmonics constants, src/metal/kernels/gaussian.metal:11-28.
+__device__ __forceinline__ ShConsts sh_consts() {
+  ShConsts k = {{1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+                 -1.0925484305920792f, 0.5462742152960396f},
+                {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+                 0.3731763325901154f, -0.4570457994644658f, 1.445305721320277f,
+                 -0.5900435899266435f}};
+  return k;
+}
+
+__device__ __forceinline__ float pow2i(int j) { return __int_as_float((j + 127) << 23); }
+
+// exp(x) in fp32: Cody & Waite (1980) reduction x = k ln2 + r with ln 2
+// split into a 16-bit head and a tail, e^r by its Taylor series to degree 7
+// in Horner form with fused multiply-adds, then an exact scale by 2^k
+// (two steps in the subnormal range). Max error about 1 ulp over the
+// normal range; identical results on any IEEE target that runs the same
+// operations.
+__device__ __forceinline__ float gs_expf(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x < -103.97208404541015625f) return 0.0f;
+  float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(-k, 0.693145751953125f, x);
+  r = __fmaf_rn(-k, 1.428606765330187045e-06f, r);
+  float p = 1.98412698412698412698e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666666666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666666666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ki = (int)k;
+  if (ki > 127) return p * pow2i(127) * pow2i(ki - 127);
+  if (ki < -126) return p * pow2i(ki + 64) * pow2i(-64);
+  return p * pow2i(ki);
+}
+
+__device__ __forceinline__ float gs_sigmoid(float x) { return 1.0f / (1.0f + gs_expf(-x)); }
+
+// C `int(f)` (truncation toward zero) after saturating to +-1e9, so that
+// out-of-range values are defined the same way on every target.
+__device__ __forceinline__ int trunc_sat(float f) {
+  f = fmaxf(f, -1.0e9f);
+  f = fminf(f, 1.0e9f);
+  return (int)f;
+}
+
+// Tile bounds of a splat, src/metal/kernels/gaussian.metal:338-341 with
+// tiles_x = ceil(W/16), tiles_y = ceil(H/16).
+__device__ __forceinline__ void tile_bounds(float px, float py, float r, int tiles_x, int tiles_y,
+                                            int* x0, int* x1, int* y0, int* y1) {
+  *x0 = max(0, trunc_sat(px - r) / GS_TILE);
+  *x1 = min(tiles_x - 1, trunc_sat(px + r) / GS_TILE);
+  *y0 = max(0, trunc_sat(py - r) / GS_TILE);
+  *y1 = min(tiles_y - 1, trunc_sat(py + r) / GS_TILE);
+}
+
+}  // namespace gs
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+// A device allocation that grows on demand and never shrinks.
+struct GsBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+struct gsc_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  GsBuf scratch;              // per-call temporary storage (sort double buffer, ...)
+  uint32_t* err = nullptr;    // device error word
+  void* pinned = nullptr;     // 4 KB pinned host staging for small readbacks
+};
+
+namespace gs {
+
+void set_error(const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+int ensure(gsc_ctx* ctx, GsBuf* b, size_t bytes);
+// Scratch carve-out: returns a 256-byte-aligned pointer inside ctx->scratch,
+// growing it (which invalidates earlier carve-outs of the same call) first.
+int scratch_reserve(gsc_ctx* ctx, size_t bytes);
+inline char* scratch_base(gsc_ctx* ctx) { return (char*)ctx->scratch.ptr; }
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace gs
+
+#define GS_CK(call)                                            \
+  do {                                                         \
+    cudaError_t _e = (call);                                   \
+    if (_e != cudaSuccess) return gs::cuda_fail(_e, #call);    \
+  } while (0)
+
+#define GS_CK_LAUNCH(name)                                     \
+  do {                                                         \
+    cudaError_t _e = cudaGetLastError();                       \
+    if (_e != cudaSuccess) return gs::cuda_fail(_e, name);     \
+  } while (0)
+
+#define GS_REQUIRE(cond, msg)                                  \
+  do {                                                         \
+    if (!(cond)) {                                             \
+      gs::set_error(msg);                                      \
+      return GSC_ERR_INVALID;                                  \
+    }                                                          \
+  } while (0)

@@ -1,0 +1,243 @@
+// composite.cu — per-tile alpha compositing, forward and backward.
+//
+// Forward replaces rasterize_tile (src/metal/kernels/gaussian.metal:364-445)
+// over EVERY 16x16 tile (the reference's dispatch covers only
+// ceil(tx/16) x ceil(ty/16) of them, rasterizer.cr:332). One CTA of 256
+// threads per tile, one pixel per thread; the tile's sorted Gaussians are
+// staged 256 at a time into shared memory as packed records (two float4 and
+// one float per Gaussian) and every thread walks the batch front to back while
+// T > t_stop. The CTA leaves as soon as every pixel is done.
+//
+// Backward replaces rasterize_backward (gaussian.metal:452-567): batches are
+// staged back to front; per Gaussian each thread forms its 9 partials, a warp
+// butterfly reduces them and lane 0 issues the global atomics. The L1 loss
+// gradient (src/ops/loss.cr:33-57) is fused into the per-pixel load.
+//
+// Skip test: a Gaussian with power < power_cut has o*G < alpha_min for every
+// opacity <= 1, so it is rejected before the exponential; power_cut is
+// ln(alpha_min) minus a margin far above the exponential's error, so the
+// accepted set is exactly the one the full test gives.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace gs {
+
+__global__ void __launch_bounds__(256) composite_fwd_kernel(CompositeFwdArgs a) {
+  __shared__ float4 s0[256];
+  __shared__ float4 s1[256];
+  __shared__ float s2[256];
+  const int tile = blockIdx.x;
+  const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
+  const int tid = threadIdx.x;
+  const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4);
+  const bool inside = x < a.width && y < a.height;
+  const float pxf = (float)x + 0.5f, pyf = (float)y + 0.5f;
+  const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
+  const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
+  const float t_stop = a.t_stop, amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
+
+  float T = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f;
+  uint32_t cnt = 0, lst = 0;
+  bool done = !inside;
+  for (uint32_t b = start; b < end; b += 256) {
+    if (__syncthreads_count(done) == 256) break;
+    const uint32_t idx = b + tid;
+    if (idx < end) {
+      const uint32_t gid = a.vals[idx];
+      s0[tid] = splats[(size_t)gid * 3];
+      s1[tid] = splats[(size_t)gid * 3 + 1];
+      s2[tid] = splats[(size_t)gid * 3 + 2].x;
+    }
+    __syncthreads();
+    if (!done) {
+      const int m = (int)min(256u, end - b);
+      for (int j = 0; j < m; j++) {
+        if (!(T > t_stop)) break;
+        const float4 g0 = s0[j];
+        const float dx = pxf - g0.x, dy = pyf - g0.y;
+        const float4 g1 = s1[j];
+        const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
+        if (power > 0.0f || power < cut) continue;
+        const float G = gs_expf(power);
+        const float alpha = fminf(amax, g1.y * G);
+        if (alpha < amin) continue;
+        C0 += T * alpha * g1.z;
+        C1 += T * alpha * g1.w;
+        C2 += T * alpha * s2[j];
+        T *= (1.0f - alpha);
+        cnt++;
+        lst = b + j - start + 1;
+      }
+      if (!(T > t_stop)) done = true;
+    }
+  }
+  if (!inside) return;
+  const size_t pix = (size_t)y * a.width + x;
+  a.image[pix * 3 + 0] = C0 + T * a.bg[0];
+  a.image[pix * 3 + 1] = C1 + T * a.bg[1];
+  a.image[pix * 3 + 2] = C2 + T * a.bg[2];
+  if (a.n_contrib) a.n_contrib[pix] = cnt;
+  if (a.final_T) a.final_T[pix] = T;
+  if (a.last) a.last[pix] = lst;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+template <bool FULL, bool L1>
+__global__ void __launch_bounds__(256) composite_bwd_kernel(CompositeBwdArgs a) {
+  __shared__ float4 s0[256];
+  __shared__ float4 s1[256];
+  __shared__ float s2[256];
+  __shared__ uint32_t s_gid[256];
+  __shared__ uint32_t s_hi;
+  __shared__ float s_loss[8];
+  const int tile = blockIdx.x;
+  const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4);
+  const bool inside = x < a.width && y < a.height;
+  const float pxf = (float)x + 0.5f, pyf = (float)y + 0.5f;
+  const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
+  const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
+  const float amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
+  const size_t pix = inside ? (size_t)y * a.width + x : 0;
+
+  float g[3] = {0.0f, 0.0f, 0.0f};
+  float loss = 0.0f;
+  float T = 1.0f;
+  uint32_t my_hi = start;
+  if (inside) {
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+      if (L1) {
+        const float diff = a.image[pix * 3 + c] - a.target[pix * 3 + c];
+        const float sg = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+        g[c] = sg * a.l1_scale;
+        loss += fabsf(diff) * a.l1_scale;
+      } else {
+        g[c] = a.dL_dimage[pix * 3 + c];
+      }
+    }
+    T = a.final_T[pix];
+    my_hi = FULL ? start + a.last[pix] : end;
+  }
+  float acc[3] = {a.bg[0] * T, a.bg[1] * T, a.bg[2] * T};
+
+  if (L1 && a.loss_sum) {
+    float l = warp_sum(loss);
+    if (lane == 0) s_loss[tid >> 5] = l;
+  }
+  if (tid == 0) s_hi = start;
+  __syncthreads();
+  if (L1 && a.loss_sum && tid == 0) {
+    float t = 0.0f;
+    for (int w = 0; w < 8; w++) t += s_loss[w];
+    if (t != 0.0f) atomicAdd(a.loss_sum, t);
+  }
+  if (FULL) atomicMax(&s_hi, my_hi);
+  __syncthreads();
+  const uint32_t hi = FULL ? s_hi : end;
+
+  for (int64_t bend = hi; bend > (int64_t)start; bend -= 256) {
+    const int64_t bstart = max((int64_t)start, bend - 256);
+    const int m = (int)(bend - bstart);
+    __syncthreads();
+    if (tid < m) {
+      const uint32_t gid = a.vals[bend - 1 - tid];
+      s_gid[tid] = gid;
+      s0[tid] = splats[(size_t)gid * 3];
+      s1[tid] = splats[(size_t)gid * 3 + 1];
+      s2[tid] = splats[(size_t)gid * 3 + 2].x;
+    }
+    __syncthreads();
+    for (int j = 0; j < m; j++) {
+      const uint32_t idx = (uint32_t)(bend - 1 - j);
+      float v[9];
+#pragma unroll
+      for (int k = 0; k < 9; k++) v[k] = 0.0f;
+      bool ok = inside && idx < my_hi;
+      if (ok) {
+        const float4 g0 = s0[j];
+        const float4 g1 = s1[j];
+        const float dx = pxf - g0.x, dy = pyf - g0.y;
+        const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
+        ok = !(power > 0.0f || power < cut);
+        float G = 0.0f, alpha = 0.0f;
+        if (ok) {
+          G = gs_expf(power);
+          alpha = fminf(amax, g1.y * G);
+          ok = !(alpha < amin);
+        }
+        if (ok) {
+          const float o = g1.y;
+          const float c[3] = {g1.z, g1.w, s2[j]};
+          const float T_before = T / (1.0f - alpha);
+#pragma unroll
+          for (int k = 0; k < 3; k++) v[6 + k] = T_before * alpha * g[k];
+          float dL_dalpha = 0.0f;
+#pragma unroll
+          for (int k = 0; k < 3; k++) dL_dalpha += (T_before * (c[k] - acc[k] / T)) * g[k];
+          float dL_dG, dL_do;
+          if (FULL && !(o * G <= amax)) {
+            dL_dG = 0.0f;
+            dL_do = 0.0f;
+          } else {
+            dL_dG = dL_dalpha * o;
+            dL_do = dL_dalpha * G;
+          }
+          const float dL_dpower = dL_dG * G;
+          v[0] = dL_dpower * (g0.z * dx + g0.w * dy);
+          v[1] = dL_dpower * (g0.w * dx + g1.x * dy);
+          if (FULL) {
+            v[2] = dL_dpower * (-0.5f * dx * dx);
+            v[3] = dL_dpower * (-dx * dy);
+            v[4] = dL_dpower * (-0.5f * dy * dy);
+          }
+          v[5] = dL_do;
+          T = T_before;
+#pragma unroll
+          for (int k = 0; k < 3; k++) {
+            const float contrib = T_before * alpha * c[k];
+            acc[k] = FULL ? acc[k] + contrib : acc[k] - contrib;
+          }
+        }
+      }
+      if (__any_sync(0xffffffffu, ok)) {
+#pragma unroll
+        for (int k = 0; k < 9; k++) v[k] = warp_sum(v[k]);
+        if (lane == 0) {
+          float* gd = a.grad2d + (size_t)s_gid[j] * 9;
+#pragma unroll
+          for (int k = 0; k < 9; k++)
+            if (v[k] != 0.0f) atomicAdd(gd + k, v[k]);
+        }
+      }
+    }
+  }
+}
+
+int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream) {
+  const int tiles = a.tiles_x * a.tiles_y;
+  if (tiles == 0) return GSC_OK;
+  composite_fwd_kernel<<<tiles, 256, 0, stream>>>(a);
+  GS_CK_LAUNCH("composite_fwd_kernel");
+  return GSC_OK;
+}
+
+int launch_composite_bwd(const CompositeBwdArgs& a, bool full, cudaStream_t stream) {
+  const int tiles = a.tiles_x * a.tiles_y;
+  if (tiles == 0) return GSC_OK;
+  const bool l1 = a.target != nullptr;
+  if (full && l1) composite_bwd_kernel<true, true><<<tiles, 256, 0, stream>>>(a);
+  else if (full) composite_bwd_kernel<true, false><<<tiles, 256, 0, stream>>>(a);
+  else if (l1) composite_bwd_kernel<false, true><<<tiles, 256, 0, stream>>>(a);
+  else composite_bwd_kernel<false, false><<<tiles, 256, 0, stream>>>(a);
+  GS_CK_LAUNCH("composite_bwd_kernel");
+  return GSC_OK;
+}
+
+}  // namespace gs

@@ -1,0 +1,120 @@
+// kernels.cuh — kernel argument blocks and launchers (internal).
+#pragma once
+#include "common.cuh"
+
+namespace gs {
+
+struct PreprocessArgs {
+  int64_t n;
+  const float* pos;
+  const float* log_scale;
+  const float* rot;
+  const float* logit_opacity;
+  const float* sh;
+  gsc_camera cam;
+  gsc_raster_config cfg;
+  int tiles_x, tiles_y;
+  float* splats;
+  uint32_t* block_sums;  // one per 256 Gaussians, may be null
+  float* mean2d;
+  float* cov2d;
+  float* conic;
+  float* depth;
+  float* radius;
+  float* colors;
+  float* opacity;
+  uint32_t* tiles_touched;
+  float* cov3d;
+};
+
+struct CompositeFwdArgs {
+  const float* splats;
+  const uint32_t* vals;
+  const uint32_t* ranges;
+  int width, height, tiles_x, tiles_y;
+  float t_stop, alpha_min, alpha_max, power_cut;
+  float bg[3];
+  float* image;
+  uint32_t* n_contrib;
+  float* final_T;
+  uint32_t* last;
+};
+
+struct CompositeBwdArgs {
+  const float* splats;
+  const uint32_t* vals;
+  const uint32_t* ranges;
+  int width, height, tiles_x, tiles_y;
+  float alpha_min, alpha_max, power_cut;
+  float bg[3];
+  const float* dL_dimage;
+  const float* image;
+  const float* target;
+  float l1_scale;
+  const float* final_T;
+  const uint32_t* last;
+  float* grad2d;
+  float* loss_sum;
+};
+
+struct PreprocessBwdArgs {
+  int64_t n;
+  const float* pos;
+  const float* log_scale;
+  const float* rot;
+  const float* logit_opacity;
+  const float* sh;
+  gsc_camera cam;
+  gsc_raster_config cfg;
+  const float* grad2d;
+  float* g_pos;
+  float* g_log_scale;
+  float* g_rot;
+  float* g_logit_opacity;
+  float* g_sh;
+  float* d_mean2d;
+  float* d_cov2d;
+  float* d_opacity;
+  float* d_colors;
+};
+
+constexpr int kMaxAdamGroups = 8;
+
+struct AdamGroupDev {
+  float* param;
+  const float* grad;
+  float* m;
+  float* v;
+  int64_t numel;
+  float lr;
+  float weight_decay;
+  float decay;  // 1 - lr * weight_decay
+  int vec;      // all four pointers 16-byte aligned
+};
+
+struct AdamArgs {
+  AdamGroupDev g[kMaxAdamGroups];
+  int64_t chunk_end[kMaxAdamGroups];  // inclusive prefix of ceil(numel/4)
+  int ngroups;
+  float beta1, beta2, eps, bc1, bc2, grad_scale;
+};
+
+int launch_preprocess(const PreprocessArgs& a, cudaStream_t stream);
+int launch_block_sums(const float* splats, int64_t n, uint32_t* sums, cudaStream_t stream);
+int launch_scan_block_sums(const uint32_t* sums, int64_t nb, uint64_t* offsets, uint64_t* total,
+                           cudaStream_t stream);
+int launch_emit_keys(const float* splats, int64_t n, const uint64_t* offsets, int tiles_x,
+                     int tiles_y, uint64_t* keys, uint32_t* vals, cudaStream_t stream);
+int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint32_t* ranges,
+                       cudaStream_t stream);
+size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit);
+int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
+                      int end_bit, char* scratch);
+int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream);
+int launch_composite_bwd(const CompositeBwdArgs& a, bool full, cudaStream_t stream);
+int launch_preprocess_bwd(const PreprocessBwdArgs& a, bool full, cudaStream_t stream);
+int launch_adam(const AdamArgs& a, cudaStream_t stream);
+int launch_l1(const float* pred, const float* target, int64_t numel, float scale, float* grad,
+              float* loss_sum, int num_sms, cudaStream_t stream);
+
+}  // namespace gs

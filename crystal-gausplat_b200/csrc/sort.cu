@@ -1,0 +1,245 @@
+// sort.cu — stable LSD radix sort of (u64 key, u32 value) pairs, replacing
+// GPURadixSort.sort! (src/metal/gpu_radix_sort.cr:46-200,
+// src/metal/kernels/radix_sort.metal:21-281: 4-bit digits, 5 dispatches per
+// pass, and a digit-0-only scan that breaks it beyond 512 keys).
+//
+// Design (onesweep): 8-bit digits over the requested bit range only.
+//   1. histogram_kernel reads the keys once and builds the digit histograms of
+//      every pass.
+//   2. One onesweep_kernel per pass: a CTA takes the next partition of 4096
+//      pairs by atomic ticket, ranks its keys stably with warp match/ballot
+//      and per-warp digit counters in shared memory, publishes its per-digit
+//      counts, resolves its global digit offsets by decoupled look-back over
+//      earlier partitions (bounded spin: on give-up it sets the device error
+//      word and never writes out of bounds), reorders the tile in shared
+//      memory and scatters keys then values with coalesced runs.
+// Traffic per pair: 8 B (histogram) + 24 B per pass.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace gs {
+
+namespace {
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kItems = 16;
+constexpr int kWarpKeys = 32 * kItems;           // 512
+constexpr int kTileKeys = kWarps * kWarpKeys;    // 4096
+constexpr uint32_t kFlagAgg = 1u << 30;
+constexpr uint32_t kFlagInc = 2u << 30;
+constexpr uint32_t kValMask = (1u << 30) - 1u;
+constexpr uint32_t kSpinLimit = 1u << 21;
+}  // namespace
+
+__global__ void __launch_bounds__(256) histogram_kernel(const uint64_t* __restrict__ keys, int64_t n,
+                                                        int begin_bit, int end_bit, int npass,
+                                                        uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[8][256];
+  for (int k = threadIdx.x; k < 8 * 256; k += 256) (&s_hist[0][0])[k] = 0;
+  __syncthreads();
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+    const uint64_t key = keys[i];
+    for (int p = 0; p < npass; p++) {
+      const int shift = begin_bit + 8 * p;
+      const int bits = min(8, end_bit - shift);
+      const uint32_t d = (uint32_t)(key >> shift) & ((1u << bits) - 1u);
+      atomicAdd(&s_hist[p][d], 1u);
+    }
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < npass * 256; k += 256) {
+    const uint32_t c = (&s_hist[0][0])[k];
+    if (c) atomicAdd(&hist[k], c);
+  }
+}
+
+// Exclusive scan of one u32 per thread over 256 threads.
+__device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_warp) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t t = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += t;
+  }
+  if (lane == 31) s_warp[w] = x;
+  __syncthreads();
+  uint32_t add = 0;
+  for (int k = 0; k < w; k++) add += s_warp[k];
+  __syncthreads();
+  return x - v + add;
+}
+
+__global__ void __launch_bounds__(kThreads) onesweep_kernel(
+    const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+    uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
+    uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
+    uint32_t* err) {
+  __shared__ uint64_t s_keys[kTileKeys];  // reused for values
+  __shared__ uint32_t s_whist[kWarps][256];
+  __shared__ uint32_t s_local_excl[256];
+  __shared__ uint32_t s_gbase[256];
+  __shared__ uint8_t s_dig[kTileKeys];
+  __shared__ uint32_t s_warp[kWarps];
+  __shared__ uint32_t s_part;
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) s_part = atomicAdd(ticket, 1u);
+  for (int k = tid; k < kWarps * 256; k += kThreads) (&s_whist[0][0])[k] = 0;
+  __syncthreads();
+  const uint32_t part = s_part;
+  const int64_t tile_base = (int64_t)part * kTileKeys;
+  const int64_t warp_base = tile_base + (int64_t)w * kWarpKeys;
+  const uint32_t num_valid = (uint32_t)min((int64_t)kTileKeys, n - tile_base);
+
+  uint64_t k[kItems];
+  uint32_t v[kItems];
+  uint32_t rank[kItems];
+#pragma unroll
+  for (int i = 0; i < kItems; i++) {
+    const int64_t idx = warp_base + i * 32 + lane;
+    const bool valid = idx < n;
+    k[i] = valid ? keys_in[idx] : ~0ull;
+    v[i] = valid ? vals_in[idx] : 0u;
+  }
+  const uint32_t lt_mask = (1u << lane) - 1u;
+#pragma unroll
+  for (int i = 0; i < kItems; i++) {
+    const int64_t idx = warp_base + i * 32 + lane;
+    // Pairs past the end take the largest digit, so they sort behind every
+    // valid pair of the tile.
+    const uint32_t d = idx < n ? ((uint32_t)(k[i] >> shift) & digit_mask) : 255u;
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const int leader = __ffs(peers) - 1;
+    uint32_t b = 0;
+    if (lane == leader) {
+      b = s_whist[w][d];
+      s_whist[w][d] = b + __popc(peers);
+    }
+    b = __shfl_sync(0xffffffffu, b, leader);
+    rank[i] = b + __popc(peers & lt_mask);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Thread d owns digit d: warp offsets, tile count, tile-local prefix.
+  const uint32_t d = tid;
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int ww = 0; ww < kWarps; ww++) {
+    const uint32_t c = s_whist[ww][d];
+    s_whist[ww][d] = cnt;
+    cnt += c;
+  }
+  const uint32_t valid_cnt = d == 255u ? cnt - (kTileKeys - num_valid) : cnt;
+  const uint32_t local_excl = block_excl_scan_256(cnt, s_warp);
+  const uint32_t gexcl = block_excl_scan_256(hist[d], s_warp);
+  s_local_excl[d] = local_excl;
+
+  // Decoupled look-back.
+  uint32_t* my = status + (size_t)part * 256 + d;
+  uint32_t excl = 0;
+  if (part == 0) {
+    *(volatile uint32_t*)my = kFlagInc | valid_cnt;
+  } else {
+    *(volatile uint32_t*)my = kFlagAgg | valid_cnt;
+    int64_t j = (int64_t)part - 1;
+    uint32_t spins = 0;
+    while (j >= 0) {
+      const uint32_t s = *(volatile const uint32_t*)(status + (size_t)j * 256 + d);
+      const uint32_t flag = s & ~kValMask;
+      if (flag == 0) {
+        if (++spins > kSpinLimit) {
+          atomicOr(err, GS_DEVERR_TIMEOUT);
+          break;
+        }
+        __nanosleep(32);
+        continue;
+      }
+      excl += s & kValMask;
+      if (flag == kFlagInc) break;
+      j--;
+    }
+    *(volatile uint32_t*)my = kFlagInc | ((excl + valid_cnt) & kValMask);
+  }
+  s_gbase[d] = gexcl + excl - local_excl;  // global position = s_gbase[d] + tile position
+  __syncthreads();
+
+#pragma unroll
+  for (int i = 0; i < kItems; i++) {
+    const int64_t idx = warp_base + i * 32 + lane;
+    const uint32_t dd = idx < n ? ((uint32_t)(k[i] >> shift) & digit_mask) : 255u;
+    const uint32_t pos = s_local_excl[dd] + s_whist[w][dd] + rank[i];
+    s_keys[pos] = k[i];
+    rank[i] = pos;
+  }
+  __syncthreads();
+  for (uint32_t j = tid; j < num_valid; j += kThreads) {
+    const uint64_t key = s_keys[j];
+    const uint32_t dd = (uint32_t)(key >> shift) & digit_mask;
+    s_dig[j] = (uint8_t)dd;
+    const uint32_t gpos = s_gbase[dd] + j;
+    if ((int64_t)gpos < n) keys_out[gpos] = key;
+    else atomicOr(err, GS_DEVERR_BOUNDS);
+  }
+  __syncthreads();
+  uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys);
+#pragma unroll
+  for (int i = 0; i < kItems; i++) s_vals[rank[i]] = v[i];
+  __syncthreads();
+  for (uint32_t j = tid; j < num_valid; j += kThreads) {
+    const uint32_t gpos = s_gbase[s_dig[j]] + j;
+    if ((int64_t)gpos < n) vals_out[gpos] = s_vals[j];
+  }
+}
+
+size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit) {
+  const int npass = (end_bit - begin_bit + 7) / 8;
+  const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
+  size_t b = align256((size_t)n * 8) + align256((size_t)n * 4);
+  b += align256((size_t)npass * 256 * 4 + (size_t)npass * parts * 256 * 4 + (size_t)npass * 4);
+  return b;
+}
+
+int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
+                      int end_bit, char* scratch) {
+  cudaStream_t stream = ctx->stream;
+  if (n <= 1 || end_bit <= begin_bit) return GSC_OK;
+  const int npass = (end_bit - begin_bit + 7) / 8;
+  const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
+  uint64_t* alt_keys = reinterpret_cast<uint64_t*>(scratch);
+  scratch += align256((size_t)n * 8);
+  uint32_t* alt_vals = reinterpret_cast<uint32_t*>(scratch);
+  scratch += align256((size_t)n * 4);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(scratch);
+  uint32_t* status = hist + npass * 256;
+  uint32_t* tickets = status + (size_t)npass * parts * 256;
+  const size_t meta = (size_t)npass * 256 * 4 + (size_t)npass * parts * 256 * 4 + (size_t)npass * 4;
+  GS_CK(cudaMemsetAsync(hist, 0, meta, stream));
+
+  const int64_t hblocks = min((int64_t)ctx->num_sms * 8, (n + 4095) / 4096);
+  histogram_kernel<<<(unsigned)max((int64_t)1, hblocks), 256, 0, stream>>>(keys, n, begin_bit, end_bit,
+                                                                          npass, hist);
+  GS_CK_LAUNCH("histogram_kernel");
+  uint64_t* src_k = keys;
+  uint32_t* src_v = vals;
+  uint64_t* dst_k = alt_keys;
+  uint32_t* dst_v = alt_vals;
+  for (int p = 0; p < npass; p++) {
+    const int shift = begin_bit + 8 * p;
+    const int bits = min(8, end_bit - shift);
+    onesweep_kernel<<<(unsigned)parts, kThreads, 0, stream>>>(
+        src_k, src_v, dst_k, dst_v, n, shift, (1u << bits) - 1u, hist + p * 256,
+        status + (size_t)p * parts * 256, tickets + p, ctx->err);
+    GS_CK_LAUNCH("onesweep_kernel");
+    std::swap(src_k, dst_k);
+    std::swap(src_v, dst_v);
+  }
+  if (src_k != keys) {
+    GS_CK(cudaMemcpyAsync(keys, src_k, (size_t)n * 8, cudaMemcpyDeviceToDevice, stream));
+    GS_CK(cudaMemcpyAsync(vals, src_v, (size_t)n * 4, cudaMemcpyDeviceToDevice, stream));
+  }
+  return GSC_OK;
+}
+
+}  // namespace gs

@@ -1,0 +1,297 @@
+/*
+ * gsplat_cuda.h — C ABI of libgsplat_cuda.so, the sm_100a (B200) Gaussian-splatting
+ * rasterizer hot path of crystal-gausplat.
+ *
+ * The library replaces, for this path only, the Metal backend that the Crystal
+ * host reaches through its `lib` FFI blocks:
+ *   src/core/buffer.cr:201-211      (lib MetalFFI: buffers)
+ *   src/metal/device.cr:205-231     (lib MetalDeviceFFI: device, queue)
+ *   src/metal/dispatch.cr:237-254   (lib MetalDispatchFFI: encoders, dispatch)
+ *   src/metal/bridge.mm:361-482     (extern "C" gs_* implementation)
+ * and the kernels they launch (src/metal/kernels/gaussian.metal,
+ * src/metal/kernels/radix_sort.metal) plus the host loops on the same path
+ * (src/gaussian_splatting/rasterizer.cr:375-460, src/optim/adam.cr:127-176,
+ * src/ops/loss.cr:33-57).
+ *
+ * Conventions
+ *  - Every entry point returns GSC_OK (0) or a negative GSC_ERR_* code; the
+ *    message of the last failure on the calling thread is gsc_last_error().
+ *    No C++ exception crosses this boundary.
+ *  - All array pointers are DEVICE pointers owned by the caller (from
+ *    gsc_alloc, cudaMalloc or a torch tensor) unless a parameter says "host".
+ *    Layouts are the reference's: row-major fp32, u64 keys, u32 ids,
+ *    u32 tile ranges [T,2] (src/gaussian_splatting/rasterizer_context.cr:17-36).
+ *  - Work is enqueued asynchronously on the context's stream (gsc_set_stream);
+ *    gsc_sync() waits and reports device-side errors (bounded spin timeouts).
+ *  - One gsc_ctx per device per host thread; a context is not thread-safe.
+ */
+#ifndef GSPLAT_CUDA_H
+#define GSPLAT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GSC_API __attribute__((visibility("default")))
+#else
+#define GSC_API
+#endif
+
+#define GSC_VERSION 1
+
+/* ---- status codes ---------------------------------------------------- */
+#define GSC_OK 0
+#define GSC_ERR_INVALID (-1)  /* bad argument (null pointer, negative size, ...) */
+#define GSC_ERR_CUDA (-2)     /* a CUDA runtime call failed */
+#define GSC_ERR_CAPACITY (-3) /* output buffer too small (e.g. key capacity) */
+#define GSC_ERR_TIMEOUT (-4)  /* a bounded device-side wait gave up */
+#define GSC_ERR_NOMEM (-5)    /* device allocation failed */
+#define GSC_ERR_NODEVICE (-6) /* no CUDA device / device index out of range */
+#define GSC_ERR_UNSUPPORTED (-7)
+
+/* ---- arithmetic modes -------------------------------------------------
+ * GSC_MODE_FULL : mathematically complete 3DGS forward/backward with the
+ *                 reference's constants: SH evaluated to cfg.sh_degree (<= 3),
+ *                 normalised quaternions, analytic gradients for all 59
+ *                 floats per Gaussian.
+ * GSC_MODE_REF  : the reference's literal per-thread arithmetic:
+ *                 truncated SH (gaussian.metal:283-302), quaternion as given,
+ *                 backward over the whole tile list with the reference's
+ *                 running-colour update (gaussian.metal:503-566), host chain
+ *                 of rasterizer.cr:375-460 (position via the mean only, DC
+ *                 SH gradient dL/dc / C0, nothing for scale/rotation/cov2d). */
+#define GSC_MODE_FULL 0
+#define GSC_MODE_REF 1
+
+/* Camera block. Byte-for-byte the reference's CameraParamsGPU
+ * (src/gaussian_splatting/rasterizer.cr:467-500, 176 bytes, packed), so the
+ * Crystal host can keep build_camera_params (rasterizer.cr:502-531).
+ * view: world_to_camera, ROW-major (camera.cr:185-187): x_cam = view[0..3]·[p,1].
+ * proj is carried for layout compatibility and not read. */
+typedef struct gsc_camera {
+  float view[16];
+  float proj[16];
+  float fx, fy, cx, cy;
+  int32_t width, height;
+  float tan_fov_x, tan_fov_y; /* tan of half field of view (camera.cr:39-45) */
+  float campos[3];            /* camera centre in world space (camera.cr:133-137) */
+  float _pad;
+} gsc_camera;
+
+/* Rasterizer constants. gsc_raster_config_default() fills the reference
+ * values (gaussian.metal:160,174,227-228,400,425-426; trainer.cr:186). */
+typedef struct gsc_raster_config {
+  int32_t mode;      /* GSC_MODE_FULL or GSC_MODE_REF */
+  int32_t sh_degree; /* 0..3, reference SH_DEGREE = 3 (gaussian.cr:14) */
+  float t_stop;      /* stop while T > t_stop fails: 1e-3 */
+  float alpha_min;   /* skip alpha < alpha_min: 1/255 */
+  float alpha_max;   /* alpha = min(alpha_max, o*G): 0.99 */
+  float lowpass;     /* added to the cov2d diagonal: 0.3 */
+  float fov_cull;    /* cull |x/z| > fov_cull * tan_fov_x: 1.3 */
+  float near_z;      /* cull z <= near_z: 0.01 */
+  float far_z;       /* cull z > far_z: 1000 */
+  float background[3];
+} gsc_raster_config;
+
+/* The trainable state of Gaussian3D (src/gaussian_splatting/gaussian.cr:19-37):
+ * position [N,3], log_scale [N,3], rotation [N,4] (w,x,y,z),
+ * logit_opacity [N,1], sh_coeffs [N,16,3] (coefficient-major, channel-minor). */
+typedef struct gsc_gaussians {
+  const float* position;
+  const float* log_scale;
+  const float* rotation;
+  const float* logit_opacity;
+  const float* sh;
+  int64_t count;
+} gsc_gaussians;
+
+/* Gradients with the same shapes as gsc_gaussians; kernels ACCUMULATE (+=)
+ * into them, so the caller zeroes them once per step (Variable#zero_grad!,
+ * src/autograd/variable.cr:86-88). d_logit_opacity is dL/dlogit
+ * (trainer.cr:234-241 sigmoid chain applied). */
+typedef struct gsc_gaussian_grads {
+  float* position;
+  float* log_scale;
+  float* rotation;
+  float* logit_opacity;
+  float* sh;
+} gsc_gaussian_grads;
+
+/* Per-view outputs of preprocess. `splats` is required (12 floats per
+ * Gaussian, private packed layout used by binning and compositing); every
+ * other pointer may be NULL. They mirror RasterizerContext
+ * (rasterizer_context.cr:17-23): mean2d [N,2], cov2d [N,3] (xx,xy,yy, with
+ * the low-pass), conic [N,3] (inverse cov2d: xx,xy,yy), depth [N],
+ * radius [N], colors [N,3], opacity [N], tiles_touched [N] (u32), cov3d [N,6]. */
+typedef struct gsc_projected {
+  float* splats;
+  float* mean2d;
+  float* cov2d;
+  float* conic;
+  float* depth;
+  float* radius;
+  float* colors;
+  float* opacity;
+  uint32_t* tiles_touched;
+  float* cov3d;
+} gsc_projected;
+
+/* Per-Gaussian screen-space gradients in the reference's RasterizerGradients
+ * shapes (rasterizer_context.cr:133-140). Any pointer may be NULL. */
+typedef struct gsc_grads2d {
+  float* mean2d;  /* [N,2] */
+  float* cov2d;   /* [N,3] (zero in GSC_MODE_REF, as gaussian.metal:464 never writes it) */
+  float* opacity; /* [N]   dL/d(sigmoid opacity) */
+  float* colors;  /* [N,3] */
+} gsc_grads2d;
+
+/* One Adam parameter group (src/optim/adam.cr:86-110 loops over these). */
+typedef struct gsc_adam_group {
+  float* param;
+  const float* grad;
+  float* m;
+  float* v;
+  int64_t numel;
+  float lr;
+  float weight_decay; /* decoupled (AdamW), 0 = plain Adam (adam.cr:112-125) */
+} gsc_adam_group;
+
+/* ---- context ---------------------------------------------------------- */
+GSC_API int gsc_version(void);
+GSC_API const char* gsc_last_error(void);
+GSC_API void gsc_raster_config_default(gsc_raster_config* cfg);
+
+typedef struct gsc_ctx gsc_ctx;
+typedef struct gsc_frame gsc_frame;
+
+/* Replaces gs_init_device (bridge.mm:17-49): 0 ok, GSC_ERR_NODEVICE. */
+GSC_API int gsc_init(int device, gsc_ctx** out);
+GSC_API int gsc_destroy(gsc_ctx* ctx);
+/* Use `stream` (a cudaStream_t; NULL = legacy default) for all later work. */
+GSC_API int gsc_set_stream(gsc_ctx* ctx, void* stream);
+/* Wait for the stream; returns GSC_ERR_TIMEOUT if a device wait gave up. */
+GSC_API int gsc_sync(gsc_ctx* ctx);
+
+/* ---- memory (replaces gs_create_buffer / gs_buffer_* , bridge.mm:131-146) */
+GSC_API int gsc_alloc(gsc_ctx* ctx, size_t bytes, void** out);
+GSC_API int gsc_free(gsc_ctx* ctx, void* ptr);
+GSC_API int gsc_memcpy_h2d(gsc_ctx* ctx, void* dst, const void* host_src, size_t bytes);
+GSC_API int gsc_memcpy_d2h(gsc_ctx* ctx, void* host_dst, const void* src, size_t bytes);
+GSC_API int gsc_memset(gsc_ctx* ctx, void* dst, int value, size_t bytes);
+
+/* ---- stages ----------------------------------------------------------- */
+
+/* Fused compute_cov3d + project_gaussians + eval_sh + opacity sigmoid + tile
+ * count (gaussian.metal:90-308, gaussian.cr:119-142). One thread per Gaussian. */
+GSC_API int gsc_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
+                           const gsc_raster_config* cfg, const gsc_projected* out);
+
+/* create_tile_keys (gaussian.metal:315-357) with exact allocation: a scan of
+ * tiles_touched, then each Gaussian writes its keys in canonical order
+ * (Gaussian id, then ty, then tx). key = tile_id << 32 | float_bits(depth),
+ * value = Gaussian id. *num_keys (host) receives the total; GSC_ERR_CAPACITY
+ * if it exceeds `capacity` (nothing is written then). */
+GSC_API int gsc_bin(gsc_ctx* ctx, int64_t n, const float* splats, int32_t tiles_x, int32_t tiles_y,
+                    uint64_t* keys, uint32_t* values, int64_t capacity, int64_t* num_keys);
+
+/* GPURadixSort.sort!(keys, values, n) (src/metal/gpu_radix_sort.cr:46-57):
+ * in-place STABLE ascending sort of (u64 key, u32 value) pairs by the key
+ * bits [begin_bit, end_bit) (0, 64 = whole key). Onesweep LSD radix,
+ * 8-bit digits. Scratch comes from the context. */
+GSC_API int gsc_sort_pairs_u64(gsc_ctx* ctx, uint64_t* keys, uint32_t* values, int64_t n,
+                               int begin_bit, int end_bit);
+
+/* GPURadixSort.compute_tile_ranges! (gpu_radix_sort.cr:204-233,
+ * radix_sort.metal:288-324): ranges[t] = [first, last+1) of tile t in the
+ * sorted keys, (0,0) for empty tiles. */
+GSC_API int gsc_tile_ranges(gsc_ctx* ctx, const uint64_t* sorted_keys, int64_t n, int32_t num_tiles,
+                            uint32_t* ranges);
+
+/* rasterize_tile (gaussian.metal:364-445) over every 16x16 tile.
+ * image [H,W,3]; n_contrib [H,W] u32 (Gaussians that contributed);
+ * final_T [H,W]; last [H,W] u32 (tile-list position after the last
+ * contributor, for the backward; may be NULL in GSC_MODE_REF). */
+GSC_API int gsc_composite_forward(gsc_ctx* ctx, const float* splats, const uint32_t* values,
+                                  const uint32_t* ranges, int32_t width, int32_t height,
+                                  const gsc_raster_config* cfg, float* image, uint32_t* n_contrib,
+                                  float* final_T, uint32_t* last);
+
+/* rasterize_backward (gaussian.metal:452-567). Accumulates into grad2d
+ * [N,9] = (dmean.x, dmean.y, dconic.xx, dconic.xy, dconic.yy, dopacity,
+ * dcolor.r, dcolor.g, dcolor.b). If `target` is non-NULL the pixel gradient
+ * is the L1 gradient sign(image - target) * l1_scale (loss.cr:33-57, fused)
+ * and dL_dimage is ignored; `loss_sum` (device float, may be NULL) then
+ * receives += sum |image - target| * l1_scale. */
+GSC_API int gsc_composite_backward(gsc_ctx* ctx, const float* splats, const uint32_t* values,
+                                   const uint32_t* ranges, int32_t width, int32_t height,
+                                   const gsc_raster_config* cfg, const float* dL_dimage,
+                                   const float* image, const float* target, float l1_scale,
+                                   const float* final_T, const uint32_t* last, float* grad2d,
+                                   float* loss_sum);
+
+/* project_backward! + sh_backward! + covariance_backward! + the sigmoid chain
+ * (rasterizer.cr:375-460, trainer.cr:218-255), as one kernel. Reads grad2d
+ * [N,9] from gsc_composite_backward, accumulates into `grads` and writes the
+ * optional screen-space views into `g2d`. */
+GSC_API int gsc_preprocess_backward(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
+                                    const gsc_raster_config* cfg, const float* grad2d,
+                                    const gsc_gaussian_grads* grads, const gsc_grads2d* g2d);
+
+/* Loss.l1_with_grad (src/ops/loss.cr:33-57): grad = sign(pred - target) * scale,
+ * *loss_sum (device) += sum |pred - target| * scale. scale = 1/numel matches
+ * the reference. */
+GSC_API int gsc_l1_loss_grad(gsc_ctx* ctx, const float* pred, const float* target, int64_t numel,
+                             float scale, float* grad, float* loss_sum);
+
+/* Adam#step (src/optim/adam.cr:86-176) over all groups in one launch.
+ * `step` is the 1-based step count after increment (AdamState#step);
+ * every gradient is multiplied by grad_scale first (1/views for a view mean). */
+GSC_API int gsc_adam_step(gsc_ctx* ctx, const gsc_adam_group* groups, int32_t ngroups, float beta1,
+                          float beta2, float eps, int32_t step, float grad_scale);
+
+/* ---- whole-view orchestration (Rasterizer.forward/backward,
+ *      src/gaussian_splatting/rasterizer.cr:48-104) ----------------------- */
+
+/* A frame holds the per-view state kept between forward and backward
+ * (RasterizerContext): splats, keys, values, ranges, per-pixel final_T / last,
+ * the rendered image and grad2d. Buffers grow on demand and are reused. */
+GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out);
+GSC_API int gsc_frame_destroy(gsc_frame* frame);
+
+/* preprocess -> bin -> sort -> ranges -> composite. `image` [H,W,3] may be
+ * NULL (the frame's own buffer is used); n_contrib / final_T may be NULL.
+ * *num_rendered (host, may be NULL) = number of keys (ctx.num_rendered). */
+GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* frame, const gsc_gaussians* g,
+                                  const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
+                                  uint32_t* n_contrib, float* final_T, int64_t* num_rendered);
+
+/* composite backward -> preprocess backward for the frame's last forward.
+ * Exactly one of dL_dimage / target is non-NULL (target = fused L1 with
+ * l1_scale, loss accumulated into the device float *loss_sum if non-NULL).
+ * Gradients accumulate into `grads`; `g2d` (may be NULL) gets screen-space views. */
+GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* frame, const gsc_gaussians* g,
+                                   const gsc_camera* cam, const gsc_raster_config* cfg,
+                                   const float* dL_dimage, const float* target, float l1_scale,
+                                   float* loss_sum, const gsc_gaussian_grads* grads,
+                                   const gsc_grads2d* g2d);
+
+/* Frame internals (device pointers, valid until the next forward on the frame). */
+#define GSC_FRAME_SPLATS 0
+#define GSC_FRAME_KEYS 1
+#define GSC_FRAME_VALUES 2
+#define GSC_FRAME_RANGES 3
+#define GSC_FRAME_IMAGE 4
+#define GSC_FRAME_FINAL_T 5
+#define GSC_FRAME_LAST 6
+#define GSC_FRAME_N_CONTRIB 7
+#define GSC_FRAME_GRAD2D 8
+GSC_API int gsc_frame_get(gsc_frame* frame, int which, void** ptr, int64_t* count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSPLAT_CUDA_H */

@@ -1,0 +1,216 @@
+"""numpy front end of the CPU oracle (oracle/_build/libgs_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: used by tests/, __graft_entry__.smoke() and the
+bench.py CPU-baseline / reference arm as the checker. The product path never
+imports it. Parity is unpinned by the reference (no golden vectors exist for
+this path upstream); the oracle is pinned by known-answer tests and float64
+finite differences in tests/.
+"""
+import ctypes as C
+import importlib
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "_build", "libgs_oracle.so")
+
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+_abi = importlib.import_module("crystal-gausplat_b200._abi")  # struct layouts of include/gsplat_cuda.h
+
+P = C.c_void_p
+_lib = None
+
+
+def build():
+    subprocess.check_call(["make", "-s", "-C", HERE])
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(
+                os.path.getmtime(os.path.join(HERE, f)) for f in ("gs_oracle.cpp", "gs_oracle.h")):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.gso_expf.restype = C.c_float
+        L.gso_expf.argtypes = [C.c_float]
+        L.gso_emit_keys.restype = C.c_int64
+        L.gso_render_view.restype = C.c_int64
+        _lib = L
+    return _lib
+
+
+def set_threads(n):
+    lib().gso_set_threads(int(n))
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(P)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def expf(x):
+    x = _f32(x).reshape(-1)
+    return np.array([lib().gso_expf(C.c_float(v)) for v in x], dtype=np.float32)
+
+
+class Scene:
+    """Host Gaussian arrays (dict from gaussian.synthetic_arrays) as a C struct."""
+
+    def __init__(self, arrays):
+        self.pos = _f32(arrays["position"]).reshape(-1, 3)
+        self.log_scale = _f32(arrays["log_scale"]).reshape(-1, 3)
+        self.rot = _f32(arrays["rotation"]).reshape(-1, 4)
+        self.logit = _f32(arrays["logit_opacity"]).reshape(-1)
+        self.sh = _f32(arrays["sh_coeffs"]).reshape(-1, 48)
+        self.n = self.pos.shape[0]
+        s = _abi.Gaussians()
+        s.position = self.pos.ctypes.data
+        s.log_scale = self.log_scale.ctypes.data
+        s.rotation = self.rot.ctypes.data
+        s.logit_opacity = self.logit.ctypes.data
+        s.sh = self.sh.ctypes.data
+        s.count = self.n
+        self.struct = s
+
+    def zero_grads(self):
+        g = {"position": np.zeros((self.n, 3), np.float32), "log_scale": np.zeros((self.n, 3), np.float32),
+             "rotation": np.zeros((self.n, 4), np.float32), "logit_opacity": np.zeros(self.n, np.float32),
+             "sh_coeffs": np.zeros((self.n, 48), np.float32)}
+        s = _abi.GaussianGrads()
+        s.position = g["position"].ctypes.data
+        s.log_scale = g["log_scale"].ctypes.data
+        s.rotation = g["rotation"].ctypes.data
+        s.logit_opacity = g["logit_opacity"].ctypes.data
+        s.sh = g["sh_coeffs"].ctypes.data
+        return g, s
+
+
+def preprocess(scene, cam, cfg):
+    n = scene.n
+    out = {"mean2d": np.zeros((n, 2), np.float32), "cov2d": np.zeros((n, 3), np.float32),
+           "conic": np.zeros((n, 3), np.float32), "depth": np.zeros(n, np.float32),
+           "radius": np.zeros(n, np.float32), "colors": np.zeros((n, 3), np.float32),
+           "opacity": np.zeros(n, np.float32), "tiles_touched": np.zeros(n, np.uint32),
+           "cov3d": np.zeros((n, 6), np.float32)}
+    lib().gso_preprocess(C.byref(scene.struct), C.byref(cam), C.byref(cfg), *(_p(out[k]) for k in (
+        "mean2d", "cov2d", "conic", "depth", "radius", "colors", "opacity", "tiles_touched", "cov3d")))
+    return out
+
+
+def emit_keys(pre, tiles_x, tiles_y):
+    n = pre["depth"].shape[0]
+    m = lib().gso_emit_keys(C.c_int64(n), _p(pre["mean2d"]), _p(pre["depth"]), _p(pre["radius"]),
+                            tiles_x, tiles_y, None, None, C.c_int64(0))
+    keys = np.zeros(m, np.uint64)
+    vals = np.zeros(m, np.uint32)
+    lib().gso_emit_keys(C.c_int64(n), _p(pre["mean2d"]), _p(pre["depth"]), _p(pre["radius"]),
+                        tiles_x, tiles_y, _p(keys), _p(vals), C.c_int64(m))
+    return keys, vals
+
+
+def sort_pairs(keys, vals, begin_bit=0, end_bit=64):
+    keys = np.ascontiguousarray(keys, np.uint64).copy()
+    vals = np.ascontiguousarray(vals, np.uint32).copy()
+    lib().gso_sort_pairs(C.c_int64(keys.size), _p(keys), _p(vals), begin_bit, end_bit)
+    return keys, vals
+
+
+def tile_ranges(keys, num_tiles):
+    ranges = np.zeros(num_tiles * 2, np.uint32)
+    lib().gso_tile_ranges(C.c_int64(keys.size), _p(keys), num_tiles, _p(ranges))
+    return ranges
+
+
+def composite_forward(W, H, ranges, vals, pre, cfg):
+    img = np.zeros((H, W, 3), np.float32)
+    nc = np.zeros((H, W), np.uint32)
+    fT = np.zeros((H, W), np.float32)
+    last = np.zeros((H, W), np.uint32)
+    lib().gso_composite_forward(W, H, _p(ranges), _p(vals), _p(pre["mean2d"]), _p(pre["cov2d"]),
+                                _p(pre["opacity"]), _p(pre["colors"]), C.byref(cfg), _p(img),
+                                _p(nc), _p(fT), _p(last))
+    return img, nc, fT, last
+
+
+def composite_backward(W, H, ranges, vals, pre, cfg, final_T, last, dL_dimage=None, image=None,
+                       target=None, l1_scale=0.0):
+    n = pre["depth"].shape[0]
+    g2d = np.zeros((n, 9), np.float32)
+    loss = C.c_double(0.0)
+    lib().gso_composite_backward(W, H, _p(ranges), _p(vals), _p(pre["mean2d"]), _p(pre["cov2d"]),
+                                 _p(pre["opacity"]), _p(pre["colors"]), C.byref(cfg),
+                                 _p(None if dL_dimage is None else _f32(dL_dimage)),
+                                 _p(None if image is None else _f32(image)),
+                                 _p(None if target is None else _f32(target)), C.c_float(l1_scale),
+                                 _p(final_T), _p(last), _p(g2d), C.byref(loss))
+    return g2d, loss.value
+
+
+def preprocess_backward(scene, cam, cfg, grad2d):
+    g, gs = scene.zero_grads()
+    n = scene.n
+    views = {"mean2d": np.zeros((n, 2), np.float32), "cov2d": np.zeros((n, 3), np.float32),
+             "opacity": np.zeros(n, np.float32), "colors": np.zeros((n, 3), np.float32)}
+    lib().gso_preprocess_backward(C.byref(scene.struct), C.byref(cam), C.byref(cfg),
+                                  _p(_f32(grad2d)), C.byref(gs), _p(views["mean2d"]),
+                                  _p(views["cov2d"]), _p(views["opacity"]), _p(views["colors"]))
+    return g, views
+
+
+def l1_loss_grad(pred, target, scale):
+    pred, target = _f32(pred), _f32(target)
+    grad = np.zeros_like(pred)
+    loss = C.c_double(0.0)
+    lib().gso_l1_loss_grad(C.c_int64(pred.size), _p(pred), _p(target), C.c_float(scale), _p(grad),
+                           C.byref(loss))
+    return loss.value, grad
+
+
+def adam_step(groups, beta1, beta2, eps, step, grad_scale=1.0):
+    """groups: list of dicts with numpy param/grad/m/v (updated in place), lr, weight_decay."""
+    arr = (_abi.AdamGroup * len(groups))()
+    for i, g in enumerate(groups):
+        arr[i].param = g["param"].ctypes.data
+        arr[i].grad = g["grad"].ctypes.data
+        arr[i].m = g["m"].ctypes.data
+        arr[i].v = g["v"].ctypes.data
+        arr[i].numel = g["param"].size
+        arr[i].lr = g["lr"]
+        arr[i].weight_decay = g.get("weight_decay", 0.0)
+    lib().gso_adam_step(arr, len(groups), C.c_float(beta1), C.c_float(beta2), C.c_float(eps), step,
+                        C.c_float(grad_scale))
+
+
+def forward_pipeline(scene, cam, cfg):
+    """All forward intermediates of one view (preprocess .. composite)."""
+    W, H = cam.width, cam.height
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    pre = preprocess(scene, cam, cfg)
+    keys, vals = emit_keys(pre, tx, ty)
+    end_bit = 32 + max(0, int(np.ceil(np.log2(tx * ty))) if tx * ty > 1 else 0)
+    skeys, svals = sort_pairs(keys, vals, 0, end_bit)
+    ranges = tile_ranges(skeys, tx * ty)
+    img, nc, fT, last = composite_forward(W, H, ranges, svals, pre, cfg)
+    return {"pre": pre, "keys": keys, "vals": vals, "sorted_keys": skeys, "sorted_vals": svals,
+            "ranges": ranges, "image": img, "n_contrib": nc, "final_T": fT, "last": last}
+
+
+def render_view(scene, cam, cfg, target=None, l1_scale=0.0):
+    """Whole view through the oracle (forward; + fused L1 backward with a target)."""
+    img = np.zeros((cam.height, cam.width, 3), np.float32)
+    grads, gs = scene.zero_grads()
+    loss = C.c_double(0.0)
+    m = lib().gso_render_view(C.byref(scene.struct), C.byref(cam), C.byref(cfg), _p(img),
+                              _p(None if target is None else _f32(target)), C.c_float(l1_scale),
+                              C.byref(gs) if target is not None else None, C.byref(loss))
+    return img, (grads if target is not None else None), loss.value, m

@@ -1,0 +1,281 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Bars: bit-exact for keys, values, tile ranges and the
+per-tile lists; images within 1e-5 relative (the shared fp32 operation
+order makes them bit-exact in practice, which is asserted where it holds);
+gradients within 1e-4 relative, measured as
+    |gpu - oracle| <= 1e-4 * max(|oracle|, 1e-3 * max|oracle|)
+per element, because float atomics reorder the per-Gaussian sums.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from helpers import (R, _abi, gpu_preprocess, gs, host, rel_err, scene, to_dev, u32_dev,
+                     u32_host, u64_dev, u64_host)
+
+pytestmark = pytest.mark.gpu
+
+GRAD_RTOL = 1e-4
+IMG_RTOL = 1e-5
+
+
+def grad_close(a, b, rtol=GRAD_RTOL):
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    floor = max(1e-3 * float(np.max(np.abs(b))) if b.size else 0.0, 1e-30)
+    err = np.abs(a - b) / np.maximum(np.abs(b), floor)
+    return float(err.max()) if err.size else 0.0
+
+
+def make(n, W, H, seed=7, extent=1.0, eye=(0.0, 0.0, 4.0)):
+    arrays = scene(n, seed, extent)
+    g = gs.Gaussian3D(arrays)
+    cam = gs.make_camera(W, H, eye)
+    return arrays, g, cam
+
+
+CASES = [  # (n, W, H, eye)
+    (2000, 64, 48, (0.0, 0.0, 4.0)),
+    (5000, 100, 75, (1.5, -2.0, 3.0)),   # ragged tile grid, off-axis camera
+    (20000, 256, 256, (0.0, 0.0, 4.0)),
+]
+
+
+@pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF])
+@pytest.mark.parametrize("case", CASES)
+def test_preprocess_bit_exact(cuda, oracle, case, mode):
+    n, W, H, eye = case
+    arrays, g, cam = make(n, W, H, eye=eye)
+    cs = cam.to_struct()
+    cfg = gs.default_config(mode=mode)
+    got = gpu_preprocess(g, cs, cfg)
+    ref = oracle.preprocess(oracle.Scene(arrays), cs, cfg)
+    for k in ("mean2d", "cov2d", "conic", "depth", "radius", "colors", "opacity", "cov3d"):
+        np.testing.assert_array_equal(host(got[k]).reshape(ref[k].shape), ref[k], err_msg=k)
+    np.testing.assert_array_equal(u32_host(got["tiles_touched"]), ref["tiles_touched"])
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_binning_sort_ranges_bit_exact(cuda, oracle, case):
+    n, W, H, eye = case
+    arrays, g, cam = make(n, W, H, eye=eye)
+    cs = cam.to_struct()
+    cfg = gs.default_config()
+    got = gpu_preprocess(g, cs, cfg)
+    ref = oracle.forward_pipeline(oracle.Scene(arrays), cs, cfg)
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    m = ref["keys"].size
+    keys = cuda.zeros(m + 1, dtype=cuda.int64, device="cuda")
+    vals = cuda.zeros(m + 1, dtype=cuda.int32, device="cuda")
+    nk = C.c_int64()
+    lib = _abi.lib()
+    _abi.check(lib.gsc_bin(R.context(), n, R.ptr(got["splats"]), tx, ty, R.ptr(keys), R.ptr(vals),
+                           m + 1, C.byref(nk)))
+    assert nk.value == m
+    np.testing.assert_array_equal(u64_host(keys)[:m], ref["keys"])
+    np.testing.assert_array_equal(u32_host(vals)[:m], ref["vals"])
+    # capacity error, nothing written
+    rc = lib.gsc_bin(R.context(), n, R.ptr(got["splats"]), tx, ty, R.ptr(keys), R.ptr(vals), m - 1,
+                     C.byref(nk))
+    assert rc == _abi.GSC_ERR_CAPACITY
+    end_bit = 32 + int(np.ceil(np.log2(tx * ty)))
+    _abi.check(lib.gsc_sort_pairs_u64(R.context(), R.ptr(keys), R.ptr(vals), m, 0, end_bit))
+    np.testing.assert_array_equal(u64_host(keys)[:m], ref["sorted_keys"])
+    np.testing.assert_array_equal(u32_host(vals)[:m], ref["sorted_vals"])
+    ranges = cuda.zeros(tx * ty * 2, dtype=cuda.int32, device="cuda")
+    _abi.check(lib.gsc_tile_ranges(R.context(), R.ptr(keys), m, tx * ty, R.ptr(ranges)))
+    np.testing.assert_array_equal(u32_host(ranges), ref["ranges"])
+    R.sync()
+
+
+@pytest.mark.parametrize("n,begin,end", [(0, 0, 64), (1, 0, 64), (2, 0, 64), (511, 0, 64),
+                                          (4096, 0, 64), (4097, 0, 45), (100003, 0, 45),
+                                          (300000, 8, 40), (1 << 20, 0, 64)])
+def test_sort_pairs_bit_exact(cuda, oracle, n, begin, end):
+    rng = np.random.default_rng(n + begin)
+    tiles = rng.integers(0, 8160, n, dtype=np.uint64)
+    depth = rng.uniform(0.5, 10.0, n).astype(np.float32).view(np.uint32).astype(np.uint64)
+    keys = (tiles << np.uint64(32)) | depth
+    if n > 10:  # duplicate keys exercise stability
+        keys[: n // 10] = keys[n // 10: 2 * (n // 10)]
+    if end == 64 and n > 3:
+        keys[::3] = rng.integers(0, 2**63, keys[::3].size, dtype=np.uint64) * np.uint64(2) + np.uint64(1)
+    vals = np.arange(n, dtype=np.uint32)
+    rk, rv = oracle.sort_pairs(keys, vals, begin, end)
+    dk = u64_dev(keys) if n else cuda.zeros(1, dtype=cuda.int64, device="cuda")
+    dv = u32_dev(vals) if n else cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    gs.GPURadixSort.sort(dk, dv, n, begin, end)
+    R.sync()
+    np.testing.assert_array_equal(u64_host(dk)[:n], rk)
+    np.testing.assert_array_equal(u32_host(dv)[:n], rv)
+
+
+def test_sort_c1_distribution_sorted(cuda, oracle):
+    """Config-1 key distribution at 4M pairs: sortedness, permutation, stability."""
+    n = 4_000_000
+    rng = np.random.default_rng(1)
+    tiles = rng.integers(0, 8160, n, dtype=np.uint64)
+    depth = rng.uniform(0.5, 10.0, n).astype(np.float32).view(np.uint32).astype(np.uint64)
+    keys = (tiles << np.uint64(32)) | depth
+    vals = np.arange(n, dtype=np.uint32)
+    dk, dv = u64_dev(keys), u32_dev(vals)
+    gs.GPURadixSort.sort(dk, dv, n, 0, 45)
+    R.sync()
+    k, v = u64_host(dk), u32_host(dv)
+    order = np.argsort(keys, kind="stable")
+    np.testing.assert_array_equal(k, keys[order])
+    np.testing.assert_array_equal(v, vals[order])
+
+
+@pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF])
+@pytest.mark.parametrize("case", CASES)
+def test_rasterize_forward_matches_oracle(cuda, oracle, case, mode):
+    n, W, H, eye = case
+    arrays, g, cam = make(n, W, H, eye=eye)
+    cfg = gs.default_config(mode=mode, background=(0.1, 0.2, 0.3))
+    img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+    nc = ctx.get(_abi.GSC_FRAME_N_CONTRIB, np.uint32)
+    fT = ctx.get(_abi.GSC_FRAME_FINAL_T, np.float32)
+    last = ctx.get(_abi.GSC_FRAME_LAST, np.uint32)
+    ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
+    assert ctx.num_rendered == ref["keys"].size
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
+    im = host(img)
+    assert rel_err(im, ref["image"], 1e-6) <= IMG_RTOL
+    np.testing.assert_array_equal(im, ref["image"])  # shared operation order: exact
+    np.testing.assert_array_equal(nc.reshape(H, W), ref["n_contrib"])
+    np.testing.assert_array_equal(fT.reshape(H, W), ref["final_T"])
+    np.testing.assert_array_equal(last.reshape(H, W), ref["last"])
+
+
+@pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF])
+@pytest.mark.parametrize("case", CASES)
+def test_rasterize_backward_matches_oracle(cuda, oracle, case, mode):
+    n, W, H, eye = case
+    arrays, g, cam = make(n, W, H, eye=eye)
+    cfg = gs.default_config(mode=mode)
+    img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+    target = np.random.default_rng(3).uniform(0, 1, (H, W, 3)).astype(np.float32)
+    scale = 1.0 / target.size
+    loss = cuda.zeros(1, device="cuda")
+    grads = gs.Rasterizer.backward(None, g, cam, ctx, target=to_dev(target), l1_scale=scale,
+                                   loss_sum=loss)
+    R.sync()
+    sc = oracle.Scene(arrays)
+    ref = oracle.forward_pipeline(sc, cam.to_struct(), cfg)
+    g2d, rloss = oracle.composite_backward(W, H, ref["ranges"], ref["sorted_vals"], ref["pre"], cfg,
+                                           ref["final_T"], ref["last"], image=ref["image"],
+                                           target=target, l1_scale=scale)
+    rg, views = oracle.preprocess_backward(sc, cam.to_struct(), cfg, g2d)
+    assert abs(float(loss.item()) - rloss) <= 1e-5 * abs(rloss)
+    pairs = [(grads.dL_dmean2d, views["mean2d"]), (grads.dL_dopacity, views["opacity"]),
+             (grads.dL_dcolors, views["colors"]), (grads.dL_dcov2d, views["cov2d"]),
+             (grads.dL_dposition, rg["position"]), (grads.dL_dlog_scale, rg["log_scale"]),
+             (grads.dL_drotation, rg["rotation"]), (grads.dL_dlogit_opacity, rg["logit_opacity"]),
+             (grads.dL_dsh, rg["sh_coeffs"])]
+    names = ["mean2d", "opacity", "colors", "cov2d", "position", "log_scale", "rotation", "logit", "sh"]
+    for name, (a, b) in zip(names, pairs):
+        e = grad_close(host(a), b)
+        assert e <= GRAD_RTOL, f"{name}: {e}"
+
+
+def test_backward_with_explicit_dl_dimage(cuda, oracle):
+    n, W, H = 3000, 80, 64
+    arrays, g, cam = make(n, W, H)
+    cfg = gs.default_config()
+    img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+    dl = np.random.default_rng(5).standard_normal((H, W, 3)).astype(np.float32) * 1e-3
+    grads = gs.Rasterizer.backward(to_dev(dl), g, cam, ctx)
+    R.sync()
+    sc = oracle.Scene(arrays)
+    ref = oracle.forward_pipeline(sc, cam.to_struct(), cfg)
+    g2d, _ = oracle.composite_backward(W, H, ref["ranges"], ref["sorted_vals"], ref["pre"], cfg,
+                                       ref["final_T"], ref["last"], dL_dimage=dl)
+    rg, _ = oracle.preprocess_backward(sc, cam.to_struct(), cfg, g2d)
+    assert grad_close(host(grads.dL_dposition), rg["position"]) <= GRAD_RTOL
+    assert grad_close(host(grads.dL_dsh), rg["sh_coeffs"]) <= GRAD_RTOL
+    assert grad_close(host(grads.dL_drotation), rg["rotation"]) <= GRAD_RTOL
+
+
+def test_empty_and_culled(cuda, oracle):
+    # all Gaussians behind the camera -> background everywhere, no keys
+    arrays = scene(500, 11)
+    arrays["position"][:, 2] = 10.0  # camera at z=4 looking to -z: all behind
+    g = gs.Gaussian3D(arrays)
+    cam = gs.make_camera(40, 40, (0.0, 0.0, 4.0))
+    cfg = gs.default_config(background=(0.25, 0.5, 0.75))
+    img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+    assert ctx.num_rendered == 0
+    np.testing.assert_array_equal(host(img), np.broadcast_to(np.float32([0.25, 0.5, 0.75]), (40, 40, 3)))
+    grads = gs.Rasterizer.backward(None, g, cam, ctx, target=to_dev(np.zeros((40, 40, 3), np.float32)))
+    R.sync()
+    assert float(grads.arena.abs().max()) == 0.0
+    # zero Gaussians
+    g0 = gs.Gaussian3D(scene(0, 1))
+    img0, ctx0 = gs.Rasterizer.forward(g0, cam, config=cfg)
+    assert ctx0.num_rendered == 0
+
+
+def test_adam_bit_exact(cuda, oracle):
+    rng = np.random.default_rng(9)
+    sizes = [30001, 7, 4096, 3]
+    host_groups, dev_groups = [], []
+    for i, s in enumerate(sizes):
+        p = rng.standard_normal(s).astype(np.float32)
+        gr = rng.standard_normal(s).astype(np.float32)
+        m = rng.standard_normal(s).astype(np.float32) * 0.1
+        v = np.abs(rng.standard_normal(s).astype(np.float32)) * 0.01
+        lr = [1.6e-4, 5e-3, 5e-2, 1e-3][i]
+        wd = 0.01 if i == 2 else 0.0
+        host_groups.append({"param": p.copy(), "grad": gr, "m": m.copy(), "v": v.copy(), "lr": lr,
+                            "weight_decay": wd})
+        dev_groups.append((to_dev(p), to_dev(gr), to_dev(m), to_dev(v), lr, wd))
+    for step in (1, 2, 7):
+        arr = (_abi.AdamGroup * len(sizes))()
+        for i, (p, gr, m, v, lr, wd) in enumerate(dev_groups):
+            arr[i].param, arr[i].grad, arr[i].m, arr[i].v = (p.data_ptr(), gr.data_ptr(), m.data_ptr(),
+                                                             v.data_ptr())
+            arr[i].numel, arr[i].lr, arr[i].weight_decay = p.numel(), lr, wd
+        _abi.check(_abi.lib().gsc_adam_step(R.context(), arr, len(sizes), 0.9, 0.999, 1e-8, step, 0.5))
+        oracle.adam_step(host_groups, 0.9, 0.999, 1e-8, step, 0.5)
+    R.sync()
+    for hg, dg in zip(host_groups, dev_groups):
+        np.testing.assert_array_equal(host(dg[0]), hg["param"])
+        np.testing.assert_array_equal(host(dg[2]), hg["m"])
+        np.testing.assert_array_equal(host(dg[3]), hg["v"])
+
+
+def test_l1_loss_grad(cuda, oracle):
+    rng = np.random.default_rng(2)
+    a = rng.uniform(0, 1, (37, 51, 3)).astype(np.float32)
+    b = rng.uniform(0, 1, (37, 51, 3)).astype(np.float32)
+    b[0, 0] = a[0, 0]
+    loss, grad = gs.l1_with_grad(to_dev(a), to_dev(b))
+    R.sync()
+    rl, rg = oracle.l1_loss_grad(a, b, 1.0 / a.size)
+    np.testing.assert_array_equal(host(grad), rg)
+    assert abs(float(loss.item()) - rl) <= 1e-5 * rl
+
+
+def test_training_step_decreases_loss(cuda):
+    """Forward, fused L1 backward and Adam for a few steps on one view."""
+    n, W, H = 5000, 96, 96
+    arrays, g, cam = make(n, W, H)
+    target = to_dev(np.random.default_rng(4).uniform(0, 1, (H, W, 3)).astype(np.float32))
+    grads = gs.RasterizerGradients(g, screen=False)
+    opt = gs.Adam.for_gaussians(g, grads)
+    ctx = gs.RasterizerContext()
+    losses = []
+    for _ in range(20):
+        grads.zero_()
+        loss = cuda.zeros(1, device="cuda")
+        gs.Rasterizer.forward(g, cam, context=ctx)
+        gs.Rasterizer.backward(None, g, cam, ctx, grads=grads, target=target, loss_sum=loss)
+        opt.step()
+        losses.append(float(loss.item()))
+    R.sync()
+    assert losses[-1] < losses[0]
