@@ -1,0 +1,679 @@
+"""Benchmark of the Gaussian-splatting hot path on B200 (BASELINE.json metric).
+
+Default workload (config 3): full data-parallel training step, 3M Gaussians,
+SH degree 3, 64 views at 1920x1080 on seeded radius-4 sphere poses, L1 loss
+against seeded uniform targets, view-sharded forward+backward, NCCL
+all-reduce of the gradient arena, fused Adam. Metric: views/s (whole job).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c3|c2|c4|c1]
+
+For N > 1 launch with torch.distributed.run (one rank per GPU). Rank 0 prints
+one JSON line. Timing: CUDA events on the working stream, barrier +
+synchronize on both sides, max over ranks. Inputs (708 MB of parameters,
+1.6 GB of targets) are larger than the 126 MB L2, so no flush is needed.
+"""
+import argparse
+import ctypes as C
+import importlib
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# Nominal FP32 (non-tensor) rate of a B200: 148 SMs x 128 lanes x 2 flop x 1.965 GHz.
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+CONFIGS = {
+    "c3": dict(n=3_000_000, seed=0x6A5D0003, extent=1.0, views=64, W=1920, H=1080, radius=4.0,
+               poses="sphere", train=True),
+    "c2": dict(n=1_000_000, seed=0x6A5D0002, extent=1.0, views=1, W=1920, H=1080, radius=4.0,
+               poses="sphere", train=True),
+    "c4": dict(n=6_000_000, seed=0x6A5D0004, extent=3.0, views=256, W=3840, H=2160, radius=8.0,
+               poses="orbit", train=False),
+    "c1": dict(pairs=30_000_000, seed=0x6A5D0001, tiles=8160),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        med = float(np.median(sm)) if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# setup
+# ---------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def make_cameras(gs, cfg):
+    if cfg["poses"] == "sphere":
+        eyes = gs.sphere_poses(cfg["views"], cfg["radius"], cfg["seed"] + 101)
+    else:
+        eyes = gs.orbit_poses(cfg["views"], cfg["radius"])
+    return [gs.make_camera(cfg["W"], cfg["H"], tuple(e)) for e in eyes]
+
+
+def make_targets(cfg, lo, hi):
+    """Seeded U[0,1] RGB targets of views [lo, hi) in pinned host memory."""
+    import torch
+    H, W = cfg["H"], cfg["W"]
+    out = torch.empty(hi - lo, H, W, 3, dtype=torch.float32).pin_memory()
+    for v in range(lo, hi):
+        rng = np.random.default_rng(cfg["seed"] * 1000 + v)
+        out[v - lo].copy_(torch.from_numpy(rng.random((H, W, 3), dtype=np.float32)))
+    return out
+
+
+class Timer:
+    """CUDA events on the working stream, barrier + synchronize on both sides."""
+
+    def __init__(self, torch, world):
+        self.torch, self.world = torch, world
+
+    def _fence(self):
+        if self.world > 1:
+            self.torch.distributed.barrier()
+        self.torch.cuda.synchronize()
+
+    def __enter__(self):
+        self._fence()
+        self.a = self.torch.cuda.Event(enable_timing=True)
+        self.b = self.torch.cuda.Event(enable_timing=True)
+        self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        self.b.record()
+        self._fence()
+        self.ms = self.a.elapsed_time(self.b)
+
+    def max_over_ranks(self):
+        if self.world == 1:
+            return self.ms
+        t = self.torch.tensor([self.ms], device="cuda", dtype=self.torch.float64)
+        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+
+def profile_read(gs, ctx, reset=True):
+    _abi = gs._abi
+    ms = (C.c_double * len(_abi.STAGES))()
+    calls = (C.c_int64 * len(_abi.STAGES))()
+    kern = (C.c_int64 * len(_abi.STAGES))()
+    _abi.check(_abi.lib().gsc_profile_read(ctx, ms, calls, kern, 1 if reset else 0))
+    return {name: {"ms": ms[i], "calls": calls[i], "kernels": kern[i]}
+            for i, name in enumerate(_abi.STAGES)}
+
+
+def pge_count(gs, rctx):
+    """Pixel-Gaussian evaluations of the frame's last forward: per pixel, the
+    tile-list entries visited before the T > t_stop test failed."""
+    _abi = gs._abi
+    W, H = rctx.width, rctx.height
+    last = rctx.get(_abi.GSC_FRAME_LAST, np.uint32).reshape(H, W).astype(np.int64)
+    fT = rctx.get(_abi.GSC_FRAME_FINAL_T, np.float32).reshape(H, W)
+    rng = rctx.get(_abi.GSC_FRAME_RANGES, np.uint32).reshape(-1, 2).astype(np.int64)
+    tx = (W + 15) // 16
+    ty_idx = np.arange(H)[:, None] // 16
+    tx_idx = np.arange(W)[None, :] // 16
+    tile = ty_idx * tx + tx_idx
+    length = (rng[:, 1] - rng[:, 0])[tile]
+    stopped = fT <= rctx.config.t_stop
+    visited = np.where(stopped, last, length)
+    return int(visited.sum())
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work per stage (bytes, or FP32 ops for compositing)
+# ---------------------------------------------------------------------------
+PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
+EMIT_B_PER_G = 32       # read mean/radius/depth/tiles (two float4 of the record)
+EMIT_B_PER_KEY = 12     # write u64 key + u32 value
+RANGES_B_PER_KEY = 8
+PREPROCESS_BWD_B = 556  # read 236 params + 36 grad2d, read+write 236 grads (visible Gaussians)
+ADAM_B = 28 * 59        # read p, g, m, v + write p, m, v per float
+FWD_FLOP_PER_PGE = 15
+BWD_FLOP_PER_PGE = 30
+
+
+def sort_bytes_per_pair(end_bit):
+    passes = (end_bit + 7) // 8
+    return 8 + 24 * passes
+
+
+def stage_work(stats, n, keys_per_view, pge, tiles, end_bit):
+    """Algorithmic bytes (or flops) per launch of each stage."""
+    return {
+        "preprocess": ("hbm", PREPROCESS_B * n),
+        "emit": ("hbm", EMIT_B_PER_G * n + EMIT_B_PER_KEY * keys_per_view),
+        "sort": ("hbm", sort_bytes_per_pair(end_bit) * keys_per_view),
+        "ranges": ("hbm", RANGES_B_PER_KEY * keys_per_view + 8 * tiles),
+        "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge),
+        "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge),
+        "preprocess_bwd": ("hbm", PREPROCESS_BWD_B * n),
+        "adam": ("hbm", ADAM_B * n),
+    }
+
+
+def rooflines(stats, work, peaks):
+    out = {}
+    for name, (bound, amount) in work.items():
+        s = stats.get(name)
+        if not s or s["calls"] == 0 or s["ms"] <= 0:
+            continue
+        per_launch_s = s["ms"] / 1e3 / s["calls"]
+        if bound == "hbm":
+            ach = amount / per_launch_s / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        else:
+            ach = amount / per_launch_s / 1e12
+            peak = FP32_NOMINAL_TFLOPS
+            unit = "TFLOP/s"
+        out[name] = {"bound": bound, "achieved": round(ach, 2), "peak": round(peak, 1), "unit": unit,
+                     "frac": round(ach / peak, 4), "ms_per_launch": round(per_launch_s * 1e3, 4),
+                     "launches": s["calls"], "share": None}
+    tot = sum(stats[k]["ms"] for k in stats)
+    for k in out:
+        out[k]["share"] = round(stats[k]["ms"] / tot, 4) if tot else None
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port on the host cores (bounded sample)
+# ---------------------------------------------------------------------------
+def cpu_view_seconds(gs, arrays, cam, rcfg, target, threads, with_backward=True):
+    from oracle import oracle as O
+    O.set_threads(threads)
+    sc = O.Scene(arrays)
+    t = time.perf_counter()
+    if with_backward:
+        O.render_view(sc, cam.to_struct(), rcfg, target, 1.0 / target.size)
+    else:
+        O.render_view(sc, cam.to_struct(), rcfg)
+    return time.perf_counter() - t
+
+
+def cpu_adam_seconds(n, threads):
+    from oracle import oracle as O
+    O.set_threads(threads)
+    rng = np.random.default_rng(0)
+    groups = []
+    for w, lr in ((3, 1.6e-4), (3, 5e-3), (4, 1e-3), (1, 5e-2), (48, 2.5e-3)):
+        p = rng.standard_normal(n * w, dtype=np.float32)
+        groups.append({"param": p, "grad": p.copy(), "m": np.zeros_like(p), "v": np.zeros_like(p),
+                       "lr": lr})
+    t = time.perf_counter()
+    O.adam_step(groups, 0.9, 0.999, 1e-8, 1, 1.0 / 64)
+    return time.perf_counter() - t
+
+
+def cpu_baseline_train(gs, cfg, arrays, cams, rcfg, targets_host, threads):
+    """One full view forward+backward (+ Adam over all parameters / views)."""
+    tgt = targets_host[0].numpy()
+    tv = cpu_view_seconds(gs, arrays, cams[0], rcfg, tgt, threads)
+    ta = cpu_adam_seconds(cfg["n"], threads)
+    per_view = tv + ta / cfg["views"]
+    return {"value": round(1.0 / per_view, 4), "unit": "views/s", "cores": threads, "kind": "port",
+            "sample": (f"1 view (view 0, {cfg['W']}x{cfg['H']}, {cfg['n']} Gaussians) fwd+bwd+L1 "
+                       f"in {tv:.2f} s + Adam over all {cfg['n']}x59 floats in {ta:.2f} s / "
+                       f"{cfg['views']} views; CPU oracle (C++ restatement, OpenMP)")}
+
+
+# ---------------------------------------------------------------------------
+# ours: training configs (c3, c2)
+# ---------------------------------------------------------------------------
+def run_train(args, cfg, rank, world, local, peaks, peak_kind):
+    import torch
+    gs = importlib.import_module("crystal-gausplat_b200")
+    trainer_mod = importlib.import_module("crystal-gausplat_b200.trainer")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = torch.distributed.group.WORLD if world > 1 else None
+    arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
+    g = gs.Gaussian3D(arrays, device=dev)
+    cams = make_cameras(gs, cfg)
+    rcfg = gs.default_config()
+    tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg)
+    host_t = make_targets(cfg, tr.lo, tr.hi)
+    dev_t = host_t.to(dev)
+    ctx = gs.context(dev)
+    lib = gs._abi.lib()
+
+    def targets(v):
+        return dev_t[v - tr.lo]
+
+    for _ in range(args.warmup):
+        tr.step(targets)
+    torch.cuda.synchronize()
+    profile_read(gs, ctx, reset=True)
+    k0 = lib.gsc_kernel_count(ctx)
+    keys_total = 0
+    lib.gsc_profile_enable(ctx, 1)
+    with ClockSampler(local) as clk:
+        with Timer(torch, world) as tm:
+            for _ in range(args.steps):
+                tr.zero()
+                for v in tr.my_views:
+                    tr.view_fwd_bwd(v, targets(v))
+                    keys_total += tr.ctx.num_rendered
+                tr.reduce_and_step()
+    lib.gsc_profile_enable(ctx, 0)
+    ms = tm.max_over_ranks()
+    stats = profile_read(gs, ctx, reset=True)
+    launches = int(lib.gsc_kernel_count(ctx) - k0)
+    views_done = args.steps * cfg["views"]
+    value = views_done / (ms / 1e3)
+
+    # roofline sample: the last view rendered on this rank
+    pge = pge_count(gs, tr.ctx)
+    my_views = max(1, tr.hi - tr.lo)
+    keys_per_view = keys_total / (args.steps * my_views)
+    tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
+    end_bit = 32 + int(math.ceil(math.log2(tiles)))
+    work = stage_work(stats, cfg["n"], keys_per_view, pge, tiles, end_bit)
+    roof = rooflines(stats, work, peaks)
+
+    e2e = None
+    if not args.no_e2e:
+        stage = torch.empty_like(dev_t[0])
+        for _ in range(1):
+            tr.zero()
+            for v in tr.my_views:
+                stage.copy_(host_t[v - tr.lo], non_blocking=True)
+                tr.view_fwd_bwd(v, stage)
+            tr.reduce_and_step()
+            tr.loss.item()
+        with Timer(torch, world) as tm2:
+            for _ in range(args.steps):
+                tr.zero()
+                for v in tr.my_views:
+                    stage.copy_(host_t[v - tr.lo], non_blocking=True)
+                    tr.view_fwd_bwd(v, stage)
+                tr.reduce_and_step()
+                float(tr.loss.item())  # device -> host read of the step's loss
+        ms2 = tm2.max_over_ranks()
+        e2e = {"value": round(views_done / (ms2 / 1e3), 3), "unit": "views/s",
+               "h2d_bytes_per_step": int(cfg["views"] * cfg["H"] * cfg["W"] * 3 * 4),
+               "d2h_bytes_per_step": 4 * world,
+               "path": "Rasterizer.forward/backward + Adam through the C ABI; targets from pinned host"}
+
+    result = None
+    if rank == 0:
+        dominant = max(roof, key=lambda k: roof[k]["share"] or 0) if roof else None
+        hbm_stages = [k for k in roof if roof[k]["bound"] == "hbm"]
+        top_hbm = max(hbm_stages, key=lambda k: roof[k]["share"] or 0) if hbm_stages else None
+        result = {
+            "metric": f"views/s fwd+bwd ({cfg['n'] // 1_000_000}M Gauss, {cfg['H']}p)",
+            "value": round(value, 3), "unit": "views/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Gaussians, poses and U[0,1] targets per BASELINE.json)",
+            "config": {"workload": f"{args.config}: train step, {cfg['n']} Gaussians SH3, {cfg['views']} views "
+                                   f"{cfg['W']}x{cfg['H']}, L1, all-reduce + fused Adam",
+                       "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
+                       "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush",
+                       "keys_per_view": round(keys_per_view), "pge_sample_view": pge},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "e2e": e2e,
+            "roofline": dict(roof[dominant], kernel=dominant,
+                             peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind,
+                             traffic=None) if dominant else None,
+            "roofline_hbm": dict(roof[top_hbm], kernel=top_hbm, peak_kind=peak_kind, traffic=None)
+            if top_hbm else None,
+            "stages": roof,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_train(gs, cfg, arrays, cams, rcfg, host_t, os.cpu_count())
+    return result
+
+
+def reference_train(args, cfg):
+    """--impl reference: the oracle port on all host threads, one view per step."""
+    gs = importlib.import_module("crystal-gausplat_b200")
+    arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
+    cams = make_cameras(gs, cfg)
+    rcfg = gs.default_config()
+    threads = os.cpu_count()
+    H, W = cfg["H"], cfg["W"]
+    ta = cpu_adam_seconds(cfg["n"], threads)
+    times = []
+    for i in range(args.warmup + args.steps):
+        v = i % cfg["views"]
+        tgt = np.random.default_rng(cfg["seed"] * 1000 + v).random((H, W, 3), dtype=np.float32)
+        t = cpu_view_seconds(gs, arrays, cams[v], rcfg, tgt, threads)
+        if i >= args.warmup:
+            times.append(t + ta / cfg["views"])
+    per_view = float(np.mean(times))
+    value = 1.0 / per_view
+    return {"impl": "reference", "metric": f"views/s fwd+bwd ({cfg['n'] // 1_000_000}M Gauss, {H}p)",
+            "value": round(value, 4), "unit": "views/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_view * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config}: one view fwd+bwd per step + Adam/views"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "views/s", "cores": threads, "kind": "port",
+                             "sample": "one view per step (fwd+bwd+L1) + Adam over all parameters / views; "
+                                       "the reference (Crystal + Metal) cannot build here, so the C++ "
+                                       "oracle restating it runs"},
+            "e2e": {"value": round(value, 4), "unit": "views/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------------------
+# ours: render sweep (c4) and sort alone (c1)
+# ---------------------------------------------------------------------------
+def run_render(args, cfg, rank, world, local, peaks, peak_kind):
+    import torch
+    gs = importlib.import_module("crystal-gausplat_b200")
+    trainer_mod = importlib.import_module("crystal-gausplat_b200.trainer")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
+    g = gs.Gaussian3D(arrays, device=dev)
+    cams = make_cameras(gs, cfg)
+    rcfg = gs.default_config()
+    lo, hi = trainer_mod.shard(len(cams), rank, world)
+    rctx = gs.RasterizerContext(dev)
+    img = torch.empty(cfg["H"], cfg["W"], 3, device=dev)
+    ctx = gs.context(dev)
+    lib = gs._abi.lib()
+    for _ in range(args.warmup):
+        for v in range(lo, hi):
+            gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
+    torch.cuda.synchronize()
+    profile_read(gs, ctx, reset=True)
+    k0 = lib.gsc_kernel_count(ctx)
+    keys_total = 0
+    lib.gsc_profile_enable(ctx, 1)
+    with ClockSampler(local) as clk:
+        with Timer(torch, world) as tm:
+            for _ in range(args.steps):
+                for v in range(lo, hi):
+                    gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
+                    keys_total += rctx.num_rendered
+    lib.gsc_profile_enable(ctx, 0)
+    ms = tm.max_over_ranks()
+    stats = profile_read(gs, ctx, reset=True)
+    launches = int(lib.gsc_kernel_count(ctx) - k0)
+    pix = args.steps * cfg["views"] * cfg["W"] * cfg["H"]
+    value = pix / 1e6 / (ms / 1e3)
+    pge = pge_count(gs, rctx)
+    tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
+    end_bit = 32 + int(math.ceil(math.log2(tiles)))
+    kpv = keys_total / max(1, args.steps * (hi - lo))
+    roof = rooflines(stats, stage_work(stats, cfg["n"], kpv, pge, tiles, end_bit), peaks)
+    e2e = None
+    if not args.no_e2e:
+        host_img = torch.empty(cfg["H"], cfg["W"], 3).pin_memory()
+        with Timer(torch, world) as tm2:
+            for _ in range(args.steps):
+                for v in range(lo, hi):
+                    gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
+                    host_img.copy_(img, non_blocking=True)
+        ms2 = tm2.max_over_ranks()
+        e2e = {"value": round(pix / 1e6 / (ms2 / 1e3), 2), "unit": "MPix/s", "h2d_bytes_per_step": 0,
+               "d2h_bytes_per_step": int(cfg["views"] * cfg["H"] * cfg["W"] * 12),
+               "path": "Rasterizer.forward through the C ABI; every image read back to pinned host"}
+    if rank != 0:
+        return None
+    dominant = max(roof, key=lambda k: roof[k]["share"] or 0)
+    res = {"metric": "render MPix/s (6M Gauss, 4K)", "value": round(value, 2), "unit": "MPix/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": f"c4: render-only, {cfg['n']} Gaussians, {cfg['views']} views "
+                                  f"{cfg['W']}x{cfg['H']}", "parallelism": f"views/{world}",
+                      "l2": "inputs larger than L2, no flush", "keys_per_view": round(kpv)},
+           "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
+           "roofline": dict(roof[dominant], kernel=dominant, traffic=None,
+                            peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind),
+           "stages": roof}
+    if world == 1 and not args.no_cpu_baseline:
+        t = cpu_view_seconds(gs, arrays, cams[0], rcfg, None, os.cpu_count(), with_backward=False)
+        res["cpu_baseline"] = {"value": round(cfg["W"] * cfg["H"] / 1e6 / t, 3), "unit": "MPix/s",
+                               "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"1 view (view 0) forward, {t:.2f} s, CPU oracle (OpenMP)"}
+    return res
+
+
+def sort_input(cfg, n):
+    rng = np.random.default_rng(cfg["seed"])
+    tiles = rng.integers(0, cfg["tiles"], n, dtype=np.uint64)
+    depth = rng.uniform(0.5, 10.0, n).astype(np.float32).view(np.uint32).astype(np.uint64)
+    return (tiles << np.uint64(32)) | depth, np.arange(n, dtype=np.uint32)
+
+
+def run_sort(args, cfg, rank, world, local, peaks, peak_kind):
+    import torch
+    gs = importlib.import_module("crystal-gausplat_b200")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = cfg["pairs"]
+    keys, vals = sort_input(cfg, n)
+    k0d = torch.from_numpy(keys.view(np.int64)).to(dev)
+    v0d = torch.from_numpy(vals.view(np.int32)).to(dev)
+    kd, vd = k0d.clone(), v0d.clone()
+    end_bit = 32 + int(math.ceil(math.log2(cfg["tiles"])))
+    ctx = gs.context(dev)
+    lib = gs._abi.lib()
+    for _ in range(args.warmup):
+        kd.copy_(k0d); vd.copy_(v0d)
+        gs.GPURadixSort.sort(kd, vd, n, 0, end_bit)
+    torch.cuda.synchronize()
+    profile_read(gs, ctx, reset=True)
+    k0 = lib.gsc_kernel_count(ctx)
+    lib.gsc_profile_enable(ctx, 1)
+    with ClockSampler(local) as clk:
+        with Timer(torch, world) as tm:
+            for _ in range(args.steps):
+                kd.copy_(k0d); vd.copy_(v0d)  # restore the unsorted input (outside the sort stage)
+                gs.GPURadixSort.sort(kd, vd, n, 0, end_bit)
+    lib.gsc_profile_enable(ctx, 0)
+    stats = profile_read(gs, ctx, reset=True)
+    sort_ms = stats["sort"]["ms"]
+    if world > 1:
+        t = torch.tensor([sort_ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        sort_ms = float(t.item())
+    value = world * args.steps * n / 1e6 / (sort_ms / 1e3)
+    per = sort_ms / 1e3 / args.steps
+    ach = sort_bytes_per_pair(end_bit) * n / per / 1e9
+    e2e = None
+    if not args.no_e2e:
+        hk = torch.from_numpy(keys.view(np.int64)).pin_memory()
+        hv = torch.from_numpy(vals.view(np.int32)).pin_memory()
+        with Timer(torch, world) as tm2:
+            for _ in range(args.steps):
+                kd.copy_(hk, non_blocking=True); vd.copy_(hv, non_blocking=True)
+                gs.GPURadixSort.sort(kd, vd, n, 0, end_bit)
+                hk2 = kd.to("cpu", non_blocking=False)
+                hv2 = vd.to("cpu", non_blocking=False)
+        ms2 = tm2.max_over_ranks()
+        e2e = {"value": round(world * args.steps * n / 1e6 / (ms2 / 1e3), 1), "unit": "Mkey/s",
+               "h2d_bytes_per_step": n * 12, "d2h_bytes_per_step": n * 12,
+               "path": "GPURadixSort.sort (gsc_sort_pairs_u64) with host keys/values in and out"}
+    if rank != 0:
+        return None
+    res = {"metric": "sort Mkey/s (30M u64/u32 pairs)", "value": round(value, 1), "unit": "Mkey/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
+           "data": "synthetic (tile in [0,8160) << 32 | fp32 depth bits, depth U[0.5,10])",
+           "config": {"workload": f"c1: stable sort of {n} pairs by bits [0,{end_bit})",
+                      "l2": "inputs (360 MB) larger than L2, no flush"},
+           "gpu_launches": int(lib.gsc_kernel_count(ctx) - k0), "clocks": clk.summary(), "e2e": e2e,
+           "roofline": {"kernel": "sort", "bound": "hbm", "achieved": round(ach, 1),
+                        "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4),
+                        "traffic": None, "peak_kind": peak_kind,
+                        "bytes_per_pair": sort_bytes_per_pair(end_bit)}}
+    if world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = reference_sort(args, cfg, bounded=True)["cpu_baseline"]
+    return res
+
+
+def reference_sort(args, cfg, bounded=False):
+    from oracle import oracle as O
+    n = 3_000_000
+    keys, vals = sort_input(cfg, n)
+    times = []
+    reps = 2 if bounded else args.warmup + args.steps
+    for i in range(reps):
+        t = time.perf_counter()
+        O.sort_pairs(keys, vals, 0, 45)
+        times.append(time.perf_counter() - t)
+    per = float(np.mean(times[-max(1, len(times) - (0 if bounded else args.warmup)):]))
+    v = n / 1e6 / per
+    return {"impl": "reference", "metric": "sort Mkey/s (30M u64/u32 pairs)", "value": round(v, 2),
+            "unit": "Mkey/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": "c1 sample: 3M of the 30M pairs per step"},
+            "cpu_baseline": {"value": round(v, 2), "unit": "Mkey/s", "cores": 1, "kind": "port",
+                             "sample": "3M pairs per step, std::stable_sort (the reference's CPU key "
+                                       "sort, rasterizer.cr:250-255, is a comparison sort)"},
+            "e2e": {"value": round(v, 2), "unit": "Mkey/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def reference_render(args, cfg):
+    gs = importlib.import_module("crystal-gausplat_b200")
+    arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
+    cams = make_cameras(gs, cfg)
+    rcfg = gs.default_config()
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = cpu_view_seconds(gs, arrays, cams[i % len(cams)], rcfg, None, os.cpu_count(), False)
+        if i >= args.warmup:
+            times.append(t)
+    v = cfg["W"] * cfg["H"] / 1e6 / float(np.mean(times))
+    return {"impl": "reference", "metric": "render MPix/s (6M Gauss, 4K)", "value": round(v, 3),
+            "unit": "MPix/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(float(np.mean(times)) * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "c4 sample: one 4K view forward per step"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "MPix/s", "cores": os.cpu_count(),
+                             "kind": "port", "sample": "one view per step, CPU oracle (OpenMP)"},
+            "e2e": {"value": round(v, 3), "unit": "MPix/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        if rank == 0:
+            if args.config == "c1":
+                res = reference_sort(args, cfg)
+            elif args.config == "c4":
+                res = reference_render(args, cfg)
+            else:
+                res = reference_train(args, cfg)
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    peaks, peak_kind = load_peaks()
+    if args.config in ("c3", "c2"):
+        res = run_train(args, cfg, rank, world, local, peaks, peak_kind)
+    elif args.config == "c4":
+        res = run_render(args, cfg, rank, world, local, peaks, peak_kind)
+    else:
+        res = run_sort(args, cfg, rank, world, local, peaks, peak_kind)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

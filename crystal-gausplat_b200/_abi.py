@@ -115,7 +115,14 @@ _SIGS = {
                                          C.POINTER(RasterConfig), P, P, C.c_float, P,
                                          C.POINTER(GaussianGrads), C.POINTER(Grads2D)]),
     "gsc_frame_get": (C.c_int, [P, C.c_int, C.POINTER(P), C.POINTER(C.c_int64)]),
+    "gsc_profile_enable": (C.c_int, [P, C.c_int]),
+    "gsc_profile_read": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_int64),
+                                   C.POINTER(C.c_int64), C.c_int]),
+    "gsc_kernel_count": (C.c_int64, [P]),
 }
+
+STAGES = ("preprocess", "scan", "emit", "sort", "ranges", "composite_fwd", "composite_bwd",
+          "preprocess_bwd", "adam", "l1")
 
 EXPORTED = tuple(_SIGS)
 

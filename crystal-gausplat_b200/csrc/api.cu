@@ -245,6 +245,8 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
   a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
+  StageScope sc(ctx, GSC_STAGE_PREPROCESS);
+  sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
 }
 
@@ -253,7 +255,12 @@ static int do_scan(gsc_ctx* ctx, int64_t n, const uint32_t* sums, uint64_t* offs
                    uint64_t* host_total) {
   *host_total = 0;
   if (n == 0) return GSC_OK;
-  int rc = launch_scan_block_sums(sums, (n + 255) / 256, offsets, total, ctx->stream);
+  int rc;
+  {
+    StageScope sc(ctx, GSC_STAGE_SCAN);
+    sc.kernels(1);
+    rc = launch_scan_block_sums(sums, (n + 255) / 256, offsets, total, ctx->stream);
+  }
   if (rc) return rc;
   return read_u64(ctx, total, host_total);
 }
@@ -295,6 +302,8 @@ static int do_preprocess_bwd(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_cam
   if (g2d) {
     a.d_mean2d = g2d->mean2d; a.d_cov2d = g2d->cov2d; a.d_opacity = g2d->opacity; a.d_colors = g2d->colors;
   }
+  StageScope sc(ctx, GSC_STAGE_PREPROCESS_BWD);
+  sc.kernels(g->count ? 1 : 0);
   return launch_preprocess_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream);
 }
 
@@ -337,7 +346,11 @@ GSC_API int gsc_bin(gsc_ctx* ctx, int64_t n, const float* splats, int32_t tiles_
   uint32_t* sums = (uint32_t*)scratch_base(ctx);
   uint64_t* offsets = (uint64_t*)(scratch_base(ctx) + align256(nb * 4));
   uint64_t* total = (uint64_t*)(scratch_base(ctx) + align256(nb * 4) + align256(nb * 8));
-  GS_TRY(launch_block_sums(splats, n, sums, ctx->stream));
+  {
+    StageScope sc(ctx, GSC_STAGE_SCAN);
+    sc.kernels(1);
+    GS_TRY(launch_block_sums(splats, n, sums, ctx->stream));
+  }
   uint64_t m = 0;
   GS_TRY(do_scan(ctx, n, sums, offsets, total, &m));
   *num_keys = (int64_t)m;
@@ -347,6 +360,8 @@ GSC_API int gsc_bin(gsc_ctx* ctx, int64_t n, const float* splats, int32_t tiles_
   }
   if (m == 0) return GSC_OK;
   GS_REQUIRE(keys && values, "gsc_bin: null keys/values");
+  StageScope sc(ctx, GSC_STAGE_EMIT);
+  sc.kernels(1);
   return launch_emit_keys(splats, n, offsets, tiles_x, tiles_y, keys, values, ctx->stream);
 }
 
@@ -358,6 +373,8 @@ GSC_API int gsc_sort_pairs_u64(gsc_ctx* ctx, uint64_t* keys, uint32_t* values, i
   if (n <= 1 || begin_bit == end_bit) return GSC_OK;
   GS_REQUIRE(keys && values, "gsc_sort_pairs_u64: null keys/values");
   GS_TRY(scratch_reserve(ctx, sort_scratch_bytes(n, begin_bit, end_bit)));
+  StageScope sc(ctx, GSC_STAGE_SORT);
+  sc.kernels(1 + (end_bit - begin_bit + 7) / 8);
   return launch_sort_pairs(ctx, keys, values, n, begin_bit, end_bit, scratch_base(ctx));
 }
 
@@ -365,6 +382,8 @@ GSC_API int gsc_tile_ranges(gsc_ctx* ctx, const uint64_t* sorted_keys, int64_t n
                             uint32_t* ranges) {
   GS_REQUIRE(ctx && ranges && num_tiles > 0, "gsc_tile_ranges: bad argument");
   GS_REQUIRE(n >= 0 && (n == 0 || sorted_keys), "gsc_tile_ranges: bad keys");
+  StageScope sc(ctx, GSC_STAGE_RANGES);
+  sc.kernels(n ? 1 : 0);
   return launch_tile_ranges(sorted_keys, n, num_tiles, ranges, ctx->stream);
 }
 
@@ -377,6 +396,8 @@ GSC_API int gsc_composite_forward(gsc_ctx* ctx, const float* splats, const uint3
   CompositeFwdArgs a;
   fill_fwd(&a, splats, values, ranges, width, height, cfg);
   a.image = image; a.n_contrib = n_contrib; a.final_T = final_T; a.last = last;
+  StageScope sc(ctx, GSC_STAGE_COMPOSITE_FWD);
+  sc.kernels(1);
   return launch_composite_fwd(a, ctx->stream);
 }
 
@@ -395,6 +416,8 @@ GSC_API int gsc_composite_backward(gsc_ctx* ctx, const float* splats, const uint
   fill_bwd(&a, splats, values, ranges, width, height, cfg);
   a.dL_dimage = dL_dimage; a.image = image; a.target = target; a.l1_scale = l1_scale;
   a.final_T = final_T; a.last = last; a.grad2d = grad2d; a.loss_sum = loss_sum;
+  StageScope sc(ctx, GSC_STAGE_COMPOSITE_BWD);
+  sc.kernels(1);
   return launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream);
 }
 
@@ -412,6 +435,8 @@ GSC_API int gsc_preprocess_backward(gsc_ctx* ctx, const gsc_gaussians* g, const 
 GSC_API int gsc_l1_loss_grad(gsc_ctx* ctx, const float* pred, const float* target, int64_t numel,
                              float scale, float* grad, float* loss_sum) {
   GS_REQUIRE(ctx && numel >= 0 && (numel == 0 || (pred && target && grad)), "gsc_l1_loss_grad: bad argument");
+  StageScope sc(ctx, GSC_STAGE_L1);
+  sc.kernels(numel ? 1 : 0);
   return launch_l1(pred, target, numel, scale, grad, loss_sum, ctx->num_sms, ctx->stream);
 }
 
@@ -438,6 +463,8 @@ GSC_API int gsc_adam_step(gsc_ctx* ctx, const gsc_adam_group* groups, int32_t ng
     run += (G.numel + 3) / 4;
     a.chunk_end[i] = run;
   }
+  StageScope sc(ctx, GSC_STAGE_ADAM);
+  sc.kernels(run ? 1 : 0);
   return launch_adam(a, ctx->stream);
 }
 
@@ -512,19 +539,33 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   uint64_t* keys = (uint64_t*)f->keys.ptr;
   uint32_t* vals = (uint32_t*)f->vals.ptr;
   if (m) {
-    GS_TRY(launch_emit_keys(splats, n, (const uint64_t*)f->offsets.ptr, tx, ty, keys, vals, ctx->stream));
+    {
+      StageScope sc(ctx, GSC_STAGE_EMIT);
+      sc.kernels(1);
+      GS_TRY(launch_emit_keys(splats, n, (const uint64_t*)f->offsets.ptr, tx, ty, keys, vals, ctx->stream));
+    }
     const int end_bit = 32 + tile_bits_of(tx * ty);
     GS_TRY(scratch_reserve(ctx, sort_scratch_bytes((int64_t)m, 0, end_bit)));
+    StageScope sc(ctx, GSC_STAGE_SORT);
+    sc.kernels(1 + (end_bit + 7) / 8);
     GS_TRY(launch_sort_pairs(ctx, keys, vals, (int64_t)m, 0, end_bit, scratch_base(ctx)));
   }
-  GS_TRY(launch_tile_ranges(keys, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
+  {
+    StageScope sc(ctx, GSC_STAGE_RANGES);
+    sc.kernels(m ? 1 : 0);
+    GS_TRY(launch_tile_ranges(keys, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
+  }
   CompositeFwdArgs a;
   fill_fwd(&a, splats, vals, (const uint32_t*)f->ranges.ptr, W, H, cfg);
   a.image = image;
   a.final_T = (float*)f->final_T.ptr;
   a.last = (uint32_t*)f->last.ptr;
   a.n_contrib = (uint32_t*)f->n_contrib.ptr;
-  GS_TRY(launch_composite_fwd(a, ctx->stream));
+  {
+    StageScope sc(ctx, GSC_STAGE_COMPOSITE_FWD);
+    sc.kernels(1);
+    GS_TRY(launch_composite_fwd(a, ctx->stream));
+  }
   if (n_contrib)
     GS_CK(cudaMemcpyAsync(n_contrib, f->n_contrib.ptr, npix * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   if (final_T)
@@ -562,7 +603,11 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussia
   a.last = (const uint32_t*)f->last.ptr;
   a.grad2d = grad2d;
   a.loss_sum = loss_sum;
-  GS_TRY(launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream));
+  {
+    StageScope sc(ctx, GSC_STAGE_COMPOSITE_BWD);
+    sc.kernels(1);
+    GS_TRY(launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream));
+  }
   return do_preprocess_bwd(ctx, g, cam, cfg, grad2d, grads, g2d);
 }
 
@@ -587,5 +632,83 @@ GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {
   if (count) *count = c;
   return GSC_OK;
 }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Tracing
+// ---------------------------------------------------------------------------
+namespace gs {
+
+static cudaEvent_t take_event(gsc_ctx* ctx) {
+  if (!ctx->ev_pool.empty()) {
+    cudaEvent_t e = ctx->ev_pool.back();
+    ctx->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return e;
+}
+
+StageScope::StageScope(gsc_ctx* c, int s) : ctx(c), stage(s) {
+  ctx->calls[stage]++;
+  if (ctx->profiling) {
+    a = take_event(ctx);
+    if (a) cudaEventRecord(a, ctx->stream);
+  }
+}
+
+StageScope::~StageScope() {
+  if (!a) return;
+  cudaEvent_t b = take_event(ctx);
+  if (!b) return;
+  cudaEventRecord(b, ctx->stream);
+  ctx->marks.push_back({stage, a, b});
+}
+
+void StageScope::kernels(int k) {
+  ctx->kernels += k;
+  ctx->stage_kernels[stage] += k;
+}
+
+}  // namespace gs
+
+extern "C" {
+
+GSC_API int gsc_profile_enable(gsc_ctx* ctx, int on) {
+  GS_REQUIRE(ctx, "gsc_profile_enable: null context");
+  ctx->profiling = on != 0;
+  return GSC_OK;
+}
+
+GSC_API int gsc_profile_read(gsc_ctx* ctx, double* ms, int64_t* calls, int64_t* kernels, int reset) {
+  GS_REQUIRE(ctx, "gsc_profile_read: null context");
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  for (auto& m : ctx->marks) {
+    float t = 0.0f;
+    if (cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess) ctx->ms[m.stage] += t;
+    else cudaGetLastError();
+    ctx->ev_pool.push_back(m.a);
+    ctx->ev_pool.push_back(m.b);
+  }
+  ctx->marks.clear();
+  for (int s = 0; s < GSC_STAGE_COUNT; s++) {
+    if (ms) ms[s] = ctx->ms[s];
+    if (calls) calls[s] = ctx->calls[s];
+    if (kernels) kernels[s] = ctx->stage_kernels[s];
+    if (reset) {
+      ctx->ms[s] = 0.0;
+      ctx->calls[s] = 0;
+      ctx->stage_kernels[s] = 0;
+    }
+  }
+  return GSC_OK;
+}
+
+GSC_API int64_t gsc_kernel_count(gsc_ctx* ctx) { return ctx ? ctx->kernels : 0; }
 
 }  // extern "C"

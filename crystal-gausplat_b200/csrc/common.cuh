@@ -12,6 +12,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "../../include/gsplat_cuda.h"
 
@@ -110,7 +111,29 @@ struct gsc_ctx {
   GsBuf scratch;              // per-call temporary storage (sort double buffer, ...)
   uint32_t* err = nullptr;    // device error word
   void* pinned = nullptr;     // 4 KB pinned host staging for small readbacks
+  // tracing
+  bool profiling = false;
+  int64_t kernels = 0;
+  std::vector<cudaEvent_t> ev_pool;
+  struct Mark { int stage; cudaEvent_t a, b; };
+  std::vector<Mark> marks;
+  int64_t calls[GSC_STAGE_COUNT] = {};
+  int64_t stage_kernels[GSC_STAGE_COUNT] = {};
+  double ms[GSC_STAGE_COUNT] = {};
 };
+
+namespace gs {
+// Brackets one stage invocation with CUDA events (when profiling) and counts
+// its kernel launches (always).
+struct StageScope {
+  gsc_ctx* ctx;
+  int stage;
+  cudaEvent_t a = nullptr;
+  StageScope(gsc_ctx* c, int s);
+  ~StageScope();
+  void kernels(int k);
+};
+}  // namespace gs
 
 namespace gs {
 

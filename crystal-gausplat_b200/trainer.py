@@ -1,0 +1,71 @@
+"""View-sharded data-parallel training step (Trainer#train_step,
+src/gaussian_splatting/trainer.cr:178-215, batched over views).
+
+One process per GPU. Every rank holds a full replica of the Gaussians and
+renders + backpropagates its own slice of the view batch, accumulating fp32
+gradients in one flat arena; one all-reduce (NCCL over NVLink) sums the
+arena, and the fused Adam kernel applies the view mean (grad_scale = 1/views).
+The order is grads -> all-reduce -> Adam -> zero (the reference zeroes the
+gradients BEFORE its optimiser step, trainer.cr:202-203, so it never updates).
+"""
+import ctypes as C
+
+import torch
+
+from ._abi import check, lib
+from .optim import Adam
+from .rasterizer import Rasterizer, RasterizerContext, RasterizerGradients, context
+
+
+def shard(n_items, rank, world):
+    """Contiguous slice of [0, n_items) owned by `rank`."""
+    lo = (n_items * rank) // world
+    hi = (n_items * (rank + 1)) // world
+    return lo, hi
+
+
+class DataParallelTrainer:
+    def __init__(self, gaussians, cameras, config, lrs=None, process_group=None):
+        self.g = gaussians
+        self.cameras = cameras
+        self.cfg = config
+        self.pg = process_group
+        self.world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
+        self.rank = torch.distributed.get_rank(process_group) if process_group is not None else 0
+        self.lo, self.hi = shard(len(cameras), self.rank, self.world)
+        self.grads = RasterizerGradients(gaussians, screen=False)
+        self.opt = Adam.for_gaussians(gaussians, self.grads, lrs)
+        self.ctx = RasterizerContext(gaussians.arena.device)
+        self.loss = torch.zeros(1, device=gaussians.arena.device)
+        self.cam_structs = [c.to_struct() for c in cameras]
+
+    @property
+    def my_views(self):
+        return range(self.lo, self.hi)
+
+    def zero(self):
+        ctx = context(self.g.arena.device)
+        check(lib().gsc_memset(ctx, C.c_void_p(self.grads.arena.data_ptr()), 0,
+                               self.grads.arena.numel() * 4), "gsc_memset")
+        check(lib().gsc_memset(ctx, C.c_void_p(self.loss.data_ptr()), 0, 4), "gsc_memset")
+
+    def view_fwd_bwd(self, v, target):
+        """Forward + fused-L1 backward of view v against a device target [H,W,3]."""
+        cam = self.cameras[v]
+        Rasterizer.forward(self.g, cam, context=self.ctx, config=self.cfg)
+        Rasterizer.backward(None, self.g, cam, self.ctx, grads=self.grads, target=target,
+                            l1_scale=1.0 / target.numel(), loss_sum=self.loss, config=self.cfg)
+
+    def reduce_and_step(self):
+        if self.world > 1:
+            torch.distributed.all_reduce(self.grads.arena, group=self.pg)
+            torch.distributed.all_reduce(self.loss, group=self.pg)
+        self.opt.step(grad_scale=1.0 / len(self.cameras))
+
+    def step(self, targets):
+        """One training step over all views; `targets(v)` gives view v's device target."""
+        self.zero()
+        for v in self.my_views:
+            self.view_fwd_bwd(v, targets(v))
+        self.reduce_and_step()
+        return self.loss

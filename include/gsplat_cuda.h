@@ -291,6 +291,29 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* frame, const gsc_gau
 #define GSC_FRAME_GRAD2D 8
 GSC_API int gsc_frame_get(gsc_frame* frame, int which, void** ptr, int64_t* count);
 
+/* ---- tracing (no reference counterpart: the reference times whole
+ *      self-test loops with Time.instant, src/main.cr:871-1061) -----------
+ * When enabled, every stage brackets its kernels with CUDA events on the
+ * context's stream; gsc_profile_read syncs the stream and returns, per
+ * stage, the summed device milliseconds, the number of stage invocations
+ * and the number of kernels launched. */
+#define GSC_STAGE_PREPROCESS 0
+#define GSC_STAGE_SCAN 1
+#define GSC_STAGE_EMIT 2
+#define GSC_STAGE_SORT 3
+#define GSC_STAGE_RANGES 4
+#define GSC_STAGE_COMPOSITE_FWD 5
+#define GSC_STAGE_COMPOSITE_BWD 6
+#define GSC_STAGE_PREPROCESS_BWD 7
+#define GSC_STAGE_ADAM 8
+#define GSC_STAGE_L1 9
+#define GSC_STAGE_COUNT 10
+GSC_API int gsc_profile_enable(gsc_ctx* ctx, int on);
+GSC_API int gsc_profile_read(gsc_ctx* ctx, double* ms, int64_t* calls, int64_t* kernels, int reset);
+/* Kernels launched by this context since creation (counted whether or not
+ * profiling is on). */
+GSC_API int64_t gsc_kernel_count(gsc_ctx* ctx);
+
 #ifdef __cplusplus
 }
 #endif
