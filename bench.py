@@ -213,41 +213,46 @@ def pge_count(gs, rctx):
 # algorithmic work per stage (bytes, or FP32 ops for compositing)
 # ---------------------------------------------------------------------------
 PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
-EMIT_B_PER_G = 32       # read mean/radius/depth/tiles (two float4 of the record)
-EMIT_B_PER_KEY = 12     # write u64 key + u32 value
-RANGES_B_PER_KEY = 8
 PREPROCESS_BWD_B = 556  # read 236 params + 36 grad2d, read+write 236 grads (visible Gaussians)
 ADAM_B = 28 * 59        # read p, g, m, v + write p, m, v per float
 FWD_FLOP_PER_PGE = 15
 BWD_FLOP_PER_PGE = 30
 
 
-def sort_bytes_per_pair(end_bit):
+def sort_bytes_per_pair(end_bit, key_bytes=8):
+    """Histogram read + one read and one write of the pair per 8-bit pass."""
     passes = (end_bit + 7) // 8
-    return 8 + 24 * passes
+    return key_bytes + 2 * (key_bytes + 4) * passes
 
 
 def stage_work(stats, n, keys_per_view, pge, tiles, end_bit):
-    """Algorithmic bytes (or flops) per launch of each stage."""
+    """Algorithmic work of each stage for ONE view: (bound, bytes or flops, stage calls per view).
+
+    Binning of a view = a stable 32-bit depth sort of the N Gaussians (4 passes),
+    a gather-scan and emission of (tile u32, id u32) pairs in depth order, and a
+    stable sort of those pairs by the tile bits (end_bit - 32 bits)."""
+    tb = end_bit - 32
+    m = keys_per_view
     return {
-        "preprocess": ("hbm", PREPROCESS_B * n),
-        "emit": ("hbm", EMIT_B_PER_G * n + EMIT_B_PER_KEY * keys_per_view),
-        "sort": ("hbm", sort_bytes_per_pair(end_bit) * keys_per_view),
-        "ranges": ("hbm", RANGES_B_PER_KEY * keys_per_view + 8 * tiles),
-        "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge),
-        "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge),
-        "preprocess_bwd": ("hbm", PREPROCESS_BWD_B * n),
-        "adam": ("hbm", ADAM_B * n),
+        "preprocess": ("hbm", PREPROCESS_B * n, 1),
+        "scan": ("hbm", 4 * n + 16 * n, 2),  # order gather + splat word, then the block-sum scan
+        "emit": ("hbm", (4 + 32) * n + 8 * m, 1),
+        "sort": ("hbm", sort_bytes_per_pair(32, 4) * n + sort_bytes_per_pair(tb, 4) * m, 2),
+        "ranges": ("hbm", 4 * m + 8 * tiles, 1),
+        "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge, 1),
+        "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge, 1),
+        "preprocess_bwd": ("hbm", PREPROCESS_BWD_B * n, 1),
+        "adam": ("hbm", ADAM_B * n, 1),
     }
 
 
 def rooflines(stats, work, peaks):
     out = {}
-    for name, (bound, amount) in work.items():
+    for name, (bound, amount, calls_per_unit) in work.items():
         s = stats.get(name)
         if not s or s["calls"] == 0 or s["ms"] <= 0:
             continue
-        per_launch_s = s["ms"] / 1e3 / s["calls"]
+        per_launch_s = s["ms"] / 1e3 / (s["calls"] / calls_per_unit)
         if bound == "hbm":
             ach = amount / per_launch_s / 1e9
             peak = peaks["hbm_gbs"]
@@ -257,8 +262,8 @@ def rooflines(stats, work, peaks):
             peak = FP32_NOMINAL_TFLOPS
             unit = "TFLOP/s"
         out[name] = {"bound": bound, "achieved": round(ach, 2), "peak": round(peak, 1), "unit": unit,
-                     "frac": round(ach / peak, 4), "ms_per_launch": round(per_launch_s * 1e3, 4),
-                     "launches": s["calls"], "share": None}
+                     "frac": round(ach / peak, 4), "ms_per_unit": round(per_launch_s * 1e3, 4),
+                     "stage_calls": s["calls"], "kernels": s["kernels"], "share": None}
     tot = sum(stats[k]["ms"] for k in stats)
     for k in out:
         out[k]["share"] = round(stats[k]["ms"] / tot, 4) if tot else None
@@ -564,7 +569,7 @@ def run_sort(args, cfg, rank, world, local, peaks, peak_kind):
         sort_ms = float(t.item())
     value = world * args.steps * n / 1e6 / (sort_ms / 1e3)
     per = sort_ms / 1e3 / args.steps
-    ach = sort_bytes_per_pair(end_bit) * n / per / 1e9
+    ach = sort_bytes_per_pair(end_bit) * n / per / 1e9  # 8-byte keys, 8-bit digits
     e2e = None
     if not args.no_e2e:
         hk = torch.from_numpy(keys.view(np.int64)).pin_memory()

@@ -73,7 +73,9 @@ using namespace gs;
 
 struct gsc_frame {
   gsc_ctx* ctx = nullptr;
-  GsBuf splats, block_sums, offsets, total, keys, vals, ranges, image, final_T, last, n_contrib, grad2d;
+  GsBuf splats, depth_keys, order, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
+      last, n_contrib, grad2d;
+  bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
   float* image_ptr = nullptr;  // image the last forward wrote (caller's or frame's)
@@ -232,7 +234,8 @@ static int check_view(const gsc_camera* cam, const gsc_raster_config* cfg) {
 }
 
 static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
-                         const gsc_raster_config* cfg, const gsc_projected* o, uint32_t* block_sums) {
+                         const gsc_raster_config* cfg, const gsc_projected* o, uint32_t* block_sums,
+                         uint32_t* depth_keys = nullptr, uint32_t* order = nullptr) {
   PreprocessArgs a;
   std::memset(&a, 0, sizeof a);
   a.n = g->count;
@@ -242,6 +245,7 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.tiles_x = (cam->width + GS_TILE - 1) / GS_TILE;
   a.tiles_y = (cam->height + GS_TILE - 1) / GS_TILE;
   a.splats = o->splats; a.block_sums = block_sums;
+  a.depth_keys = depth_keys; a.order = order;
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
   a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
@@ -486,8 +490,9 @@ GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out) {
 GSC_API int gsc_frame_destroy(gsc_frame* f) {
   if (!f) return GSC_OK;
   cudaStreamSynchronize(f->ctx->stream);
-  GsBuf* bufs[] = {&f->splats, &f->block_sums, &f->offsets, &f->total, &f->keys, &f->vals, &f->ranges,
-                   &f->image, &f->final_T, &f->last, &f->n_contrib, &f->grad2d};
+  GsBuf* bufs[] = {&f->splats, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
+                   &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
+                   &f->n_contrib, &f->grad2d};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
   delete f;
@@ -507,9 +512,11 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   const size_t npix = (size_t)W * H;
   f->has_forward = false;
   f->n = n; f->width = W; f->height = H; f->tiles_x = tx; f->tiles_y = ty;
-  GS_TRY(ensure(ctx, &f->splats, (size_t)n * 48));
-  GS_TRY(ensure(ctx, &f->block_sums, (size_t)nb * 4));
-  GS_TRY(ensure(ctx, &f->offsets, (size_t)nb * 8));
+  GS_TRY(ensure(ctx, &f->splats, (size_t)n * 48 + 48));
+  GS_TRY(ensure(ctx, &f->depth_keys, (size_t)n * 4 + 4));
+  GS_TRY(ensure(ctx, &f->order, (size_t)n * 4 + 4));
+  GS_TRY(ensure(ctx, &f->block_sums, (size_t)nb * 4 + 4));
+  GS_TRY(ensure(ctx, &f->offsets, (size_t)nb * 8 + 8));
   GS_TRY(ensure(ctx, &f->total, 8));
   GS_TRY(ensure(ctx, &f->ranges, (size_t)tx * ty * 8));
   GS_TRY(ensure(ctx, &f->final_T, npix * 4));
@@ -520,12 +527,28 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
     image = (float*)f->image.ptr;
   }
   f->image_ptr = image;
+  f->keys_valid = false;
   float* splats = (float*)f->splats.ptr;
+  uint32_t* depth_keys = (uint32_t*)f->depth_keys.ptr;
+  uint32_t* order = (uint32_t*)f->order.ptr;
 
   gsc_projected proj;
   std::memset(&proj, 0, sizeof proj);
   proj.splats = splats;
-  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, (uint32_t*)f->block_sums.ptr));
+  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, nullptr, depth_keys, order));
+  // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and sink)
+  if (n > 1) {
+    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_u32(n, 0, 32)));
+    StageScope sc(ctx, GSC_STAGE_SORT);
+    sc.kernels(1 + 4);
+    GS_TRY(launch_sort_pairs_u32(ctx, depth_keys, order, n, 0, 32, scratch_base(ctx)));
+  }
+  // 2. exact allocation in depth order, then emission of (tile, id)
+  {
+    StageScope sc(ctx, GSC_STAGE_SCAN);
+    sc.kernels(n ? 1 : 0);
+    GS_TRY(launch_block_sums_gather(splats, order, n, (uint32_t*)f->block_sums.ptr, ctx->stream));
+  }
   uint64_t m = 0;
   GS_TRY(do_scan(ctx, n, (uint32_t*)f->block_sums.ptr, (uint64_t*)f->offsets.ptr, (uint64_t*)f->total.ptr, &m));
   if (m >= (1ull << 30)) {
@@ -534,26 +557,30 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   }
   f->num_keys = (int64_t)m;
   if (num_rendered) *num_rendered = (int64_t)m;
-  GS_TRY(ensure(ctx, &f->keys, (size_t)m * 8 + 8));
+  GS_TRY(ensure(ctx, &f->tiles, (size_t)m * 4 + 4));
   GS_TRY(ensure(ctx, &f->vals, (size_t)m * 4 + 4));
-  uint64_t* keys = (uint64_t*)f->keys.ptr;
+  uint32_t* tiles = (uint32_t*)f->tiles.ptr;
   uint32_t* vals = (uint32_t*)f->vals.ptr;
   if (m) {
     {
       StageScope sc(ctx, GSC_STAGE_EMIT);
       sc.kernels(1);
-      GS_TRY(launch_emit_keys(splats, n, (const uint64_t*)f->offsets.ptr, tx, ty, keys, vals, ctx->stream));
+      GS_TRY(launch_emit_tiles(splats, order, n, (const uint64_t*)f->offsets.ptr, tx, ty, tiles, vals,
+                               ctx->stream));
     }
-    const int end_bit = 32 + tile_bits_of(tx * ty);
-    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes((int64_t)m, 0, end_bit)));
-    StageScope sc(ctx, GSC_STAGE_SORT);
-    sc.kernels(1 + (end_bit + 7) / 8);
-    GS_TRY(launch_sort_pairs(ctx, keys, vals, (int64_t)m, 0, end_bit, scratch_base(ctx)));
+    // 3. stable sort by tile bits only
+    const int tb = tile_bits_of(tx * ty);
+    if (tb > 0) {
+      GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_u32((int64_t)m, 0, tb)));
+      StageScope sc(ctx, GSC_STAGE_SORT);
+      sc.kernels(1 + (tb + 7) / 8);
+      GS_TRY(launch_sort_pairs_u32(ctx, tiles, vals, (int64_t)m, 0, tb, scratch_base(ctx)));
+    }
   }
   {
     StageScope sc(ctx, GSC_STAGE_RANGES);
     sc.kernels(m ? 1 : 0);
-    GS_TRY(launch_tile_ranges(keys, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
+    GS_TRY(launch_tile_ranges_u32(tiles, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
   }
   CompositeFwdArgs a;
   fill_fwd(&a, splats, vals, (const uint32_t*)f->ranges.ptr, W, H, cfg);
@@ -618,7 +645,17 @@ GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {
   int64_t c = 0;
   switch (which) {
     case GSC_FRAME_SPLATS: p = f->splats.ptr; c = f->n * 12; break;
-    case GSC_FRAME_KEYS: p = f->keys.ptr; c = f->num_keys; break;
+    case GSC_FRAME_KEYS:
+      if (!f->keys_valid) {
+        GS_TRY(ensure(f->ctx, &f->keys, (size_t)f->num_keys * 8 + 8));
+        GS_TRY(launch_make_keys((const uint32_t*)f->tiles.ptr, (const uint32_t*)f->vals.ptr,
+                                (const float*)f->splats.ptr, f->num_keys, (uint64_t*)f->keys.ptr,
+                                f->ctx->stream));
+        f->keys_valid = true;
+      }
+      p = f->keys.ptr;
+      c = f->num_keys;
+      break;
     case GSC_FRAME_VALUES: p = f->vals.ptr; c = f->num_keys; break;
     case GSC_FRAME_RANGES: p = f->ranges.ptr; c = (int64_t)f->tiles_x * f->tiles_y * 2; break;
     case GSC_FRAME_IMAGE: p = f->image_ptr; c = npix * 3; break;

@@ -164,4 +164,131 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
   return GSC_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Depth-first binning for whole-view rasterization.
+//
+// The sorted (key, value) list that a stable sort of the canonical emission
+// by key = tile << 32 | bits(depth) produces is ordered by (tile, depth,
+// Gaussian id): a Gaussian emits at most one key per tile, and equal keys
+// keep emission (= id) order. The same list comes out of
+//   1. a stable sort of the Gaussians by depth bits (N pairs, 32-bit keys),
+//   2. emission of (tile, id) pairs in that depth order,
+//   3. a stable sort of those pairs by the tile bits only,
+// which moves 8-byte pairs through ceil(tile_bits / 8) passes instead of
+// 12-byte pairs through ceil((32 + tile_bits) / 8) passes. The 64-bit keys are
+// rebuilt on request (make_keys_kernel).
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) block_sums_gather_kernel(const float4* __restrict__ splats,
+                                                                const uint32_t* __restrict__ order,
+                                                                int64_t n, uint32_t* __restrict__ sums) {
+  __shared__ uint32_t s_warp[8];
+  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  uint32_t t = p < n ? __float_as_uint(splats[(size_t)order[p] * 3 + 2].w) : 0u;
+  uint32_t incl = block_incl_scan_256(t, s_warp);
+  if (threadIdx.x == 255) sums[blockIdx.x] = incl;
+}
+
+__global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restrict__ splats,
+                                                         const uint32_t* __restrict__ order, int64_t n,
+                                                         const uint64_t* __restrict__ offsets,
+                                                         int tiles_x, int tiles_y,
+                                                         uint32_t* __restrict__ tile_out,
+                                                         uint32_t* __restrict__ id_out) {
+  __shared__ uint32_t s_incl[256];
+  __shared__ int s_x0[256], s_y0[256], s_wx[256];
+  __shared__ uint32_t s_id[256];
+  __shared__ uint32_t s_warp[8];
+  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  uint32_t t = 0;
+  if (p < n) {
+    const uint32_t gid = order[p];
+    const float4 s0 = splats[(size_t)gid * 3], s2 = splats[(size_t)gid * 3 + 2];
+    t = __float_as_uint(s2.w);
+    if (t) {
+      int x0, x1, y0, y1;
+      tile_bounds(s0.x, s0.y, s2.z, tiles_x, tiles_y, &x0, &x1, &y0, &y1);
+      s_x0[threadIdx.x] = x0;
+      s_y0[threadIdx.x] = y0;
+      s_wx[threadIdx.x] = x1 - x0 + 1;
+      s_id[threadIdx.x] = gid;
+    }
+  }
+  uint32_t incl = block_incl_scan_256(t, s_warp);
+  s_incl[threadIdx.x] = incl;
+  __syncthreads();
+  const uint32_t total = s_incl[255];
+  const uint64_t out = offsets[blockIdx.x];
+  for (uint32_t k = threadIdx.x; k < total; k += 256) {
+    int lo = 0, hi = 255;
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if (s_incl[mid] > k) hi = mid; else lo = mid + 1;
+    }
+    const uint32_t local = k - (lo ? s_incl[lo - 1] : 0u);
+    const int wx = s_wx[lo];
+    const int ty = s_y0[lo] + (int)(local / (uint32_t)wx);
+    const int tx = s_x0[lo] + (int)(local % (uint32_t)wx);
+    tile_out[out + k] = (uint32_t)(ty * tiles_x + tx);
+    id_out[out + k] = s_id[lo];
+  }
+}
+
+__global__ void __launch_bounds__(256) tile_ranges_u32_kernel(const uint32_t* __restrict__ tiles, int64_t n,
+                                                              uint32_t num_tiles, uint32_t* __restrict__ ranges) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t t = tiles[i];
+  const uint32_t prev = i > 0 ? tiles[i - 1] : 0xFFFFFFFFu;
+  const uint32_t next = i < n - 1 ? tiles[i + 1] : 0xFFFFFFFFu;
+  if (t != prev && t < num_tiles) ranges[(size_t)t * 2] = (uint32_t)i;
+  if (t != next && t < num_tiles) ranges[(size_t)t * 2 + 1] = (uint32_t)(i + 1);
+}
+
+__global__ void __launch_bounds__(256) make_keys_kernel(const uint32_t* __restrict__ tiles,
+                                                        const uint32_t* __restrict__ ids,
+                                                        const float4* __restrict__ splats, int64_t m,
+                                                        uint64_t* __restrict__ keys) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= m) return;
+  const uint32_t depth_bits = __float_as_uint(splats[(size_t)ids[i] * 3 + 2].y);
+  keys[i] = ((uint64_t)tiles[i] << 32) | depth_bits;
+}
+
+int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t n, uint32_t* sums,
+                             cudaStream_t stream) {
+  if (n == 0) return GSC_OK;
+  block_sums_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(splats), order, n, sums);
+  GS_CK_LAUNCH("block_sums_gather_kernel");
+  return GSC_OK;
+}
+
+int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
+                      int tiles_x, int tiles_y, uint32_t* tile_out, uint32_t* id_out, cudaStream_t stream) {
+  if (n == 0) return GSC_OK;
+  emit_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(splats), order, n, offsets, tiles_x, tiles_y, tile_out, id_out);
+  GS_CK_LAUNCH("emit_tiles_kernel");
+  return GSC_OK;
+}
+
+int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
+                           cudaStream_t stream) {
+  GS_CK(cudaMemsetAsync(ranges, 0, sizeof(uint32_t) * 2 * (size_t)num_tiles, stream));
+  if (n == 0) return GSC_OK;
+  tile_ranges_u32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(tiles, n, (uint32_t)num_tiles, ranges);
+  GS_CK_LAUNCH("tile_ranges_u32_kernel");
+  return GSC_OK;
+}
+
+int launch_make_keys(const uint32_t* tiles, const uint32_t* ids, const float* splats, int64_t m,
+                     uint64_t* keys, cudaStream_t stream) {
+  if (m == 0) return GSC_OK;
+  make_keys_kernel<<<(unsigned)((m + 255) / 256), 256, 0, stream>>>(
+      tiles, ids, reinterpret_cast<const float4*>(splats), m, keys);
+  GS_CK_LAUNCH("make_keys_kernel");
+  return GSC_OK;
+}
+
 }  // namespace gs

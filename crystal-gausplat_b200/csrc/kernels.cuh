@@ -16,6 +16,8 @@ struct PreprocessArgs {
   int tiles_x, tiles_y;
   float* splats;
   uint32_t* block_sums;  // one per 256 Gaussians, may be null
+  uint32_t* depth_keys;  // bits(depth) if the Gaussian emits keys, else ~0; may be null
+  uint32_t* order;       // identity permutation (input of the depth sort); may be null
   float* mean2d;
   float* cov2d;
   float* conic;
@@ -107,9 +109,20 @@ int launch_emit_keys(const float* splats, int64_t n, const uint64_t* offsets, in
                      int tiles_y, uint64_t* keys, uint32_t* vals, cudaStream_t stream);
 int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint32_t* ranges,
                        cudaStream_t stream);
+int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t n, uint32_t* sums,
+                             cudaStream_t stream);
+int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
+                      int tiles_x, int tiles_y, uint32_t* tile_out, uint32_t* id_out, cudaStream_t stream);
+int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
+                           cudaStream_t stream);
+int launch_make_keys(const uint32_t* tiles, const uint32_t* ids, const float* splats, int64_t m,
+                     uint64_t* keys, cudaStream_t stream);
 size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit);
 int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                       int end_bit, char* scratch);
+size_t sort_scratch_bytes_u32(int64_t n, int begin_bit, int end_bit);
+int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,
+                          int end_bit, char* scratch);
 int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream);
 int launch_composite_bwd(const CompositeBwdArgs& a, bool full, cudaStream_t stream);
 int launch_preprocess_bwd(const PreprocessBwdArgs& a, bool full, cudaStream_t stream);

@@ -83,6 +83,10 @@ __global__ void __launch_bounds__(256) preprocess_kernel(PreprocessArgs a) {
     if (a.colors) { a.colors[i * 3] = col[0]; a.colors[i * 3 + 1] = col[1]; a.colors[i * 3 + 2] = col[2]; }
     if (a.opacity) a.opacity[i] = o;
     if (a.tiles_touched) a.tiles_touched[i] = tiles;
+    if (a.depth_keys) {
+      a.depth_keys[i] = tiles ? __float_as_uint(depth) : 0xFFFFFFFFu;
+      a.order[i] = (uint32_t)i;
+    }
     if (a.cov3d) {
 #pragma unroll
       for (int k = 0; k < 6; k++) a.cov3d[i * 6 + k] = c3[k];

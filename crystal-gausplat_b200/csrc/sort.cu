@@ -31,14 +31,15 @@ constexpr uint32_t kValMask = (1u << 30) - 1u;
 constexpr uint32_t kSpinLimit = 1u << 21;
 }  // namespace
 
-__global__ void __launch_bounds__(256) histogram_kernel(const uint64_t* __restrict__ keys, int64_t n,
+template <typename K>
+__global__ void __launch_bounds__(256) histogram_kernel(const K* __restrict__ keys, int64_t n,
                                                         int begin_bit, int end_bit, int npass,
                                                         uint32_t* __restrict__ hist) {
   __shared__ uint32_t s_hist[8][256];
   for (int k = threadIdx.x; k < 8 * 256; k += 256) (&s_hist[0][0])[k] = 0;
   __syncthreads();
   for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
-    const uint64_t key = keys[i];
+    const K key = keys[i];
     for (int p = 0; p < npass; p++) {
       const int shift = begin_bit + 8 * p;
       const int bits = min(8, end_bit - shift);
@@ -70,12 +71,13 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
   return x - v + add;
 }
 
+template <typename K>
 __global__ void __launch_bounds__(kThreads) onesweep_kernel(
-    const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-    uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
+    const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+    K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
     uint32_t* err) {
-  __shared__ uint64_t s_keys[kTileKeys];  // reused for values
+  __shared__ K s_keys[kTileKeys];  // reused for values
   __shared__ uint32_t s_whist[kWarps][256];
   __shared__ uint32_t s_local_excl[256];
   __shared__ uint32_t s_gbase[256];
@@ -92,14 +94,14 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
   const int64_t warp_base = tile_base + (int64_t)w * kWarpKeys;
   const uint32_t num_valid = (uint32_t)min((int64_t)kTileKeys, n - tile_base);
 
-  uint64_t k[kItems];
+  K k[kItems];
   uint32_t v[kItems];
   uint32_t rank[kItems];
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
     const int64_t idx = warp_base + i * 32 + lane;
     const bool valid = idx < n;
-    k[i] = valid ? keys_in[idx] : ~0ull;
+    k[i] = valid ? keys_in[idx] : (K)~(K)0;
     v[i] = valid ? vals_in[idx] : 0u;
   }
   const uint32_t lt_mask = (1u << lane) - 1u;
@@ -112,13 +114,9 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     const int leader = __ffs(peers) - 1;
     uint32_t b = 0;
-    if (lane == leader) {
-      b = s_whist[w][d];
-      s_whist[w][d] = b + __popc(peers);
-    }
+    if (lane == leader) b = atomicAdd(&s_whist[w][d], (uint32_t)__popc(peers));
     b = __shfl_sync(0xffffffffu, b, leader);
     rank[i] = b + __popc(peers & lt_mask);
-    __syncwarp();
   }
   __syncthreads();
 
@@ -175,7 +173,7 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
   }
   __syncthreads();
   for (uint32_t j = tid; j < num_valid; j += kThreads) {
-    const uint64_t key = s_keys[j];
+    const K key = s_keys[j];
     const uint32_t dd = (uint32_t)(key >> shift) & digit_mask;
     s_dig[j] = (uint8_t)dd;
     const uint32_t gpos = s_gbase[dd] + j;
@@ -193,22 +191,31 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
   }
 }
 
-size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit) {
+template <typename K>
+size_t sort_scratch_bytes_t(int64_t n, int begin_bit, int end_bit) {
   const int npass = (end_bit - begin_bit + 7) / 8;
   const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
-  size_t b = align256((size_t)n * 8) + align256((size_t)n * 4);
+  size_t b = align256((size_t)n * sizeof(K)) + align256((size_t)n * 4);
   b += align256((size_t)npass * 256 * 4 + (size_t)npass * parts * 256 * 4 + (size_t)npass * 4);
   return b;
 }
 
-int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
-                      int end_bit, char* scratch) {
+size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit) {
+  return sort_scratch_bytes_t<uint64_t>(n, begin_bit, end_bit);
+}
+size_t sort_scratch_bytes_u32(int64_t n, int begin_bit, int end_bit) {
+  return sort_scratch_bytes_t<uint32_t>(n, begin_bit, end_bit);
+}
+
+template <typename K>
+static int sort_pairs_t(gsc_ctx* ctx, K* keys, uint32_t* vals, int64_t n, int begin_bit, int end_bit,
+                        char* scratch) {
   cudaStream_t stream = ctx->stream;
   if (n <= 1 || end_bit <= begin_bit) return GSC_OK;
   const int npass = (end_bit - begin_bit + 7) / 8;
   const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
-  uint64_t* alt_keys = reinterpret_cast<uint64_t*>(scratch);
-  scratch += align256((size_t)n * 8);
+  K* alt_keys = reinterpret_cast<K*>(scratch);
+  scratch += align256((size_t)n * sizeof(K));
   uint32_t* alt_vals = reinterpret_cast<uint32_t*>(scratch);
   scratch += align256((size_t)n * 4);
   uint32_t* hist = reinterpret_cast<uint32_t*>(scratch);
@@ -218,17 +225,17 @@ int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, i
   GS_CK(cudaMemsetAsync(hist, 0, meta, stream));
 
   const int64_t hblocks = min((int64_t)ctx->num_sms * 8, (n + 4095) / 4096);
-  histogram_kernel<<<(unsigned)max((int64_t)1, hblocks), 256, 0, stream>>>(keys, n, begin_bit, end_bit,
-                                                                          npass, hist);
+  histogram_kernel<K><<<(unsigned)max((int64_t)1, hblocks), 256, 0, stream>>>(keys, n, begin_bit, end_bit,
+                                                                             npass, hist);
   GS_CK_LAUNCH("histogram_kernel");
-  uint64_t* src_k = keys;
+  K* src_k = keys;
   uint32_t* src_v = vals;
-  uint64_t* dst_k = alt_keys;
+  K* dst_k = alt_keys;
   uint32_t* dst_v = alt_vals;
   for (int p = 0; p < npass; p++) {
     const int shift = begin_bit + 8 * p;
     const int bits = min(8, end_bit - shift);
-    onesweep_kernel<<<(unsigned)parts, kThreads, 0, stream>>>(
+    onesweep_kernel<K><<<(unsigned)parts, kThreads, 0, stream>>>(
         src_k, src_v, dst_k, dst_v, n, shift, (1u << bits) - 1u, hist + p * 256,
         status + (size_t)p * parts * 256, tickets + p, ctx->err);
     GS_CK_LAUNCH("onesweep_kernel");
@@ -236,10 +243,20 @@ int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, i
     std::swap(src_v, dst_v);
   }
   if (src_k != keys) {
-    GS_CK(cudaMemcpyAsync(keys, src_k, (size_t)n * 8, cudaMemcpyDeviceToDevice, stream));
+    GS_CK(cudaMemcpyAsync(keys, src_k, (size_t)n * sizeof(K), cudaMemcpyDeviceToDevice, stream));
     GS_CK(cudaMemcpyAsync(vals, src_v, (size_t)n * 4, cudaMemcpyDeviceToDevice, stream));
   }
   return GSC_OK;
+}
+
+int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
+                      int end_bit, char* scratch) {
+  return sort_pairs_t<uint64_t>(ctx, keys, vals, n, begin_bit, end_bit, scratch);
+}
+
+int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,
+                          int end_bit, char* scratch) {
+  return sort_pairs_t<uint32_t>(ctx, keys, vals, n, begin_bit, end_bit, scratch);
 }
 
 }  // namespace gs
