@@ -23,6 +23,8 @@ GSC_ERR_UNSUPPORTED = -7
 GSC_MODE_FULL = 0
 GSC_MODE_REF = 1
 
+GSC_STATIC_SORT_MAX_PAIRS = 262144
+
 GSC_FRAME_SPLATS = 0
 GSC_FRAME_KEYS = 1
 GSC_FRAME_VALUES = 2
@@ -96,6 +98,7 @@ _SIGS = {
     "gsc_bin": (C.c_int, [P, C.c_int64, P, C.c_int32, C.c_int32, P, P, C.c_int64,
                           C.POINTER(C.c_int64)]),
     "gsc_sort_pairs_u64": (C.c_int, [P, P, P, C.c_int64, C.c_int, C.c_int]),
+    "gsc_sort_pairs_u64_static": (C.c_int, [P, P, C.c_int64, C.c_int, C.c_int, P]),
     "gsc_tile_ranges": (C.c_int, [P, P, C.c_int64, C.c_int32, P]),
     "gsc_composite_forward": (C.c_int, [P, P, P, P, C.c_int32, C.c_int32, C.POINTER(RasterConfig),
                                         P, P, P, P]),

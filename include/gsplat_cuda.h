@@ -205,6 +205,20 @@ GSC_API int gsc_bin(gsc_ctx* ctx, int64_t n, const float* splats, int32_t tiles_
 GSC_API int gsc_sort_pairs_u64(gsc_ctx* ctx, uint64_t* keys, uint32_t* values, int64_t n,
                                int begin_bit, int end_bit);
 
+/* Allocation-free variant of gsc_sort_pairs_u64, with no counterpart in the
+ * reference. For callers that cannot allocate device memory (a host whose own
+ * pool owns all device memory, a thread that must not take the driver's
+ * allocation locks, a caller without a gsc_ctx): same stable sort and
+ * arguments, but the scratch is a fixed device array inside the library
+ * (about 3.7 MB, held on every GPU that loads the library until exit), so
+ * n <= GSC_STATIC_SORT_MAX_PAIRS; larger n returns GSC_ERR_INVALID. Work is
+ * queued on `stream` (a cudaStream_t, NULL = legacy default). The first call
+ * on a device looks up the array's address; make it before any stream
+ * capture. All calls share the array: calls whose GPU work overlaps race. */
+#define GSC_STATIC_SORT_MAX_PAIRS 262144
+GSC_API int gsc_sort_pairs_u64_static(uint64_t* keys, uint32_t* values, int64_t n, int begin_bit,
+                                      int end_bit, void* stream);
+
 /* GPURadixSort.compute_tile_ranges! (gpu_radix_sort.cr:204-233,
  * radix_sort.metal:288-324): ranges[t] = [first, last+1) of tile t in the
  * sorted keys, (0,0) for empty tiles. */
