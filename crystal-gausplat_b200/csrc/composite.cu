@@ -22,7 +22,68 @@
 
 namespace gs {
 
-__global__ void __launch_bounds__(256) composite_fwd_kernel(CompositeFwdArgs a) {
+// Whole-tile rejection. True only if NO pixel centre of the tile's rectangle
+// [rx0, rx1] x [ry0, ry1] can pass the alpha test for this Gaussian:
+// the minimum of the Mahalanobis form q(d) = d^T conic d over the rectangle
+// (zero if the mean is inside, else attained on an edge) is compared, in
+// double precision, with the opacity-aware threshold
+//     o * exp(-q/2) < alpha_min  <=>  q > -2 ln(alpha_min / o),
+// with margins that cover the fp32 evaluation of the per-pixel test: the fp32
+// quadratic form has relative error <= 4 eps / (1 - rho), rho = |B|/sqrt(AC),
+// so the cull is refused when 1 - rho < 1e-3, and the threshold is raised by
+// 1e-3 relative + 1e-3 absolute and lowered in ln by 1e-4. Non-finite or
+// non-positive-definite inputs are never culled. The set of Gaussians that
+// reach the per-pixel loop therefore changes, but not the result.
+__device__ __forceinline__ bool tile_culled(float4 g0, float conic_c, float o, float rx0, float rx1,
+                                            float ry0, float ry1, float alpha_min) {
+  if (!isfinite(g0.x) || !isfinite(g0.y)) return false;
+  if (!(o > 0.0f)) return o == 0.0f && isfinite(g0.z) && isfinite(g0.w) && isfinite(conic_c);
+  const double A = g0.z, B = g0.w, C = conic_c;
+  if (!(A > 0.0 && C > 0.0) || !isfinite(A) || !isfinite(B) || !isfinite(C)) return false;
+  const double rho = fabs(B) / sqrt(A * C);
+  if (!(1.0 - rho >= 1e-3)) return false;
+  const double cut = (double)logf(alpha_min / o) - 1e-4;  // logf error << the 1e-4 margin
+  if (cut >= 0.0) return true;  // o < alpha_min: alpha = o*G <= o never reaches alpha_min
+  const double mx = g0.x, my = g0.y;
+  const double x0 = rx0 - mx, x1 = rx1 - mx, y0 = ry0 - my, y1 = ry1 - my;
+  if (x0 <= 0.0 && x1 >= 0.0 && y0 <= 0.0 && y1 >= 0.0) return false;  // mean inside
+  double qmin = INFINITY;
+  // edges x = x0, x1: minimise over dy in [y0, y1] (dy* = -B dx / C)
+#pragma unroll
+  for (int e = 0; e < 2; e++) {
+    const double dx = e ? x1 : x0;
+    const double dy = fmin(fmax(-B * dx / C, y0), y1);
+    qmin = fmin(qmin, A * dx * dx + 2.0 * B * dx * dy + C * dy * dy);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; e++) {
+    const double dy = e ? y1 : y0;
+    const double dx = fmin(fmax(-B * dy / A, x0), x1);
+    qmin = fmin(qmin, A * dx * dx + 2.0 * B * dx * dy + C * dy * dy);
+  }
+  const double thr = -2.0 * cut * (1.0 + 1e-3) + 1e-3;
+  return qmin > thr;
+}
+
+// Stable compaction of the batch survivors: returns this thread's slot (or
+// -1) and the survivor count; needs a 8-entry shared scratch.
+__device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+  if (lane == 0) s_cnt[w] = __popc(bal);
+  __syncthreads();
+  int base = 0, tot = 0;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const int c = (int)s_cnt[k];
+    base += k < w ? c : 0;
+    tot += c;
+  }
+  *total = tot;
+  return keep ? base + __popc(bal & ((1u << lane) - 1u)) : -1;
+}
+
+__global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs a) {
   __shared__ float4 s0[256];
   __shared__ float4 s1[256];
   __shared__ float s2[256];
@@ -36,39 +97,58 @@ __global__ void __launch_bounds__(256) composite_fwd_kernel(CompositeFwdArgs a) 
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float t_stop = a.t_stop, amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
 
+  __shared__ uint32_t s_idx[256];
+  __shared__ uint32_t s_cnt[8];
+  const float rx0 = tx * GS_TILE + 0.5f, ry0 = ty * GS_TILE + 0.5f;
+  const float rx1 = min(tx * GS_TILE + GS_TILE, a.width) - 0.5f;
+  const float ry1 = min(ty * GS_TILE + GS_TILE, a.height) - 0.5f;
+
   float T = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f;
   uint32_t cnt = 0, lst = 0;
-  bool done = !inside;
+  bool done = !inside || !(T > t_stop);
   for (uint32_t b = start; b < end; b += 256) {
     if (__syncthreads_count(done) == 256) break;
     const uint32_t idx = b + tid;
+    float4 g0, g1;
+    float g2 = 0.0f;
+    bool keep = false;
     if (idx < end) {
       const uint32_t gid = a.vals[idx];
-      s0[tid] = splats[(size_t)gid * 3];
-      s1[tid] = splats[(size_t)gid * 3 + 1];
-      s2[tid] = splats[(size_t)gid * 3 + 2].x;
+      g0 = splats[(size_t)gid * 3];
+      g1 = splats[(size_t)gid * 3 + 1];
+      g2 = splats[(size_t)gid * 3 + 2].x;
+      keep = !tile_culled(g0, g1.x, g1.y, rx0, rx1, ry0, ry1, amin);
+    }
+    int m;
+    const int slot = compact_slot(keep, s_cnt, &m);
+    if (slot >= 0) {
+      s0[slot] = g0;
+      s1[slot] = g1;
+      s2[slot] = g2;
+      s_idx[slot] = idx - start;
     }
     __syncthreads();
     if (!done) {
-      const int m = (int)min(256u, end - b);
       for (int j = 0; j < m; j++) {
-        if (!(T > t_stop)) break;
-        const float4 g0 = s0[j];
-        const float dx = pxf - g0.x, dy = pyf - g0.y;
-        const float4 g1 = s1[j];
-        const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
+        const float4 q0 = s0[j];
+        const float dx = pxf - q0.x, dy = pyf - q0.y;
+        const float4 q1 = s1[j];
+        const float power = -0.5f * (dx * dx * q0.z + 2.0f * dx * dy * q0.w + dy * dy * q1.x);
         if (power > 0.0f || power < cut) continue;
         const float G = gs_expf(power);
-        const float alpha = fminf(amax, g1.y * G);
+        const float alpha = fminf(amax, q1.y * G);
         if (alpha < amin) continue;
-        C0 += T * alpha * g1.z;
-        C1 += T * alpha * g1.w;
+        C0 += T * alpha * q1.z;
+        C1 += T * alpha * q1.w;
         C2 += T * alpha * s2[j];
         T *= (1.0f - alpha);
         cnt++;
-        lst = b + j - start + 1;
+        lst = s_idx[j] + 1;
+        if (!(T > t_stop)) {
+          done = true;
+          break;
+        }
       }
-      if (!(T > t_stop)) done = true;
     }
   }
   if (!inside) return;
@@ -88,7 +168,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 template <bool FULL, bool L1>
-__global__ void __launch_bounds__(256) composite_bwd_kernel(CompositeBwdArgs a) {
+__global__ void __launch_bounds__(256, 4) composite_bwd_kernel(CompositeBwdArgs a) {
   __shared__ float4 s0[256];
   __shared__ float4 s1[256];
   __shared__ float s2[256];
@@ -142,20 +222,38 @@ __global__ void __launch_bounds__(256) composite_bwd_kernel(CompositeBwdArgs a) 
   __syncthreads();
   const uint32_t hi = FULL ? s_hi : end;
 
+  __shared__ uint32_t s_idx[256];
+  __shared__ uint32_t s_cnt[8];
+  const float rx0 = tx * GS_TILE + 0.5f, ry0 = ty * GS_TILE + 0.5f;
+  const float rx1 = min(tx * GS_TILE + GS_TILE, a.width) - 0.5f;
+  const float ry1 = min(ty * GS_TILE + GS_TILE, a.height) - 0.5f;
   for (int64_t bend = hi; bend > (int64_t)start; bend -= 256) {
     const int64_t bstart = max((int64_t)start, bend - 256);
-    const int m = (int)(bend - bstart);
+    const int mb = (int)(bend - bstart);
     __syncthreads();
-    if (tid < m) {
-      const uint32_t gid = a.vals[bend - 1 - tid];
-      s_gid[tid] = gid;
-      s0[tid] = splats[(size_t)gid * 3];
-      s1[tid] = splats[(size_t)gid * 3 + 1];
-      s2[tid] = splats[(size_t)gid * 3 + 2].x;
+    bool keep = false;
+    float4 q0, q1;
+    float q2 = 0.0f;
+    uint32_t gid = 0;
+    if (tid < mb) {
+      gid = a.vals[bend - 1 - tid];
+      q0 = splats[(size_t)gid * 3];
+      q1 = splats[(size_t)gid * 3 + 1];
+      q2 = splats[(size_t)gid * 3 + 2].x;
+      keep = !tile_culled(q0, q1.x, q1.y, rx0, rx1, ry0, ry1, amin);
+    }
+    int m;
+    const int slot = compact_slot(keep, s_cnt, &m);
+    if (slot >= 0) {
+      s_gid[slot] = gid;
+      s0[slot] = q0;
+      s1[slot] = q1;
+      s2[slot] = q2;
+      s_idx[slot] = (uint32_t)(bend - 1 - tid);
     }
     __syncthreads();
     for (int j = 0; j < m; j++) {
-      const uint32_t idx = (uint32_t)(bend - 1 - j);
+      const uint32_t idx = s_idx[j];
       float v[9];
 #pragma unroll
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
