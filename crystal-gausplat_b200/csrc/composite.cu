@@ -67,6 +67,7 @@ __device__ __forceinline__ bool tile_culled(float4 g0, float conic_c, float o, f
 
 // Stable compaction of the batch survivors: returns this thread's slot (or
 // -1) and the survivor count; needs a 8-entry shared scratch.
+template <int NW = 8>
 __device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* total) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const uint32_t bal = __ballot_sync(0xffffffffu, keep);
@@ -74,7 +75,7 @@ __device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* tot
   __syncthreads();
   int base = 0, tot = 0;
 #pragma unroll
-  for (int k = 0; k < 8; k++) {
+  for (int k = 0; k < NW; k++) {
     const int c = (int)s_cnt[k];
     base += k < w ? c : 0;
     tot += c;
@@ -167,68 +168,158 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Sum of 9 per-lane values over the warp by transposed halving: at each of
+// the first four levels a lane keeps half of its slots and receives the
+// partner's sums for them, so 8 + 4 + 2 + 1 + 1 shuffles replace 9 x 5.
+// On return, even lane 2k < 18 holds the warp total of slot k.
+__device__ __forceinline__ float warp_reduce9(const float v[9], int lane) {
+  float a[16];
+#pragma unroll
+  for (int i = 0; i < 16; i++) a[i] = i < 9 ? v[i] : 0.0f;
+#pragma unroll
+  for (int lvl = 0; lvl < 4; lvl++) {
+    const int off = 16 >> lvl, half = 8 >> lvl;
+    const bool up = lane & off;
+#pragma unroll
+    for (int i = 0; i < half; i++) {
+      const float send = up ? a[i] : a[i + half];
+      const float keep = up ? a[i + half] : a[i];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return a[0] + __shfl_xor_sync(0xffffffffu, a[0], 1);
+}
+
+// One pixel's backward state.
+struct BwdPixel {
+  bool inside;
+  float pxf, pyf;
+  float g[3];
+  float T;
+  float acc[3];
+  uint32_t hi;
+};
+
+// Partials of one pixel for one Gaussian (gaussian.metal:505-566; FULL mode
+// adds the conic gradient, the alpha clamp and the corrected running colour).
+template <bool FULL>
+__device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, float4 g1, float g2,
+                                          float amin, float amax, float cut, float v[9]) {
+  if (!(P.inside && idx < P.hi)) return false;
+  const float dx = P.pxf - g0.x, dy = P.pyf - g0.y;
+  const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
+  if (power > 0.0f || power < cut) return false;
+  const float G = gs_expf(power);
+  const float alpha = fminf(amax, g1.y * G);
+  if (alpha < amin) return false;
+  const float o = g1.y;
+  const float c[3] = {g1.z, g1.w, g2};
+  const float T_before = P.T / (1.0f - alpha);
+#pragma unroll
+  for (int k = 0; k < 3; k++) v[6 + k] += T_before * alpha * P.g[k];
+  float dL_dalpha = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 3; k++) dL_dalpha += (T_before * (c[k] - P.acc[k] / P.T)) * P.g[k];
+  float dL_dG, dL_do;
+  if (FULL && !(o * G <= amax)) {
+    dL_dG = 0.0f;
+    dL_do = 0.0f;
+  } else {
+    dL_dG = dL_dalpha * o;
+    dL_do = dL_dalpha * G;
+  }
+  const float dL_dpower = dL_dG * G;
+  v[0] += dL_dpower * (g0.z * dx + g0.w * dy);
+  v[1] += dL_dpower * (g0.w * dx + g1.x * dy);
+  if (FULL) {
+    v[2] += dL_dpower * (-0.5f * dx * dx);
+    v[3] += dL_dpower * (-dx * dy);
+    v[4] += dL_dpower * (-0.5f * dy * dy);
+  }
+  v[5] += dL_do;
+  P.T = T_before;
+#pragma unroll
+  for (int k = 0; k < 3; k++) {
+    const float contrib = T_before * alpha * c[k];
+    P.acc[k] = FULL ? P.acc[k] + contrib : P.acc[k] - contrib;
+  }
+  return true;
+}
+
+// 128 threads per tile, two pixels per thread (rows r and r + 8), so each
+// warp reduction covers 64 pixels.
+constexpr int kBwdThreads = 128;
+constexpr int kBwdWarps = kBwdThreads / 32;
+
 template <bool FULL, bool L1>
-__global__ void __launch_bounds__(256, 4) composite_bwd_kernel(CompositeBwdArgs a) {
-  __shared__ float4 s0[256];
-  __shared__ float4 s1[256];
-  __shared__ float s2[256];
-  __shared__ uint32_t s_gid[256];
+__global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(CompositeBwdArgs a) {
+  __shared__ float4 s0[kBwdThreads];
+  __shared__ float4 s1[kBwdThreads];
+  __shared__ float s2[kBwdThreads];
+  __shared__ uint32_t s_gid[kBwdThreads];
+  __shared__ uint32_t s_idx[kBwdThreads];
+  __shared__ uint32_t s_cnt[kBwdWarps];
   __shared__ uint32_t s_hi;
-  __shared__ float s_loss[8];
+  __shared__ float s_loss[kBwdWarps];
   const int tile = blockIdx.x;
   const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
   const int tid = threadIdx.x, lane = tid & 31;
-  const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4);
-  const bool inside = x < a.width && y < a.height;
-  const float pxf = (float)x + 0.5f, pyf = (float)y + 0.5f;
   const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
-  const size_t pix = inside ? (size_t)y * a.width + x : 0;
 
-  float g[3] = {0.0f, 0.0f, 0.0f};
+  BwdPixel P[2];
   float loss = 0.0f;
-  float T = 1.0f;
-  uint32_t my_hi = start;
-  if (inside) {
 #pragma unroll
-    for (int c = 0; c < 3; c++) {
-      if (L1) {
-        const float diff = a.image[pix * 3 + c] - a.target[pix * 3 + c];
-        const float sg = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-        g[c] = sg * a.l1_scale;
-        loss += fabsf(diff) * a.l1_scale;
-      } else {
-        g[c] = a.dL_dimage[pix * 3 + c];
+  for (int h = 0; h < 2; h++) {
+    const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4) + 8 * h;
+    BwdPixel& Q = P[h];
+    Q.inside = x < a.width && y < a.height;
+    Q.pxf = (float)x + 0.5f;
+    Q.pyf = (float)y + 0.5f;
+    Q.T = 1.0f;
+    Q.hi = start;
+    Q.g[0] = Q.g[1] = Q.g[2] = 0.0f;
+    if (Q.inside) {
+      const size_t pix = (size_t)y * a.width + x;
+#pragma unroll
+      for (int c = 0; c < 3; c++) {
+        if (L1) {
+          const float diff = a.image[pix * 3 + c] - a.target[pix * 3 + c];
+          const float sg = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
+          Q.g[c] = sg * a.l1_scale;
+          loss += fabsf(diff) * a.l1_scale;
+        } else {
+          Q.g[c] = a.dL_dimage[pix * 3 + c];
+        }
       }
+      Q.T = a.final_T[pix];
+      Q.hi = FULL ? start + a.last[pix] : end;
     }
-    T = a.final_T[pix];
-    my_hi = FULL ? start + a.last[pix] : end;
+#pragma unroll
+    for (int c = 0; c < 3; c++) Q.acc[c] = a.bg[c] * Q.T;
   }
-  float acc[3] = {a.bg[0] * T, a.bg[1] * T, a.bg[2] * T};
 
   if (L1 && a.loss_sum) {
-    float l = warp_sum(loss);
+    const float l = warp_sum(loss);
     if (lane == 0) s_loss[tid >> 5] = l;
   }
   if (tid == 0) s_hi = start;
   __syncthreads();
   if (L1 && a.loss_sum && tid == 0) {
     float t = 0.0f;
-    for (int w = 0; w < 8; w++) t += s_loss[w];
+    for (int w = 0; w < kBwdWarps; w++) t += s_loss[w];
     if (t != 0.0f) atomicAdd(a.loss_sum, t);
   }
-  if (FULL) atomicMax(&s_hi, my_hi);
+  if (FULL) atomicMax(&s_hi, max(P[0].hi, P[1].hi));
   __syncthreads();
   const uint32_t hi = FULL ? s_hi : end;
 
-  __shared__ uint32_t s_idx[256];
-  __shared__ uint32_t s_cnt[8];
   const float rx0 = tx * GS_TILE + 0.5f, ry0 = ty * GS_TILE + 0.5f;
   const float rx1 = min(tx * GS_TILE + GS_TILE, a.width) - 0.5f;
   const float ry1 = min(ty * GS_TILE + GS_TILE, a.height) - 0.5f;
-  for (int64_t bend = hi; bend > (int64_t)start; bend -= 256) {
-    const int64_t bstart = max((int64_t)start, bend - 256);
+  for (int64_t bend = hi; bend > (int64_t)start; bend -= kBwdThreads) {
+    const int64_t bstart = max((int64_t)start, bend - kBwdThreads);
     const int mb = (int)(bend - bstart);
     __syncthreads();
     bool keep = false;
@@ -243,7 +334,7 @@ __global__ void __launch_bounds__(256, 4) composite_bwd_kernel(CompositeBwdArgs 
       keep = !tile_culled(q0, q1.x, q1.y, rx0, rx1, ry0, ry1, amin);
     }
     int m;
-    const int slot = compact_slot(keep, s_cnt, &m);
+    const int slot = compact_slot<kBwdWarps>(keep, s_cnt, &m);
     if (slot >= 0) {
       s_gid[slot] = gid;
       s0[slot] = q0;
@@ -254,65 +345,18 @@ __global__ void __launch_bounds__(256, 4) composite_bwd_kernel(CompositeBwdArgs 
     __syncthreads();
     for (int j = 0; j < m; j++) {
       const uint32_t idx = s_idx[j];
+      const float4 g0 = s0[j];
+      const float4 g1 = s1[j];
+      const float g2 = s2[j];
       float v[9];
 #pragma unroll
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
-      bool ok = inside && idx < my_hi;
-      if (ok) {
-        const float4 g0 = s0[j];
-        const float4 g1 = s1[j];
-        const float dx = pxf - g0.x, dy = pyf - g0.y;
-        const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
-        ok = !(power > 0.0f || power < cut);
-        float G = 0.0f, alpha = 0.0f;
-        if (ok) {
-          G = gs_expf(power);
-          alpha = fminf(amax, g1.y * G);
-          ok = !(alpha < amin);
-        }
-        if (ok) {
-          const float o = g1.y;
-          const float c[3] = {g1.z, g1.w, s2[j]};
-          const float T_before = T / (1.0f - alpha);
-#pragma unroll
-          for (int k = 0; k < 3; k++) v[6 + k] = T_before * alpha * g[k];
-          float dL_dalpha = 0.0f;
-#pragma unroll
-          for (int k = 0; k < 3; k++) dL_dalpha += (T_before * (c[k] - acc[k] / T)) * g[k];
-          float dL_dG, dL_do;
-          if (FULL && !(o * G <= amax)) {
-            dL_dG = 0.0f;
-            dL_do = 0.0f;
-          } else {
-            dL_dG = dL_dalpha * o;
-            dL_do = dL_dalpha * G;
-          }
-          const float dL_dpower = dL_dG * G;
-          v[0] = dL_dpower * (g0.z * dx + g0.w * dy);
-          v[1] = dL_dpower * (g0.w * dx + g1.x * dy);
-          if (FULL) {
-            v[2] = dL_dpower * (-0.5f * dx * dx);
-            v[3] = dL_dpower * (-dx * dy);
-            v[4] = dL_dpower * (-0.5f * dy * dy);
-          }
-          v[5] = dL_do;
-          T = T_before;
-#pragma unroll
-          for (int k = 0; k < 3; k++) {
-            const float contrib = T_before * alpha * c[k];
-            acc[k] = FULL ? acc[k] + contrib : acc[k] - contrib;
-          }
-        }
-      }
-      if (__any_sync(0xffffffffu, ok)) {
-#pragma unroll
-        for (int k = 0; k < 9; k++) v[k] = warp_sum(v[k]);
-        if (lane == 0) {
-          float* gd = a.grad2d + (size_t)s_gid[j] * 9;
-#pragma unroll
-          for (int k = 0; k < 9; k++)
-            if (v[k] != 0.0f) atomicAdd(gd + k, v[k]);
-        }
+      const bool ok0 = bwd_pixel<FULL>(P[0], idx, g0, g1, g2, amin, amax, cut, v);
+      const bool ok1 = bwd_pixel<FULL>(P[1], idx, g0, g1, g2, amin, amax, cut, v);
+      if (__any_sync(0xffffffffu, ok0 || ok1)) {
+        const float r = warp_reduce9(v, lane);
+        const int k = lane >> 1;
+        if (!(lane & 1) && k < 9 && r != 0.0f) atomicAdd(a.grad2d + (size_t)s_gid[j] * 9 + k, r);
       }
     }
   }
@@ -330,10 +374,10 @@ int launch_composite_bwd(const CompositeBwdArgs& a, bool full, cudaStream_t stre
   const int tiles = a.tiles_x * a.tiles_y;
   if (tiles == 0) return GSC_OK;
   const bool l1 = a.target != nullptr;
-  if (full && l1) composite_bwd_kernel<true, true><<<tiles, 256, 0, stream>>>(a);
-  else if (full) composite_bwd_kernel<true, false><<<tiles, 256, 0, stream>>>(a);
-  else if (l1) composite_bwd_kernel<false, true><<<tiles, 256, 0, stream>>>(a);
-  else composite_bwd_kernel<false, false><<<tiles, 256, 0, stream>>>(a);
+  if (full && l1) composite_bwd_kernel<true, true><<<tiles, kBwdThreads, 0, stream>>>(a);
+  else if (full) composite_bwd_kernel<true, false><<<tiles, kBwdThreads, 0, stream>>>(a);
+  else if (l1) composite_bwd_kernel<false, true><<<tiles, kBwdThreads, 0, stream>>>(a);
+  else composite_bwd_kernel<false, false><<<tiles, kBwdThreads, 0, stream>>>(a);
   GS_CK_LAUNCH("composite_bwd_kernel");
   return GSC_OK;
 }
