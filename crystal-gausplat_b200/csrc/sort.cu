@@ -72,7 +72,7 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
 }
 
 template <typename K>
-__global__ void __launch_bounds__(kThreads) onesweep_kernel(
+__global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
@@ -94,29 +94,31 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
   const int64_t warp_base = tile_base + (int64_t)w * kWarpKeys;
   const uint32_t num_valid = (uint32_t)min((int64_t)kTileKeys, n - tile_base);
 
-  K k[kItems];
-  uint32_t v[kItems];
+  // Only the packed digits and ranks stay live across the look-back; keys
+  // and values are read again (from L2) when the tile is reordered, which
+  // keeps the kernel at four CTAs per SM.
   uint32_t rank[kItems];
+  uint32_t dig[kItems / 4];  // four 8-bit digits per register
 #pragma unroll
-  for (int i = 0; i < kItems; i++) {
-    const int64_t idx = warp_base + i * 32 + lane;
-    const bool valid = idx < n;
-    k[i] = valid ? keys_in[idx] : (K)~(K)0;
-    v[i] = valid ? vals_in[idx] : 0u;
-  }
-  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int i = 0; i < kItems / 4; i++) dig[i] = 0;
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
     const int64_t idx = warp_base + i * 32 + lane;
     // Pairs past the end take the largest digit, so they sort behind every
     // valid pair of the tile.
-    const uint32_t d = idx < n ? ((uint32_t)(k[i] >> shift) & digit_mask) : 255u;
+    const uint32_t d = idx < n ? ((uint32_t)(keys_in[idx] >> shift) & digit_mask) : 255u;
+    dig[i / 4] |= d << (8 * (i % 4));
+  }
+  const uint32_t lt_mask = (1u << lane) - 1u;
+#pragma unroll
+  for (int i = 0; i < kItems; i++) {
+    const uint32_t d = (dig[i / 4] >> (8 * (i % 4))) & 255u;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     const int leader = __ffs(peers) - 1;
     uint32_t b = 0;
     if (lane == leader) b = atomicAdd(&s_whist[w][d], (uint32_t)__popc(peers));
     b = __shfl_sync(0xffffffffu, b, leader);
-    rank[i] = b + __popc(peers & lt_mask);
+    rank[i] = (d << 16) | (b + __popc(peers & lt_mask));
   }
   __syncthreads();
 
@@ -166,9 +168,9 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
     const int64_t idx = warp_base + i * 32 + lane;
-    const uint32_t dd = idx < n ? ((uint32_t)(k[i] >> shift) & digit_mask) : 255u;
-    const uint32_t pos = s_local_excl[dd] + s_whist[w][dd] + rank[i];
-    s_keys[pos] = k[i];
+    const uint32_t dd = rank[i] >> 16;
+    const uint32_t pos = s_local_excl[dd] + s_whist[w][dd] + (rank[i] & 0xFFFFu);
+    if (idx < n) s_keys[pos] = keys_in[idx];
     rank[i] = pos;
   }
   __syncthreads();
@@ -183,7 +185,10 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
   __syncthreads();
   uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys);
 #pragma unroll
-  for (int i = 0; i < kItems; i++) s_vals[rank[i]] = v[i];
+  for (int i = 0; i < kItems; i++) {
+    const int64_t idx = warp_base + i * 32 + lane;
+    if (idx < n) s_vals[rank[i]] = vals_in[idx];
+  }
   __syncthreads();
   for (uint32_t j = tid; j < num_valid; j += kThreads) {
     const uint32_t gpos = s_gbase[s_dig[j]] + j;
