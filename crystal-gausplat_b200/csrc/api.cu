@@ -244,7 +244,8 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.cam = *cam; a.cfg = *cfg;
   a.tiles_x = (cam->width + GS_TILE - 1) / GS_TILE;
   a.tiles_y = (cam->height + GS_TILE - 1) / GS_TILE;
-  a.splats = o->splats; a.block_sums = block_sums;
+  a.splats = o->splats;
+  (void)block_sums;
   a.depth_keys = depth_keys; a.order = order;
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;

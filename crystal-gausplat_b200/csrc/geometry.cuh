@@ -180,4 +180,30 @@ __device__ __forceinline__ void sh_eval(ShRead S, float x, float y, float z, con
   }
 }
 
+// Partial derivatives of the real SH basis with respect to the unit view
+// direction (k = 1..15); zero where basis k does not depend on a component.
+__device__ __forceinline__ void sh_basis_derivs(float x, float y, float z, float DX[16], float DY[16],
+                                                float DZ[16]) {
+  const ShConsts K = sh_consts();
+  const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+#pragma unroll
+  for (int k = 0; k < 16; k++) DX[k] = DY[k] = DZ[k] = 0.0f;
+  DY[1] = -kShC1;
+  DZ[2] = kShC1;
+  DX[3] = -kShC1;
+  DX[4] = K.c2[0] * y; DY[4] = K.c2[0] * x;
+  DY[5] = K.c2[1] * z; DZ[5] = K.c2[1] * y;
+  DX[6] = K.c2[2] * (-2.0f * x); DY[6] = K.c2[2] * (-2.0f * y); DZ[6] = K.c2[2] * (4.0f * z);
+  DX[7] = K.c2[3] * z; DZ[7] = K.c2[3] * x;
+  DX[8] = K.c2[4] * (2.0f * x); DY[8] = K.c2[4] * (-2.0f * y);
+  DX[9] = K.c3[0] * (6.0f * xy); DY[9] = K.c3[0] * (3.0f * xx - 3.0f * yy);
+  DX[10] = K.c3[1] * yz; DY[10] = K.c3[1] * xz; DZ[10] = K.c3[1] * xy;
+  DX[11] = K.c3[2] * (-2.0f * xy); DY[11] = K.c3[2] * (4.0f * zz - xx - 3.0f * yy); DZ[11] = K.c3[2] * (8.0f * yz);
+  DX[12] = K.c3[3] * (-6.0f * xz); DY[12] = K.c3[3] * (-6.0f * yz);
+  DZ[12] = K.c3[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+  DX[13] = K.c3[4] * (4.0f * zz - 3.0f * xx - yy); DY[13] = K.c3[4] * (-2.0f * xy); DZ[13] = K.c3[4] * (8.0f * xz);
+  DX[14] = K.c3[5] * (2.0f * xz); DY[14] = K.c3[5] * (-2.0f * yz); DZ[14] = K.c3[5] * (xx - yy);
+  DX[15] = K.c3[6] * (3.0f * xx - 3.0f * yy); DY[15] = K.c3[6] * (-6.0f * xy);
+}
+
 }  // namespace gs

@@ -15,7 +15,6 @@ struct PreprocessArgs {
   gsc_raster_config cfg;
   int tiles_x, tiles_y;
   float* splats;
-  uint32_t* block_sums;  // one per 256 Gaussians, may be null
   uint32_t* depth_keys;  // bits(depth) if the Gaussian emits keys, else ~0; may be null
   uint32_t* order;       // identity permutation (input of the depth sort); may be null
   float* mean2d;

@@ -3,9 +3,9 @@
 // colour and opacity sigmoid (src/metal/kernels/gaussian.metal:90-308,
 // src/gaussian_splatting/gaussian.cr:119-142, rasterizer.cr:110-171).
 //
-// One thread per Gaussian, 256 per block. The 192-byte SH rows of a block are
-// staged through shared memory with coalesced float4 loads. Each block also
-// writes the sum of its tiles_touched, consumed by the binning scan.
+// One thread per Gaussian, 128 per block. The 192-byte SH rows of a block are
+// staged through shared memory with coalesced float4 loads, into rows padded
+// to 13 float4 so that the per-thread float4 reads are free of bank conflicts.
 //
 // Packed splat record (12 floats, private to this library):
 //   s0 = {mean.x, mean.y, conic.xx, conic.xy}
@@ -16,9 +16,12 @@
 
 namespace gs {
 
-__global__ void __launch_bounds__(256) preprocess_kernel(PreprocessArgs a) {
-  __shared__ float4 s_sh[256 * 12];
-  const int64_t base = (int64_t)blockIdx.x * 256;
+constexpr int kPreThreads = 128;
+constexpr int kShRow = 13;  // float4 per staged SH row (12 used + 1 pad)
+
+__global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs a) {
+  __shared__ float4 s_sh[kPreThreads * kShRow];
+  const int64_t base = (int64_t)blockIdx.x * kPreThreads;
   const int64_t i = base + threadIdx.x;
   const int64_t n = a.n;
   const gsc_camera& cam = a.cam;
@@ -26,9 +29,9 @@ __global__ void __launch_bounds__(256) preprocess_kernel(PreprocessArgs a) {
 
   // Coalesced staging of this block's SH coefficients (48 floats each).
   {
-    const int64_t cnt = min((int64_t)256, n - base);
+    const int64_t cnt = min((int64_t)kPreThreads, n - base);
     const float4* src = reinterpret_cast<const float4*>(a.sh + base * 48);
-    for (int k = threadIdx.x; k < cnt * 12; k += 256) s_sh[k] = src[k];
+    for (int k = threadIdx.x; k < cnt * 12; k += kPreThreads) s_sh[(k / 12) * kShRow + k % 12] = src[k];
   }
   __syncthreads();
 
@@ -52,9 +55,14 @@ __global__ void __launch_bounds__(256) preprocess_kernel(PreprocessArgs a) {
     view_dir(p, cam, d, &len);
     float b[16];
     sh_basis_hi(d[0], d[1], d[2], b);
-    const float* shrow = reinterpret_cast<const float*>(s_sh) + threadIdx.x * 48;
+    float shv[48];
+#pragma unroll
+    for (int q = 0; q < 12; q++) {
+      const float4 v = s_sh[threadIdx.x * kShRow + q];
+      shv[4 * q] = v.x; shv[4 * q + 1] = v.y; shv[4 * q + 2] = v.z; shv[4 * q + 3] = v.w;
+    }
     float raw[3];
-    sh_eval([&](int k) { return shrow[k]; }, d[0], d[1], d[2], b, cfg.sh_degree, cfg.mode, raw);
+    sh_eval([&](int k) { return shv[k]; }, d[0], d[1], d[2], b, cfg.sh_degree, cfg.mode, raw);
     float col[3];
 #pragma unroll
     for (int c = 0; c < 3; c++) col[c] = fmaxf(0.0f, raw[c] + 0.5f);
@@ -92,27 +100,12 @@ __global__ void __launch_bounds__(256) preprocess_kernel(PreprocessArgs a) {
       for (int k = 0; k < 6; k++) a.cov3d[i * 6 + k] = c3[k];
     }
   }
-  // Block sum of tiles_touched for the binning scan.
-  if (a.block_sums) {
-    uint32_t v = tiles;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    __syncthreads();  // every thread is done with s_sh; reuse its head for the warp sums
-    uint32_t* s_sum = reinterpret_cast<uint32_t*>(s_sh);
-    if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t t = 0;
-      for (int w = 0; w < 8; w++) t += s_sum[w];
-      a.block_sums[blockIdx.x] = t;
-    }
-  }
 }
 
 int launch_preprocess(const PreprocessArgs& a, cudaStream_t stream) {
   if (a.n == 0) return GSC_OK;
-  const int64_t blocks = (a.n + 255) / 256;
-  preprocess_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a);
+  const int64_t blocks = (a.n + kPreThreads - 1) / kPreThreads;
+  preprocess_kernel<<<(unsigned)blocks, kPreThreads, 0, stream>>>(a);
   GS_CK_LAUNCH("preprocess_kernel");
   return GSC_OK;
 }

@@ -225,6 +225,29 @@ inline void sh_eval(const float* sh, const ShBasis& B, int degree, int mode, flo
   }
 }
 
+// Partial derivatives of the real SH basis (reference constants) with respect
+// to the unit view direction; zero where basis k does not depend on a component.
+inline void sh_basis_derivs(float x, float y, float z, float DX[16], float DY[16], float DZ[16]) {
+  const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+  for (int k = 0; k < 16; k++) DX[k] = DY[k] = DZ[k] = 0.0f;
+  DY[1] = -SH_C1;
+  DZ[2] = SH_C1;
+  DX[3] = -SH_C1;
+  DX[4] = SH_C2[0] * y; DY[4] = SH_C2[0] * x;
+  DY[5] = SH_C2[1] * z; DZ[5] = SH_C2[1] * y;
+  DX[6] = SH_C2[2] * (-2.0f * x); DY[6] = SH_C2[2] * (-2.0f * y); DZ[6] = SH_C2[2] * (4.0f * z);
+  DX[7] = SH_C2[3] * z; DZ[7] = SH_C2[3] * x;
+  DX[8] = SH_C2[4] * (2.0f * x); DY[8] = SH_C2[4] * (-2.0f * y);
+  DX[9] = SH_C3[0] * (6.0f * xy); DY[9] = SH_C3[0] * (3.0f * xx - 3.0f * yy);
+  DX[10] = SH_C3[1] * yz; DY[10] = SH_C3[1] * xz; DZ[10] = SH_C3[1] * xy;
+  DX[11] = SH_C3[2] * (-2.0f * xy); DY[11] = SH_C3[2] * (4.0f * zz - xx - 3.0f * yy); DZ[11] = SH_C3[2] * (8.0f * yz);
+  DX[12] = SH_C3[3] * (-6.0f * xz); DY[12] = SH_C3[3] * (-6.0f * yz);
+  DZ[12] = SH_C3[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+  DX[13] = SH_C3[4] * (4.0f * zz - 3.0f * xx - yy); DY[13] = SH_C3[4] * (-2.0f * xy); DZ[13] = SH_C3[4] * (8.0f * xz);
+  DX[14] = SH_C3[5] * (2.0f * xz); DY[14] = SH_C3[5] * (-2.0f * yz); DZ[14] = SH_C3[5] * (xx - yy);
+  DX[15] = SH_C3[6] * (3.0f * xx - 3.0f * yy); DY[15] = SH_C3[6] * (-6.0f * xy);
+}
+
 // Gaussian3D#opacity, gaussian.cr:132-142.
 inline float sigmoid(float x) { return 1.0f / (1.0f + gso_expf(-x)); }
 
@@ -603,7 +626,6 @@ void gso_preprocess_backward(const gsc_gaussians* g, const gsc_camera* cam,
       float raw[3];
       sh_eval(g->sh + i * 48, B, cfg->sh_degree, cfg->mode, raw);
       const float x = d[0], y = d[1], z = d[2];
-      const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
       const int deg = cfg->sh_degree;
       const int ncoef = (deg + 1) * (deg + 1);
       float basis[16];
@@ -611,38 +633,22 @@ void gso_preprocess_backward(const gsc_gaussians* g, const gsc_camera* cam,
       basis[1] = SH_C1 * -y; basis[2] = SH_C1 * z; basis[3] = SH_C1 * -x;
       for (int k = 4; k < 16; k++) basis[k] = B.b[k];
       const float* sh = g->sh + i * 48;
-      float gx = 0.0f, gy = 0.0f, gz = 0.0f;
+      float w[3];
       for (int c = 0; c < 3; c++) {
-        float w = raw[c] + 0.5f > 0.0f ? dcol[c] : 0.0f;  // max(0, .) mask
-        if (w == 0.0f) continue;
-        for (int k = 0; k < ncoef; k++) grads->sh[i * 48 + k * 3 + c] += basis[k] * w;
-        auto S = [&](int k) { return sh[k * 3 + c]; };
-        float ex = 0.0f, ey = 0.0f, ez = 0.0f;
-        if (deg >= 1) {
-          ex += -SH_C1 * S(3);
-          ey += -SH_C1 * S(1);
-          ez += SH_C1 * S(2);
-        }
-        if (deg >= 2) {
-          ex += SH_C2[0] * y * S(4) + SH_C2[2] * (-2.0f * x) * S(6) + SH_C2[3] * z * S(7) +
-                SH_C2[4] * (2.0f * x) * S(8);
-          ey += SH_C2[0] * x * S(4) + SH_C2[1] * z * S(5) + SH_C2[2] * (-2.0f * y) * S(6) +
-                SH_C2[4] * (-2.0f * y) * S(8);
-          ez += SH_C2[1] * y * S(5) + SH_C2[2] * (4.0f * z) * S(6) + SH_C2[3] * x * S(7);
-        }
-        if (deg >= 3) {
-          ex += SH_C3[0] * (6.0f * xy) * S(9) + SH_C3[1] * yz * S(10) + SH_C3[2] * (-2.0f * xy) * S(11) +
-                SH_C3[3] * (-6.0f * xz) * S(12) + SH_C3[4] * (4.0f * zz - 3.0f * xx - yy) * S(13) +
-                SH_C3[5] * (2.0f * xz) * S(14) + SH_C3[6] * (3.0f * xx - 3.0f * yy) * S(15);
-          ey += SH_C3[0] * (3.0f * xx - 3.0f * yy) * S(9) + SH_C3[1] * xz * S(10) +
-                SH_C3[2] * (4.0f * zz - xx - 3.0f * yy) * S(11) + SH_C3[3] * (-6.0f * yz) * S(12) +
-                SH_C3[4] * (-2.0f * xy) * S(13) + SH_C3[5] * (-2.0f * yz) * S(14) +
-                SH_C3[6] * (-6.0f * xy) * S(15);
-          ez += SH_C3[1] * xy * S(10) + SH_C3[2] * (8.0f * yz) * S(11) +
-                SH_C3[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy) * S(12) + SH_C3[4] * (8.0f * xz) * S(13) +
-                SH_C3[5] * (xx - yy) * S(14);
-        }
-        gx += w * ex; gy += w * ey; gz += w * ez;
+        w[c] = raw[c] + 0.5f > 0.0f ? dcol[c] : 0.0f;  // max(0, .) mask
+        if (w[c] == 0.0f) continue;
+        for (int k = 0; k < ncoef; k++) grads->sh[i * 48 + k * 3 + c] += basis[k] * w[c];
+      }
+      // Direction gradient, one coefficient at a time: t_k = sum_c w_c S(k,c)
+      // times the partial derivatives of basis k.
+      float DX[16], DY[16], DZ[16];
+      sh_basis_derivs(x, y, z, DX, DY, DZ);
+      float gx = 0.0f, gy = 0.0f, gz = 0.0f;
+      for (int k = 1; k < ncoef; k++) {
+        const float t = w[0] * sh[k * 3] + w[1] * sh[k * 3 + 1] + w[2] * sh[k * 3 + 2];
+        gx += t * DX[k];
+        gy += t * DY[k];
+        gz += t * DZ[k];
       }
       // d = v/|v|, v = campos - p
       float dd = x * gx + y * gy + z * gz;
