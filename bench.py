@@ -367,27 +367,19 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
 
     e2e = None
     if not args.no_e2e:
-        stage = torch.empty_like(dev_t[0])
-        for _ in range(1):
-            tr.zero()
-            for v in tr.my_views:
-                stage.copy_(host_t[v - tr.lo], non_blocking=True)
-                tr.view_fwd_bwd(v, stage)
-            tr.reduce_and_step()
-            tr.loss.item()
+        feeder = trainer_mod.HostTargetFeeder(host_t, dev)
+        tr.step_from_host(feeder)
+        tr.loss.item()
         with Timer(torch, world) as tm2:
             for _ in range(args.steps):
-                tr.zero()
-                for v in tr.my_views:
-                    stage.copy_(host_t[v - tr.lo], non_blocking=True)
-                    tr.view_fwd_bwd(v, stage)
-                tr.reduce_and_step()
+                tr.step_from_host(feeder)
                 float(tr.loss.item())  # device -> host read of the step's loss
         ms2 = tm2.max_over_ranks()
         e2e = {"value": round(views_done / (ms2 / 1e3), 3), "unit": "views/s",
                "h2d_bytes_per_step": int(cfg["views"] * cfg["H"] * cfg["W"] * 3 * 4),
                "d2h_bytes_per_step": 4 * world,
-               "path": "Rasterizer.forward/backward + Adam through the C ABI; targets from pinned host"}
+               "path": "DataParallelTrainer.step_from_host: Rasterizer.forward/backward + Adam through "
+                       "the C ABI, each view's target copied from pinned host on a side stream"}
 
     result = None
     if rank == 0:

@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
   const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float t_stop = a.t_stop, amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
+  // every power that reaches the exponential lies in [cut, 0]
+  const bool short_exp = cut >= -103.0f;
 
   __shared__ uint32_t s_idx[256];
   __shared__ uint32_t s_cnt[8];
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
         const float4 q1 = s1[j];
         const float power = -0.5f * (dx * dx * q0.z + 2.0f * dx * dy * q0.w + dy * dy * q1.x);
         if (power > 0.0f || power < cut) continue;
-        const float G = gs_expf(power);
+        const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
         const float alpha = fminf(amax, q1.y * G);
         if (alpha < amin) continue;
         C0 += T * alpha * q1.z;
@@ -204,22 +206,26 @@ struct BwdPixel {
 // adds the conic gradient, the alpha clamp and the corrected running colour).
 template <bool FULL>
 __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, float4 g1, float g2,
-                                          float amin, float amax, float cut, float v[9]) {
+                                          float amin, float amax, float cut, bool short_exp, float v[9]) {
   if (!(P.inside && idx < P.hi)) return false;
   const float dx = P.pxf - g0.x, dy = P.pyf - g0.y;
   const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
   if (power > 0.0f || power < cut) return false;
-  const float G = gs_expf(power);
+  // Same exponential and tests as the forward, so the accepted set matches it.
+  const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
   const float alpha = fminf(amax, g1.y * G);
   if (alpha < amin) return false;
   const float o = g1.y;
   const float c[3] = {g1.z, g1.w, g2};
-  const float T_before = P.T / (1.0f - alpha);
+  // T_before = T / (1 - alpha); T_before * (c - acc / T) = T_before c - acc / (1 - alpha):
+  // one correctly rounded reciprocal instead of four divisions.
+  const float inv = __frcp_rn(1.0f - alpha);
+  const float T_before = P.T * inv;
 #pragma unroll
   for (int k = 0; k < 3; k++) v[6 + k] += T_before * alpha * P.g[k];
   float dL_dalpha = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 3; k++) dL_dalpha += (T_before * (c[k] - P.acc[k] / P.T)) * P.g[k];
+  for (int k = 0; k < 3; k++) dL_dalpha += (T_before * c[k] - P.acc[k] * inv) * P.g[k];
   float dL_dG, dL_do;
   if (FULL && !(o * G <= amax)) {
     dL_dG = 0.0f;
@@ -267,6 +273,7 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
   const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
+  const bool short_exp = cut >= -103.0f;
 
   BwdPixel P[2];
   float loss = 0.0f;
@@ -351,8 +358,8 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
       float v[9];
 #pragma unroll
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
-      const bool ok0 = bwd_pixel<FULL>(P[0], idx, g0, g1, g2, amin, amax, cut, v);
-      const bool ok1 = bwd_pixel<FULL>(P[1], idx, g0, g1, g2, amin, amax, cut, v);
+      const bool ok0 = bwd_pixel<FULL>(P[0], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
+      const bool ok1 = bwd_pixel<FULL>(P[1], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
       if (__any_sync(0xffffffffu, ok0 || ok1)) {
         const float r = warp_reduce9(v, lane);
         const int k = lane >> 1;

@@ -62,6 +62,14 @@ class DataParallelTrainer:
             torch.distributed.all_reduce(self.loss, group=self.pg)
         self.opt.step(grad_scale=1.0 / len(self.cameras))
 
+    def step_from_host(self, feeder):
+        """One training step with targets streamed from pinned host memory
+        (feeder: HostTargetFeeder over this rank's views, indexed from 0)."""
+        self.zero()
+        feeder.run(range(self.hi - self.lo), lambda k, t: self.view_fwd_bwd(self.lo + k, t))
+        self.reduce_and_step()
+        return self.loss
+
     def step(self, targets):
         """One training step over all views; `targets(v)` gives view v's device target."""
         self.zero()
@@ -69,3 +77,39 @@ class DataParallelTrainer:
             self.view_fwd_bwd(v, targets(v))
         self.reduce_and_step()
         return self.loss
+
+
+class HostTargetFeeder:
+    """Streams per-view targets from pinned host memory to the device on a
+    side stream, double-buffered, so that the copy of view v+1 overlaps the
+    forward/backward of view v. `host` is a pinned [V, H, W, 3] tensor."""
+
+    def __init__(self, host, device):
+        self.host = host
+        self.copy_stream = torch.cuda.Stream(device=device)
+        self.bufs = [torch.empty_like(host[0], device=device) for _ in range(2)]
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.free = [torch.cuda.Event() for _ in range(2)]
+        for e in self.free:
+            e.record(torch.cuda.current_stream(device))
+
+    def _issue(self, slot, v):
+        with torch.cuda.stream(self.copy_stream):
+            self.copy_stream.wait_event(self.free[slot])
+            self.bufs[slot].copy_(self.host[v], non_blocking=True)
+            self.ready[slot].record(self.copy_stream)
+
+    def run(self, views, fn):
+        """Calls fn(v, device_target) for each view, prefetching the next."""
+        views = list(views)
+        if not views:
+            return
+        cur = torch.cuda.current_stream(self.bufs[0].device)
+        self._issue(0, views[0])
+        for k, v in enumerate(views):
+            slot = k % 2
+            if k + 1 < len(views):
+                self._issue((k + 1) % 2, views[k + 1])
+            cur.wait_event(self.ready[slot])
+            fn(v, self.bufs[slot])
+            self.free[slot].record(cur)
