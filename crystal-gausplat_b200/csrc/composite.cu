@@ -125,8 +125,10 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
     int m;
     const int slot = compact_slot(keep, s_cnt, &m);
     if (slot >= 0) {
-      s0[slot] = g0;
-      s1[slot] = g1;
+      // conic pre-scaled by powers of two (-A/2, -B, -C/2): the power below
+      // then rounds to exactly -0.5 * ((dx dx A + (2 dx) dy B) + dy dy C)
+      s0[slot] = make_float4(g0.x, g0.y, -0.5f * g0.z, -g0.w);
+      s1[slot] = make_float4(-0.5f * g1.x, g1.y, g1.z, g1.w);
       s2[slot] = g2;
       s_idx[slot] = idx - start;
     }
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
         const float4 q0 = s0[j];
         const float dx = pxf - q0.x, dy = pyf - q0.y;
         const float4 q1 = s1[j];
-        const float power = -0.5f * (dx * dx * q0.z + 2.0f * dx * dy * q0.w + dy * dy * q1.x);
+        const float power = dx * dx * q0.z + dx * dy * q0.w + dy * dy * q1.x;
         if (power > 0.0f || power < cut) continue;
         const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
         const float alpha = fminf(amax, q1.y * G);
