@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
+                    help="N>1 gradient exchange: fused NVLink reduce+Adam+broadcast kernel, or NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -325,7 +327,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     g = gs.Gaussian3D(arrays, device=dev)
     cams = make_cameras(gs, cfg)
     rcfg = gs.default_config()
-    tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg)
+    tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg, exchange=args.exchange)
     host_t = make_targets(cfg, tr.lo, tr.hi)
     dev_t = host_t.to(dev)
     ctx = gs.context(dev)
@@ -395,6 +397,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "config": {"workload": f"{args.config}: train step, {cfg['n']} Gaussians SH3, {cfg['views']} views "
                                    f"{cfg['W']}x{cfg['H']}, L1, all-reduce + fused Adam",
                        "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
+                       "exchange": tr.exchange,
                        "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush",
                        "keys_per_view": round(keys_per_view), "pge_sample_view": pge},
             "gpu_launches": launches,

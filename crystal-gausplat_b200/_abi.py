@@ -78,6 +78,15 @@ class AdamGroup(C.Structure):
                 ("lr", C.c_float), ("weight_decay", C.c_float)]
 
 
+class DpAdamArgs(C.Structure):
+    _fields_ = [("nranks", C.c_int32), ("rank", C.c_int32),
+                ("peer_grads", P * 8), ("peer_params", P * 8), ("m", P), ("v", P),
+                ("ngroups", C.c_int32), ("offset", C.c_int64 * 8), ("numel", C.c_int64 * 8),
+                ("lr", C.c_float * 8), ("weight_decay", C.c_float * 8),
+                ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float), ("step", C.c_int32),
+                ("grad_scale", C.c_float)]
+
+
 assert C.sizeof(Camera) == 176, C.sizeof(Camera)
 
 _SIGS = {
@@ -110,6 +119,7 @@ _SIGS = {
     "gsc_l1_loss_grad": (C.c_int, [P, P, P, C.c_int64, C.c_float, P, P]),
     "gsc_adam_step": (C.c_int, [P, C.POINTER(AdamGroup), C.c_int32, C.c_float, C.c_float,
                                 C.c_float, C.c_int32, C.c_float]),
+    "gsc_dp_adam_step": (C.c_int, [P, C.POINTER(DpAdamArgs)]),
     "gsc_frame_create": (C.c_int, [P, C.POINTER(P)]),
     "gsc_frame_destroy": (C.c_int, [P]),
     "gsc_rasterize_forward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),

@@ -59,6 +59,13 @@ class Gaussian3D:
             shape = (n, SH_COEFFS, 3) if name == "sh_coeffs" else (n, w)
             setattr(self, name, view.view(*shape))
 
+    def rebind_arena(self, arena):
+        """Use `arena` (same size and layout, e.g. in symmetric memory) for the parameters."""
+        assert arena.numel() == self.arena.numel()
+        self.arena = arena
+        for name, t in self.views_of(arena).items():
+            setattr(self, name, t)
+
     @classmethod
     def synthetic(cls, n, seed, extent=1.0, device="cuda"):
         return cls(synthetic_arrays(n, seed, extent), device)

@@ -12,7 +12,9 @@ import ctypes as C
 
 import torch
 
+from . import _abi
 from ._abi import check, lib
+from .gaussian import FIELDS
 from .optim import Adam
 from .rasterizer import Rasterizer, RasterizerContext, RasterizerGradients, context
 
@@ -24,8 +26,28 @@ def shard(n_items, rank, world):
     return lo, hi
 
 
+def _symmetric_copy(t, group):
+    """t copied into torch symmetric memory (peer-addressable over NVLink)."""
+    import torch.distributed._symmetric_memory as symm_mem
+    s = symm_mem.empty(t.numel(), dtype=t.dtype, device=t.device)
+    s.copy_(t)
+    hdl = symm_mem.rendezvous(s, group.group_name)
+    return s, hdl
+
+
+def _peer_ptrs(t, hdl):
+    base = hdl.buffer_ptrs[hdl.rank]
+    off = t.data_ptr() - base
+    return [p + off for p in hdl.buffer_ptrs]
+
+
 class DataParallelTrainer:
-    def __init__(self, gaussians, cameras, config, lrs=None, process_group=None):
+    """exchange="nccl": all-reduce of the gradient arena, then Adam on every
+    replica. exchange="fused": gsc_dp_adam_step -- each rank sums its shard of
+    the peers' gradients over NVLink, applies Adam once and stores the new
+    parameters into every replica (arenas in torch symmetric memory)."""
+
+    def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl"):
         self.g = gaussians
         self.cameras = cameras
         self.cfg = config
@@ -33,8 +55,16 @@ class DataParallelTrainer:
         self.world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
         self.rank = torch.distributed.get_rank(process_group) if process_group is not None else 0
         self.lo, self.hi = shard(len(cameras), self.rank, self.world)
-        self.grads = RasterizerGradients(gaussians, screen=False)
+        self.exchange = exchange if self.world > 1 else "nccl"
+        grad_arena = None
+        if self.exchange == "fused":
+            arena, self.hdl_params = _symmetric_copy(gaussians.arena, process_group)
+            gaussians.rebind_arena(arena)
+            grad_arena, self.hdl_grads = _symmetric_copy(torch.zeros_like(arena), process_group)
+        self.grads = RasterizerGradients(gaussians, arena=grad_arena, screen=False)
         self.opt = Adam.for_gaussians(gaussians, self.grads, lrs)
+        if self.exchange == "fused":
+            self._setup_fused()
         self.ctx = RasterizerContext(gaussians.arena.device)
         self.loss = torch.zeros(1, device=gaussians.arena.device)
         self.cam_structs = [c.to_struct() for c in cameras]
@@ -56,7 +86,37 @@ class DataParallelTrainer:
         Rasterizer.backward(None, self.g, cam, self.ctx, grads=self.grads, target=target,
                             l1_scale=1.0 / target.numel(), loss_sum=self.loss, config=self.cfg)
 
+    def _setup_fused(self):
+        g = self.g
+        self.m = torch.zeros_like(g.arena)
+        self.v = torch.zeros_like(g.arena)
+        a = _abi.DpAdamArgs()
+        a.nranks, a.rank = self.world, self.rank
+        for p, (pg, pp) in enumerate(zip(_peer_ptrs(self.grads.arena, self.hdl_grads),
+                                         _peer_ptrs(g.arena, self.hdl_params))):
+            a.peer_grads[p] = pg
+            a.peer_params[p] = pp
+        a.m, a.v = self.m.data_ptr(), self.v.data_ptr()
+        a.ngroups = len(FIELDS)
+        for i, (name, w) in enumerate(FIELDS):
+            a.offset[i] = g.offsets[name]
+            a.numel[i] = g.count * w
+            a.lr[i] = self.opt.groups[i]["lr"]
+            a.weight_decay[i] = self.opt.groups[i]["weight_decay"]
+        a.beta1, a.beta2, a.eps = self.opt.beta1, self.opt.beta2, self.opt.eps
+        a.grad_scale = 1.0 / len(self.cameras)
+        self.dp_args = a
+
     def reduce_and_step(self):
+        if self.exchange == "fused":
+            torch.distributed.all_reduce(self.loss, group=self.pg)
+            self.opt.step_count += 1
+            self.dp_args.step = self.opt.step_count
+            self.hdl_grads.barrier(channel=0)   # every rank's gradients are complete
+            check(lib().gsc_dp_adam_step(context(self.g.arena.device), C.byref(self.dp_args)),
+                  "gsc_dp_adam_step")
+            self.hdl_params.barrier(channel=1)  # every shard's parameters have landed
+            return
         if self.world > 1:
             torch.distributed.all_reduce(self.grads.arena, group=self.pg)
             torch.distributed.all_reduce(self.loss, group=self.pg)

@@ -267,6 +267,38 @@ GSC_API int gsc_l1_loss_grad(gsc_ctx* ctx, const float* pred, const float* targe
 GSC_API int gsc_adam_step(gsc_ctx* ctx, const gsc_adam_group* groups, int32_t ngroups, float beta1,
                           float beta2, float eps, int32_t step, float grad_scale);
 
+/* Data-parallel exchange + optimiser step for view-sharded training, with no
+ * reference counterpart (the reference trains one view at a time on one
+ * device, trainer.cr:178-215). One kernel per rank: for its 1/nranks shard of
+ * the flat parameter arena it sums the ranks' gradient arenas with NVLink
+ * peer loads (rank order 0..nranks-1), applies Adam#step to the shard
+ * (adam.cr:127-176) and stores the new parameters into every rank's
+ * parameter arena with peer stores. It replaces all-reduce + a replicated
+ * Adam. All pointers must be device pointers valid in this process (peer
+ * pointers from CUDA IPC or symmetric memory); every rank's gradients must be
+ * complete before the call and the peers must not read parameters until every
+ * rank's call has finished (the caller fences both with a cross-rank
+ * barrier). Groups are [offset, offset + numel) float ranges of the arenas;
+ * offsets must be multiples of 4. */
+#define GSC_DP_MAX_RANKS 8
+typedef struct gsc_dp_adam_args {
+  int32_t nranks;
+  int32_t rank;
+  float* peer_grads[GSC_DP_MAX_RANKS];
+  float* peer_params[GSC_DP_MAX_RANKS];
+  float* m; /* this rank's first-moment arena (only its shard is read/written) */
+  float* v; /* this rank's second-moment arena */
+  int32_t ngroups;
+  int64_t offset[8];
+  int64_t numel[8];
+  float lr[8];
+  float weight_decay[8];
+  float beta1, beta2, eps;
+  int32_t step;
+  float grad_scale;
+} gsc_dp_adam_args;
+GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* args);
+
 /* ---- whole-view orchestration (Rasterizer.forward/backward,
  *      src/gaussian_splatting/rasterizer.cr:48-104) ----------------------- */
 

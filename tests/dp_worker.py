@@ -61,3 +61,39 @@ def dp_rank(rank, world, port, out_dir, fail_rank=-1):
         f.write(status)
     if status == "ok":
         dist.destroy_process_group()
+
+
+def gpu_rank(rank, world, port, out_dir, steps=2):
+    """One GPU rank: the same training steps with the NCCL exchange and with the
+    fused exchange (gsc_dp_adam_step); saves the final parameter arenas."""
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    gs = importlib.import_module("crystal-gausplat_b200")
+    trainer = importlib.import_module("crystal-gausplat_b200.trainer")
+    arrays = gs.synthetic_arrays(20000, 31)
+    eyes = gs.sphere_poses(8, 4.0, 32)
+    cams = [gs.make_camera(128, 96, tuple(e)) for e in eyes]
+    targets = [torch.from_numpy(np.random.default_rng(200 + v).uniform(0, 1, (96, 128, 3))
+                                .astype(np.float32)).to(dev) for v in range(len(cams))]
+    cfg = gs.default_config()
+    out = {}
+    for mode in ("nccl", "fused"):
+        g = gs.Gaussian3D(arrays, device=dev)
+        tr = trainer.DataParallelTrainer(g, cams, cfg, process_group=dist.group.WORLD, exchange=mode)
+        for _ in range(steps):
+            tr.step(lambda v: targets[v])
+        torch.cuda.synchronize()
+        out[mode] = g.arena.detach().cpu().numpy().copy()
+        out[mode + "_loss"] = float(tr.loss.item())
+    np.save(os.path.join(out_dir, f"gpu_rank{rank}_nccl.npy"), out["nccl"])
+    np.save(os.path.join(out_dir, f"gpu_rank{rank}_fused.npy"), out["fused"])
+    with open(os.path.join(out_dir, f"gpu_rank{rank}.status"), "w") as f:
+        f.write("ok")
+    dist.barrier()
+    dist.destroy_process_group()
