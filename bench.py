@@ -183,6 +183,12 @@ class Timer:
         return float(t.item())
 
 
+def profile_pge(gs, ctx, reset=True):
+    v = C.c_uint64()
+    gs._abi.check(gs._abi.lib().gsc_profile_pge(ctx, C.byref(v), 1 if reset else 0))
+    return int(v.value)
+
+
 def profile_read(gs, ctx, reset=True):
     _abi = gs._abi
     ms = (C.c_double * len(_abi.STAGES))()
@@ -340,6 +346,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
         tr.step(targets)
     torch.cuda.synchronize()
     profile_read(gs, ctx, reset=True)
+    profile_pge(gs, ctx, reset=True)
     k0 = lib.gsc_kernel_count(ctx)
     keys_total = 0
     lib.gsc_profile_enable(ctx, 1)
@@ -358,9 +365,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     views_done = args.steps * cfg["views"]
     value = views_done / (ms / 1e3)
 
-    # roofline sample: the last view rendered on this rank
-    pge = pge_count(gs, tr.ctx)
     my_views = max(1, tr.hi - tr.lo)
+    pge = profile_pge(gs, ctx) / (args.steps * my_views)  # exact mean over this rank's views
     keys_per_view = keys_total / (args.steps * my_views)
     tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
@@ -399,7 +405,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
                        "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
                        "exchange": tr.exchange,
                        "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush",
-                       "keys_per_view": round(keys_per_view), "pge_sample_view": pge},
+                       "keys_per_view": round(keys_per_view), "pge_per_view": round(pge)},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "e2e": e2e,
@@ -469,6 +475,7 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
             gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
     torch.cuda.synchronize()
     profile_read(gs, ctx, reset=True)
+    profile_pge(gs, ctx, reset=True)
     k0 = lib.gsc_kernel_count(ctx)
     keys_total = 0
     lib.gsc_profile_enable(ctx, 1)
@@ -484,7 +491,7 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     launches = int(lib.gsc_kernel_count(ctx) - k0)
     pix = args.steps * cfg["views"] * cfg["W"] * cfg["H"]
     value = pix / 1e6 / (ms / 1e3)
-    pge = pge_count(gs, rctx)
+    pge = profile_pge(gs, ctx) / max(1, args.steps * (hi - lo))
     tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
     kpv = keys_total / max(1, args.steps * (hi - lo))

@@ -589,6 +589,7 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   a.final_T = (float*)f->final_T.ptr;
   a.last = (uint32_t*)f->last.ptr;
   a.n_contrib = (uint32_t*)f->n_contrib.ptr;
+  if (ctx->profiling) a.pge = reinterpret_cast<unsigned long long*>(ctx->err + 2);
   {
     StageScope sc(ctx, GSC_STAGE_COMPOSITE_FWD);
     sc.kernels(1);
@@ -748,5 +749,17 @@ GSC_API int gsc_profile_read(gsc_ctx* ctx, double* ms, int64_t* calls, int64_t* 
 }
 
 GSC_API int64_t gsc_kernel_count(gsc_ctx* ctx) { return ctx ? ctx->kernels : 0; }
+
+GSC_API int gsc_profile_pge(gsc_ctx* ctx, uint64_t* out, int reset) {
+  GS_REQUIRE(ctx && out, "gsc_profile_pge: null argument");
+  GS_CK(cudaMemcpyAsync(ctx->pinned, ctx->err + 2, 8, cudaMemcpyDeviceToHost, ctx->stream));
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  std::memcpy(out, ctx->pinned, 8);
+  if (reset) {
+    GS_CK(cudaMemsetAsync(ctx->err + 2, 0, 8, ctx->stream));
+    GS_CK(cudaStreamSynchronize(ctx->stream));
+  }
+  return GSC_OK;
+}
 
 }  // extern "C"

@@ -156,6 +156,15 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
       }
     }
   }
+  if (a.pge) {  // tracing: entries visited before the stop (whole list if never stopped)
+    __shared__ unsigned long long s_pge;
+    if (tid == 0) s_pge = 0;
+    __syncthreads();
+    const uint32_t visited = !inside ? 0u : (!(T > t_stop) ? lst : end - start);
+    atomicAdd(&s_pge, (unsigned long long)visited);
+    __syncthreads();
+    if (tid == 0) atomicAdd(a.pge, s_pge);
+  }
   if (!inside) return;
   const size_t pix = (size_t)y * a.width + x;
   a.image[pix * 3 + 0] = C0 + T * a.bg[0];

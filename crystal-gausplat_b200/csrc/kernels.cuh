@@ -39,6 +39,7 @@ struct CompositeFwdArgs {
   uint32_t* n_contrib;
   float* final_T;
   uint32_t* last;
+  unsigned long long* pge;  // if set: += pixel-Gaussian evaluations (tile-list entries visited)
 };
 
 struct CompositeBwdArgs {

@@ -359,6 +359,10 @@ GSC_API int gsc_profile_read(gsc_ctx* ctx, double* ms, int64_t* calls, int64_t* 
 /* Kernels launched by this context since creation (counted whether or not
  * profiling is on). */
 GSC_API int64_t gsc_kernel_count(gsc_ctx* ctx);
+/* Pixel-Gaussian evaluations counted by whole-view forwards while profiling
+ * was enabled: per pixel, the tile-list entries up to the transmittance stop
+ * (the whole list if the pixel never stopped). */
+GSC_API int gsc_profile_pge(gsc_ctx* ctx, uint64_t* out, int reset);
 
 #ifdef __cplusplus
 }
