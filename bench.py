@@ -220,6 +220,10 @@ def pge_count(gs, rctx):
 # ---------------------------------------------------------------------------
 # algorithmic work per stage (bytes, or FP32 ops for compositing)
 # ---------------------------------------------------------------------------
+# DRAM bytes per launch measured by ncu for the config-3 compositing kernels
+# (profiles/composite_traffic_c3.md).
+TRAFFIC_C3 = {"composite_fwd": 83.75e6, "composite_bwd": 146.49e6}
+
 PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
 PREPROCESS_BWD_B = 556  # read 236 params + 36 grad2d, read+write 236 grads (visible Gaussians)
 ADAM_B = 28 * 59        # read p, g, m, v + write p, m, v per float
@@ -411,7 +415,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "e2e": e2e,
             "roofline": dict(roof[dominant], kernel=dominant,
                              peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind,
-                             traffic=None) if dominant else None,
+                             traffic=TRAFFIC_C3.get(dominant) if args.config == "c3" else None)
+            if dominant else None,
             "roofline_hbm": dict(roof[top_hbm], kernel=top_hbm, peak_kind=peak_kind, traffic=None)
             if top_hbm else None,
             "stages": roof,

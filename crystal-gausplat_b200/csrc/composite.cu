@@ -160,8 +160,10 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
     __shared__ unsigned long long s_pge;
     if (tid == 0) s_pge = 0;
     __syncthreads();
-    const uint32_t visited = !inside ? 0u : (!(T > t_stop) ? lst : end - start);
-    atomicAdd(&s_pge, (unsigned long long)visited);
+    uint32_t visited = !inside ? 0u : (!(T > t_stop) ? lst : end - start);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) visited += __shfl_xor_sync(0xffffffffu, visited, off);
+    if ((tid & 31) == 0) atomicAdd(&s_pge, (unsigned long long)visited);
     __syncthreads();
     if (tid == 0) atomicAdd(a.pge, s_pge);
   }
