@@ -267,8 +267,10 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
 
 // 128 threads per tile, two pixels per thread (rows r and r + 8), so each
 // warp reduction covers 64 pixels.
-constexpr int kBwdThreads = 128;
+constexpr int kBwdPix = 2;                        // pixels per thread
+constexpr int kBwdThreads = GS_TILE_PIXELS / kBwdPix;  // 64
 constexpr int kBwdWarps = kBwdThreads / 32;
+constexpr int kBwdRowStep = GS_TILE / kBwdPix;        // rows between a thread's pixels
 
 template <bool FULL, bool L1>
 __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(CompositeBwdArgs a) {
@@ -288,11 +290,11 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
   const float amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
   const bool short_exp = cut >= -103.0f;
 
-  BwdPixel P[2];
+  BwdPixel P[kBwdPix];
   float loss = 0.0f;
 #pragma unroll
-  for (int h = 0; h < 2; h++) {
-    const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4) + 8 * h;
+  for (int h = 0; h < kBwdPix; h++) {
+    const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4) + kBwdRowStep * h;
     BwdPixel& Q = P[h];
     Q.inside = x < a.width && y < a.height;
     Q.pxf = (float)x + 0.5f;
@@ -331,7 +333,12 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
     for (int w = 0; w < kBwdWarps; w++) t += s_loss[w];
     if (t != 0.0f) atomicAdd(a.loss_sum, t);
   }
-  if (FULL) atomicMax(&s_hi, max(P[0].hi, P[1].hi));
+  if (FULL) {
+    uint32_t mh = P[0].hi;
+#pragma unroll
+    for (int h = 1; h < kBwdPix; h++) mh = max(mh, P[h].hi);
+    atomicMax(&s_hi, mh);
+  }
   __syncthreads();
   const uint32_t hi = FULL ? s_hi : end;
 
@@ -371,9 +378,10 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
       float v[9];
 #pragma unroll
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
-      const bool ok0 = bwd_pixel<FULL>(P[0], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
-      const bool ok1 = bwd_pixel<FULL>(P[1], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
-      if (__any_sync(0xffffffffu, ok0 || ok1)) {
+      bool ok = false;
+#pragma unroll
+      for (int h = 0; h < kBwdPix; h++) ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
+      if (__any_sync(0xffffffffu, ok)) {
         const float r = warp_reduce9(v, lane);
         const int k = lane >> 1;
         if (!(lane & 1) && k < 9 && r != 0.0f) atomicAdd(a.grad2d + (size_t)s_gid[j] * 9 + k, r);
