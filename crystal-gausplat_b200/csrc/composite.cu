@@ -211,7 +211,7 @@ struct BwdPixel {
   float pxf, pyf;
   float g[3];
   float T;
-  float acc[3];
+  float ag;  // (colour behind this Gaussian, incl. background) . g -- the only use of it
   uint32_t hi;
 };
 
@@ -222,23 +222,23 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
                                           float amin, float amax, float cut, bool short_exp, float v[9]) {
   if (!(P.inside && idx < P.hi)) return false;
   const float dx = P.pxf - g0.x, dy = P.pyf - g0.y;
-  const float power = -0.5f * (dx * dx * g0.z + 2.0f * dx * dy * g0.w + dy * dy * g1.x);
+  const float power = dx * dx * g0.z + dx * dy * g0.w + dy * dy * g1.x;  // == forward's power
   if (power > 0.0f || power < cut) return false;
   // Same exponential and tests as the forward, so the accepted set matches it.
   const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
   const float alpha = fminf(amax, g1.y * G);
   if (alpha < amin) return false;
   const float o = g1.y;
-  const float c[3] = {g1.z, g1.w, g2};
-  // T_before = T / (1 - alpha); T_before * (c - acc / T) = T_before c - acc / (1 - alpha):
-  // one correctly rounded reciprocal instead of four divisions.
+  // T_before = T / (1 - alpha) and dL/dalpha = T_before c.g - (acc / (1 - alpha)).g,
+  // with one correctly rounded reciprocal and the running colour kept as acc.g.
   const float inv = __frcp_rn(1.0f - alpha);
   const float T_before = P.T * inv;
-#pragma unroll
-  for (int k = 0; k < 3; k++) v[6 + k] += T_before * alpha * P.g[k];
-  float dL_dalpha = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 3; k++) dL_dalpha += (T_before * c[k] - P.acc[k] * inv) * P.g[k];
+  const float wgt = T_before * alpha;
+  const float cg = g1.z * P.g[0] + g1.w * P.g[1] + g2 * P.g[2];
+  v[6] += wgt * P.g[0];
+  v[7] += wgt * P.g[1];
+  v[8] += wgt * P.g[2];
+  const float dL_dalpha = T_before * cg - P.ag * inv;
   float dL_dG, dL_do;
   if (FULL && !(o * G <= amax)) {
     dL_dG = 0.0f;
@@ -248,8 +248,9 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
     dL_do = dL_dalpha * G;
   }
   const float dL_dpower = dL_dG * G;
-  v[0] += dL_dpower * (g0.z * dx + g0.w * dy);
-  v[1] += dL_dpower * (g0.w * dx + g1.x * dy);
+  // g0 = {mean, -A/2, -B}, g1.x = -C/2 (pre-scaled conic, see fwd)
+  v[0] += dL_dpower * (-2.0f * g0.z * dx - g0.w * dy);
+  v[1] += dL_dpower * (-g0.w * dx - 2.0f * g1.x * dy);
   if (FULL) {
     v[2] += dL_dpower * (-0.5f * dx * dx);
     v[3] += dL_dpower * (-dx * dy);
@@ -257,11 +258,7 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
   }
   v[5] += dL_do;
   P.T = T_before;
-#pragma unroll
-  for (int k = 0; k < 3; k++) {
-    const float contrib = T_before * alpha * c[k];
-    P.acc[k] = FULL ? P.acc[k] + contrib : P.acc[k] - contrib;
-  }
+  P.ag = FULL ? P.ag + wgt * cg : P.ag - wgt * cg;  // REF keeps gaussian.metal:566
   return true;
 }
 
@@ -318,8 +315,7 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
       Q.T = a.final_T[pix];
       Q.hi = FULL ? start + a.last[pix] : end;
     }
-#pragma unroll
-    for (int c = 0; c < 3; c++) Q.acc[c] = a.bg[c] * Q.T;
+    Q.ag = (a.bg[0] * Q.T) * Q.g[0] + (a.bg[1] * Q.T) * Q.g[1] + (a.bg[2] * Q.T) * Q.g[2];
   }
 
   if (L1 && a.loss_sum) {
@@ -364,8 +360,8 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
     const int slot = compact_slot<kBwdWarps>(keep, s_cnt, &m);
     if (slot >= 0) {
       s_gid[slot] = gid;
-      s0[slot] = q0;
-      s1[slot] = q1;
+      s0[slot] = make_float4(q0.x, q0.y, -0.5f * q0.z, -q0.w);
+      s1[slot] = make_float4(-0.5f * q1.x, q1.y, q1.z, q1.w);
       s2[slot] = q2;
       s_idx[slot] = (uint32_t)(bend - 1 - tid);
     }
