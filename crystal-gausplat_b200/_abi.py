@@ -78,6 +78,15 @@ class AdamGroup(C.Structure):
                 ("lr", C.c_float), ("weight_decay", C.c_float)]
 
 
+class GaussiansOut(C.Structure):
+    _fields_ = [("position", P), ("log_scale", P), ("rotation", P), ("logit_opacity", P), ("sh", P)]
+
+
+GSC_DENSIFY_CLONE = 1
+GSC_DENSIFY_SPLIT = 2
+GSC_DENSIFY_PRUNE = 4
+
+
 class DpAdamArgs(C.Structure):
     _fields_ = [("nranks", C.c_int32), ("rank", C.c_int32),
                 ("peer_grads", P * 8), ("peer_params", P * 8), ("m", P), ("v", P),
@@ -120,6 +129,12 @@ _SIGS = {
     "gsc_adam_step": (C.c_int, [P, C.POINTER(AdamGroup), C.c_int32, C.c_float, C.c_float,
                                 C.c_float, C.c_int32, C.c_float]),
     "gsc_dp_adam_step": (C.c_int, [P, C.POINTER(DpAdamArgs)]),
+    "gsc_grad_accumulate": (C.c_int, [P, P, C.c_int32, C.c_int64, P, P]),
+    "gsc_densify_plan": (C.c_int, [P, C.POINTER(Gaussians), P, P, C.c_float, C.c_float, C.c_float,
+                                   P, C.POINTER(C.c_int64)]),
+    "gsc_densify_apply": (C.c_int, [P, C.POINTER(Gaussians), P, C.POINTER(GaussiansOut), C.c_float,
+                                    C.c_float, C.c_uint64]),
+    "gsc_reset_opacity": (C.c_int, [P, P, C.c_int64, C.c_float]),
     "gsc_frame_create": (C.c_int, [P, C.POINTER(P)]),
     "gsc_frame_destroy": (C.c_int, [P]),
     "gsc_rasterize_forward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),

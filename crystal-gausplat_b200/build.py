@@ -15,7 +15,8 @@ LIB = os.path.join(HERE, "libgsplat_cuda.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 SOURCES = ["api.cu", "preprocess.cu", "binning.cu", "sort.cu", "composite.cu",
-           "preprocess_bwd.cu", "optim.cu", "sort_static.cu", "dp.cu"]
+           "preprocess_bwd.cu", "optim.cu", "sort_static.cu", "dp.cu",
+           "densify.cu"]
 
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -46,18 +46,24 @@ def synthetic_arrays(n, seed, extent=1.0):
 class Gaussian3D:
     """The five parameter tensors, as views of one device arena."""
 
-    def __init__(self, arrays, device="cuda"):
+    def __init__(self, arrays, device="cuda", count=None):
         import torch
-        n = int(arrays["position"].shape[0])
+        n = int(arrays["position"].shape[0]) if arrays is not None else int(count)
         self.count = n
         offs, total = field_offsets(n)
         self.offsets = offs
         self.arena = torch.zeros(total, dtype=torch.float32, device=device)
         for name, w in FIELDS:
             view = self.arena[offs[name]:offs[name] + n * w]
-            view.copy_(torch.as_tensor(np.ascontiguousarray(arrays[name]).reshape(-1)))
+            if arrays is not None:
+                view.copy_(torch.as_tensor(np.ascontiguousarray(arrays[name]).reshape(-1)))
             shape = (n, SH_COEFFS, 3) if name == "sh_coeffs" else (n, w)
             setattr(self, name, view.view(*shape))
+
+    @classmethod
+    def empty(cls, n, device="cuda"):
+        """A zero-filled set of n Gaussians (the destination of densification)."""
+        return cls(None, device, count=n)
 
     def rebind_arena(self, arena):
         """Use `arena` (same size and layout, e.g. in symmetric memory) for the parameters."""

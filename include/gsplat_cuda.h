@@ -299,6 +299,54 @@ typedef struct gsc_dp_adam_args {
 } gsc_dp_adam_args;
 GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* args);
 
+/* ---- densification (Trainer#densify_and_prune!, trainer.cr:293-392) ---- */
+
+/* GradientAccumulator#accumulate (trainer.cr:86-99): for every i,
+ * accum[i] += |dL/dmean2d_i| and count[i] += 1. Row i of dmean2d starts at
+ * dmean2d + i * stride (stride 2 for an [N,2] array, 9 for a frame's grad2d). */
+GSC_API int gsc_grad_accumulate(gsc_ctx* ctx, const float* dmean2d, int32_t stride, int64_t n,
+                                float* accum, int32_t* count);
+
+#define GSC_DENSIFY_CLONE 1u
+#define GSC_DENSIFY_SPLIT 2u
+#define GSC_DENSIFY_PRUNE 4u
+
+/* The decisions of densify_and_prune! (trainer.cr:296-325): average gradient
+ * accum/count (0 when count is 0) above grad_threshold -> split if the largest
+ * exp(log_scale) exceeds size_threshold, else clone; sigmoid(logit) below
+ * opacity_threshold -> prune. flags[i] gets GSC_DENSIFY_* bits (a split
+ * Gaussian is never also kept). counts (host, 3 values) = {kept originals,
+ * clones, splits}; the new set has kept + clones + 2 * splits Gaussians.
+ * As Gaussian3D#remove! (gaussian.cr:233-235), a plan that would leave no
+ * Gaussian prunes none. */
+GSC_API int gsc_densify_plan(gsc_ctx* ctx, const gsc_gaussians* g, const float* accum,
+                             const int32_t* count, float grad_threshold, float size_threshold,
+                             float opacity_threshold, uint8_t* flags, int64_t* counts);
+
+/* Output parameter arrays of a new Gaussian set (same layouts as gsc_gaussians). */
+typedef struct gsc_gaussians_out {
+  float* position;
+  float* log_scale;
+  float* rotation;
+  float* logit_opacity;
+  float* sh;
+} gsc_gaussians_out;
+
+/* Builds the densified set in the order [kept originals][clones][first split
+ * halves][second split halves], every group in original index order (the
+ * reference's concat!/remove! order, with its pruning applied to the original
+ * indices). Clones: position += (U - 0.5) * 2 * clone_noise per axis
+ * (trainer.cr:375-386). Split halves: log_scale -= ln_split (ln 1.6 in the
+ * reference), position += exp(new log_scale.x) * 0.5 * (+1 | -1) * (U - 0.5)
+ * per axis (trainer.cr:332-370). U in [0,1) is a counter-based hash of
+ * (seed, index, draw), identical on every device and in the CPU oracle. */
+GSC_API int gsc_densify_apply(gsc_ctx* ctx, const gsc_gaussians* g, const uint8_t* flags,
+                              const gsc_gaussians_out* out, float clone_noise, float ln_split,
+                              uint64_t seed);
+
+/* Gaussian3D#reset_opacity! (gaussian.cr:269-271): logit_opacity[i] = value. */
+GSC_API int gsc_reset_opacity(gsc_ctx* ctx, float* logit_opacity, int64_t n, float value);
+
 /* ---- whole-view orchestration (Rasterizer.forward/backward,
  *      src/gaussian_splatting/rasterizer.cr:48-104) ----------------------- */
 

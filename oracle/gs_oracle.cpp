@@ -749,6 +749,105 @@ void gso_l1_loss_grad(int64_t numel, const float* pred, const float* target, flo
   if (loss_sum) *loss_sum += loss;
 }
 
+// ---- densification -------------------------------------------------------
+
+// SplitMix64 finaliser (Steele, Lea & Flood 2014) as a counter-based hash:
+// U(seed, index, draw) = top 24 bits of mix(seed ^ mix(8 * index + draw)) / 2^24.
+static uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+static float hash_u01(uint64_t seed, uint64_t idx, uint32_t draw) {
+  const uint64_t h = mix64(seed ^ mix64(idx * 8ull + draw));
+  return (float)(h >> 40) * (1.0f / 16777216.0f);
+}
+
+void gso_grad_accumulate(const float* d, int32_t stride, int64_t n, float* accum, int32_t* count) {
+  // GradientAccumulator#accumulate, trainer.cr:86-99: norm of the 2D mean gradient.
+  for (int64_t i = 0; i < n; i++) {
+    const float gx = d[i * stride], gy = d[i * stride + 1];
+    accum[i] += std::sqrt(gx * gx + gy * gy);
+    count[i] += 1;
+  }
+}
+
+void gso_densify_plan(const gsc_gaussians* g, const float* accum, const int32_t* count,
+                      float grad_thr, float size_thr, float op_thr, uint8_t* flags, int64_t* counts) {
+  // densify_and_prune!, trainer.cr:296-325: average gradient (GradientAccumulator#average,
+  // trainer.cr:101-110), largest exp(log_scale), sigmoid(logit) against the thresholds.
+  counts[0] = counts[1] = counts[2] = 0;
+  for (int64_t i = 0; i < g->count; i++) {
+    const float avg = count[i] == 0 ? 0.0f : accum[i] / (float)count[i];
+    const float* ls = g->log_scale + i * 3;
+    const float s0 = gso_expf(ls[0]), s1 = gso_expf(ls[1]), s2 = gso_expf(ls[2]);
+    const float ms = std::fmax(s0, std::fmax(s1, s2));
+    uint8_t f = 0;
+    if (avg > grad_thr) f |= ms > size_thr ? GSC_DENSIFY_SPLIT : GSC_DENSIFY_CLONE;
+    if (sigmoid(g->logit_opacity[i]) < op_thr) f |= GSC_DENSIFY_PRUNE;
+    flags[i] = f;
+    const bool split = f & GSC_DENSIFY_SPLIT, clone = f & GSC_DENSIFY_CLONE;
+    counts[0] += !split && !(f & GSC_DENSIFY_PRUNE);
+    counts[1] += clone;
+    counts[2] += split;
+  }
+  // Gaussian3D#remove! never empties the set (gaussian.cr:234-235).
+  if (g->count > 0 && counts[0] + counts[1] + counts[2] == 0) {
+    for (int64_t i = 0; i < g->count; i++) flags[i] &= (uint8_t)~GSC_DENSIFY_PRUNE;
+    counts[0] = g->count;
+  }
+}
+
+static void densify_row(const gsc_gaussians* g, int64_t i, const gsc_gaussians_out* o, int64_t d,
+                        const float p[3], const float l[3]) {
+  for (int k = 0; k < 3; k++) {
+    o->position[d * 3 + k] = p[k];
+    o->log_scale[d * 3 + k] = l[k];
+  }
+  for (int k = 0; k < 4; k++) o->rotation[d * 4 + k] = g->rotation[i * 4 + k];
+  o->logit_opacity[d] = g->logit_opacity[i];
+  for (int k = 0; k < 48; k++) o->sh[d * 48 + k] = g->sh[i * 48 + k];
+}
+
+void gso_densify_apply(const gsc_gaussians* g, const uint8_t* flags, const gsc_gaussians_out* o,
+                       float clone_noise, float ln_split, uint64_t seed) {
+  // Output [kept][clones][split halves 1][split halves 2], each in index order.
+  // Clone noise: add_position_noise!, trainer.cr:375-386. Split: split_gaussians!,
+  // trainer.cr:332-370. Pruning (remove!, gaussian.cr:233-266) acts on original indices.
+  int64_t nk = 0, nc = 0, ns = 0;
+  for (int64_t i = 0; i < g->count; i++) {
+    const uint8_t f = flags[i];
+    nk += !(f & GSC_DENSIFY_SPLIT) && !(f & GSC_DENSIFY_PRUNE);
+    nc += (f & GSC_DENSIFY_CLONE) != 0;
+    ns += (f & GSC_DENSIFY_SPLIT) != 0;
+  }
+  int64_t ik = 0, ic = nk, is = nk + nc;
+  for (int64_t i = 0; i < g->count; i++) {
+    const uint8_t f = flags[i];
+    const float* p = g->position + i * 3;
+    const float* l = g->log_scale + i * 3;
+    if (!(f & GSC_DENSIFY_SPLIT) && !(f & GSC_DENSIFY_PRUNE)) densify_row(g, i, o, ik++, p, l);
+    if (f & GSC_DENSIFY_CLONE) {
+      float q[3];
+      for (int k = 0; k < 3; k++)
+        q[k] = p[k] + (hash_u01(seed, (uint64_t)i, k) - 0.5f) * 2.0f * clone_noise;
+      densify_row(g, i, o, ic++, q, l);
+    }
+    if (f & GSC_DENSIFY_SPLIT) {
+      const float l2[3] = {l[0] - ln_split, l[1] - ln_split, l[2] - ln_split};
+      for (int h = 0; h < 2; h++) {
+        const float offset = gso_expf(l2[0]) * 0.5f * (h == 0 ? 1.0f : -1.0f);
+        float q[3];
+        for (int k = 0; k < 3; k++)
+          q[k] = p[k] + offset * (hash_u01(seed, (uint64_t)i, 3 + 3 * h + k) - 0.5f);
+        densify_row(g, i, o, is + h * ns, q, l2);
+      }
+      is++;
+    }
+  }
+}
+
 void gso_adam_step(const gsc_adam_group* groups, int32_t ngroups, float beta1, float beta2,
                    float eps, int32_t step, float grad_scale) {
   // Adam#step / update_adam! / apply_weight_decay!, src/optim/adam.cr:86-176.

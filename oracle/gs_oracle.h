@@ -73,6 +73,16 @@ void gso_l1_loss_grad(int64_t numel, const float* pred, const float* target, flo
 void gso_adam_step(const gsc_adam_group* groups, int32_t ngroups, float beta1, float beta2,
                    float eps, int32_t step, float grad_scale);
 
+/* Densification (trainer.cr:77-123, 293-392); same contract as
+ * gsc_grad_accumulate / gsc_densify_plan / gsc_densify_apply. */
+void gso_grad_accumulate(const float* dmean2d, int32_t stride, int64_t n, float* accum,
+                         int32_t* count);
+void gso_densify_plan(const gsc_gaussians* g, const float* accum, const int32_t* count,
+                      float grad_threshold, float size_threshold, float opacity_threshold,
+                      uint8_t* flags, int64_t* counts);
+void gso_densify_apply(const gsc_gaussians* g, const uint8_t* flags, const gsc_gaussians_out* out,
+                       float clone_noise, float ln_split, uint64_t seed);
+
 /* Whole view: forward (and backward with fused L1 when target != NULL).
  * Allocates its own intermediates. Returns the number of keys. */
 int64_t gso_render_view(const gsc_gaussians* g, const gsc_camera* cam,

@@ -191,6 +191,43 @@ def adam_step(groups, beta1, beta2, eps, step, grad_scale=1.0):
                         C.c_float(grad_scale))
 
 
+def grad_accumulate(dmean2d, accum, count):
+    """accum/count (numpy float32 / int32) updated in place from an [N, stride] gradient."""
+    d = _f32(dmean2d)
+    n = accum.size
+    lib().gso_grad_accumulate(_p(d), C.c_int32(d.size // max(n, 1)), C.c_int64(n), _p(accum),
+                              _p(count))
+
+
+def densify_plan(scene, accum, count, grad_threshold, size_threshold, opacity_threshold):
+    flags = np.zeros(scene.n, np.uint8)
+    counts = (C.c_int64 * 3)()
+    lib().gso_densify_plan(C.byref(scene.struct), _p(_f32(accum)),
+                           _p(np.ascontiguousarray(count, np.int32)), C.c_float(grad_threshold),
+                           C.c_float(size_threshold), C.c_float(opacity_threshold), _p(flags), counts)
+    return flags, tuple(counts)
+
+
+def densify_apply(scene, flags, clone_noise, ln_split, seed):
+    """New host arrays (position, log_scale, rotation, logit_opacity, sh_coeffs)."""
+    f = np.ascontiguousarray(flags, np.uint8)
+    split = (f & _abi.GSC_DENSIFY_SPLIT) != 0
+    keep = ~split & ((f & _abi.GSC_DENSIFY_PRUNE) == 0)
+    m = int(keep.sum() + ((f & _abi.GSC_DENSIFY_CLONE) != 0).sum() + 2 * split.sum())
+    out = {"position": np.zeros((m, 3), np.float32), "log_scale": np.zeros((m, 3), np.float32),
+           "rotation": np.zeros((m, 4), np.float32), "logit_opacity": np.zeros(m, np.float32),
+           "sh_coeffs": np.zeros((m, 48), np.float32)}
+    o = _abi.GaussiansOut()
+    o.position = out["position"].ctypes.data
+    o.log_scale = out["log_scale"].ctypes.data
+    o.rotation = out["rotation"].ctypes.data
+    o.logit_opacity = out["logit_opacity"].ctypes.data
+    o.sh = out["sh_coeffs"].ctypes.data
+    lib().gso_densify_apply(C.byref(scene.struct), _p(f), C.byref(o), C.c_float(clone_noise),
+                            C.c_float(ln_split), C.c_uint64(seed))
+    return out
+
+
 def forward_pipeline(scene, cam, cfg):
     """All forward intermediates of one view (preprocess .. composite)."""
     W, H = cam.width, cam.height
