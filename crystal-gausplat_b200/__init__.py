@@ -15,6 +15,7 @@ try:
     from .rasterizer import (GPURadixSort, Rasterizer, RasterizerContext, RasterizerGradients,
                              context, sync)
     from .optim import Adam, l1_with_grad
+    from . import loss as Loss
     from .densify import (GradientAccumulator, densify_and_prune, densify_apply, densify_plan,
                           reset_opacity)
 except ImportError:  # torch missing: camera/generator helpers stay usable

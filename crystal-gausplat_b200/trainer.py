@@ -15,6 +15,7 @@ import torch
 from . import _abi
 from ._abi import check, lib
 from .gaussian import FIELDS
+from .loss import combined_with_grad
 from .optim import Adam
 from .rasterizer import Rasterizer, RasterizerContext, RasterizerGradients, context
 
@@ -45,9 +46,15 @@ class DataParallelTrainer:
     """exchange="nccl": all-reduce of the gradient arena, then Adam on every
     replica. exchange="fused": gsc_dp_adam_step -- each rank sums its shard of
     the peers' gradients over NVLink, applies Adam once and stores the new
-    parameters into every replica (arenas in torch symmetric memory)."""
+    parameters into every replica (arenas in torch symmetric memory).
 
-    def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl"):
+    loss="l1": the L1 gradient fused into the backward compositing (the
+    benchmark configurations). loss="combined": Trainer#train_step's
+    (1 - lambda_ssim) L1 + lambda_ssim (1 - SSIM) (trainer.cr:190), computed on
+    the rendered image by gsc_combined_loss_grad and fed back as dL/dimage."""
+
+    def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl",
+                 loss="l1", lambda_ssim=0.2):
         self.g = gaussians
         self.cameras = cameras
         self.cfg = config
@@ -68,6 +75,15 @@ class DataParallelTrainer:
         self.ctx = RasterizerContext(gaussians.arena.device)
         self.loss = torch.zeros(1, device=gaussians.arena.device)
         self.cam_structs = [c.to_struct() for c in cameras]
+        if loss not in ("l1", "combined"):
+            raise ValueError(f"unknown loss {loss!r}")
+        self.loss_kind, self.lambda_ssim = loss, lambda_ssim
+        if loss == "combined":
+            dev = gaussians.arena.device
+            H, W = cameras[0].height, cameras[0].width
+            self.image = torch.empty(H, W, 3, device=dev)
+            self.dimage = torch.empty(H, W, 3, device=dev)
+            self.loss_terms = torch.zeros(3, device=dev)
 
     @property
     def my_views(self):
@@ -80,8 +96,16 @@ class DataParallelTrainer:
         check(lib().gsc_memset(ctx, C.c_void_p(self.loss.data_ptr()), 0, 4), "gsc_memset")
 
     def view_fwd_bwd(self, v, target):
-        """Forward + fused-L1 backward of view v against a device target [H,W,3]."""
+        """Forward + backward of view v against a device target [H,W,3]."""
         cam = self.cameras[v]
+        if self.loss_kind == "combined":
+            Rasterizer.forward(self.g, cam, context=self.ctx, config=self.cfg, out=self.image)
+            combined_with_grad(self.image, target, self.lambda_ssim, out=self.loss_terms,
+                               grad=self.dimage)
+            self.loss += self.loss_terms[0]
+            Rasterizer.backward(self.dimage, self.g, cam, self.ctx, grads=self.grads,
+                                config=self.cfg)
+            return
         Rasterizer.forward(self.g, cam, context=self.ctx, config=self.cfg)
         Rasterizer.backward(None, self.g, cam, self.ctx, grads=self.grads, target=target,
                             l1_scale=1.0 / target.numel(), loss_sum=self.loss, config=self.cfg)

@@ -299,6 +299,38 @@ typedef struct gsc_dp_adam_args {
 } gsc_dp_adam_args;
 GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* args);
 
+/* ---- losses beyond L1 (src/ops/loss.cr:59-249) --------------------------
+ * Images are [height, width, channels] fp32 row-major, 1 <= channels <= 4.
+ * `out` is a DEVICE array of 3 floats: {loss, mean |pred - target|, SSIM}.
+ * SSIM (Loss.ssim, loss.cr:117-186) is the mean over the valid region (pixels
+ * at least window/2 from every border) and channels of the local SSIM with a
+ * Gaussian window of sigma 1.5 and C1 = 0.01^2, C2 = 0.03^2; 0 when the image
+ * has no valid pixel. GSC_MODE_REF evaluates it literally (2D window,
+ * two-pass variance); GSC_MODE_FULL applies the same window separably.
+ * Partial sums are double and reduced in a fixed order. */
+
+/* Loss.ssim_loss_with_grad (loss.cr:189-216): loss = 1 - SSIM. grad
+ * (nullable, written): REF = the reference's surrogate 2 (pred - target) / n;
+ * FULL = the exact gradient of 1 - SSIM. ssim_map (nullable, [H, W, C]) gets
+ * the per-pixel SSIM on the valid region; other entries are left as they are. */
+GSC_API int gsc_ssim_loss_grad(gsc_ctx* ctx, const float* pred, const float* target,
+                               int32_t height, int32_t width, int32_t channels,
+                               int32_t window_size, int32_t mode, float* grad, float* ssim_map,
+                               float* out);
+
+/* Loss.combined_with_grad (loss.cr:227-249), window 11: loss =
+ * (1 - lambda) * L1 + lambda * (1 - SSIM); grad (nullable, written) =
+ * (1 - lambda) * sign(pred - target) / n + lambda * d(1 - SSIM) (as above). */
+GSC_API int gsc_combined_loss_grad(gsc_ctx* ctx, const float* pred, const float* target,
+                                   int32_t height, int32_t width, int32_t channels,
+                                   float lambda_ssim, int32_t mode, float* grad, float* out);
+
+/* Loss.mse_with_grad (loss.cr:83-105): out[0] = out[1] = mean (pred - target)^2,
+ * grad (nullable, written) = 2 (pred - target) / numel. Loss.psnr
+ * (loss.cr:291-296) is 10 log10(max^2 / out[0]) on the host. */
+GSC_API int gsc_mse_loss_grad(gsc_ctx* ctx, const float* pred, const float* target,
+                              int64_t numel, float* grad, float* out);
+
 /* ---- densification (Trainer#densify_and_prune!, trainer.cr:293-392) ---- */
 
 /* GradientAccumulator#accumulate (trainer.cr:86-99): for every i,

@@ -749,6 +749,153 @@ void gso_l1_loss_grad(int64_t numel, const float* pred, const float* target, flo
   if (loss_sum) *loss_sum += loss;
 }
 
+// ---- losses beyond L1 -------------------------------------------------------
+
+// Gaussian window of Loss#gaussian_window (loss.cr:262-281), sigma 1.5: fp32
+// exp, fp32 row-major sum, each value divided by it. 1D (two_d false) for the
+// separable form.
+static std::vector<float> ssim_window(int win, bool two_d) {
+  const int c = win / 2, n = two_d ? win * win : win;
+  std::vector<float> w(n);
+  for (int i = 0; i < n; i++) {
+    const int dx = (two_d ? i % win : i) - c, dy = two_d ? i / win - c : 0;
+    w[i] = gso_expf((float)(-(dx * dx + dy * dy)) / (2.0f * 1.5f * 1.5f));
+  }
+  float sum = 0.0f;
+  for (int i = 0; i < n; i++) sum += w[i];
+  for (int i = 0; i < n; i++) w[i] = w[i] / sum;
+  return w;
+}
+
+void gso_loss_grad(const float* pred, const float* target, int32_t H, int32_t W, int32_t C,
+                   int32_t win, int32_t mode, float w_l1, float w_ssim, float* grad,
+                   float* ssim_map, float* out) {
+  // Loss.ssim (loss.cr:117-186) per valid pixel and channel; REF literally
+  // (2D window, means then variances), FULL separably with moments
+  // blur(x), blur(y), blur(x^2), blur(y^2), blur(xy) and the analytic gradient
+  // dSum S/dx_q = blur(A) + 2 x_q blur(B) + y_q blur(C).
+  const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
+  const int pad = win / 2, vw = W - 2 * pad, vh = H - 2 * pad;
+  const bool any = vw > 0 && vh > 0, full = mode == GSC_MODE_FULL;
+  const int64_t numel = (int64_t)H * W * C, plane = (int64_t)H * W;
+  const float n_f = (float)numel, count_f = any ? (float)((int64_t)vw * vh * C) : 0.0f;
+  auto at = [&](const float* img, int y, int x, int c) { return img[((int64_t)y * W + x) * C + c]; };
+  const std::vector<float> w2 = ssim_window(win, true), g = ssim_window(win, false);
+  const bool need_abc = full && grad && w_ssim != 0.0f && any;
+  std::vector<float> abc(need_abc ? 3 * numel : 0, 0.0f);
+  double ssum = 0.0;
+  for (int c = 0; c < C && any; c++)
+    for (int y = pad; y < H - pad; y++)
+      for (int x = pad; x < W - pad; x++) {
+        float S;
+        if (!full) {
+          float mu_x = 0.0f, mu_y = 0.0f, sx = 0.0f, sy = 0.0f, sxy = 0.0f;
+          for (int wy = 0; wy < win; wy++)
+            for (int wx = 0; wx < win; wx++) {
+              const float w = w2[wy * win + wx];
+              mu_x += w * at(pred, y - pad + wy, x - pad + wx, c);
+              mu_y += w * at(target, y - pad + wy, x - pad + wx, c);
+            }
+          for (int wy = 0; wy < win; wy++)
+            for (int wx = 0; wx < win; wx++) {
+              const float w = w2[wy * win + wx];
+              const float px = at(pred, y - pad + wy, x - pad + wx, c);
+              const float py = at(target, y - pad + wy, x - pad + wx, c);
+              sx += w * (px - mu_x) * (px - mu_x);
+              sy += w * (py - mu_y) * (py - mu_y);
+              sxy += w * (px - mu_x) * (py - mu_y);
+            }
+          const float num = (2.0f * mu_x * mu_y + C1) * (2.0f * sxy + C2);
+          const float den = (mu_x * mu_x + mu_y * mu_y + C1) * (sx + sy + C2);
+          S = num / den;
+        } else {
+          float m[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+          for (int k = 0; k < win; k++) {
+            float h[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            for (int j = 0; j < win; j++) {
+              const float p = at(pred, y - pad + k, x - pad + j, c);
+              const float t = at(target, y - pad + k, x - pad + j, c);
+              h[0] += g[j] * p;
+              h[1] += g[j] * t;
+              h[2] += g[j] * (p * p);
+              h[3] += g[j] * (t * t);
+              h[4] += g[j] * (p * t);
+            }
+            for (int q = 0; q < 5; q++) m[q] += g[k] * h[q];
+          }
+          const float mu_x = m[0], mu_y = m[1];
+          const float sxx = m[2] - mu_x * mu_x, syy = m[3] - mu_y * mu_y, sxy = m[4] - mu_x * mu_y;
+          const float n1 = 2.0f * mu_x * mu_y + C1, n2 = 2.0f * sxy + C2;
+          const float d1 = mu_x * mu_x + mu_y * mu_y + C1, d2 = sxx + syy + C2;
+          const float dd = d1 * d2;
+          S = (n1 * n2) / dd;
+          if (need_abc) {
+            const float dmu = 2.0f * mu_y * n2 / dd - 2.0f * mu_x * S / d1;
+            const float dsxx = -S / d2;
+            const float dsxy = 2.0f * n1 / dd;
+            const int64_t o = (int64_t)y * W + x;
+            abc[(0 * C + c) * plane + o] = dmu - 2.0f * mu_x * dsxx - mu_y * dsxy;
+            abc[(1 * C + c) * plane + o] = dsxx;
+            abc[(2 * C + c) * plane + o] = dsxy;
+          }
+        }
+        ssum += (double)S;
+        if (ssim_map) ssim_map[((int64_t)y * W + x) * C + c] = S;
+      }
+  // Gradient (loss.cr:33-57, 194-216, 227-249) and the L1 sum.
+  auto abc_at = [&](int j, int c, int y, int x) -> float {
+    if (y < pad || y >= H - pad || x < pad || x >= W - pad) return 0.0f;
+    return abc[(j * C + c) * plane + (int64_t)y * W + x];
+  };
+  double l1 = 0.0;
+  for (int y = 0; y < H; y++)
+    for (int x = 0; x < W; x++)
+      for (int c = 0; c < C; c++) {
+        const int64_t e = ((int64_t)y * W + x) * C + c;
+        const float p = pred[e], t = target[e], diff = p - t;
+        l1 += (double)std::fabs(diff);
+        if (!grad) continue;
+        float sd;
+        if (need_abc) {
+          float b[3] = {0.0f, 0.0f, 0.0f};
+          for (int k = 0; k < win; k++) {
+            float h[3] = {0.0f, 0.0f, 0.0f};
+            for (int j = 0; j < win; j++)
+              for (int q = 0; q < 3; q++) h[q] += g[j] * abc_at(q, c, y - pad + k, x - pad + j);
+            for (int q = 0; q < 3; q++) b[q] += g[k] * h[q];
+          }
+          const float dS = b[0] + 2.0f * p * b[1] + t * b[2];
+          sd = -(dS / count_f);
+        } else if (full) {
+          sd = 0.0f;  // no valid pixel (or no SSIM term): SSIM is the constant 0
+        } else {
+          sd = 2.0f * diff / n_f;
+        }
+        const float l1d = (diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f)) / n_f;
+        grad[e] = w_l1 * l1d + w_ssim * sd;
+      }
+  const float ssim = count_f > 0.0f ? (float)(ssum / (double)count_f) : 0.0f;
+  const float l1v = n_f > 0.0f ? (float)(l1 / (double)n_f) : 0.0f;
+  out[0] = w_l1 * l1v + w_ssim * (1.0f - ssim);
+  out[1] = l1v;
+  out[2] = ssim;
+}
+
+void gso_mse_loss_grad(const float* pred, const float* target, int64_t numel, float* grad,
+                       float* out) {
+  // Loss.mse_with_grad, loss.cr:83-105 (sum in double).
+  double s = 0.0;
+  for (int64_t i = 0; i < numel; i++) {
+    const float diff = pred[i] - target[i];
+    s += (double)(diff * diff);
+    if (grad) grad[i] = 2.0f * diff / (float)numel;
+  }
+  const float v = numel > 0 ? (float)(s / (double)numel) : 0.0f;
+  out[0] = v;
+  out[1] = v;
+  out[2] = 0.0f;
+}
+
 // ---- densification -------------------------------------------------------
 
 // SplitMix64 finaliser (Steele, Lea & Flood 2014) as a counter-based hash:

@@ -73,6 +73,14 @@ void gso_l1_loss_grad(int64_t numel, const float* pred, const float* target, flo
 void gso_adam_step(const gsc_adam_group* groups, int32_t ngroups, float beta1, float beta2,
                    float eps, int32_t step, float grad_scale);
 
+/* Losses (loss.cr:59-249); same contract as gsc_ssim_loss_grad /
+ * gsc_combined_loss_grad / gsc_mse_loss_grad, `out` a host array of 3. */
+void gso_loss_grad(const float* pred, const float* target, int32_t height, int32_t width,
+                   int32_t channels, int32_t window_size, int32_t mode, float w_l1, float w_ssim,
+                   float* grad, float* ssim_map, float* out);
+void gso_mse_loss_grad(const float* pred, const float* target, int64_t numel, float* grad,
+                       float* out);
+
 /* Densification (trainer.cr:77-123, 293-392); same contract as
  * gsc_grad_accumulate / gsc_densify_plan / gsc_densify_apply. */
 void gso_grad_accumulate(const float* dmean2d, int32_t stride, int64_t n, float* accum,

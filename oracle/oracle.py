@@ -191,6 +191,27 @@ def adam_step(groups, beta1, beta2, eps, step, grad_scale=1.0):
                         C.c_float(grad_scale))
 
 
+def loss_grad(pred, target, window_size=11, mode=0, w_l1=0.0, w_ssim=1.0, want_grad=True,
+              want_map=False):
+    """gso_loss_grad on [H, W, C] arrays: (out[3], grad or None, ssim map or None)."""
+    pred, target = _f32(pred), _f32(target)
+    H, W, Cn = pred.shape
+    out = np.zeros(3, np.float32)
+    grad = np.zeros_like(pred) if want_grad else None
+    smap = np.zeros_like(pred) if want_map else None
+    lib().gso_loss_grad(_p(pred), _p(target), H, W, Cn, window_size, mode, C.c_float(w_l1),
+                        C.c_float(w_ssim), _p(grad), _p(smap), _p(out))
+    return out, grad, smap
+
+
+def mse_loss_grad(pred, target):
+    pred, target = _f32(pred), _f32(target)
+    out = np.zeros(3, np.float32)
+    grad = np.zeros_like(pred)
+    lib().gso_mse_loss_grad(_p(pred), _p(target), C.c_int64(pred.size), _p(grad), _p(out))
+    return out, grad
+
+
 def grad_accumulate(dmean2d, accum, count):
     """accum/count (numpy float32 / int32) updated in place from an [N, stride] gradient."""
     d = _f32(dmean2d)
