@@ -8,8 +8,11 @@ data-parallel trainer. Import it with importlib.import_module("crystal-gausplat_
 """
 from . import _abi
 from ._abi import GSC_MODE_FULL, GSC_MODE_REF, GscError, default_config
-from .camera import Camera, CameraIntrinsics, make_camera, orbit_poses, sphere_poses
+from .camera import Camera, CameraIntrinsics, CameraSet, make_camera, orbit_poses, sphere_poses
 from .gaussian import Gaussian3D, synthetic_arrays
+from . import scene_io
+from .scene_io import (COLMAPLoader, Image, load_colmap, load_ply, load_png, save_ply,
+                       save_png)
 
 try:
     from .rasterizer import (GPURadixSort, Rasterizer, RasterizerContext, RasterizerGradients,

@@ -134,6 +134,8 @@ _SIGS = {
     "gsc_combined_loss_grad": (C.c_int, [P, P, P, C.c_int32, C.c_int32, C.c_int32, C.c_float,
                                          C.c_int32, P, P]),
     "gsc_mse_loss_grad": (C.c_int, [P, P, P, C.c_int64, P, P]),
+    "gsc_image_to_target": (C.c_int, [P, P, C.c_int32, C.c_int32, C.c_int32, P, C.c_int32,
+                                      C.c_int32, C.c_int32]),
     "gsc_grad_accumulate": (C.c_int, [P, P, C.c_int32, C.c_int64, P, P]),
     "gsc_densify_plan": (C.c_int, [P, C.POINTER(Gaussians), P, P, C.c_float, C.c_float, C.c_float,
                                    P, C.POINTER(C.c_int64)]),

@@ -16,7 +16,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 SOURCES = ["api.cu", "preprocess.cu", "binning.cu", "sort.cu", "composite.cu",
            "preprocess_bwd.cu", "optim.cu", "sort_static.cu", "dp.cu",
-           "densify.cu", "ssim.cu"]
+           "densify.cu", "ssim.cu",
+           "image.cu"]
 
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -115,3 +115,60 @@ def orbit_poses(n, radius):
 def make_camera(width, height, eye, fov_x_deg=60.0, target=(0.0, 0.0, 0.0)):
     cam = Camera(CameraIntrinsics.from_fov(width, height, math.radians(fov_x_deg)))
     return cam.look_at(eye, target)
+
+
+class CameraSet(list):
+    """CameraSet (camera.cr:259-286): a list of cameras."""
+
+    def sample(self, rng=None):
+        rng = rng or np.random.default_rng()
+        return self[int(rng.integers(len(self)))]
+
+    @classmethod
+    def from_colmap(cls, images_txt_path, cameras_txt_path):
+        """CameraSet.from_colmap (camera.cr:288-358): PINHOLE / SIMPLE_PINHOLE
+        intrinsics; the pose quaternion is normalised and turned into R in fp32
+        arithmetic, as there. Images are read as COLMAP's line pairs (the
+        second, 2D-point line of each record is skipped even when it is empty
+        or has ten or more fields)."""
+        f32 = np.float32
+        intr = {}
+        with open(cameras_txt_path) as f:
+            for line in f:
+                if line.startswith("#") or not line.strip():
+                    continue
+                p = line.split()
+                if len(p) < 5:
+                    continue
+                w, h = int(p[2]), int(p[3])
+                if p[1] == "PINHOLE":
+                    intr[int(p[0])] = CameraIntrinsics(w, h, f32(p[4]), f32(p[5]), f32(p[6]), f32(p[7]))
+                elif p[1] == "SIMPLE_PINHOLE":
+                    intr[int(p[0])] = CameraIntrinsics(w, h, f32(p[4]), f32(p[4]), f32(p[5]), f32(p[6]))
+        out = cls()
+        with open(images_txt_path) as f:
+            lines = [ln for ln in f if not ln.startswith("#")]
+        i = 0
+        while i < len(lines):
+            p = lines[i].split()
+            if not p:
+                i += 1
+                continue
+            i += 2
+            if len(p) < 10 or int(p[8]) not in intr:
+                continue
+            w, x, y, z = (f32(v) for v in p[1:5])
+            n = f32(np.sqrt(f32(f32(f32(w * w) + f32(x * x)) + f32(y * y)) + f32(z * z)))
+            w, x, y, z = w / n, x / n, y / n, z / n
+            one, two = f32(1), f32(2)
+            R = [one - two * y * y - two * z * z, two * x * y - two * z * w, two * x * z + two * y * w,
+                 two * x * y + two * z * w, one - two * x * x - two * z * z, two * y * z - two * x * w,
+                 two * x * z - two * y * w, two * y * z + two * x * w, one - two * x * x - two * y * y]
+            m = np.zeros((4, 4), np.float32)
+            m[:3, :3] = np.array(R, np.float32).reshape(3, 3)
+            m[:3, 3] = [f32(p[5]), f32(p[6]), f32(p[7])]
+            m[3, 3] = 1
+            cam = Camera(intr[int(p[8])]).set_world_to_camera(m)
+            cam.image_path = p[9]
+            out.append(cam)
+        return out

@@ -331,6 +331,17 @@ GSC_API int gsc_combined_loss_grad(gsc_ctx* ctx, const float* pred, const float*
 GSC_API int gsc_mse_loss_grad(gsc_ctx* ctx, const float* pred, const float* target,
                               int64_t numel, float* grad, float* out);
 
+/* ---- training targets from 8-bit images ---------------------------------
+ * ImageIO.resize (src/utils/image_io.cr:289-335: bilinear, pixel centres,
+ * clamped, each value clamped to [0, 255] and truncated to a byte) to
+ * width x height when the sizes differ, then Image#to_tensor's byte / 255
+ * (image_io.cr:83-97), keeping the first `channels` of `src_channels`
+ * (RGBA -> RGB). src: device [src_height, src_width, src_channels] u8;
+ * dst: device [height, width, channels] fp32. */
+GSC_API int gsc_image_to_target(gsc_ctx* ctx, const uint8_t* src, int32_t src_width,
+                                int32_t src_height, int32_t src_channels, float* dst,
+                                int32_t width, int32_t height, int32_t channels);
+
 /* ---- densification (Trainer#densify_and_prune!, trainer.cr:293-392) ---- */
 
 /* GradientAccumulator#accumulate (trainer.cr:86-99): for every i,

@@ -896,6 +896,37 @@ void gso_mse_loss_grad(const float* pred, const float* target, int64_t numel, fl
   out[2] = 0.0f;
 }
 
+// ---- 8-bit images -> targets ------------------------------------------------
+
+void gso_image_to_target(const uint8_t* src, int32_t sw, int32_t sh, int32_t sc, float* dst,
+                         int32_t dw, int32_t dh, int32_t dc) {
+  // ImageIO.resize (image_io.cr:289-335), then byte / 255 (image_io.cr:83-97).
+  const bool same = sw == dw && sh == dh;
+  const float scale_x = (float)sw / (float)dw, scale_y = (float)sh / (float)dh;
+  for (int y = 0; y < dh; y++)
+    for (int x = 0; x < dw; x++) {
+      float* out = dst + ((int64_t)y * dw + x) * dc;
+      if (same) {
+        for (int c = 0; c < dc; c++) out[c] = (float)src[((int64_t)y * sw + x) * sc + c] / 255.0f;
+        continue;
+      }
+      float sx = ((float)x + 0.5f) * scale_x - 0.5f, sy = ((float)y + 0.5f) * scale_y - 0.5f;
+      sx = std::min(std::max(sx, 0.0f), (float)(sw - 1));
+      sy = std::min(std::max(sy, 0.0f), (float)(sh - 1));
+      const int x0 = std::min(std::max((int)sx, 0), sw - 1), y0 = std::min(std::max((int)sy, 0), sh - 1);
+      const int x1 = std::min(x0 + 1, sw - 1), y1 = std::min(y0 + 1, sh - 1);
+      const float fx = sx - (float)x0, fy = sy - (float)y0;
+      for (int c = 0; c < dc; c++) {
+        const float v00 = src[((int64_t)y0 * sw + x0) * sc + c], v10 = src[((int64_t)y0 * sw + x1) * sc + c];
+        const float v01 = src[((int64_t)y1 * sw + x0) * sc + c], v11 = src[((int64_t)y1 * sw + x1) * sc + c];
+        const float v0 = v00 * (1.0f - fx) + v10 * fx;
+        const float v1 = v01 * (1.0f - fx) + v11 * fx;
+        const float v = v0 * (1.0f - fy) + v1 * fy;
+        out[c] = (float)(uint8_t)std::min(std::max(v, 0.0f), 255.0f) / 255.0f;
+      }
+    }
+}
+
 // ---- densification -------------------------------------------------------
 
 // SplitMix64 finaliser (Steele, Lea & Flood 2014) as a counter-based hash:

@@ -81,6 +81,11 @@ void gso_loss_grad(const float* pred, const float* target, int32_t height, int32
 void gso_mse_loss_grad(const float* pred, const float* target, int64_t numel, float* grad,
                        float* out);
 
+/* ImageIO.resize + Image#to_tensor (image_io.cr:83-97, 289-335); same
+ * contract as gsc_image_to_target. */
+void gso_image_to_target(const uint8_t* src, int32_t sw, int32_t sh, int32_t sc, float* dst,
+                         int32_t dw, int32_t dh, int32_t dc);
+
 /* Densification (trainer.cr:77-123, 293-392); same contract as
  * gsc_grad_accumulate / gsc_densify_plan / gsc_densify_apply. */
 void gso_grad_accumulate(const float* dmean2d, int32_t stride, int64_t n, float* accum,

@@ -212,6 +212,15 @@ def mse_loss_grad(pred, target):
     return out, grad
 
 
+def image_to_target(img, width, height, channels):
+    """gso_image_to_target on an [h, w, c] uint8 array."""
+    img = np.ascontiguousarray(img, np.uint8)
+    sh, sw, sc = img.shape
+    out = np.zeros((height, width, channels), np.float32)
+    lib().gso_image_to_target(_p(img), sw, sh, sc, _p(out), width, height, channels)
+    return out
+
+
 def grad_accumulate(dmean2d, accum, count):
     """accum/count (numpy float32 / int32) updated in place from an [N, stride] gradient."""
     d = _f32(dmean2d)
