@@ -54,7 +54,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1 gradient exchange: fused NVLink reduce+Adam+broadcast kernel, or NCCL all-reduce")
+    ap.add_argument("--binning", default="contributing", choices=["contributing", "reference"],
+                    help="tile lists: contributing pairs only (default) or the reference's full lists")
     return ap.parse_args()
+
+
+def binning_of(gs, args):
+    return gs._abi.GSC_BIN_CONTRIBUTING if args.binning == "contributing" else gs._abi.GSC_BIN_REFERENCE
 
 
 def load_peaks():
@@ -336,7 +342,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     g = gs.Gaussian3D(arrays, device=dev)
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config()
+    rcfg = gs.default_config(binning=binning_of(gs, args))
     tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg, exchange=args.exchange)
     host_t = make_targets(cfg, tr.lo, tr.hi)
     dev_t = host_t.to(dev)
@@ -407,7 +413,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "config": {"workload": f"{args.config}: train step, {cfg['n']} Gaussians SH3, {cfg['views']} views "
                                    f"{cfg['W']}x{cfg['H']}, L1, all-reduce + fused Adam",
                        "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
-                       "exchange": tr.exchange,
+                       "exchange": tr.exchange, "binning": args.binning,
                        "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush",
                        "keys_per_view": round(keys_per_view), "pge_per_view": round(pge)},
             "gpu_launches": launches,
@@ -422,7 +428,9 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "stages": roof,
         }
         if world == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_baseline_train(gs, cfg, arrays, cams, rcfg, host_t, os.cpu_count())
+            result["cpu_baseline"] = cpu_baseline_train(
+                gs, cfg, arrays, cams, gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE), host_t,
+                os.cpu_count())
     return result
 
 
@@ -431,7 +439,7 @@ def reference_train(args, cfg):
     gs = importlib.import_module("crystal-gausplat_b200")
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config()
+    rcfg = gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE)  # the reference's CPU path
     threads = os.cpu_count()
     H, W = cfg["H"], cfg["W"]
     ta = cpu_adam_seconds(cfg["n"], threads)
@@ -469,7 +477,7 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     g = gs.Gaussian3D(arrays, device=dev)
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config()
+    rcfg = gs.default_config(binning=binning_of(gs, args))
     lo, hi = trainer_mod.shard(len(cams), rank, world)
     rctx = gs.RasterizerContext(dev)
     img = torch.empty(cfg["H"], cfg["W"], 3, device=dev)
@@ -522,13 +530,14 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "config": {"workload": f"c4: render-only, {cfg['n']} Gaussians, {cfg['views']} views "
                                   f"{cfg['W']}x{cfg['H']}", "parallelism": f"views/{world}",
-                      "l2": "inputs larger than L2, no flush", "keys_per_view": round(kpv)},
+                      "l2": "inputs larger than L2, no flush", "keys_per_view": round(kpv),
+                      "binning": args.binning},
            "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
            "roofline": dict(roof[dominant], kernel=dominant, traffic=None,
                             peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind),
            "stages": roof}
     if world == 1 and not args.no_cpu_baseline:
-        t = cpu_view_seconds(gs, arrays, cams[0], rcfg, None, os.cpu_count(), with_backward=False)
+        t = cpu_view_seconds(gs, arrays, cams[0], gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE), None, os.cpu_count(), with_backward=False)
         res["cpu_baseline"] = {"value": round(cfg["W"] * cfg["H"] / 1e6 / t, 3), "unit": "MPix/s",
                                "cores": os.cpu_count(), "kind": "port",
                                "sample": f"1 view (view 0) forward, {t:.2f} s, CPU oracle (OpenMP)"}
@@ -637,7 +646,7 @@ def reference_render(args, cfg):
     gs = importlib.import_module("crystal-gausplat_b200")
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config()
+    rcfg = gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE)  # the reference's CPU path
     times = []
     for i in range(args.warmup + args.steps):
         t = cpu_view_seconds(gs, arrays, cams[i % len(cams)], rcfg, None, os.cpu_count(), False)

@@ -23,6 +23,9 @@ GSC_ERR_UNSUPPORTED = -7
 GSC_MODE_FULL = 0
 GSC_MODE_REF = 1
 
+GSC_BIN_REFERENCE = 0
+GSC_BIN_CONTRIBUTING = 1
+
 GSC_STATIC_SORT_MAX_PAIRS = 262144
 
 GSC_FRAME_SPLATS = 0
@@ -51,7 +54,7 @@ class RasterConfig(C.Structure):
     _fields_ = [("mode", C.c_int32), ("sh_degree", C.c_int32), ("t_stop", C.c_float),
                 ("alpha_min", C.c_float), ("alpha_max", C.c_float), ("lowpass", C.c_float),
                 ("fov_cull", C.c_float), ("near_z", C.c_float), ("far_z", C.c_float),
-                ("background", C.c_float * 3)]
+                ("background", C.c_float * 3), ("binning", C.c_int32)]
 
 
 class Gaussians(C.Structure):
@@ -194,9 +197,13 @@ def check(rc, what=""):
     return rc
 
 
-def default_config(mode=GSC_MODE_FULL, sh_degree=3, background=(0.0, 0.0, 0.0), t_stop=None):
+def default_config(mode=GSC_MODE_FULL, sh_degree=3, background=(0.0, 0.0, 0.0), t_stop=None,
+                   binning=None):
+    """gsc_raster_config_default with overrides (binning: GSC_BIN_*, default CONTRIBUTING)."""
     cfg = RasterConfig()
     lib().gsc_raster_config_default(C.byref(cfg))
+    if binning is not None:
+        cfg.binning = binning
     cfg.mode = mode
     cfg.sh_degree = sh_degree
     for i in range(3):

@@ -74,7 +74,7 @@ using namespace gs;
 struct gsc_frame {
   gsc_ctx* ctx = nullptr;
   GsBuf splats, depth_keys, order, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
-      last, n_contrib, grad2d;
+      last, n_contrib, grad2d, tile_mask;
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
@@ -100,6 +100,7 @@ GSC_API void gsc_raster_config_default(gsc_raster_config* cfg) {
   cfg->near_z = 0.01f;
   cfg->far_z = 1000.0f;
   cfg->background[0] = cfg->background[1] = cfg->background[2] = 0.0f;
+  cfg->binning = GSC_BIN_CONTRIBUTING;
 }
 
 GSC_API int gsc_init(int device, gsc_ctx** out) {
@@ -230,12 +231,14 @@ static int check_view(const gsc_camera* cam, const gsc_raster_config* cfg) {
              "camera width/height out of range");
   GS_REQUIRE(cfg->mode == GSC_MODE_FULL || cfg->mode == GSC_MODE_REF, "unknown mode");
   GS_REQUIRE(cfg->sh_degree >= 0 && cfg->sh_degree <= 3, "sh_degree must be 0..3");
+  GS_REQUIRE(cfg->binning == GSC_BIN_REFERENCE || cfg->binning == GSC_BIN_CONTRIBUTING, "unknown binning");
   return GSC_OK;
 }
 
 static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
                          const gsc_raster_config* cfg, const gsc_projected* o, uint32_t* block_sums,
-                         uint32_t* depth_keys = nullptr, uint32_t* order = nullptr) {
+                         uint32_t* depth_keys = nullptr, uint32_t* order = nullptr,
+                         uint64_t* tile_mask = nullptr) {
   PreprocessArgs a;
   std::memset(&a, 0, sizeof a);
   a.n = g->count;
@@ -250,6 +253,7 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
   a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
+  a.tile_mask = tile_mask;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
@@ -493,7 +497,7 @@ GSC_API int gsc_frame_destroy(gsc_frame* f) {
   cudaStreamSynchronize(f->ctx->stream);
   GsBuf* bufs[] = {&f->splats, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
-                   &f->n_contrib, &f->grad2d};
+                   &f->n_contrib, &f->grad2d, &f->tile_mask};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
   delete f;
@@ -536,7 +540,12 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   gsc_projected proj;
   std::memset(&proj, 0, sizeof proj);
   proj.splats = splats;
-  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, nullptr, depth_keys, order));
+  uint64_t* tile_mask = nullptr;
+  if (cfg->binning == GSC_BIN_CONTRIBUTING) {
+    GS_TRY(ensure(ctx, &f->tile_mask, (size_t)n * 8 + 8));
+    tile_mask = (uint64_t*)f->tile_mask.ptr;
+  }
+  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, nullptr, depth_keys, order, tile_mask));
   // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and sink)
   if (n > 1) {
     GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_u32(n, 0, 32)));
@@ -566,8 +575,8 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
     {
       StageScope sc(ctx, GSC_STAGE_EMIT);
       sc.kernels(1);
-      GS_TRY(launch_emit_tiles(splats, order, n, (const uint64_t*)f->offsets.ptr, tx, ty, tiles, vals,
-                               ctx->stream));
+      GS_TRY(launch_emit_tiles(splats, order, n, (const uint64_t*)f->offsets.ptr, tx, ty, tile_mask, tiles,
+                               vals, ctx->stream));
     }
     // 3. stable sort by tile bits only
     const int tb = tile_bits_of(tx * ty);

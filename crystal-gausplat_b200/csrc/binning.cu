@@ -189,15 +189,32 @@ __global__ void __launch_bounds__(256) block_sums_gather_kernel(const float4* __
   if (threadIdx.x == 255) sums[blockIdx.x] = incl;
 }
 
+// Position of the k-th (0-based) set bit of m; m has more than k set bits.
+__device__ __forceinline__ uint32_t select_bit64(uint64_t m, uint32_t k) {
+  uint32_t pos = 0;
+#pragma unroll
+  for (int w = 32; w >= 1; w >>= 1) {
+    const uint32_t c = __popcll(m & ((1ull << w) - 1ull));
+    if (k >= c) {
+      k -= c;
+      m >>= w;
+      pos += w;
+    }
+  }
+  return pos;
+}
+
 __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restrict__ splats,
                                                          const uint32_t* __restrict__ order, int64_t n,
                                                          const uint64_t* __restrict__ offsets,
                                                          int tiles_x, int tiles_y,
+                                                         const uint64_t* __restrict__ tile_mask,
                                                          uint32_t* __restrict__ tile_out,
                                                          uint32_t* __restrict__ id_out) {
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
   __shared__ uint32_t s_id[256];
+  __shared__ uint64_t s_mask[256];
   __shared__ uint32_t s_warp[8];
   const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
   uint32_t t = 0;
@@ -212,6 +229,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
       s_y0[threadIdx.x] = y0;
       s_wx[threadIdx.x] = x1 - x0 + 1;
       s_id[threadIdx.x] = gid;
+      s_mask[threadIdx.x] = tile_mask ? tile_mask[gid] : ~0ull;
     }
   }
   uint32_t incl = block_incl_scan_256(t, s_warp);
@@ -225,7 +243,9 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
       int mid = (lo + hi) >> 1;
       if (s_incl[mid] > k) hi = mid; else lo = mid + 1;
     }
-    const uint32_t local = k - (lo ? s_incl[lo - 1] : 0u);
+    uint32_t local = k - (lo ? s_incl[lo - 1] : 0u);
+    const uint64_t mk = s_mask[lo];
+    if (mk != ~0ull) local = select_bit64(mk, local);  // local-th contributing tile of the rect
     const int wx = s_wx[lo];
     const int ty = s_y0[lo] + (int)(local / (uint32_t)wx);
     const int tx = s_x0[lo] + (int)(local % (uint32_t)wx);
@@ -265,10 +285,11 @@ int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t
 }
 
 int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, int tiles_y, uint32_t* tile_out, uint32_t* id_out, cudaStream_t stream) {
+                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint32_t* tile_out, uint32_t* id_out,
+                      cudaStream_t stream) {
   if (n == 0) return GSC_OK;
   emit_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const float4*>(splats), order, n, offsets, tiles_x, tiles_y, tile_out, id_out);
+      reinterpret_cast<const float4*>(splats), order, n, offsets, tiles_x, tiles_y, tile_mask, tile_out, id_out);
   GS_CK_LAUNCH("emit_tiles_kernel");
   return GSC_OK;
 }

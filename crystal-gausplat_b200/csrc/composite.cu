@@ -18,52 +18,12 @@
 // ln(alpha_min) minus a margin far above the exponential's error, so the
 // accepted set is exactly the one the full test gives.
 #include "common.cuh"
+#include "cull.cuh"
 #include "kernels.cuh"
 
 namespace gs {
 
-// Whole-tile rejection. True only if NO pixel centre of the tile's rectangle
-// [rx0, rx1] x [ry0, ry1] can pass the alpha test for this Gaussian:
-// the minimum of the Mahalanobis form q(d) = d^T conic d over the rectangle
-// (zero if the mean is inside, else attained on an edge) is compared, in
-// double precision, with the opacity-aware threshold
-//     o * exp(-q/2) < alpha_min  <=>  q > -2 ln(alpha_min / o),
-// with margins that cover the fp32 evaluation of the per-pixel test: the fp32
-// quadratic form has relative error <= 4 eps / (1 - rho), rho = |B|/sqrt(AC),
-// so the cull is refused when 1 - rho < 1e-3, and the threshold is raised by
-// 1e-3 relative + 1e-3 absolute and lowered in ln by 1e-4. Non-finite or
-// non-positive-definite inputs are never culled. The set of Gaussians that
-// reach the per-pixel loop therefore changes, but not the result.
-__device__ __forceinline__ bool tile_culled(float4 g0, float conic_c, float o, float rx0, float rx1,
-                                            float ry0, float ry1, float alpha_min) {
-  if (!isfinite(g0.x) || !isfinite(g0.y)) return false;
-  if (!(o > 0.0f)) return o == 0.0f && isfinite(g0.z) && isfinite(g0.w) && isfinite(conic_c);
-  const double A = g0.z, B = g0.w, C = conic_c;
-  if (!(A > 0.0 && C > 0.0) || !isfinite(A) || !isfinite(B) || !isfinite(C)) return false;
-  const double rho = fabs(B) / sqrt(A * C);
-  if (!(1.0 - rho >= 1e-3)) return false;
-  const double cut = (double)logf(alpha_min / o) - 1e-4;  // logf error << the 1e-4 margin
-  if (cut >= 0.0) return true;  // o < alpha_min: alpha = o*G <= o never reaches alpha_min
-  const double mx = g0.x, my = g0.y;
-  const double x0 = rx0 - mx, x1 = rx1 - mx, y0 = ry0 - my, y1 = ry1 - my;
-  if (x0 <= 0.0 && x1 >= 0.0 && y0 <= 0.0 && y1 >= 0.0) return false;  // mean inside
-  double qmin = INFINITY;
-  // edges x = x0, x1: minimise over dy in [y0, y1] (dy* = -B dx / C)
-#pragma unroll
-  for (int e = 0; e < 2; e++) {
-    const double dx = e ? x1 : x0;
-    const double dy = fmin(fmax(-B * dx / C, y0), y1);
-    qmin = fmin(qmin, A * dx * dx + 2.0 * B * dx * dy + C * dy * dy);
-  }
-#pragma unroll
-  for (int e = 0; e < 2; e++) {
-    const double dy = e ? y1 : y0;
-    const double dx = fmin(fmax(-B * dy / A, x0), x1);
-    qmin = fmin(qmin, A * dx * dx + 2.0 * B * dx * dy + C * dy * dy);
-  }
-  const double thr = -2.0 * cut * (1.0 + 1e-3) + 1e-3;
-  return qmin > thr;
-}
+// Whole-tile rejection (tile_culled) lives in cull.cuh.
 
 // Stable compaction of the batch survivors: returns this thread's slot (or
 // -1) and the survivor count; needs a 8-entry shared scratch.

@@ -26,6 +26,8 @@ struct PreprocessArgs {
   float* opacity;
   uint32_t* tiles_touched;
   float* cov3d;
+  uint64_t* tile_mask;   // if set: contributing-pairs binning (bit k = k-th tile of the rect, row-major;
+                         // ~0 = the whole rect) and the record's tile count is the contributing one
 };
 
 struct CompositeFwdArgs {
@@ -112,7 +114,8 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t n, uint32_t* sums,
                              cudaStream_t stream);
 int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, int tiles_y, uint32_t* tile_out, uint32_t* id_out, cudaStream_t stream);
+                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint32_t* tile_out, uint32_t* id_out,
+                      cudaStream_t stream);
 int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
                            cudaStream_t stream);
 int launch_make_keys(const uint32_t* tiles, const uint32_t* ids, const float* splats, int64_t m,

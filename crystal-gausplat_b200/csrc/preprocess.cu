@@ -11,6 +11,7 @@
 //   s0 = {mean.x, mean.y, conic.xx, conic.xy}
 //   s1 = {conic.yy, opacity (0 if culled or det <= 0), r, g}
 //   s2 = {b, depth, radius, bits(tiles_touched)}
+#include "cull.cuh"
 #include "geometry.cuh"
 #include "kernels.cuh"
 
@@ -21,6 +22,11 @@ constexpr int kShRow = 13;  // float4 per staged SH row (12 used + 1 pad)
 
 __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs a) {
   __shared__ float4 s_sh[kPreThreads * kShRow];
+  // contributing-pairs binning: per-thread cull terms, rect {x0, y0, width, 2^16/width rounded up},
+  // number of tile tests and the warp's inclusive scan of it
+  __shared__ CullGauss s_cg[kPreThreads];
+  __shared__ int4 s_rect[kPreThreads];
+  __shared__ uint32_t s_incl[kPreThreads];
   const int64_t base = (int64_t)blockIdx.x * kPreThreads;
   const int64_t i = base + threadIdx.x;
   const int64_t n = a.n;
@@ -36,6 +42,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
   __syncthreads();
 
   uint32_t tiles = 0;
+  float col_b = 0.0f, depth_o = 0.0f, radius_o = 0.0f;
+  uint32_t nt = 0;  // tile tests of this thread's Gaussian (contributing-pairs binning)
   if (i < n) {
     const float p[3] = {a.pos[i * 3], a.pos[i * 3 + 1], a.pos[i * 3 + 2]};
     const float s[3] = {gs_expf(a.log_scale[i * 3]), gs_expf(a.log_scale[i * 3 + 1]),
@@ -69,19 +77,27 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
     const float o = gs_sigmoid(a.logit_opacity[i]);
 
     float px = -1000.0f, py = -1000.0f, depth = 0.0f, radius = 0.0f;
+    int x0 = 0, x1 = -1, y0 = 0, y1 = -1;
     if (pr.visible) {
       px = pr.px; py = pr.py; depth = pr.zc; radius = pr.r;
       if (pr.r > 0.0f && pr.zc > 0.0f) {
-        int x0, x1, y0, y1;
         tile_bounds(px, py, pr.r, a.tiles_x, a.tiles_y, &x0, &x1, &y0, &y1);
         if (x1 >= x0 && y1 >= y0) tiles = (uint32_t)((x1 - x0 + 1) * (y1 - y0 + 1));
       }
     }
     const float o_eff = (pr.visible && pr.det > 0.0f) ? o : 0.0f;
+    const float4 g0 = make_float4(px, py, pr.A, pr.B);
+    // Contributing-pairs binning: the rect's tiles (<= 64) are tested below by the whole warp.
+    if (a.tile_mask && tiles > 0 && tiles <= 64) {
+      s_cg[threadIdx.x] = cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
+      const int w = x1 - x0 + 1;
+      s_rect[threadIdx.x] = make_int4(x0, y0, w, (65536 + w - 1) / w);
+      nt = tiles;
+    }
     float4* sp = reinterpret_cast<float4*>(a.splats) + i * 3;
-    sp[0] = make_float4(px, py, pr.A, pr.B);
+    sp[0] = g0;
     sp[1] = make_float4(pr.Cc, o_eff, col[0], col[1]);
-    sp[2] = make_float4(col[2], depth, radius, __uint_as_float(tiles));
+    col_b = col[2]; depth_o = depth; radius_o = radius;
 
     if (a.mean2d) { a.mean2d[i * 2] = px; a.mean2d[i * 2 + 1] = py; }
     if (a.depth) a.depth[i] = depth;
@@ -91,13 +107,60 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
     if (a.colors) { a.colors[i * 3] = col[0]; a.colors[i * 3 + 1] = col[1]; a.colors[i * 3 + 2] = col[2]; }
     if (a.opacity) a.opacity[i] = o;
     if (a.tiles_touched) a.tiles_touched[i] = tiles;
-    if (a.depth_keys) {
-      a.depth_keys[i] = tiles ? __float_as_uint(depth) : 0xFFFFFFFFu;
-      a.order[i] = (uint32_t)i;
-    }
     if (a.cov3d) {
 #pragma unroll
       for (int k = 0; k < 6; k++) a.cov3d[i * 6 + k] = c3[k];
+    }
+  }
+
+  // Tile tests of the warp's Gaussians, flattened over its lanes so that one
+  // large rectangle does not hold the other 31 lanes: in round `base`, lane l
+  // runs test base + l, which belongs to the first lane whose inclusive count
+  // exceeds it. The round's results come back as one ballot, from which every
+  // lane copies the bits of its own tests into its mask (bit = row-major
+  // position in its rect). The row of test t of a rect of width w is
+  // (t * ceil(2^16 / w)) >> 16, exact for t < 64 <= 2^16 / w.
+  uint32_t emit = tiles;
+  if (a.tile_mask) {
+    const int lane = threadIdx.x & 31, wb = threadIdx.x & ~31;
+    uint32_t incl = nt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += t;
+    }
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    const uint32_t first = incl - nt;  // this lane's tests are [first, incl)
+    s_incl[threadIdx.x] = incl;
+    __syncwarp();
+    uint64_t mask = 0ull;
+    int own = 0;
+    for (uint32_t base = 0; base < total; base += 32) {
+      const uint32_t k = base + lane;
+      bool keep = false;
+      if (k < total) {
+        while (s_incl[wb + own] <= k) own++;
+        const uint32_t local = k - (own ? s_incl[wb + own - 1] : 0u);
+        const int4 r = s_rect[wb + own];
+        const uint32_t ry = (local * (uint32_t)r.w) >> 16, rx = local - ry * (uint32_t)r.z;
+        float rx0, rx1, ry0, ry1;
+        tile_pixel_rect(r.x + (int)rx, r.y + (int)ry, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
+        keep = !cull_tile(s_cg[wb + own], rx0, rx1, ry0, ry1);
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+      const uint32_t lo = max(first, base), hi = min(incl, base + 32);
+      if (lo < hi) mask |= ((uint64_t)(bal >> (lo - base)) & ((1ull << (hi - lo)) - 1ull)) << (lo - first);
+    }
+    if (i < n) {
+      if (nt) emit = (uint32_t)__popcll(mask);
+      a.tile_mask[i] = nt ? mask : ~0ull;
+    }
+  }
+  if (i < n) {
+    reinterpret_cast<float4*>(a.splats)[i * 3 + 2] = make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
+    if (a.depth_keys) {
+      a.depth_keys[i] = emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu;
+      a.order[i] = (uint32_t)i;
     }
   }
 }

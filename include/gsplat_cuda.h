@@ -95,7 +95,20 @@ typedef struct gsc_raster_config {
   float near_z;      /* cull z <= near_z: 0.01 */
   float far_z;       /* cull z > far_z: 1000 */
   float background[3];
+  int32_t binning;   /* GSC_BIN_*: tile lists of the whole-view calls (default CONTRIBUTING) */
 } gsc_raster_config;
+
+/* Tile lists built by gsc_rasterize_forward. REFERENCE: every tile of each
+ * Gaussian's square 3-sigma rectangle (create_tile_keys,
+ * gaussian.metal:315-357), bit-identical to the reference's sorted keys,
+ * values and ranges. CONTRIBUTING: the same lists without the (tile,
+ * Gaussian) pairs that the exact whole-tile test proves can never pass the
+ * alpha test at any pixel of the tile (Gaussians with more than 64 tiles keep
+ * all of theirs); images, n_contrib, final_T and gradients are bit-identical
+ * to REFERENCE, with fewer pairs to emit, sort and scan. The stage entry
+ * point gsc_bin always builds the reference lists. */
+#define GSC_BIN_REFERENCE 0
+#define GSC_BIN_CONTRIBUTING 1
 
 /* The trainable state of Gaussian3D (src/gaussian_splatting/gaussian.cr:19-37):
  * position [N,3], log_scale [N,3], rotation [N,4] (w,x,y,z),

@@ -749,6 +749,86 @@ void gso_l1_loss_grad(int64_t numel, const float* pred, const float* target, flo
   if (loss_sum) *loss_sum += loss;
 }
 
+// ---- contributing-pairs binning ----------------------------------------------
+
+// ln x for positive finite float x by frexp and the atanh series through
+// s^13, in a fixed order of +, *, / (identical bits on every IEEE float
+// implementation).
+static float log_series(float x) {
+  int e;
+  float m = std::frexp(x, &e);
+  if (m < 0.70710678f) {
+    m *= 2.0f;
+    e -= 1;
+  }
+  const float s = (m - 1.0f) / (m + 1.0f), s2 = s * s;
+  float p = 1.0f / 13.0f;
+  const float inv[] = {1.0f / 11.0f, 1.0f / 9.0f, 1.0f / 7.0f, 1.0f / 5.0f, 1.0f / 3.0f, 1.0f};
+  for (float c : inv) p = p * s2 + c;
+  return (float)e * 0.69314718f + 2.0f * s * p;
+}
+
+// True if no pixel centre of [rx0, rx1] x [ry0, ry1] can reach alpha_min:
+// the fp32 minimum over the rectangle of the conic's quadratic form against
+// -2 ln(alpha_min / o), with margins (2e-3 relative and absolute, 1e-4 in ln,
+// refused when 1 - |B|/sqrt(AC) < 1e-3) that cover the rounding of this and of
+// the per-pixel evaluation. Per-Gaussian terms first, then the four edge
+// candidates of the rectangle.
+static float cull_form(float A, float B, float C, float dx, float dy) {
+  return A * dx * dx + 2.0f * B * dx * dy + C * dy * dy;
+}
+
+static bool tile_culled(float mx, float my, float A, float B, float C, float o, float rx0,
+                        float rx1, float ry0, float ry1, float alpha_min) {
+  if (!std::isfinite(mx) || !std::isfinite(my)) return false;
+  if (!(o > 0.0f)) return o == 0.0f && std::isfinite(A) && std::isfinite(B) && std::isfinite(C);
+  if (!(A > 0.0f && C > 0.0f) || !std::isfinite(A) || !std::isfinite(B) || !std::isfinite(C)) return false;
+  const float rho = std::fabs(B) / std::sqrt(A * C);
+  if (!(1.0f - rho >= 1e-3f)) return false;
+  const float cut = log_series(alpha_min / o) - 1e-4f;
+  if (cut >= 0.0f) return true;
+  const float nbc = -B / C, nba = -B / A;
+  const float thr = -2.0f * cut * (1.0f + 2e-3f) + 2e-3f;
+  const float x0 = rx0 - mx, x1 = rx1 - mx, y0 = ry0 - my, y1 = ry1 - my;
+  if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return false;
+  float qmin = INFINITY;
+  for (int e = 0; e < 2; e++) {
+    const float dx = e ? x1 : x0;
+    qmin = std::fmin(qmin, cull_form(A, B, C, dx, std::fmin(std::fmax(dx * nbc, y0), y1)));
+  }
+  for (int e = 0; e < 2; e++) {
+    const float dy = e ? y1 : y0;
+    qmin = std::fmin(qmin, cull_form(A, B, C, std::fmin(std::fmax(dy * nba, x0), x1), dy));
+  }
+  return qmin > thr;
+}
+
+int64_t gso_contributing_lists(int32_t W, int32_t H, int64_t m, const uint64_t* keys,
+                               const uint32_t* vals, const float* mean2d, const float* conic,
+                               const float* opacity, const uint32_t* tiles_touched,
+                               float alpha_min, uint64_t* out_keys, uint32_t* out_vals) {
+  const int tiles_x = (W + 15) / 16;
+  int64_t k = 0;
+  for (int64_t i = 0; i < m; i++) {
+    const uint32_t id = vals[i];
+    const uint32_t tile = (uint32_t)(keys[i] >> 32);
+    bool keep = tiles_touched[id] > 64;
+    if (!keep) {
+      const int tx = (int)(tile % (uint32_t)tiles_x), ty = (int)(tile / (uint32_t)tiles_x);
+      const float rx0 = tx * 16 + 0.5f, ry0 = ty * 16 + 0.5f;
+      const float rx1 = std::min(tx * 16 + 16, W) - 0.5f, ry1 = std::min(ty * 16 + 16, H) - 0.5f;
+      keep = !tile_culled(mean2d[2 * id], mean2d[2 * id + 1], conic[3 * id], conic[3 * id + 1],
+                          conic[3 * id + 2], opacity[id], rx0, rx1, ry0, ry1, alpha_min);
+    }
+    if (keep) {
+      out_keys[k] = keys[i];
+      out_vals[k] = id;
+      k++;
+    }
+  }
+  return k;
+}
+
 // ---- losses beyond L1 -------------------------------------------------------
 
 // Gaussian window of Loss#gaussian_window (loss.cr:262-281), sigma 1.5: fp32

@@ -42,6 +42,15 @@ int64_t gso_emit_keys(int64_t n, const float* mean2d, const float* depth, const 
                       int32_t tiles_x, int32_t tiles_y, uint64_t* keys, uint32_t* vals,
                       int64_t capacity);
 
+/* Contributing-pairs binning (GSC_BIN_CONTRIBUTING): drops from sorted
+ * reference lists every (tile, Gaussian) pair that the exact whole-tile test
+ * rejects, except for Gaussians whose rectangle has more than 64 tiles; the
+ * order of the rest is kept. Returns the number of pairs written. */
+int64_t gso_contributing_lists(int32_t width, int32_t height, int64_t m, const uint64_t* keys,
+                               const uint32_t* vals, const float* mean2d, const float* conic,
+                               const float* opacity, const uint32_t* tiles_touched,
+                               float alpha_min, uint64_t* out_keys, uint32_t* out_vals);
+
 /* Stable ascending sort of (key, value) pairs by key bits [begin_bit, end_bit). */
 void gso_sort_pairs(int64_t n, uint64_t* keys, uint32_t* vals, int begin_bit, int end_bit);
 

@@ -258,6 +258,19 @@ def densify_apply(scene, flags, clone_noise, ln_split, seed):
     return out
 
 
+def contributing_lists(W, H, skeys, svals, pre, alpha_min):
+    """gso_contributing_lists: the sorted lists without provably non-contributing pairs."""
+    m = skeys.size
+    ok = np.zeros(m, np.uint64)
+    ov = np.zeros(m, np.uint32)
+    L = lib()
+    L.gso_contributing_lists.restype = C.c_int64
+    k = L.gso_contributing_lists(W, H, C.c_int64(m), _p(skeys), _p(svals), _p(pre["mean2d"]),
+                                 _p(pre["conic"]), _p(pre["opacity"]), _p(pre["tiles_touched"]),
+                                 C.c_float(alpha_min), _p(ok), _p(ov))
+    return ok[:k].copy(), ov[:k].copy()
+
+
 def forward_pipeline(scene, cam, cfg):
     """All forward intermediates of one view (preprocess .. composite)."""
     W, H = cam.width, cam.height
@@ -266,6 +279,8 @@ def forward_pipeline(scene, cam, cfg):
     keys, vals = emit_keys(pre, tx, ty)
     end_bit = 32 + max(0, int(np.ceil(np.log2(tx * ty))) if tx * ty > 1 else 0)
     skeys, svals = sort_pairs(keys, vals, 0, end_bit)
+    if getattr(cfg, "binning", _abi.GSC_BIN_REFERENCE) == _abi.GSC_BIN_CONTRIBUTING:
+        skeys, svals = contributing_lists(W, H, skeys, svals, pre, cfg.alpha_min)
     ranges = tile_ranges(skeys, tx * ty)
     img, nc, fT, last = composite_forward(W, H, ranges, svals, pre, cfg)
     return {"pre": pre, "keys": keys, "vals": vals, "sorted_keys": skeys, "sorted_vals": svals,

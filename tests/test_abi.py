@@ -38,7 +38,7 @@ def test_struct_layouts():
     # gsc_camera is byte-for-byte the reference's packed CameraParamsGPU.
     assert C.sizeof(_abi.Camera) == 176
     assert _abi.Camera.fx.offset == 128 and _abi.Camera.campos.offset == 160
-    assert C.sizeof(_abi.RasterConfig) == 12 * 4
+    assert C.sizeof(_abi.RasterConfig) == 13 * 4
     assert C.sizeof(_abi.Gaussians) == 6 * 8
     assert C.sizeof(_abi.AdamGroup) == 6 * 8
 

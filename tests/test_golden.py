@@ -17,7 +17,8 @@ def load(path):
     z = np.load(path)
     arrays = {k[3:]: z[k] for k in z.files if k.startswith("in_")}
     cam = gs.make_camera(int(z["W"]), int(z["H"]), tuple(z["eye"]))
-    cfg = gs.default_config(mode=int(z["mode"]), background=(0.05, 0.1, 0.15))
+    cfg = gs.default_config(mode=int(z["mode"]), background=(0.05, 0.1, 0.15),
+                            binning=_abi.GSC_BIN_REFERENCE)
     return z, arrays, cam, cfg
 
 

@@ -73,7 +73,7 @@ def test_binning_sort_ranges_bit_exact(cuda, oracle, case):
     n, W, H, eye = case
     arrays, g, cam = make(n, W, H, eye=eye)
     cs = cam.to_struct()
-    cfg = gs.default_config()
+    cfg = gs.default_config(binning=_abi.GSC_BIN_REFERENCE)  # the stage entry points build reference lists
     got = gpu_preprocess(g, cs, cfg)
     ref = oracle.forward_pipeline(oracle.Scene(arrays), cs, cfg)
     tx, ty = (W + 15) // 16, (H + 15) // 16
@@ -140,18 +140,24 @@ def test_sort_c1_distribution_sorted(cuda, oracle):
     np.testing.assert_array_equal(v, vals[order])
 
 
+BINNINGS = [_abi.GSC_BIN_REFERENCE, _abi.GSC_BIN_CONTRIBUTING]
+
+
+@pytest.mark.parametrize("binning", BINNINGS, ids=["reference_lists", "contributing_lists"])
 @pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF])
 @pytest.mark.parametrize("case", CASES)
-def test_rasterize_forward_matches_oracle(cuda, oracle, case, mode):
+def test_rasterize_forward_matches_oracle(cuda, oracle, case, mode, binning):
     n, W, H, eye = case
     arrays, g, cam = make(n, W, H, eye=eye)
-    cfg = gs.default_config(mode=mode, background=(0.1, 0.2, 0.3))
+    cfg = gs.default_config(mode=mode, background=(0.1, 0.2, 0.3), binning=binning)
     img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
     nc = ctx.get(_abi.GSC_FRAME_N_CONTRIB, np.uint32)
     fT = ctx.get(_abi.GSC_FRAME_FINAL_T, np.float32)
     last = ctx.get(_abi.GSC_FRAME_LAST, np.uint32)
     ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
-    assert ctx.num_rendered == ref["keys"].size
+    assert ctx.num_rendered == ref["sorted_keys"].size
+    if binning == _abi.GSC_BIN_REFERENCE:
+        assert ctx.num_rendered == ref["keys"].size
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
@@ -192,6 +198,37 @@ def test_rasterize_backward_matches_oracle(cuda, oracle, case, mode):
     for name, (a, b) in zip(names, pairs):
         e = grad_close(host(a), b)
         assert e <= GRAD_RTOL, f"{name}: {e}"
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_contributing_lists_change_nothing_but_the_lists(cuda, oracle, case):
+    """CONTRIBUTING vs REFERENCE binning on the GPU: same image, n_contrib and
+    final_T bit for bit, gradients within the atomics' reordering, and the
+    contributing lists are an order-preserving subset of the reference ones."""
+    n, W, H, eye = case
+    arrays, g, cam = make(n, W, H, eye=eye)
+    target = to_dev(np.random.default_rng(4).uniform(0, 1, (H, W, 3)).astype(np.float32))
+    out = {}
+    for b in BINNINGS:
+        cfg = gs.default_config(binning=b)
+        img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+        grads = gs.Rasterizer.backward(None, g, cam, ctx, target=target)
+        R.sync()
+        out[b] = (host(img), ctx.get(_abi.GSC_FRAME_N_CONTRIB, np.uint32),
+                  ctx.get(_abi.GSC_FRAME_FINAL_T, np.float32), ctx.get(_abi.GSC_FRAME_KEYS, np.uint64),
+                  ctx.get(_abi.GSC_FRAME_VALUES, np.uint32), host(grads.arena).copy())
+    r, c = out[_abi.GSC_BIN_REFERENCE], out[_abi.GSC_BIN_CONTRIBUTING]
+    for k in range(3):
+        np.testing.assert_array_equal(c[k], r[k])
+    assert c[3].size < r[3].size
+    pairs_r = r[3] >> np.uint64(32) << np.uint64(32) | r[4].astype(np.uint64)
+    pairs_c = c[3] >> np.uint64(32) << np.uint64(32) | c[4].astype(np.uint64)
+    o = np.argsort(pairs_r, kind="stable")  # (tile, id) pairs are unique
+    pos = o[np.searchsorted(pairs_r[o], pairs_c)]
+    np.testing.assert_array_equal(pairs_r[pos], pairs_c)
+    assert np.all(np.diff(pos) > 0)  # order preserved
+    np.testing.assert_array_equal(r[3][pos], c[3])
+    assert grad_close(c[5], r[5]) <= GRAD_RTOL
 
 
 def test_backward_with_explicit_dl_dimage(cuda, oracle):

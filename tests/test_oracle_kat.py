@@ -5,6 +5,8 @@ import math
 import numpy as np
 import pytest
 
+from helpers import _abi, gs
+
 
 def test_expf_within_one_ulp(oracle):
     x = np.concatenate([np.linspace(-103.9, 88.7, 200001, dtype=np.float32),
@@ -175,3 +177,40 @@ def test_ref_mode_sh_truncation(gs, oracle):
     assert ref[1] == pytest.approx(0.5) and ref[2] == pytest.approx(0.5)
     assert ref[0] != pytest.approx(0.5)
     assert full[1] != pytest.approx(0.5)
+
+
+@pytest.mark.parametrize("seed", [1, 2])
+def test_oracle_contributing_lists_render_identically(oracle, seed):
+    """Dropping the pairs the exact whole-tile test rejects changes no pixel."""
+    a = gs.synthetic_arrays(4000, seed)
+    a["log_scale"] = (a["log_scale"] + np.float32(0.8)).astype(np.float32)  # larger footprints
+    cam = gs.make_camera(97, 75, (0.3, -0.2, 3.0)).to_struct()
+    sc = oracle.Scene(a)
+    ref = oracle.forward_pipeline(sc, cam, gs.default_config(binning=_abi.GSC_BIN_REFERENCE))
+    con = oracle.forward_pipeline(sc, cam, gs.default_config(binning=_abi.GSC_BIN_CONTRIBUTING))
+    assert 0 < con["sorted_keys"].size < 0.9 * ref["sorted_keys"].size
+    for k in ("image", "n_contrib", "final_T"):
+        np.testing.assert_array_equal(con[k], ref[k], err_msg=k)
+
+
+def test_oracle_contributing_lists_adversarial(oracle):
+    """Gaussians at the edge of the cull: opacities just above alpha_min,
+    strongly elongated conics, means on tile borders. No pixel may change."""
+    rng = np.random.default_rng(7)
+    n = 6000
+    a = gs.synthetic_arrays(n, 7)
+    cam = gs.make_camera(96, 80, (0.0, 0.0, 3.0))
+    # opacity in (1/255, 3/255]: logit = ln(o / (1 - o))
+    o = rng.uniform(1.0001 / 255, 3.0 / 255, n)
+    a["logit_opacity"][:, 0] = np.log(o / (1 - o)).astype(np.float32)
+    # elongated: one axis 20x another
+    a["log_scale"][:, 0] = rng.uniform(-4.0, -2.5, n).astype(np.float32)
+    a["log_scale"][:, 1] = (a["log_scale"][:, 0] - np.float32(3.0)).astype(np.float32)
+    a["position"][:, 2] = rng.uniform(-0.2, 0.2, n).astype(np.float32)
+    sc = oracle.Scene(a)
+    cs = cam.to_struct()
+    ref = oracle.forward_pipeline(sc, cs, gs.default_config(binning=_abi.GSC_BIN_REFERENCE))
+    con = oracle.forward_pipeline(sc, cs, gs.default_config(binning=_abi.GSC_BIN_CONTRIBUTING))
+    assert con["sorted_keys"].size < ref["sorted_keys"].size
+    for k in ("image", "n_contrib", "final_T"):
+        np.testing.assert_array_equal(con[k], ref[k], err_msg=k)
