@@ -189,16 +189,18 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
   const float alpha = fminf(amax, g1.y * G);
   if (alpha < amin) return false;
   const float o = g1.y;
+  // From here on the gradients only need to be within tolerance, so products
+  // and sums are fused (explicit fmaf; the file is built without contraction).
   // T_before = T / (1 - alpha) and dL/dalpha = T_before c.g - (acc / (1 - alpha)).g,
   // with one correctly rounded reciprocal and the running colour kept as acc.g.
   const float inv = __frcp_rn(1.0f - alpha);
   const float T_before = P.T * inv;
   const float wgt = T_before * alpha;
-  const float cg = g1.z * P.g[0] + g1.w * P.g[1] + g2 * P.g[2];
-  v[6] += wgt * P.g[0];
-  v[7] += wgt * P.g[1];
-  v[8] += wgt * P.g[2];
-  const float dL_dalpha = T_before * cg - P.ag * inv;
+  const float cg = fmaf(g2, P.g[2], fmaf(g1.w, P.g[1], g1.z * P.g[0]));
+  v[6] = fmaf(wgt, P.g[0], v[6]);
+  v[7] = fmaf(wgt, P.g[1], v[7]);
+  v[8] = fmaf(wgt, P.g[2], v[8]);
+  const float dL_dalpha = fmaf(T_before, cg, -P.ag * inv);
   float dL_dG, dL_do;
   if (FULL && !(o * G <= amax)) {
     dL_dG = 0.0f;
@@ -208,17 +210,19 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
     dL_do = dL_dalpha * G;
   }
   const float dL_dpower = dL_dG * G;
-  // g0 = {mean, -A/2, -B}, g1.x = -C/2 (pre-scaled conic, see fwd)
-  v[0] += dL_dpower * (-2.0f * g0.z * dx - g0.w * dy);
-  v[1] += dL_dpower * (-g0.w * dx - 2.0f * g1.x * dy);
+  // g0 = {mean, -A/2, -B}, g1.x = -C/2 (pre-scaled conic, see fwd):
+  // dpower/dmean = -(2 g0.z dx + g0.w dy, g0.w dx + 2 g1.x dy)
+  const float px_ = dL_dpower * dx, py_ = dL_dpower * dy;
+  v[0] = fmaf(-2.0f * g0.z, px_, fmaf(-g0.w, py_, v[0]));
+  v[1] = fmaf(-2.0f * g1.x, py_, fmaf(-g0.w, px_, v[1]));
   if (FULL) {
-    v[2] += dL_dpower * (-0.5f * dx * dx);
-    v[3] += dL_dpower * (-dx * dy);
-    v[4] += dL_dpower * (-0.5f * dy * dy);
+    v[2] = fmaf(-0.5f * dx, px_, v[2]);
+    v[3] = fmaf(-dx, py_, v[3]);
+    v[4] = fmaf(-0.5f * dy, py_, v[4]);
   }
   v[5] += dL_do;
   P.T = T_before;
-  P.ag = FULL ? P.ag + wgt * cg : P.ag - wgt * cg;  // REF keeps gaussian.metal:566
+  P.ag = fmaf(FULL ? wgt : -wgt, cg, P.ag);  // REF keeps gaussian.metal:566
   return true;
 }
 
