@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
                                                          uint32_t* __restrict__ id_out) {
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
+  __shared__ uint32_t s_inv[256];  // ceil(2^16 / width): row of a test < 64 by multiply and shift
   __shared__ uint32_t s_id[256];
   __shared__ uint64_t s_mask[256];
   __shared__ uint32_t s_warp[8];
@@ -228,6 +229,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
       s_x0[threadIdx.x] = x0;
       s_y0[threadIdx.x] = y0;
       s_wx[threadIdx.x] = x1 - x0 + 1;
+      s_inv[threadIdx.x] = (65536u + (uint32_t)(x1 - x0)) / (uint32_t)(x1 - x0 + 1);
       s_id[threadIdx.x] = gid;
       s_mask[threadIdx.x] = tile_mask ? tile_mask[gid] : ~0ull;
     }
@@ -235,34 +237,54 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
   uint32_t incl = block_incl_scan_256(t, s_warp);
   s_incl[threadIdx.x] = incl;
   __syncthreads();
-  const uint32_t total = s_incl[255];
+  // Each warp writes the contiguous output range of its 32 Gaussians; a
+  // lane's output index grows by 32 per round, so the Gaussian that owns it
+  // is found by advancing a pointer instead of searching.
   const uint64_t out = offsets[blockIdx.x];
-  for (uint32_t k = threadIdx.x; k < total; k += 256) {
-    int lo = 0, hi = 255;
-    while (lo < hi) {
-      int mid = (lo + hi) >> 1;
-      if (s_incl[mid] > k) hi = mid; else lo = mid + 1;
+  const int wb = threadIdx.x & ~31;
+  const uint32_t wend = s_incl[wb + 31];
+  int own = wb;
+  for (uint32_t k = (wb ? s_incl[wb - 1] : 0u) + (threadIdx.x & 31); k < wend; k += 32) {
+    while (s_incl[own] <= k) own++;
+    uint32_t local = k - (own ? s_incl[own - 1] : 0u);
+    const uint64_t mk = s_mask[own];
+    const uint32_t wx = (uint32_t)s_wx[own];
+    uint32_t ry;
+    if (mk != ~0ull) {
+      local = select_bit64(mk, local);  // local-th contributing tile of the rect (< 64)
+      ry = (local * s_inv[own]) >> 16;
+    } else {
+      ry = local / wx;
     }
-    uint32_t local = k - (lo ? s_incl[lo - 1] : 0u);
-    const uint64_t mk = s_mask[lo];
-    if (mk != ~0ull) local = select_bit64(mk, local);  // local-th contributing tile of the rect
-    const int wx = s_wx[lo];
-    const int ty = s_y0[lo] + (int)(local / (uint32_t)wx);
-    const int tx = s_x0[lo] + (int)(local % (uint32_t)wx);
+    const int ty = s_y0[own] + (int)ry;
+    const int tx = s_x0[own] + (int)(local - ry * wx);
     tile_out[out + k] = (uint32_t)(ty * tiles_x + tx);
-    id_out[out + k] = s_id[lo];
+    id_out[out + k] = s_id[own];
   }
 }
 
 __global__ void __launch_bounds__(256) tile_ranges_u32_kernel(const uint32_t* __restrict__ tiles, int64_t n,
                                                               uint32_t num_tiles, uint32_t* __restrict__ ranges) {
-  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  if (i >= n) return;
-  const uint32_t t = tiles[i];
-  const uint32_t prev = i > 0 ? tiles[i - 1] : 0xFFFFFFFFu;
-  const uint32_t next = i < n - 1 ? tiles[i + 1] : 0xFFFFFFFFu;
-  if (t != prev && t < num_tiles) ranges[(size_t)t * 2] = (uint32_t)i;
-  if (t != next && t < num_tiles) ranges[(size_t)t * 2 + 1] = (uint32_t)(i + 1);
+  // four keys per thread: one 16-byte load (tiles is 16-byte aligned) and the two neighbours
+  const int64_t i0 = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
+  if (i0 >= n) return;
+  uint32_t t[6];
+  t[0] = i0 > 0 ? tiles[i0 - 1] : 0xFFFFFFFFu;
+  if (i0 + 4 <= n) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tiles + i0);
+    t[1] = v.x; t[2] = v.y; t[3] = v.z; t[4] = v.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; k++) t[1 + k] = i0 + k < n ? tiles[i0 + k] : 0xFFFFFFFFu;
+  }
+  t[5] = i0 + 4 < n ? tiles[i0 + 4] : 0xFFFFFFFFu;
+#pragma unroll
+  for (int k = 1; k <= 4; k++) {
+    const uint32_t c = t[k];
+    if (c >= num_tiles) continue;  // also the padding past n
+    if (c != t[k - 1]) ranges[(size_t)c * 2] = (uint32_t)(i0 + k - 1);
+    if (c != t[k + 1]) ranges[(size_t)c * 2 + 1] = (uint32_t)(i0 + k);
+  }
 }
 
 __global__ void __launch_bounds__(256) make_keys_kernel(const uint32_t* __restrict__ tiles,
@@ -298,7 +320,7 @@ int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, 
                            cudaStream_t stream) {
   GS_CK(cudaMemsetAsync(ranges, 0, sizeof(uint32_t) * 2 * (size_t)num_tiles, stream));
   if (n == 0) return GSC_OK;
-  tile_ranges_u32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(tiles, n, (uint32_t)num_tiles, ranges);
+  tile_ranges_u32_kernel<<<(unsigned)((n + 1023) / 1024), 256, 0, stream>>>(tiles, n, (uint32_t)num_tiles, ranges);
   GS_CK_LAUNCH("tile_ranges_u32_kernel");
   return GSC_OK;
 }

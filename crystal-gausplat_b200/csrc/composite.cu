@@ -85,8 +85,8 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
     int m;
     const int slot = compact_slot(keep, s_cnt, &m);
     if (slot >= 0) {
-      // conic pre-scaled by powers of two (-A/2, -B, -C/2): the power below
-      // then rounds to exactly -0.5 * ((dx dx A + (2 dx) dy B) + dy dy C)
+      // conic pre-scaled by powers of two (-A/2, -B, -C/2); the power below is
+      // fma(dy dy, -C/2, fma(dx dy, -B, dx dx (-A/2))), the oracle's formula
       s0[slot] = make_float4(g0.x, g0.y, -0.5f * g0.z, -g0.w);
       s1[slot] = make_float4(-0.5f * g1.x, g1.y, g1.z, g1.w);
       s2[slot] = g2;
@@ -98,14 +98,15 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
         const float4 q0 = s0[j];
         const float dx = pxf - q0.x, dy = pyf - q0.y;
         const float4 q1 = s1[j];
-        const float power = dx * dx * q0.z + dx * dy * q0.w + dy * dy * q1.x;
+        const float power = fmaf(dy * dy, q1.x, fmaf(dx * dy, q0.w, dx * dx * q0.z));
         if (power > 0.0f || power < cut) continue;
         const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
         const float alpha = fminf(amax, q1.y * G);
         if (alpha < amin) continue;
-        C0 += T * alpha * q1.z;
-        C1 += T * alpha * q1.w;
-        C2 += T * alpha * s2[j];
+        const float w = T * alpha;
+        C0 = fmaf(w, q1.z, C0);
+        C1 = fmaf(w, q1.w, C1);
+        C2 = fmaf(w, s2[j], C2);
         T *= (1.0f - alpha);
         cnt++;
         lst = s_idx[j] + 1;
@@ -129,9 +130,9 @@ __global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs 
   }
   if (!inside) return;
   const size_t pix = (size_t)y * a.width + x;
-  a.image[pix * 3 + 0] = C0 + T * a.bg[0];
-  a.image[pix * 3 + 1] = C1 + T * a.bg[1];
-  a.image[pix * 3 + 2] = C2 + T * a.bg[2];
+  a.image[pix * 3 + 0] = fmaf(T, a.bg[0], C0);
+  a.image[pix * 3 + 1] = fmaf(T, a.bg[1], C1);
+  a.image[pix * 3 + 2] = fmaf(T, a.bg[2], C2);
   if (a.n_contrib) a.n_contrib[pix] = cnt;
   if (a.final_T) a.final_T[pix] = T;
   if (a.last) a.last[pix] = lst;
@@ -182,7 +183,7 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
                                           float amin, float amax, float cut, bool short_exp, float v[9]) {
   if (!(P.inside && idx < P.hi)) return false;
   const float dx = P.pxf - g0.x, dy = P.pyf - g0.y;
-  const float power = dx * dx * g0.z + dx * dy * g0.w + dy * dy * g1.x;  // == forward's power
+  const float power = fmaf(dy * dy, g1.x, fmaf(dx * dy, g0.w, dx * dx * g0.z));  // == forward's power
   if (power > 0.0f || power < cut) return false;
   // Same exponential and tests as the forward, so the accepted set matches it.
   const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);

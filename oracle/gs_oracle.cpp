@@ -424,7 +424,8 @@ inline PixelEval eval_gauss(float pxf, float pyf, const float* mean2d, const flo
   e.A = cyy * inv_det;
   e.B = -cxy * inv_det;
   e.C = cxx * inv_det;
-  e.power = -0.5f * (e.dx * e.dx * e.A + 2.0f * e.dx * e.dy * e.B + e.dy * e.dy * e.C);
+  // fma(dy dy, -C/2, fma(dx dy, -B, dx dx (-A/2))): the scalings are exact
+  e.power = std::fma(e.dy * e.dy, -0.5f * e.C, std::fma(e.dx * e.dy, -e.B, e.dx * e.dx * (-0.5f * e.A)));
   if (e.power > 0.0f) return e;
   e.G = gso_expf(e.power);
   e.alpha = std::fmin(cfg->alpha_max, opacity[gid] * e.G);
@@ -459,13 +460,14 @@ void gso_composite_forward(int32_t width, int32_t height, const uint32_t* ranges
           uint32_t gid = vals[i];
           PixelEval e = eval_gauss(pxf, pyf, mean2d, cov2d, opacity, gid, cfg);
           if (!e.ok) continue;
-          for (int c = 0; c < 3; c++) C[c] += T * e.alpha * colors[gid * 3 + c];
+          const float w = T * e.alpha;
+          for (int c = 0; c < 3; c++) C[c] = std::fma(w, colors[gid * 3 + c], C[c]);
           T *= (1.0f - e.alpha);
           cnt++;
           lst = i - start + 1;
         }
         size_t pix = (size_t)y * width + x;
-        for (int c = 0; c < 3; c++) image[pix * 3 + c] = C[c] + T * cfg->background[c];
+        for (int c = 0; c < 3; c++) image[pix * 3 + c] = std::fma(T, cfg->background[c], C[c]);
         if (n_contrib) n_contrib[pix] = cnt;
         if (final_T) final_T[pix] = T;
         if (last) last[pix] = lst;

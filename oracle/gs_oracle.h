@@ -105,7 +105,8 @@ void gso_densify_plan(const gsc_gaussians* g, const float* accum, const int32_t*
 void gso_densify_apply(const gsc_gaussians* g, const uint8_t* flags, const gsc_gaussians_out* out,
                        float clone_noise, float ln_split, uint64_t seed);
 
-/* Whole view: forward (and backward with fused L1 when target != NULL).
+/* Whole view: forward (and backward with fused L1 when target != NULL), on the
+ * reference tile lists (images and gradients do not depend on the binning).
  * Allocates its own intermediates. Returns the number of keys. */
 int64_t gso_render_view(const gsc_gaussians* g, const gsc_camera* cam,
                         const gsc_raster_config* cfg, float* image, const float* target,

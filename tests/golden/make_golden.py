@@ -30,7 +30,8 @@ def make(name, mode):
     arrays = gs.synthetic_arrays(n, seed)
     cam = gs.make_camera(W, H, eye)
     cs = cam.to_struct()
-    cfg = gs.default_config(mode=mode, background=(0.05, 0.1, 0.15))
+    cfg = gs.default_config(mode=mode, background=(0.05, 0.1, 0.15),
+                            binning=gs._abi.GSC_BIN_REFERENCE)  # the reference lists
     sc = O.Scene(arrays)
     fw = O.forward_pipeline(sc, cs, cfg)
     target = np.random.default_rng(seed + 1).uniform(0, 1, (H, W, 3)).astype(np.float32)
