@@ -73,7 +73,7 @@ using namespace gs;
 
 struct gsc_frame {
   gsc_ctx* ctx = nullptr;
-  GsBuf splats, depth_keys, order, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
+  GsBuf splats, depth_pairs, depth_keys, order, pairs, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
       last, n_contrib, grad2d, tile_mask;
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
@@ -237,7 +237,7 @@ static int check_view(const gsc_camera* cam, const gsc_raster_config* cfg) {
 
 static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
                          const gsc_raster_config* cfg, const gsc_projected* o, uint32_t* block_sums,
-                         uint32_t* depth_keys = nullptr, uint32_t* order = nullptr,
+                         uint64_t* depth_pairs = nullptr,
                          uint64_t* tile_mask = nullptr) {
   PreprocessArgs a;
   std::memset(&a, 0, sizeof a);
@@ -249,7 +249,7 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.tiles_y = (cam->height + GS_TILE - 1) / GS_TILE;
   a.splats = o->splats;
   (void)block_sums;
-  a.depth_keys = depth_keys; a.order = order;
+  a.depth_pairs = depth_pairs;
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
   a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
@@ -495,7 +495,7 @@ GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out) {
 GSC_API int gsc_frame_destroy(gsc_frame* f) {
   if (!f) return GSC_OK;
   cudaStreamSynchronize(f->ctx->stream);
-  GsBuf* bufs[] = {&f->splats, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
+  GsBuf* bufs[] = {&f->splats, &f->depth_pairs, &f->pairs, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
                    &f->n_contrib, &f->grad2d, &f->tile_mask};
   for (GsBuf* b : bufs)
@@ -518,6 +518,7 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   f->has_forward = false;
   f->n = n; f->width = W; f->height = H; f->tiles_x = tx; f->tiles_y = ty;
   GS_TRY(ensure(ctx, &f->splats, (size_t)n * 48 + 48));
+  GS_TRY(ensure(ctx, &f->depth_pairs, (size_t)n * 8 + 8));
   GS_TRY(ensure(ctx, &f->depth_keys, (size_t)n * 4 + 4));
   GS_TRY(ensure(ctx, &f->order, (size_t)n * 4 + 4));
   GS_TRY(ensure(ctx, &f->block_sums, (size_t)nb * 4 + 4));
@@ -545,13 +546,15 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
     GS_TRY(ensure(ctx, &f->tile_mask, (size_t)n * 8 + 8));
     tile_mask = (uint64_t*)f->tile_mask.ptr;
   }
-  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, nullptr, depth_keys, order, tile_mask));
-  // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and sink)
-  if (n > 1) {
-    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_u32(n, 0, 32)));
+  uint64_t* depth_pairs = (uint64_t*)f->depth_pairs.ptr;
+  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, nullptr, depth_pairs, tile_mask));
+  // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and
+  //    sink); packed (depth << 32 | index) words, split into keys and order
+  if (n > 0) {
+    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed(n, 32, 64)));
     StageScope sc(ctx, GSC_STAGE_SORT);
-    sc.kernels(1 + 4);
-    GS_TRY(launch_sort_pairs_u32(ctx, depth_keys, order, n, 0, 32, scratch_base(ctx)));
+    sc.kernels(n > 1 ? 1 + 4 : 1);
+    GS_TRY(launch_sort_packed(ctx, depth_pairs, n, 32, 64, depth_keys, order, scratch_base(ctx)));
   }
   // 2. exact allocation in depth order, then emission of (tile, id)
   {
@@ -572,20 +575,21 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   uint32_t* tiles = (uint32_t*)f->tiles.ptr;
   uint32_t* vals = (uint32_t*)f->vals.ptr;
   if (m) {
+    GS_TRY(ensure(ctx, &f->pairs, (size_t)m * 8 + 8));
+    uint64_t* pairs = (uint64_t*)f->pairs.ptr;
     {
       StageScope sc(ctx, GSC_STAGE_EMIT);
       sc.kernels(1);
-      GS_TRY(launch_emit_tiles(splats, order, n, (const uint64_t*)f->offsets.ptr, tx, ty, tile_mask, tiles,
-                               vals, ctx->stream));
+      GS_TRY(launch_emit_tiles(splats, order, n, (const uint64_t*)f->offsets.ptr, tx, ty, tile_mask, pairs,
+                               ctx->stream));
     }
-    // 3. stable sort by tile bits only
+    // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
+    //    only, split into tiles and values
     const int tb = tile_bits_of(tx * ty);
-    if (tb > 0) {
-      GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_u32((int64_t)m, 0, tb)));
-      StageScope sc(ctx, GSC_STAGE_SORT);
-      sc.kernels(1 + (tb + 7) / 8);
-      GS_TRY(launch_sort_pairs_u32(ctx, tiles, vals, (int64_t)m, 0, tb, scratch_base(ctx)));
-    }
+    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed((int64_t)m, 32, 32 + tb)));
+    StageScope sc(ctx, GSC_STAGE_SORT);
+    sc.kernels(tb > 0 && m > 1 ? 1 + (tb + 7) / 8 : 1);
+    GS_TRY(launch_sort_packed(ctx, pairs, (int64_t)m, 32, 32 + tb, tiles, vals, scratch_base(ctx)));
   }
   {
     StageScope sc(ctx, GSC_STAGE_RANGES);

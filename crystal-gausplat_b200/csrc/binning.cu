@@ -209,8 +209,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
                                                          const uint64_t* __restrict__ offsets,
                                                          int tiles_x, int tiles_y,
                                                          const uint64_t* __restrict__ tile_mask,
-                                                         uint32_t* __restrict__ tile_out,
-                                                         uint32_t* __restrict__ id_out) {
+                                                         uint64_t* __restrict__ pair_out) {
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
   __shared__ uint32_t s_inv[256];  // ceil(2^16 / width): row of a test < 64 by multiply and shift
@@ -258,8 +257,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
     }
     const int ty = s_y0[own] + (int)ry;
     const int tx = s_x0[own] + (int)(local - ry * wx);
-    tile_out[out + k] = (uint32_t)(ty * tiles_x + tx);
-    id_out[out + k] = s_id[own];
+    pair_out[out + k] = ((uint64_t)(uint32_t)(ty * tiles_x + tx) << 32) | (uint64_t)s_id[own];
   }
 }
 
@@ -307,11 +305,11 @@ int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t
 }
 
 int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint32_t* tile_out, uint32_t* id_out,
+                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint64_t* pair_out,
                       cudaStream_t stream) {
   if (n == 0) return GSC_OK;
   emit_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const float4*>(splats), order, n, offsets, tiles_x, tiles_y, tile_mask, tile_out, id_out);
+      reinterpret_cast<const float4*>(splats), order, n, offsets, tiles_x, tiles_y, tile_mask, pair_out);
   GS_CK_LAUNCH("emit_tiles_kernel");
   return GSC_OK;
 }

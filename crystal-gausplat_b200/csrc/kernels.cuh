@@ -15,8 +15,7 @@ struct PreprocessArgs {
   gsc_raster_config cfg;
   int tiles_x, tiles_y;
   float* splats;
-  uint32_t* depth_keys;  // bits(depth) if the Gaussian emits keys, else ~0; may be null
-  uint32_t* order;       // identity permutation (input of the depth sort); may be null
+  uint64_t* depth_pairs;  // bits(depth) (~0 if the Gaussian emits no pair) << 32 | index; may be null
   float* mean2d;
   float* cov2d;
   float* conic;
@@ -114,7 +113,7 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t n, uint32_t* sums,
                              cudaStream_t stream);
 int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint32_t* tile_out, uint32_t* id_out,
+                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint64_t* pair_out,
                       cudaStream_t stream);
 int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
                            cudaStream_t stream);
@@ -124,6 +123,12 @@ size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit);
 int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                       int end_bit, char* scratch);
 size_t sort_scratch_bytes_u32(int64_t n, int begin_bit, int end_bit);
+// Stable sort of packed u64 (key << 32 | value) by bits [begin_bit, end_bit) of
+// the u64 (within the key word); the sorted words go to hi_out / lo_out.
+// `pairs` is overwritten.
+size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit);
+int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
+                       uint32_t* lo_out, char* scratch);
 int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                           int end_bit, char* scratch);
 int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream);

@@ -158,10 +158,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
   }
   if (i < n) {
     reinterpret_cast<float4*>(a.splats)[i * 3 + 2] = make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
-    if (a.depth_keys) {
-      a.depth_keys[i] = emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu;
-      a.order[i] = (uint32_t)i;
-    }
+    if (a.depth_pairs)
+      a.depth_pairs[i] = ((uint64_t)(emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu) << 32) | (uint64_t)i;
   }
 }
 

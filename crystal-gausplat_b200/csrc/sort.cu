@@ -14,6 +14,11 @@
 //      word and never writes out of bounds), reorders the tile in shared
 //      memory and scatters keys then values with coalesced runs.
 // Traffic per pair: 8 B (histogram) + 24 B per pass.
+//
+// Packed mode (the whole-view binning): a pair travels as one u64, key in the
+// high word and value in the low word, sorted by key bits only; scatter runs
+// are then twice as long and there is no value phase. The last pass writes
+// the two words to separate arrays.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -71,12 +76,14 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
   return x - v + add;
 }
 
-template <typename K>
+// MODE: 0 = (key, value) pairs; 1 = packed u64, written packed; 2 = packed
+// u64, written split (high word to keys_hi, low word to vals_out).
+template <typename K, int MODE = 0>
 __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
-    uint32_t* err) {
+    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr) {
   __shared__ K s_keys[kTileKeys];  // reused for values
   __shared__ uint32_t s_whist[kWarps][256];
   __shared__ uint32_t s_local_excl[256];
@@ -104,16 +111,27 @@ __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
     const int64_t idx = warp_base + i * 32 + lane;
-    // Pairs past the end take the largest digit, so they sort behind every
-    // valid pair of the tile.
-    const uint32_t d = idx < n ? ((uint32_t)(keys_in[idx] >> shift) & digit_mask) : 255u;
+    // Pairs past the end take the largest digit (and come last in index
+    // order), so they sort behind every valid pair of the tile.
+    const uint32_t d = idx < n ? ((uint32_t)(keys_in[idx] >> shift) & digit_mask) : digit_mask;
     dig[i / 4] |= d << (8 * (i % 4));
   }
   const uint32_t lt_mask = (1u << lane) - 1u;
+  const int nbits = 32 - __clz(digit_mask);  // digit width (padding digits 255 agree on these bits)
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
     const uint32_t d = (dig[i / 4] >> (8 * (i % 4))) & 255u;
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    // Lanes holding the same digit: AND of one ballot per digit bit (constant
+    // cost, whatever the number of distinct digits in the warp).
+    uint32_t peers = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+      if (b < nbits) {
+        const bool bit = (d >> b) & 1u;
+        const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+        peers &= bit ? bal : ~bal;
+      }
+    }
     const int leader = __ffs(peers) - 1;
     uint32_t b = 0;
     if (lane == leader) b = atomicAdd(&s_whist[w][d], (uint32_t)__popc(peers));
@@ -131,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
     s_whist[ww][d] = cnt;
     cnt += c;
   }
-  const uint32_t valid_cnt = d == 255u ? cnt - (kTileKeys - num_valid) : cnt;
+  const uint32_t valid_cnt = d == digit_mask ? cnt - (kTileKeys - num_valid) : cnt;
   const uint32_t local_excl = block_excl_scan_256(cnt, s_warp);
   const uint32_t gexcl = block_excl_scan_256(hist[d], s_warp);
   s_local_excl[d] = local_excl;
@@ -177,11 +195,18 @@ __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
   for (uint32_t j = tid; j < num_valid; j += kThreads) {
     const K key = s_keys[j];
     const uint32_t dd = (uint32_t)(key >> shift) & digit_mask;
-    s_dig[j] = (uint8_t)dd;
     const uint32_t gpos = s_gbase[dd] + j;
-    if ((int64_t)gpos < n) keys_out[gpos] = key;
-    else atomicOr(err, GS_DEVERR_BOUNDS);
+    if (MODE == 0) s_dig[j] = (uint8_t)dd;
+    if ((int64_t)gpos >= n) {
+      atomicOr(err, GS_DEVERR_BOUNDS);
+    } else if (MODE == 2) {
+      keys_hi[gpos] = (uint32_t)((uint64_t)key >> 32);
+      vals_out[gpos] = (uint32_t)key;
+    } else {
+      keys_out[gpos] = key;
+    }
   }
+  if (MODE != 0) return;
   __syncthreads();
   uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys);
 #pragma unroll
@@ -262,6 +287,61 @@ int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, i
 int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                           int end_bit, char* scratch) {
   return sort_pairs_t<uint32_t>(ctx, keys, vals, n, begin_bit, end_bit, scratch);
+}
+
+__global__ void __launch_bounds__(256) split_words_kernel(const uint64_t* __restrict__ in, int64_t n,
+                                                          uint32_t* __restrict__ hi, uint32_t* __restrict__ lo) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t v = in[i];
+  hi[i] = (uint32_t)(v >> 32);
+  lo[i] = (uint32_t)v;
+}
+
+size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit) {
+  return sort_scratch_bytes_t<uint64_t>(n, begin_bit, end_bit);
+}
+
+int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
+                       uint32_t* lo_out, char* scratch) {
+  cudaStream_t stream = ctx->stream;
+  if (n <= 0) return GSC_OK;
+  const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
+  if (n == 1 || npass == 0) {
+    split_words_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(pairs, n, hi_out, lo_out);
+    GS_CK_LAUNCH("split_words_kernel");
+    return GSC_OK;
+  }
+  const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
+  uint64_t* alt = reinterpret_cast<uint64_t*>(scratch);
+  scratch += align256((size_t)n * 8) + align256((size_t)n * 4);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(scratch);
+  uint32_t* status = hist + npass * 256;
+  uint32_t* tickets = status + (size_t)npass * parts * 256;
+  const size_t meta = (size_t)npass * 256 * 4 + (size_t)npass * parts * 256 * 4 + (size_t)npass * 4;
+  GS_CK(cudaMemsetAsync(hist, 0, meta, stream));
+  const int64_t hblocks = min((int64_t)ctx->num_sms * 8, (n + 4095) / 4096);
+  histogram_kernel<uint64_t><<<(unsigned)max((int64_t)1, hblocks), 256, 0, stream>>>(pairs, n, begin_bit, end_bit,
+                                                                                    npass, hist);
+  GS_CK_LAUNCH("histogram_kernel");
+  uint64_t* src = pairs;
+  uint64_t* dst = alt;
+  for (int p = 0; p < npass; p++) {
+    const int shift = begin_bit + 8 * p;
+    const int bits = min(8, end_bit - shift);
+    if (p + 1 < npass) {
+      onesweep_kernel<uint64_t, 1><<<(unsigned)parts, kThreads, 0, stream>>>(
+          src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + p * 256,
+          status + (size_t)p * parts * 256, tickets + p, ctx->err);
+    } else {
+      onesweep_kernel<uint64_t, 2><<<(unsigned)parts, kThreads, 0, stream>>>(
+          src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + p * 256,
+          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out);
+    }
+    GS_CK_LAUNCH("onesweep_kernel");
+    std::swap(src, dst);
+  }
+  return GSC_OK;
 }
 
 }  // namespace gs
