@@ -231,7 +231,8 @@ def pge_count(gs, rctx):
 TRAFFIC_C3 = {"composite_fwd": 83.75e6, "composite_bwd": 146.49e6}
 
 PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
-PREPROCESS_BWD_B = 556  # read 236 params + 36 grad2d, read+write 236 grads (visible Gaussians)
+PARAM_ROW_B = 236  # the 59 floats of one Gaussian
+GRAD2D_B = 36      # screen-space gradient row of one view
 ADAM_B = 28 * 59        # read p, g, m, v + write p, m, v per float
 FWD_FLOP_PER_PGE = 15
 BWD_FLOP_PER_PGE = 30
@@ -243,23 +244,30 @@ def sort_bytes_per_pair(end_bit, key_bytes=8):
     return key_bytes + 2 * (key_bytes + 4) * passes
 
 
-def stage_work(stats, n, keys_per_view, pge, tiles, end_bit):
+def packed_sort_bytes(bits):
+    """Packed (key << 32 | value) u64 words: histogram read + read and write per pass."""
+    return 8 + 16 * ((bits + 7) // 8)
+
+
+def stage_work(stats, n, keys_per_view, pge, tiles, end_bit, batch=1):
     """Algorithmic work of each stage for ONE view: (bound, bytes or flops, stage calls per view).
 
     Binning of a view = a stable 32-bit depth sort of the N Gaussians (4 passes),
-    a gather-scan and emission of (tile u32, id u32) pairs in depth order, and a
-    stable sort of those pairs by the tile bits (end_bit - 32 bits)."""
+    a gather-scan and emission of packed (tile << 32 | id) words in depth order,
+    and a stable sort of those words by the tile bits (end_bit - 32 bits). The
+    preprocess backward runs once per `batch` views: parameters read once,
+    gradient rows read and written once, one grad2d row per view."""
     tb = end_bit - 32
     m = keys_per_view
     return {
         "preprocess": ("hbm", PREPROCESS_B * n, 1),
         "scan": ("hbm", 4 * n + 16 * n, 2),  # order gather + splat word, then the block-sum scan
-        "emit": ("hbm", (4 + 32) * n + 8 * m, 1),
-        "sort": ("hbm", sort_bytes_per_pair(32, 4) * n + sort_bytes_per_pair(tb, 4) * m, 2),
+        "emit": ("hbm", (4 + 32 + 8) * n + 8 * m, 1),  # order, record words, tile mask; packed pairs
+        "sort": ("hbm", packed_sort_bytes(32) * n + packed_sort_bytes(tb) * m, 2),
         "ranges": ("hbm", 4 * m + 8 * tiles, 1),
         "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge, 1),
         "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge, 1),
-        "preprocess_bwd": ("hbm", PREPROCESS_BWD_B * n, 1),
+        "preprocess_bwd": ("hbm", (3 * PARAM_ROW_B / batch + GRAD2D_B) * n, 1.0 / batch),
         "adam": ("hbm", ADAM_B * n, 1),
     }
 
@@ -366,7 +374,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
                 tr.zero()
                 for v in tr.my_views:
                     tr.view_fwd_bwd(v, targets(v))
-                    keys_total += tr.ctx.num_rendered
+                    keys_total += tr.last_ctx.num_rendered
                 tr.reduce_and_step()
     lib.gsc_profile_enable(ctx, 0)
     ms = tm.max_over_ranks()
@@ -380,7 +388,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     keys_per_view = keys_total / (args.steps * my_views)
     tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
-    work = stage_work(stats, cfg["n"], keys_per_view, pge, tiles, end_bit)
+    work = stage_work(stats, cfg["n"], keys_per_view, pge, tiles, end_bit, batch=tr.batch)
     roof = rooflines(stats, work, peaks)
 
     e2e = None
@@ -414,6 +422,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
                                    f"{cfg['W']}x{cfg['H']}, L1, all-reduce + fused Adam",
                        "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
                        "exchange": tr.exchange, "binning": args.binning,
+                       "backward_batch_views": tr.batch,
                        "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush",
                        "keys_per_view": round(keys_per_view), "pge_per_view": round(pge)},
             "gpu_launches": launches,

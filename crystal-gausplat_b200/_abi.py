@@ -23,6 +23,8 @@ GSC_ERR_UNSUPPORTED = -7
 GSC_MODE_FULL = 0
 GSC_MODE_REF = 1
 
+GSC_MAX_BATCH_VIEWS = 8
+
 GSC_BIN_REFERENCE = 0
 GSC_BIN_CONTRIBUTING = 1
 
@@ -152,6 +154,9 @@ _SIGS = {
     "gsc_rasterize_backward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),
                                          C.POINTER(RasterConfig), P, P, C.c_float, P,
                                          C.POINTER(GaussianGrads), C.POINTER(Grads2D)]),
+    "gsc_rasterize_backward_batch": (C.c_int, [P, C.POINTER(P), C.POINTER(Camera), C.c_int32,
+                                               C.POINTER(Gaussians), C.POINTER(RasterConfig),
+                                               C.POINTER(GaussianGrads)]),
     "gsc_frame_get": (C.c_int, [P, C.c_int, C.POINTER(P), C.POINTER(C.c_int64)]),
     "gsc_profile_enable": (C.c_int, [P, C.c_int]),
     "gsc_profile_read": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_int64),

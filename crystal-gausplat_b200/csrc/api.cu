@@ -80,6 +80,7 @@ struct gsc_frame {
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
   float* image_ptr = nullptr;  // image the last forward wrote (caller's or frame's)
   bool has_forward = false;
+  bool has_grad2d = false;  // a backward left grad2d for this forward
 };
 
 extern "C" {
@@ -306,6 +307,9 @@ static int do_preprocess_bwd(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_cam
   a.logit_opacity = g->logit_opacity; a.sh = g->sh;
   a.cam = *cam; a.cfg = *cfg;
   a.grad2d = grad2d;
+  a.nviews = 1;
+  a.cams[0] = *cam;
+  a.grad2d_v[0] = grad2d;
   a.g_pos = gr->position; a.g_log_scale = gr->log_scale; a.g_rot = gr->rotation;
   a.g_logit_opacity = gr->logit_opacity; a.g_sh = gr->sh;
   if (g2d) {
@@ -516,6 +520,7 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   const int64_t nb = (n + 255) / 256;
   const size_t npix = (size_t)W * H;
   f->has_forward = false;
+  f->has_grad2d = false;
   f->n = n; f->width = W; f->height = H; f->tiles_x = tx; f->tiles_y = ty;
   GS_TRY(ensure(ctx, &f->splats, (size_t)n * 48 + 48));
   GS_TRY(ensure(ctx, &f->depth_pairs, (size_t)n * 8 + 8));
@@ -625,7 +630,7 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussia
   GS_REQUIRE(f->has_forward, "gsc_rasterize_backward: no forward on this frame");
   GS_TRY(check_gaussians(g));
   GS_TRY(check_view(cam, cfg));
-  GS_TRY(check_grads(grads));
+  if (grads) GS_TRY(check_grads(grads));  // NULL: stop after the composite backward
   GS_REQUIRE(g->count == f->n && cam->width == f->width && cam->height == f->height,
              "gsc_rasterize_backward: gaussians/camera differ from the frame's forward");
   GS_REQUIRE((dL_dimage != nullptr) != (target != nullptr),
@@ -650,7 +655,48 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussia
     sc.kernels(1);
     GS_TRY(launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream));
   }
+  f->has_grad2d = true;
+  if (!grads) return GSC_OK;
   return do_preprocess_bwd(ctx, g, cam, cfg, grad2d, grads, g2d);
+}
+
+GSC_API int gsc_rasterize_backward_batch(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams,
+                                         int32_t nviews, const gsc_gaussians* g,
+                                         const gsc_raster_config* cfg, const gsc_gaussian_grads* grads) {
+  GS_REQUIRE(ctx && frames && cams, "gsc_rasterize_backward_batch: null argument");
+  GS_REQUIRE(nviews >= 1 && nviews <= GSC_MAX_BATCH_VIEWS, "gsc_rasterize_backward_batch: nviews out of range");
+  GS_TRY(check_gaussians(g));
+  GS_TRY(check_grads(grads));
+  for (int v = 0; v < nviews; v++) {
+    const gsc_frame* f = frames[v];
+    GS_REQUIRE(f && f->ctx == ctx && f->has_grad2d, "gsc_rasterize_backward_batch: frame without a backward");
+    GS_TRY(check_view(&cams[v], cfg));
+    GS_REQUIRE(f->n == g->count && cams[v].width == f->width && cams[v].height == f->height,
+               "gsc_rasterize_backward_batch: gaussians/camera differ from the frame's forward");
+  }
+  if (cfg->mode != GSC_MODE_FULL) {  // the reference's per-view host loops
+    for (int v = 0; v < nviews; v++)
+      GS_TRY(do_preprocess_bwd(ctx, g, &cams[v], cfg, (const float*)frames[v]->grad2d.ptr, grads, nullptr));
+    return GSC_OK;
+  }
+  PreprocessBwdArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.n = g->count;
+  a.pos = g->position; a.log_scale = g->log_scale; a.rot = g->rotation;
+  a.logit_opacity = g->logit_opacity; a.sh = g->sh;
+  a.cfg = *cfg;
+  a.cam = cams[0];
+  a.grad2d = (const float*)frames[0]->grad2d.ptr;
+  a.nviews = nviews;
+  for (int v = 0; v < nviews; v++) {
+    a.cams[v] = cams[v];
+    a.grad2d_v[v] = (const float*)frames[v]->grad2d.ptr;
+  }
+  a.g_pos = grads->position; a.g_log_scale = grads->log_scale; a.g_rot = grads->rotation;
+  a.g_logit_opacity = grads->logit_opacity; a.g_sh = grads->sh;
+  StageScope sc(ctx, GSC_STAGE_PREPROCESS_BWD);
+  sc.kernels(g->count ? 1 : 0);
+  return launch_preprocess_bwd(a, true, ctx->stream);
 }
 
 GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {

@@ -60,6 +60,8 @@ struct CompositeBwdArgs {
   float* loss_sum;
 };
 
+constexpr int kMaxBatchViews = GSC_MAX_BATCH_VIEWS;
+
 struct PreprocessBwdArgs {
   int64_t n;
   const float* pos;
@@ -79,6 +81,10 @@ struct PreprocessBwdArgs {
   float* d_cov2d;
   float* d_opacity;
   float* d_colors;
+  // FULL mode: views summed by one launch (cam / grad2d above are view 0)
+  int nviews;
+  const float* grad2d_v[kMaxBatchViews];
+  gsc_camera cams[kMaxBatchViews];
 };
 
 constexpr int kMaxAdamGroups = 8;

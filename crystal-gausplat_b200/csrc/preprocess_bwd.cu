@@ -72,42 +72,48 @@ __device__ __forceinline__ void unstage_rows(const float4* s4, float* g, int64_t
   for (int k = threadIdx.x; k < cnt * 12; k += kPbThreads) dst[k] = s4[(k / 12) * kRowF4 + k % 12];
 }
 
+// One Gaussian per thread, `nviews` views (camera + grad2d each) per launch.
+// The camera-independent terms (scales, rotation, 3-D covariance) are formed
+// once; per view the position gradient and the symmetric covariance gradient
+// dSigma are summed (the scale and rotation gradients are linear in dSigma),
+// the SH gradient goes straight into the staged gradient row, and every
+// gradient row is read and written once per launch. Dynamic shared memory:
+// the SH rows and the SH-gradient rows of the block.
 __global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(PreprocessBwdArgs a) {
-  __shared__ float4 s4[kPbThreads * kRowF4];
+  extern __shared__ float4 s_dyn[];
+  float4* s_par = s_dyn;                         // SH rows
+  float4* s_grd = s_dyn + kPbThreads * kRowF4;   // SH-gradient rows
   const int64_t base = (int64_t)blockIdx.x * kPbThreads;
   const int64_t i = base + threadIdx.x;
   const int cnt = (int)min((int64_t)kPbThreads, a.n - base);
   const bool valid = i < a.n;
-  const gsc_camera& cam = a.cam;
   const gsc_raster_config& cfg = a.cfg;
-  const float* W = cam.view;
-  const float fx = cam.fx, fy = cam.fy;
-  float gv[9];
+  const int nv = a.nviews;
+  bool any = false;
+  for (int v = 0; v < nv; v++) {
+    if (!valid) break;
+    const float* gv = a.grad2d_v[v] + i * 9;
 #pragma unroll
-  for (int k = 0; k < 9; k++) gv[k] = valid ? a.grad2d[i * 9 + k] : 0.0f;
-  const float dmx = gv[0], dmy = gv[1], dA = gv[2], dB = gv[3], dC = gv[4], dop = gv[5];
-  const float dcol[3] = {gv[6], gv[7], gv[8]};
-  if (valid) {
-    if (a.d_mean2d) { a.d_mean2d[i * 2] = dmx; a.d_mean2d[i * 2 + 1] = dmy; }
-    if (a.d_opacity) a.d_opacity[i] = dop;
-    if (a.d_colors) { a.d_colors[i * 3] = dcol[0]; a.d_colors[i * 3 + 1] = dcol[1]; a.d_colors[i * 3 + 2] = dcol[2]; }
+    for (int k = 0; k < 9; k++) any = any || gv[k] != 0.0f;
+  }
+  if (valid && nv == 1) {  // screen-space views of a single-view call
+    const float* gv = a.grad2d_v[0] + i * 9;
+    if (a.d_mean2d) { a.d_mean2d[i * 2] = gv[0]; a.d_mean2d[i * 2 + 1] = gv[1]; }
+    if (a.d_opacity) a.d_opacity[i] = gv[5];
+    if (a.d_colors) { a.d_colors[i * 3] = gv[6]; a.d_colors[i * 3 + 1] = gv[7]; a.d_colors[i * 3 + 2] = gv[8]; }
     if (a.d_cov2d) { a.d_cov2d[i * 3] = 0.0f; a.d_cov2d[i * 3 + 1] = 0.0f; a.d_cov2d[i * 3 + 2] = 0.0f; }
   }
-  bool any = false;
-#pragma unroll
-  for (int k = 0; k < 9; k++) any = any || gv[k] != 0.0f;
   // every term below is linear in grad2d: blocks without gradients are done
   if (!__syncthreads_or(any)) return;
-  stage_rows(s4, a.sh, base, cnt);
+  stage_rows(s_par, a.sh, base, cnt);
+  stage_rows(s_grd, a.g_sh, base, cnt);
   __syncthreads();
 
-  float b[16];
-  float w[3] = {0.0f, 0.0f, 0.0f};
-  int ncoef = 0;
   if (any) {
+    const float* row = reinterpret_cast<const float*>(s_par + threadIdx.x * kRowF4);
+    float* grow = reinterpret_cast<float*>(s_grd + threadIdx.x * kRowF4);
     const float p[3] = {a.pos[i * 3], a.pos[i * 3 + 1], a.pos[i * 3 + 2]};
     const float o = gs_sigmoid(a.logit_opacity[i]);
-    a.g_logit_opacity[i] += dop * o * (1.0f - o);
     const float s[3] = {gs_expf(a.log_scale[i * 3]), gs_expf(a.log_scale[i * 3 + 1]),
                         gs_expf(a.log_scale[i * 3 + 2])};
     const float4 q4 = reinterpret_cast<const float4*>(a.rot)[i];
@@ -117,23 +123,36 @@ __global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(Preproc
     quat_to_R(q[0], q[1], q[2], q[3], R);
     float c3[6];
     cov3d_of(s, R, c3);
-    Projected pr;
-    project(p, c3, cam, cfg, &pr);
-    any = pr.visible;
-    if (any) {
-      float dp[3] = {0.0f, 0.0f, 0.0f};
-      // ---- colour -> view direction (SH rows from shared memory) ----
+    const int ncoef = (cfg.sh_degree + 1) * (cfg.sh_degree + 1);
+    float dop = 0.0f;
+    float dp[3] = {0.0f, 0.0f, 0.0f};
+    float dS[3][3] = {{0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f}};
+    bool visible_any = false;
+    for (int v = 0; v < nv; v++) {
+      const float* gv = a.grad2d_v[v] + i * 9;
+      const float dmx = gv[0], dmy = gv[1], dA = gv[2], dB = gv[3], dC = gv[4];
+      const float dcol[3] = {gv[6], gv[7], gv[8]};
+      dop += gv[5];
+      const gsc_camera& cam = a.cams[v];
+      const float* W = cam.view;
+      const float fx = cam.fx, fy = cam.fy;
+      Projected pr;
+      project(p, c3, cam, cfg, &pr);
+      if (!pr.visible) continue;
+      visible_any = true;
+      float vdp[3] = {0.0f, 0.0f, 0.0f};
+      // ---- colour -> view direction and SH coefficients ----
       {
-        const float* row = reinterpret_cast<const float*>(s4 + threadIdx.x * kRowF4);
+        float b[16];
         float d[3], len;
         view_dir(p, cam, d, &len);
         sh_basis_hi(d[0], d[1], d[2], b);
         float raw[3];
         sh_eval([&](int k) { return row[k]; }, d[0], d[1], d[2], b, cfg.sh_degree, cfg.mode, raw);
         const float x = d[0], y = d[1], z = d[2];
-        ncoef = (cfg.sh_degree + 1) * (cfg.sh_degree + 1);
         b[0] = kShC0;
         b[1] = kShC1 * -y; b[2] = kShC1 * z; b[3] = kShC1 * -x;
+        float w[3];
 #pragma unroll
         for (int c = 0; c < 3; c++) w[c] = raw[c] + 0.5f > 0.0f ? dcol[c] : 0.0f;
         float DX[16], DY[16], DZ[16];
@@ -148,9 +167,16 @@ __global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(Preproc
           gz += t * DZ[k];
         }
         const float dd = x * gx + y * gy + z * gz;
-        dp[0] -= (gx - x * dd) / len;
-        dp[1] -= (gy - y * dd) / len;
-        dp[2] -= (gz - z * dd) / len;
+        vdp[0] -= (gx - x * dd) / len;
+        vdp[1] -= (gy - y * dd) / len;
+        vdp[2] -= (gz - z * dd) / len;
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+          if (w[c] == 0.0f) continue;
+#pragma unroll
+          for (int k = 0; k < 16; k++)
+            if (k < ncoef) grow[k * 3 + c] += b[k] * w[c];
+        }
       }
       // ---- conic -> cov2d ----
       float da = 0.0f, db = 0.0f, dc2 = 0.0f;
@@ -163,25 +189,25 @@ __global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(Preproc
         db = -2.0f * P01;
         dc2 = -P11;
       }
-      if (a.d_cov2d) { a.d_cov2d[i * 3] = da; a.d_cov2d[i * 3 + 1] = db; a.d_cov2d[i * 3 + 2] = dc2; }
+      if (a.d_cov2d && nv == 1) { a.d_cov2d[i * 3] = da; a.d_cov2d[i * 3 + 1] = db; a.d_cov2d[i * 3 + 2] = dc2; }
 
       // ---- cov2d = J C J^T ----
       const float Jm[2][3] = {{pr.J00, 0.0f, pr.J02}, {0.0f, pr.J11, pr.J12}};
       const float Gc[2][2] = {{da, 0.5f * db}, {0.5f * db, dc2}};
       float GJ[2][3];
-    #pragma unroll
+#pragma unroll
       for (int r = 0; r < 2; r++)
-    #pragma unroll
+#pragma unroll
         for (int k = 0; k < 3; k++) GJ[r][k] = Gc[r][0] * Jm[0][k] + Gc[r][1] * Jm[1][k];
       float dCm[3][3];
-    #pragma unroll
+#pragma unroll
       for (int k = 0; k < 3; k++)
-    #pragma unroll
+#pragma unroll
         for (int l = 0; l < 3; l++) dCm[k][l] = Jm[0][k] * GJ[0][l] + Jm[1][k] * GJ[1][l];
       float dJ[2][3];
-    #pragma unroll
+#pragma unroll
       for (int r = 0; r < 2; r++)
-    #pragma unroll
+#pragma unroll
         for (int k = 0; k < 3; k++)
           dJ[r][k] = 2.0f * (GJ[r][0] * sym3(pr.C, 0, k) + GJ[r][1] * sym3(pr.C, 1, k) + GJ[r][2] * sym3(pr.C, 2, k));
       const float xc = pr.xc, yc = pr.yc, zc = pr.zc;
@@ -194,40 +220,41 @@ __global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(Preproc
       dyc += dmy * fy / zc;
       dzc += -(dmx * fx * xc + dmy * fy * yc) / z2;
       const float V[3][3] = {{W[0], W[1], W[2]}, {W[4], W[5], W[6]}, {W[8], W[9], W[10]}};
-    #pragma unroll
-      for (int j = 0; j < 3; j++) dp[j] += V[0][j] * dxc + V[1][j] * dyc + V[2][j] * dzc;
-    #pragma unroll
-      for (int j = 0; j < 3; j++) a.g_pos[i * 3 + j] += dp[j];
+#pragma unroll
+      for (int j = 0; j < 3; j++) dp[j] += vdp[j] + (V[0][j] * dxc + V[1][j] * dyc + V[2][j] * dzc);
 
       // ---- C = V Sigma V^T -> Sigma ----
       float VtD[3][3];
-    #pragma unroll
+#pragma unroll
       for (int r = 0; r < 3; r++)
-    #pragma unroll
+#pragma unroll
         for (int l = 0; l < 3; l++) VtD[r][l] = V[0][r] * dCm[0][l] + V[1][r] * dCm[1][l] + V[2][r] * dCm[2][l];
-      float dS[3][3];
-    #pragma unroll
+#pragma unroll
       for (int r = 0; r < 3; r++)
-    #pragma unroll
-        for (int c = 0; c < 3; c++) dS[r][c] = VtD[r][0] * V[0][c] + VtD[r][1] * V[1][c] + VtD[r][2] * V[2][c];
-
+#pragma unroll
+        for (int c = 0; c < 3; c++) dS[r][c] += VtD[r][0] * V[0][c] + VtD[r][1] * V[1][c] + VtD[r][2] * V[2][c];
+    }
+    a.g_logit_opacity[i] += dop * o * (1.0f - o);
+    if (visible_any) {
+#pragma unroll
+      for (int j = 0; j < 3; j++) a.g_pos[i * 3 + j] += dp[j];
       // ---- Sigma = M M^T, M = R diag(s) ----
       float M[3][3];
-    #pragma unroll
+#pragma unroll
       for (int r = 0; r < 3; r++)
-    #pragma unroll
+#pragma unroll
         for (int j = 0; j < 3; j++) M[r][j] = R[r][j] * s[j];
       float dM[3][3];
-    #pragma unroll
+#pragma unroll
       for (int r = 0; r < 3; r++)
-    #pragma unroll
+#pragma unroll
         for (int j = 0; j < 3; j++) dM[r][j] = 2.0f * (dS[r][0] * M[0][j] + dS[r][1] * M[1][j] + dS[r][2] * M[2][j]);
       float dR[3][3];
-    #pragma unroll
+#pragma unroll
       for (int j = 0; j < 3; j++) {
         const float ds = dM[0][j] * R[0][j] + dM[1][j] * R[1][j] + dM[2][j] * R[2][j];
         a.g_log_scale[i * 3 + j] += ds * s[j];
-    #pragma unroll
+#pragma unroll
         for (int r = 0; r < 3; r++) dR[r][j] = dM[r][j] * s[j];
       }
 
@@ -249,28 +276,26 @@ __global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(Preproc
       }
     }
   }
-  // ---- SH coefficients: read-modify-write of the block's gradient rows ----
   __syncthreads();
-  stage_rows(s4, a.g_sh, base, cnt);
-  __syncthreads();
-  if (any) {
-    float* row = reinterpret_cast<float*>(s4 + threadIdx.x * kRowF4);
-#pragma unroll
-    for (int c = 0; c < 3; c++) {
-      if (w[c] == 0.0f) continue;
-#pragma unroll
-      for (int k = 0; k < 16; k++)
-        if (k < ncoef) row[k * 3 + c] += b[k] * w[c];
-    }
-  }
-  __syncthreads();
-  unstage_rows(s4, a.g_sh, base, cnt);
+  unstage_rows(s_grd, a.g_sh, base, cnt);
 }
+
+constexpr size_t kPbSmem = 2 * (size_t)kPbThreads * kRowF4 * sizeof(float4);
 
 int launch_preprocess_bwd(const PreprocessBwdArgs& a, bool full, cudaStream_t stream) {
   if (a.n == 0) return GSC_OK;
   const unsigned blocks = (unsigned)((a.n + 127) / 128);
-  if (full) preprocess_bwd_full_kernel<<<blocks, kPbThreads, 0, stream>>>(a);
+  if (full) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    GS_CK(cudaGetDevice(&dev));
+    if (dev < 64 && !attr_set[dev]) {
+      GS_CK(cudaFuncSetAttribute(preprocess_bwd_full_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kPbSmem));
+      attr_set[dev] = true;
+    }
+    preprocess_bwd_full_kernel<<<blocks, kPbThreads, kPbSmem, stream>>>(a);
+  }
   else preprocess_bwd_ref_kernel<<<blocks, 128, 0, stream>>>(a);
   GS_CK_LAUNCH("preprocess_bwd_kernel");
   return GSC_OK;

@@ -165,22 +165,45 @@ class Rasterizer:
 
     @staticmethod
     def backward(dL_dimage, gaussians, camera, context, grads=None, target=None, l1_scale=None,
-                 loss_sum=None, config=None):
+                 loss_sum=None, config=None, defer=False):
         """Gradients for the last forward on `context`. With `target`, the pixel
         gradient is the fused L1 gradient sign(image - target) * l1_scale
-        (default 1/numel, Loss.l1_with_grad) and dL_dimage must be None."""
+        (default 1/numel, Loss.l1_with_grad) and dL_dimage must be None.
+        defer=True stops after the compositing backward (screen-space
+        gradients stay in the context) for a later Rasterizer.backward_batch."""
         cfg = config or context.config
-        grads = grads if grads is not None else RasterizerGradients(gaussians)
         if target is not None and l1_scale is None:
             l1_scale = 1.0 / target.numel()
         g = gaussians_struct(gaussians)
         cam = camera.to_struct()
+        if defer:
+            check(lib().gsc_rasterize_backward(
+                context.ctx, context.frame, C.byref(g), C.byref(cam), C.byref(cfg), ptr(dL_dimage),
+                ptr(target), C.c_float(l1_scale or 0.0), ptr(loss_sum), None, None),
+                "gsc_rasterize_backward")
+            return None
+        grads = grads if grads is not None else RasterizerGradients(gaussians)
         gs = grads.struct()
         g2d = grads.screen_struct()
         check(lib().gsc_rasterize_backward(
             context.ctx, context.frame, C.byref(g), C.byref(cam), C.byref(cfg), ptr(dL_dimage),
             ptr(target), C.c_float(l1_scale or 0.0), ptr(loss_sum), C.byref(gs),
             C.byref(g2d) if g2d is not None else None), "gsc_rasterize_backward")
+        return grads
+
+    @staticmethod
+    def backward_batch(contexts, gaussians, cameras, grads, config=None):
+        """Parameter gradients of up to GSC_MAX_BATCH_VIEWS deferred backwards
+        (one context and camera per view), summed into `grads` in one pass."""
+        k = len(contexts)
+        cfg = config or contexts[0].config
+        frames = (C.c_void_p * k)(*[c.frame.value for c in contexts])
+        cams = (_abi.Camera * k)(*[c.to_struct() for c in cameras])
+        g = gaussians_struct(gaussians)
+        gs = grads.struct()
+        check(lib().gsc_rasterize_backward_batch(contexts[0].ctx, frames, cams, k, C.byref(g),
+                                                 C.byref(cfg), C.byref(gs)),
+              "gsc_rasterize_backward_batch")
         return grads
 
 

@@ -54,7 +54,7 @@ class DataParallelTrainer:
     the rendered image by gsc_combined_loss_grad and fed back as dL/dimage."""
 
     def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl",
-                 loss="l1", lambda_ssim=0.2):
+                 loss="l1", lambda_ssim=0.2, batch_views=_abi.GSC_MAX_BATCH_VIEWS):
         self.g = gaussians
         self.cameras = cameras
         self.cfg = config
@@ -72,7 +72,12 @@ class DataParallelTrainer:
         self.opt = Adam.for_gaussians(gaussians, self.grads, lrs)
         if self.exchange == "fused":
             self._setup_fused()
-        self.ctx = RasterizerContext(gaussians.arena.device)
+        # batch_views > 1: compositing backward per view, then one preprocess
+        # backward per batch_views views (gsc_rasterize_backward_batch)
+        self.batch = max(1, min(int(batch_views), _abi.GSC_MAX_BATCH_VIEWS))
+        self.ctxs = [RasterizerContext(gaussians.arena.device) for _ in range(self.batch)]
+        self.ctx = self.last_ctx = self.ctxs[0]
+        self._pending = []
         self.loss = torch.zeros(1, device=gaussians.arena.device)
         self.cam_structs = [c.to_struct() for c in cameras]
         if loss not in ("l1", "combined"):
@@ -98,17 +103,33 @@ class DataParallelTrainer:
     def view_fwd_bwd(self, v, target):
         """Forward + backward of view v against a device target [H,W,3]."""
         cam = self.cameras[v]
+        defer = self.batch > 1
+        ctx = self.last_ctx = self.ctxs[len(self._pending)]
         if self.loss_kind == "combined":
-            Rasterizer.forward(self.g, cam, context=self.ctx, config=self.cfg, out=self.image)
+            Rasterizer.forward(self.g, cam, context=ctx, config=self.cfg, out=self.image)
             combined_with_grad(self.image, target, self.lambda_ssim, out=self.loss_terms,
                                grad=self.dimage)
             self.loss += self.loss_terms[0]
-            Rasterizer.backward(self.dimage, self.g, cam, self.ctx, grads=self.grads,
-                                config=self.cfg)
+            Rasterizer.backward(self.dimage, self.g, cam, ctx, grads=self.grads, config=self.cfg,
+                                defer=defer)
+        else:
+            Rasterizer.forward(self.g, cam, context=ctx, config=self.cfg)
+            Rasterizer.backward(None, self.g, cam, ctx, grads=self.grads, target=target,
+                                l1_scale=1.0 / target.numel(), loss_sum=self.loss, config=self.cfg,
+                                defer=defer)
+        if defer:
+            self._pending.append(v)
+            if len(self._pending) == self.batch:
+                self.flush()
+
+    def flush(self):
+        """Preprocess backward of the views whose compositing backward is done."""
+        if not self._pending:
             return
-        Rasterizer.forward(self.g, cam, context=self.ctx, config=self.cfg)
-        Rasterizer.backward(None, self.g, cam, self.ctx, grads=self.grads, target=target,
-                            l1_scale=1.0 / target.numel(), loss_sum=self.loss, config=self.cfg)
+        k = len(self._pending)
+        Rasterizer.backward_batch(self.ctxs[:k], self.g, [self.cameras[v] for v in self._pending],
+                                  self.grads, config=self.cfg)
+        self._pending = []
 
     def _setup_fused(self):
         g = self.g
@@ -132,6 +153,7 @@ class DataParallelTrainer:
         self.dp_args = a
 
     def reduce_and_step(self):
+        self.flush()
         if self.exchange == "fused":
             torch.distributed.all_reduce(self.loss, group=self.pg)
             self.opt.step_count += 1

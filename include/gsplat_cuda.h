@@ -419,6 +419,9 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* frame, const gsc_gaus
                                   const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
                                   uint32_t* n_contrib, float* final_T, int64_t* num_rendered);
 
+/* Largest number of views gsc_rasterize_backward_batch sums in one pass. */
+#define GSC_MAX_BATCH_VIEWS 8
+
 /* composite backward -> preprocess backward for the frame's last forward.
  * Exactly one of dL_dimage / target is non-NULL (target = fused L1 with
  * l1_scale, loss accumulated into the device float *loss_sum if non-NULL).
@@ -428,6 +431,18 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* frame, const gsc_gau
                                    const float* dL_dimage, const float* target, float l1_scale,
                                    float* loss_sum, const gsc_gaussian_grads* grads,
                                    const gsc_grads2d* g2d);
+
+/* With grads == NULL, gsc_rasterize_backward stops after the composite
+ * backward and leaves the screen-space gradients (GSC_FRAME_GRAD2D) in the
+ * frame. gsc_rasterize_backward_batch then runs the preprocess backward of
+ * up to GSC_MAX_BATCH_VIEWS such frames in one pass: each Gaussian's
+ * parameters and gradient row are read once and the views' contributions are
+ * summed before they are added to `grads` (equal to calling the single-view
+ * backward per frame up to the order of the fp32 sums). cams[k] is frame k's
+ * camera; g and cfg are those of the frames' forwards. */
+GSC_API int gsc_rasterize_backward_batch(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams,
+                                         int32_t nviews, const gsc_gaussians* g,
+                                         const gsc_raster_config* cfg, const gsc_gaussian_grads* grads);
 
 /* Frame internals (device pointers, valid until the next forward on the frame). */
 #define GSC_FRAME_SPLATS 0

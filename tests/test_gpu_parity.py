@@ -358,3 +358,31 @@ def test_composite_backward_grad2d_and_chain(cuda, oracle, mode):
     np.testing.assert_array_equal(host(grads.dL_dlogit_opacity).reshape(-1), rg["logit_opacity"])
     np.testing.assert_array_equal(host(grads.dL_dsh).reshape(n, 48), rg["sh_coeffs"])
     np.testing.assert_array_equal(host(grads.dL_dcov2d), views["cov2d"])
+
+
+@pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF])
+@pytest.mark.parametrize("k", [1, 3, 8])
+def test_backward_batch_equals_per_view_backwards(cuda, mode, k):
+    """gsc_rasterize_backward_batch over k deferred views == k single-view
+    backwards (up to the order of the fp32 sums)."""
+    n, W, H = 20000, 96, 80
+    arrays, g, _ = make(n, W, H)
+    cams = [gs.make_camera(W, H, tuple(e)) for e in gs.sphere_poses(k, 4.0, seed=k)]
+    cfg = gs.default_config(mode=mode)
+    rng = np.random.default_rng(k)
+    targets = [to_dev(rng.uniform(0, 1, (H, W, 3)).astype(np.float32)) for _ in cams]
+    single = gs.RasterizerGradients(g, screen=False)
+    ctx = gs.RasterizerContext()
+    for cam, t in zip(cams, targets):
+        gs.Rasterizer.forward(g, cam, context=ctx, config=cfg)
+        gs.Rasterizer.backward(None, g, cam, ctx, grads=single, target=t, config=cfg)
+    batched = gs.RasterizerGradients(g, screen=False)
+    ctxs = [gs.RasterizerContext() for _ in cams]
+    for c, cam, t in zip(ctxs, cams, targets):
+        gs.Rasterizer.forward(g, cam, context=c, config=cfg)
+        assert gs.Rasterizer.backward(None, g, cam, c, target=t, config=cfg, defer=True) is None
+    gs.Rasterizer.backward_batch(ctxs, g, cams, batched, config=cfg)
+    R.sync()
+    a, b = host(batched.arena), host(single.arena)
+    assert np.abs(b).max() > 0
+    assert grad_close(a, b) <= GRAD_RTOL

@@ -204,6 +204,7 @@ def test_trainer_combined_loss(cuda):
     tr.zero()
     for v in range(len(cams)):
         tr.view_fwd_bwd(v, targets[v])
+    tr.flush()
     grads = gs.RasterizerGradients(g_ref, screen=False)
     for v, cam in enumerate(cams):
         img, ctx = gs.Rasterizer.forward(g_ref, cam, config=cfg)
