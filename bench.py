@@ -255,12 +255,14 @@ def stage_work(stats, n, keys_per_view, pge, tiles, end_bit, batch=1):
     Binning of a view = a stable 32-bit depth sort of the N Gaussians (4 passes),
     a gather-scan and emission of packed (tile << 32 | id) words in depth order,
     and a stable sort of those words by the tile bits (end_bit - 32 bits). The
-    preprocess backward runs once per `batch` views: parameters read once,
+    preprocess and its backward run once per `batch` views: parameters read once,
     gradient rows read and written once, one grad2d row per view."""
     tb = end_bit - 32
     m = keys_per_view
     return {
-        "preprocess": ("hbm", PREPROCESS_B * n, 1),
+        # one launch per `batch` views: parameters read once, per view a 48 B record
+        # + 8 B tile mask + 8 B packed depth word
+        "preprocess": ("hbm", (PARAM_ROW_B / batch + 64) * n, 1.0 / batch),
         "scan": ("hbm", 4 * n + 16 * n, 2),  # order gather + splat word, then the block-sum scan
         "emit": ("hbm", (4 + 32 + 8) * n + 8 * m, 1),  # order, record words, tile mask; packed pairs
         "sort": ("hbm", packed_sort_bytes(32) * n + packed_sort_bytes(tb) * m, 2),
@@ -488,13 +490,26 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     cams = make_cameras(gs, cfg)
     rcfg = gs.default_config(binning=binning_of(gs, args))
     lo, hi = trainer_mod.shard(len(cams), rank, world)
-    rctx = gs.RasterizerContext(dev)
-    img = torch.empty(cfg["H"], cfg["W"], 3, device=dev)
+    kb = gs._abi.GSC_MAX_BATCH_VIEWS  # views per Rasterizer.forward_batch (one preprocess pass)
+    rctxs = [gs.RasterizerContext(dev) for _ in range(kb)]
+    imgs = [torch.empty(cfg["H"], cfg["W"], 3, device=dev) for _ in range(kb)]
     ctx = gs.context(dev)
     lib = gs._abi.lib()
+
+    def render_all(host_imgs=None):
+        keys = 0
+        for v0 in range(lo, hi, kb):
+            views = list(range(v0, min(v0 + kb, hi)))
+            gs.Rasterizer.forward_batch(g, [cams[v] for v in views], rctxs, config=rcfg,
+                                        images=imgs[:len(views)])
+            keys += sum(c.num_rendered for c in rctxs[:len(views)])
+            if host_imgs is not None:
+                for k in range(len(views)):
+                    host_imgs[k].copy_(imgs[k], non_blocking=True)
+        return keys
+
     for _ in range(args.warmup):
-        for v in range(lo, hi):
-            gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
+        render_all()
     torch.cuda.synchronize()
     profile_read(gs, ctx, reset=True)
     profile_pge(gs, ctx, reset=True)
@@ -504,9 +519,7 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     with ClockSampler(local) as clk:
         with Timer(torch, world) as tm:
             for _ in range(args.steps):
-                for v in range(lo, hi):
-                    gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
-                    keys_total += rctx.num_rendered
+                keys_total += render_all()
     lib.gsc_profile_enable(ctx, 0)
     ms = tm.max_over_ranks()
     stats = profile_read(gs, ctx, reset=True)
@@ -517,19 +530,18 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
     kpv = keys_total / max(1, args.steps * (hi - lo))
-    roof = rooflines(stats, stage_work(stats, cfg["n"], kpv, pge, tiles, end_bit), peaks)
+    roof = rooflines(stats, stage_work(stats, cfg["n"], kpv, pge, tiles, end_bit, batch=kb), peaks)
     e2e = None
     if not args.no_e2e:
-        host_img = torch.empty(cfg["H"], cfg["W"], 3).pin_memory()
+        host_imgs = [torch.empty(cfg["H"], cfg["W"], 3).pin_memory() for _ in range(kb)]
         with Timer(torch, world) as tm2:
             for _ in range(args.steps):
-                for v in range(lo, hi):
-                    gs.Rasterizer.forward(g, cams[v], context=rctx, config=rcfg, out=img)
-                    host_img.copy_(img, non_blocking=True)
+                render_all(host_imgs)
         ms2 = tm2.max_over_ranks()
         e2e = {"value": round(pix / 1e6 / (ms2 / 1e3), 2), "unit": "MPix/s", "h2d_bytes_per_step": 0,
                "d2h_bytes_per_step": int(cfg["views"] * cfg["H"] * cfg["W"] * 12),
-               "path": "Rasterizer.forward through the C ABI; every image read back to pinned host"}
+               "path": "Rasterizer.forward_batch (8 views per preprocess pass) through the C ABI; "
+                       "every image read back to pinned host"}
     if rank != 0:
         return None
     dominant = max(roof, key=lambda k: roof[k]["share"] or 0)

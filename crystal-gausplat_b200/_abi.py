@@ -154,6 +154,9 @@ _SIGS = {
     "gsc_rasterize_backward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),
                                          C.POINTER(RasterConfig), P, P, C.c_float, P,
                                          C.POINTER(GaussianGrads), C.POINTER(Grads2D)]),
+    "gsc_rasterize_forward_batch": (C.c_int, [P, C.POINTER(P), C.POINTER(Camera), C.c_int32,
+                                              C.POINTER(Gaussians), C.POINTER(RasterConfig),
+                                              C.POINTER(P), C.POINTER(C.c_int64)]),
     "gsc_rasterize_backward_batch": (C.c_int, [P, C.POINTER(P), C.POINTER(Camera), C.c_int32,
                                                C.POINTER(Gaussians), C.POINTER(RasterConfig),
                                                C.POINTER(GaussianGrads)]),

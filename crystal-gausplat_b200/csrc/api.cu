@@ -245,16 +245,18 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.n = g->count;
   a.pos = g->position; a.log_scale = g->log_scale; a.rot = g->rotation;
   a.logit_opacity = g->logit_opacity; a.sh = g->sh;
-  a.cam = *cam; a.cfg = *cfg;
+  a.cfg = *cfg;
   a.tiles_x = (cam->width + GS_TILE - 1) / GS_TILE;
   a.tiles_y = (cam->height + GS_TILE - 1) / GS_TILE;
-  a.splats = o->splats;
+  a.nviews = 1;
+  a.cams[0] = *cam;
+  a.splats_v[0] = o->splats;
   (void)block_sums;
-  a.depth_pairs = depth_pairs;
+  a.depth_pairs_v[0] = depth_pairs;
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
   a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
-  a.tile_mask = tile_mask;
+  a.tile_mask_v[0] = tile_mask;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
@@ -508,9 +510,17 @@ GSC_API int gsc_frame_destroy(gsc_frame* f) {
   return GSC_OK;
 }
 
-GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g,
-                                  const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
-                                  uint32_t* n_contrib, float* final_T, int64_t* num_rendered) {
+}  // extern "C"
+
+namespace {
+
+// Whole-view forward in three phases, so that several views can share the
+// preprocess launch and a single host readback of their key counts:
+//   forward_prepare   -- buffers and frame fields (no GPU work)
+//   forward_sort_scan -- depth sort, per-block pair counts, scan (device only)
+//   forward_finish    -- emission, tile sort, ranges, compositing, given the pair count
+int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gsc_camera* cam,
+                    const gsc_raster_config* cfg, float* image) {
   GS_REQUIRE(ctx && f && f->ctx == ctx, "gsc_rasterize_forward: bad context/frame");
   GS_TRY(check_gaussians(g));
   GS_TRY(check_view(cam, cfg));
@@ -533,48 +543,56 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   GS_TRY(ensure(ctx, &f->final_T, npix * 4));
   GS_TRY(ensure(ctx, &f->last, npix * 4));
   GS_TRY(ensure(ctx, &f->n_contrib, npix * 4));
+  if (cfg->binning == GSC_BIN_CONTRIBUTING) GS_TRY(ensure(ctx, &f->tile_mask, (size_t)n * 8 + 8));
   if (!image) {
     GS_TRY(ensure(ctx, &f->image, npix * 12));
     image = (float*)f->image.ptr;
   }
   f->image_ptr = image;
   f->keys_valid = false;
-  float* splats = (float*)f->splats.ptr;
-  uint32_t* depth_keys = (uint32_t*)f->depth_keys.ptr;
-  uint32_t* order = (uint32_t*)f->order.ptr;
+  return GSC_OK;
+}
 
-  gsc_projected proj;
-  std::memset(&proj, 0, sizeof proj);
-  proj.splats = splats;
-  uint64_t* tile_mask = nullptr;
-  if (cfg->binning == GSC_BIN_CONTRIBUTING) {
-    GS_TRY(ensure(ctx, &f->tile_mask, (size_t)n * 8 + 8));
-    tile_mask = (uint64_t*)f->tile_mask.ptr;
-  }
-  uint64_t* depth_pairs = (uint64_t*)f->depth_pairs.ptr;
-  GS_TRY(do_preprocess(ctx, g, cam, cfg, &proj, nullptr, depth_pairs, tile_mask));
+uint64_t* frame_mask(gsc_frame* f, const gsc_raster_config* cfg) {
+  return cfg->binning == GSC_BIN_CONTRIBUTING ? (uint64_t*)f->tile_mask.ptr : nullptr;
+}
+
+int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f) {
+  const int64_t n = f->n;
   // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and
   //    sink); packed (depth << 32 | index) words, split into keys and order
   if (n > 0) {
     GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed(n, 32, 64)));
     StageScope sc(ctx, GSC_STAGE_SORT);
     sc.kernels(n > 1 ? 1 + 4 : 1);
-    GS_TRY(launch_sort_packed(ctx, depth_pairs, n, 32, 64, depth_keys, order, scratch_base(ctx)));
+    GS_TRY(launch_sort_packed(ctx, (uint64_t*)f->depth_pairs.ptr, n, 32, 64, (uint32_t*)f->depth_keys.ptr,
+                              (uint32_t*)f->order.ptr, scratch_base(ctx)));
   }
-  // 2. exact allocation in depth order, then emission of (tile, id)
+  // 2. exact allocation in depth order: per-block pair counts and their scan
+  if (n == 0) return GSC_OK;
   {
     StageScope sc(ctx, GSC_STAGE_SCAN);
-    sc.kernels(n ? 1 : 0);
-    GS_TRY(launch_block_sums_gather(splats, order, n, (uint32_t*)f->block_sums.ptr, ctx->stream));
+    sc.kernels(1);
+    GS_TRY(launch_block_sums_gather((const float*)f->splats.ptr, (const uint32_t*)f->order.ptr, n,
+                                    (uint32_t*)f->block_sums.ptr, ctx->stream));
   }
-  uint64_t m = 0;
-  GS_TRY(do_scan(ctx, n, (uint32_t*)f->block_sums.ptr, (uint64_t*)f->offsets.ptr, (uint64_t*)f->total.ptr, &m));
+  StageScope sc(ctx, GSC_STAGE_SCAN);
+  sc.kernels(1);
+  return launch_scan_block_sums((const uint32_t*)f->block_sums.ptr, (n + 255) / 256, (uint64_t*)f->offsets.ptr,
+                                (uint64_t*)f->total.ptr, ctx->stream);
+}
+
+int forward_finish(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64_t m, uint32_t* n_contrib,
+                   float* final_T) {
+  const int64_t n = f->n;
+  const int W = f->width, H = f->height, tx = f->tiles_x, ty = f->tiles_y;
+  const size_t npix = (size_t)W * H;
   if (m >= (1ull << 30)) {
     set_error("gsc_rasterize_forward: " + std::to_string(m) + " keys exceed the 2^30 limit");
     return GSC_ERR_CAPACITY;
   }
   f->num_keys = (int64_t)m;
-  if (num_rendered) *num_rendered = (int64_t)m;
+  const float* splats = (const float*)f->splats.ptr;
   GS_TRY(ensure(ctx, &f->tiles, (size_t)m * 4 + 4));
   GS_TRY(ensure(ctx, &f->vals, (size_t)m * 4 + 4));
   uint32_t* tiles = (uint32_t*)f->tiles.ptr;
@@ -585,8 +603,8 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
     {
       StageScope sc(ctx, GSC_STAGE_EMIT);
       sc.kernels(1);
-      GS_TRY(launch_emit_tiles(splats, order, n, (const uint64_t*)f->offsets.ptr, tx, ty, tile_mask, pairs,
-                               ctx->stream));
+      GS_TRY(launch_emit_tiles(splats, (const uint32_t*)f->order.ptr, n, (const uint64_t*)f->offsets.ptr, tx, ty,
+                               frame_mask(f, cfg), pairs, ctx->stream));
     }
     // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
     //    only, split into tiles and values
@@ -603,7 +621,7 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   }
   CompositeFwdArgs a;
   fill_fwd(&a, splats, vals, (const uint32_t*)f->ranges.ptr, W, H, cfg);
-  a.image = image;
+  a.image = f->image_ptr;
   a.final_T = (float*)f->final_T.ptr;
   a.last = (uint32_t*)f->last.ptr;
   a.n_contrib = (uint32_t*)f->n_contrib.ptr;
@@ -618,6 +636,75 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   if (final_T)
     GS_CK(cudaMemcpyAsync(final_T, f->final_T.ptr, npix * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   f->has_forward = true;
+  return GSC_OK;
+}
+
+// One preprocess launch for the frames (all of one image size).
+int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams, int k,
+                       const gsc_gaussians* g, const gsc_raster_config* cfg) {
+  PreprocessArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.n = g->count;
+  a.pos = g->position; a.log_scale = g->log_scale; a.rot = g->rotation;
+  a.logit_opacity = g->logit_opacity; a.sh = g->sh;
+  a.cfg = *cfg;
+  a.tiles_x = frames[0]->tiles_x;
+  a.tiles_y = frames[0]->tiles_y;
+  a.nviews = k;
+  for (int v = 0; v < k; v++) {
+    a.cams[v] = cams[v];
+    a.splats_v[v] = (float*)frames[v]->splats.ptr;
+    a.depth_pairs_v[v] = (uint64_t*)frames[v]->depth_pairs.ptr;
+    a.tile_mask_v[v] = frame_mask(frames[v], cfg);
+  }
+  StageScope sc(ctx, GSC_STAGE_PREPROCESS);
+  sc.kernels(g->count ? 1 : 0);
+  return launch_preprocess(a, ctx->stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g,
+                                  const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
+                                  uint32_t* n_contrib, float* final_T, int64_t* num_rendered) {
+  GS_TRY(forward_prepare(ctx, f, g, cam, cfg, image));
+  GS_TRY(forward_preprocess(ctx, &f, cam, 1, g, cfg));
+  GS_TRY(forward_sort_scan(ctx, f));
+  uint64_t m = 0;
+  if (f->n) GS_TRY(read_u64(ctx, (const uint64_t*)f->total.ptr, &m));
+  if (num_rendered) *num_rendered = (int64_t)m;
+  return forward_finish(ctx, f, cfg, m, n_contrib, final_T);
+}
+
+GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams,
+                                        int32_t nviews, const gsc_gaussians* g, const gsc_raster_config* cfg,
+                                        float* const* images, int64_t* num_rendered) {
+  GS_REQUIRE(ctx && frames && cams, "gsc_rasterize_forward_batch: null argument");
+  GS_REQUIRE(nviews >= 1 && nviews <= GSC_MAX_BATCH_VIEWS, "gsc_rasterize_forward_batch: nviews out of range");
+  for (int v = 0; v < nviews; v++) {
+    GS_REQUIRE(cams[v].width == cams[0].width && cams[v].height == cams[0].height,
+               "gsc_rasterize_forward_batch: the views must share one image size");
+    for (int u = 0; u < v; u++)
+      GS_REQUIRE(frames[u] != frames[v], "gsc_rasterize_forward_batch: a frame appears twice");
+    GS_TRY(forward_prepare(ctx, frames[v], g, &cams[v], cfg, images ? images[v] : nullptr));
+  }
+  GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg));
+  for (int v = 0; v < nviews; v++) GS_TRY(forward_sort_scan(ctx, frames[v]));
+  // one readback of every view's pair count
+  uint64_t m[GSC_MAX_BATCH_VIEWS] = {};
+  if (g->count) {
+    for (int v = 0; v < nviews; v++)
+      GS_CK(cudaMemcpyAsync((char*)ctx->pinned + 8 * v, frames[v]->total.ptr, 8, cudaMemcpyDeviceToHost,
+                            ctx->stream));
+    GS_CK(cudaStreamSynchronize(ctx->stream));
+    std::memcpy(m, ctx->pinned, 8 * (size_t)nviews);
+  }
+  for (int v = 0; v < nviews; v++) {
+    if (num_rendered) num_rendered[v] = (int64_t)m[v];
+    GS_TRY(forward_finish(ctx, frames[v], cfg, m[v], nullptr, nullptr));
+  }
   return GSC_OK;
 }
 

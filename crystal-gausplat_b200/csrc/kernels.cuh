@@ -4,6 +4,10 @@
 
 namespace gs {
 
+constexpr int kMaxBatchViews = GSC_MAX_BATCH_VIEWS;
+
+// Preprocess of `nviews` views of one size (the per-Gaussian outputs mean2d ..
+// tiles_touched are written only when nviews == 1).
 struct PreprocessArgs {
   int64_t n;
   const float* pos;
@@ -11,11 +15,16 @@ struct PreprocessArgs {
   const float* rot;
   const float* logit_opacity;
   const float* sh;
-  gsc_camera cam;
   gsc_raster_config cfg;
   int tiles_x, tiles_y;
-  float* splats;
-  uint64_t* depth_pairs;  // bits(depth) (~0 if the Gaussian emits no pair) << 32 | index; may be null
+  int nviews;
+  gsc_camera cams[kMaxBatchViews];
+  float* splats_v[kMaxBatchViews];
+  // bits(depth) (~0 if the Gaussian emits no pair) << 32 | index; may be null
+  uint64_t* depth_pairs_v[kMaxBatchViews];
+  // if set: contributing-pairs binning (bit k = k-th tile of the rect, row-major;
+  // ~0 = the whole rect) and the record's tile count is the contributing one
+  uint64_t* tile_mask_v[kMaxBatchViews];
   float* mean2d;
   float* cov2d;
   float* conic;
@@ -25,8 +34,6 @@ struct PreprocessArgs {
   float* opacity;
   uint32_t* tiles_touched;
   float* cov3d;
-  uint64_t* tile_mask;   // if set: contributing-pairs binning (bit k = k-th tile of the rect, row-major;
-                         // ~0 = the whole rect) and the record's tile count is the contributing one
 };
 
 struct CompositeFwdArgs {
@@ -59,8 +66,6 @@ struct CompositeBwdArgs {
   float* grad2d;
   float* loss_sum;
 };
-
-constexpr int kMaxBatchViews = GSC_MAX_BATCH_VIEWS;
 
 struct PreprocessBwdArgs {
   int64_t n;

@@ -20,6 +20,10 @@ namespace gs {
 constexpr int kPreThreads = 128;
 constexpr int kShRow = 13;  // float4 per staged SH row (12 used + 1 pad)
 
+// One Gaussian per thread; a.nviews views per launch. The camera-independent
+// terms (scales, quaternion, 3-D covariance, opacity, the staged SH row) are
+// formed once and every view's record, mask and depth word are written to that
+// view's buffers.
 __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs a) {
   __shared__ float4 s_sh[kPreThreads * kShRow];
   // contributing-pairs binning: per-thread cull terms, rect {x0, y0, width, 2^16/width rounded up},
@@ -30,7 +34,6 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
   const int64_t base = (int64_t)blockIdx.x * kPreThreads;
   const int64_t i = base + threadIdx.x;
   const int64_t n = a.n;
-  const gsc_camera& cam = a.cam;
   const gsc_raster_config& cfg = a.cfg;
 
   // Coalesced staging of this block's SH coefficients (48 floats each).
@@ -41,11 +44,9 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
   }
   __syncthreads();
 
-  uint32_t tiles = 0;
-  float col_b = 0.0f, depth_o = 0.0f, radius_o = 0.0f;
-  uint32_t nt = 0;  // tile tests of this thread's Gaussian (contributing-pairs binning)
+  float p[3] = {0.0f, 0.0f, 0.0f}, c3[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f}, o = 0.0f;
   if (i < n) {
-    const float p[3] = {a.pos[i * 3], a.pos[i * 3 + 1], a.pos[i * 3 + 2]};
+    p[0] = a.pos[i * 3]; p[1] = a.pos[i * 3 + 1]; p[2] = a.pos[i * 3 + 2];
     const float s[3] = {gs_expf(a.log_scale[i * 3]), gs_expf(a.log_scale[i * 3 + 1]),
                         gs_expf(a.log_scale[i * 3 + 2])};
     float4 q4 = reinterpret_cast<const float4*>(a.rot)[i];
@@ -53,113 +54,122 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
     load_quat(q4, cfg.mode, q, &qn);
     float R[3][3];
     quat_to_R(q[0], q[1], q[2], q[3], R);
-    float c3[6];
     cov3d_of(s, R, c3);
-    Projected pr;
-    project(p, c3, cam, cfg, &pr);
-
-    // colour
-    float d[3], len;
-    view_dir(p, cam, d, &len);
-    float b[16];
-    sh_basis_hi(d[0], d[1], d[2], b);
-    float shv[48];
-#pragma unroll
-    for (int q = 0; q < 12; q++) {
-      const float4 v = s_sh[threadIdx.x * kShRow + q];
-      shv[4 * q] = v.x; shv[4 * q + 1] = v.y; shv[4 * q + 2] = v.z; shv[4 * q + 3] = v.w;
-    }
-    float raw[3];
-    sh_eval([&](int k) { return shv[k]; }, d[0], d[1], d[2], b, cfg.sh_degree, cfg.mode, raw);
-    float col[3];
-#pragma unroll
-    for (int c = 0; c < 3; c++) col[c] = fmaxf(0.0f, raw[c] + 0.5f);
-    const float o = gs_sigmoid(a.logit_opacity[i]);
-
-    float px = -1000.0f, py = -1000.0f, depth = 0.0f, radius = 0.0f;
-    int x0 = 0, x1 = -1, y0 = 0, y1 = -1;
-    if (pr.visible) {
-      px = pr.px; py = pr.py; depth = pr.zc; radius = pr.r;
-      if (pr.r > 0.0f && pr.zc > 0.0f) {
-        tile_bounds(px, py, pr.r, a.tiles_x, a.tiles_y, &x0, &x1, &y0, &y1);
-        if (x1 >= x0 && y1 >= y0) tiles = (uint32_t)((x1 - x0 + 1) * (y1 - y0 + 1));
-      }
-    }
-    const float o_eff = (pr.visible && pr.det > 0.0f) ? o : 0.0f;
-    const float4 g0 = make_float4(px, py, pr.A, pr.B);
-    // Contributing-pairs binning: the rect's tiles (<= 64) are tested below by the whole warp.
-    if (a.tile_mask && tiles > 0 && tiles <= 64) {
-      s_cg[threadIdx.x] = cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
-      const int w = x1 - x0 + 1;
-      s_rect[threadIdx.x] = make_int4(x0, y0, w, (65536 + w - 1) / w);
-      nt = tiles;
-    }
-    float4* sp = reinterpret_cast<float4*>(a.splats) + i * 3;
-    sp[0] = g0;
-    sp[1] = make_float4(pr.Cc, o_eff, col[0], col[1]);
-    col_b = col[2]; depth_o = depth; radius_o = radius;
-
-    if (a.mean2d) { a.mean2d[i * 2] = px; a.mean2d[i * 2 + 1] = py; }
-    if (a.depth) a.depth[i] = depth;
-    if (a.radius) a.radius[i] = radius;
-    if (a.cov2d) { a.cov2d[i * 3] = pr.a; a.cov2d[i * 3 + 1] = pr.b; a.cov2d[i * 3 + 2] = pr.c; }
-    if (a.conic) { a.conic[i * 3] = pr.A; a.conic[i * 3 + 1] = pr.B; a.conic[i * 3 + 2] = pr.Cc; }
-    if (a.colors) { a.colors[i * 3] = col[0]; a.colors[i * 3 + 1] = col[1]; a.colors[i * 3 + 2] = col[2]; }
-    if (a.opacity) a.opacity[i] = o;
-    if (a.tiles_touched) a.tiles_touched[i] = tiles;
+    o = gs_sigmoid(a.logit_opacity[i]);
     if (a.cov3d) {
 #pragma unroll
       for (int k = 0; k < 6; k++) a.cov3d[i * 6 + k] = c3[k];
     }
+    if (a.opacity) a.opacity[i] = o;
   }
+  const float4* shrow = s_sh + threadIdx.x * kShRow;
 
-  // Tile tests of the warp's Gaussians, flattened over its lanes so that one
-  // large rectangle does not hold the other 31 lanes: in round `base`, lane l
-  // runs test base + l, which belongs to the first lane whose inclusive count
-  // exceeds it. The round's results come back as one ballot, from which every
-  // lane copies the bits of its own tests into its mask (bit = row-major
-  // position in its rect). The row of test t of a rect of width w is
-  // (t * ceil(2^16 / w)) >> 16, exact for t < 64 <= 2^16 / w.
-  uint32_t emit = tiles;
-  if (a.tile_mask) {
-    const int lane = threadIdx.x & 31, wb = threadIdx.x & ~31;
-    uint32_t incl = nt;
+  for (int v = 0; v < a.nviews; v++) {
+    const gsc_camera& cam = a.cams[v];
+    const bool stage_out = a.nviews == 1;  // the per-Gaussian outputs of the stage entry point
+    uint32_t tiles = 0;
+    float col_b = 0.0f, depth_o = 0.0f, radius_o = 0.0f;
+    uint32_t nt = 0;  // tile tests of this thread's Gaussian (contributing-pairs binning)
+    if (i < n) {
+      Projected pr;
+      project(p, c3, cam, cfg, &pr);
+
+      // colour
+      float d[3], len;
+      view_dir(p, cam, d, &len);
+      float b[16];
+      sh_basis_hi(d[0], d[1], d[2], b);
+      float raw[3];
+      sh_eval([&](int k) { return reinterpret_cast<const float*>(shrow)[k]; }, d[0], d[1], d[2], b,
+              cfg.sh_degree, cfg.mode, raw);
+      float col[3];
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += t;
-    }
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    const uint32_t first = incl - nt;  // this lane's tests are [first, incl)
-    s_incl[threadIdx.x] = incl;
-    __syncwarp();
-    uint64_t mask = 0ull;
-    int own = 0;
-    for (uint32_t base = 0; base < total; base += 32) {
-      const uint32_t k = base + lane;
-      bool keep = false;
-      if (k < total) {
-        while (s_incl[wb + own] <= k) own++;
-        const uint32_t local = k - (own ? s_incl[wb + own - 1] : 0u);
-        const int4 r = s_rect[wb + own];
-        const uint32_t ry = (local * (uint32_t)r.w) >> 16, rx = local - ry * (uint32_t)r.z;
-        float rx0, rx1, ry0, ry1;
-        tile_pixel_rect(r.x + (int)rx, r.y + (int)ry, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
-        keep = !cull_tile(s_cg[wb + own], rx0, rx1, ry0, ry1);
+      for (int c = 0; c < 3; c++) col[c] = fmaxf(0.0f, raw[c] + 0.5f);
+
+      float px = -1000.0f, py = -1000.0f, depth = 0.0f, radius = 0.0f;
+      int x0 = 0, x1 = -1, y0 = 0, y1 = -1;
+      if (pr.visible) {
+        px = pr.px; py = pr.py; depth = pr.zc; radius = pr.r;
+        if (pr.r > 0.0f && pr.zc > 0.0f) {
+          tile_bounds(px, py, pr.r, a.tiles_x, a.tiles_y, &x0, &x1, &y0, &y1);
+          if (x1 >= x0 && y1 >= y0) tiles = (uint32_t)((x1 - x0 + 1) * (y1 - y0 + 1));
+        }
       }
-      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-      const uint32_t lo = max(first, base), hi = min(incl, base + 32);
-      if (lo < hi) mask |= ((uint64_t)(bal >> (lo - base)) & ((1ull << (hi - lo)) - 1ull)) << (lo - first);
+      const float o_eff = (pr.visible && pr.det > 0.0f) ? o : 0.0f;
+      const float4 g0 = make_float4(px, py, pr.A, pr.B);
+      // Contributing-pairs binning: the rect's tiles (<= 64) are tested below by the whole warp.
+      if (a.tile_mask_v[v] && tiles > 0 && tiles <= 64) {
+        s_cg[threadIdx.x] = cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
+        const int w = x1 - x0 + 1;
+        s_rect[threadIdx.x] = make_int4(x0, y0, w, (65536 + w - 1) / w);
+        nt = tiles;
+      }
+      float4* sp = reinterpret_cast<float4*>(a.splats_v[v]) + i * 3;
+      sp[0] = g0;
+      sp[1] = make_float4(pr.Cc, o_eff, col[0], col[1]);
+      col_b = col[2]; depth_o = depth; radius_o = radius;
+
+      if (stage_out) {
+        if (a.mean2d) { a.mean2d[i * 2] = px; a.mean2d[i * 2 + 1] = py; }
+        if (a.depth) a.depth[i] = depth;
+        if (a.radius) a.radius[i] = radius;
+        if (a.cov2d) { a.cov2d[i * 3] = pr.a; a.cov2d[i * 3 + 1] = pr.b; a.cov2d[i * 3 + 2] = pr.c; }
+        if (a.conic) { a.conic[i * 3] = pr.A; a.conic[i * 3 + 1] = pr.B; a.conic[i * 3 + 2] = pr.Cc; }
+        if (a.colors) { a.colors[i * 3] = col[0]; a.colors[i * 3 + 1] = col[1]; a.colors[i * 3 + 2] = col[2]; }
+        if (a.tiles_touched) a.tiles_touched[i] = tiles;
+      }
+    }
+
+    // Tile tests of the warp's Gaussians, flattened over its lanes so that one
+    // large rectangle does not hold the other 31 lanes: in round `base`, lane l
+    // runs test base + l, which belongs to the first lane whose inclusive count
+    // exceeds it. The round's results come back as one ballot, from which every
+    // lane copies the bits of its own tests into its mask (bit = row-major
+    // position in its rect). The row of test t of a rect of width w is
+    // (t * ceil(2^16 / w)) >> 16, exact for t < 64 <= 2^16 / w.
+    uint32_t emit = tiles;
+    if (a.tile_mask_v[v]) {
+      const int lane = threadIdx.x & 31, wb = threadIdx.x & ~31;
+      uint32_t incl = nt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+      }
+      const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+      const uint32_t first = incl - nt;  // this lane's tests are [first, incl)
+      s_incl[threadIdx.x] = incl;
+      __syncwarp();
+      uint64_t mask = 0ull;
+      int own = 0;
+      for (uint32_t rb = 0; rb < total; rb += 32) {
+        const uint32_t k = rb + lane;
+        bool keep = false;
+        if (k < total) {
+          while (s_incl[wb + own] <= k) own++;
+          const uint32_t local = k - (own ? s_incl[wb + own - 1] : 0u);
+          const int4 r = s_rect[wb + own];
+          const uint32_t ry = (local * (uint32_t)r.w) >> 16, rx = local - ry * (uint32_t)r.z;
+          float rx0, rx1, ry0, ry1;
+          tile_pixel_rect(r.x + (int)rx, r.y + (int)ry, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
+          keep = !cull_tile(s_cg[wb + own], rx0, rx1, ry0, ry1);
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+        const uint32_t lo = max(first, rb), hi = min(incl, rb + 32);
+        if (lo < hi) mask |= ((uint64_t)(bal >> (lo - rb)) & ((1ull << (hi - lo)) - 1ull)) << (lo - first);
+      }
+      if (i < n) {
+        if (nt) emit = (uint32_t)__popcll(mask);
+        a.tile_mask_v[v][i] = nt ? mask : ~0ull;
+      }
+      __syncwarp();  // the shared rect / cull terms are rewritten by the next view
     }
     if (i < n) {
-      if (nt) emit = (uint32_t)__popcll(mask);
-      a.tile_mask[i] = nt ? mask : ~0ull;
+      reinterpret_cast<float4*>(a.splats_v[v])[i * 3 + 2] =
+          make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
+      if (a.depth_pairs_v[v])
+        a.depth_pairs_v[v][i] = ((uint64_t)(emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu) << 32) | (uint64_t)i;
     }
-  }
-  if (i < n) {
-    reinterpret_cast<float4*>(a.splats)[i * 3 + 2] = make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
-    if (a.depth_pairs)
-      a.depth_pairs[i] = ((uint64_t)(emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu) << 32) | (uint64_t)i;
   }
 }
 

@@ -164,6 +164,32 @@ class Rasterizer:
         return image, ctx
 
     @staticmethod
+    def forward_batch(gaussians, cameras, contexts, config=None, images=None):
+        """Rasterizer.forward of up to GSC_MAX_BATCH_VIEWS views of one size, one
+        context each, sharing one preprocess pass. Returns the images."""
+        k = len(cameras)
+        assert len(contexts) >= k
+        cfg = config or _abi.default_config()
+        H, W = cameras[0].height, cameras[0].width
+        dev = gaussians.arena.device
+        if images is None:
+            images = [torch.empty(H, W, 3, device=dev) for _ in range(k)]
+        frames = (C.c_void_p * k)(*[c.frame.value for c in contexts[:k]])
+        cams = (_abi.Camera * k)(*[c.to_struct() for c in cameras])
+        imgs = (C.c_void_p * k)(*[im.data_ptr() for im in images])
+        nr = (C.c_int64 * k)()
+        g = gaussians_struct(gaussians)
+        check(lib().gsc_rasterize_forward_batch(contexts[0].ctx, frames, cams, k, C.byref(g), C.byref(cfg),
+                                                imgs, nr), "gsc_rasterize_forward_batch")
+        for c, im, m in zip(contexts, images, nr):
+            c.num_rendered = m
+            c.width, c.height = W, H
+            c.rendered_image = im
+            c.background = tuple(cfg.background)
+            c.config = cfg
+        return images
+
+    @staticmethod
     def backward(dL_dimage, gaussians, camera, context, grads=None, target=None, l1_scale=None,
                  loss_sum=None, config=None, defer=False):
         """Gradients for the last forward on `context`. With `target`, the pixel

@@ -78,6 +78,10 @@ class DataParallelTrainer:
         self.ctxs = [RasterizerContext(gaussians.arena.device) for _ in range(self.batch)]
         self.ctx = self.last_ctx = self.ctxs[0]
         self._pending = []
+        self._slot = {}  # view -> context of the current forward batch
+        if self.batch > 1:
+            H, W = cameras[0].height, cameras[0].width
+            self.images = [torch.empty(H, W, 3, device=gaussians.arena.device) for _ in range(self.batch)]
         self.loss = torch.zeros(1, device=gaussians.arena.device)
         self.cam_structs = [c.to_struct() for c in cameras]
         if loss not in ("l1", "combined"):
@@ -104,32 +108,45 @@ class DataParallelTrainer:
         """Forward + backward of view v against a device target [H,W,3]."""
         cam = self.cameras[v]
         defer = self.batch > 1
-        ctx = self.last_ctx = self.ctxs[len(self._pending)]
+        if defer:
+            # forward of the next views of this rank as one batch, then one
+            # deferred backward per view, then one preprocess backward
+            if v not in self._slot:
+                self.flush()
+                views = list(range(v, min(v + self.batch, max(self.hi, v + 1))))
+                self._slot = {u: k for k, u in enumerate(views)}
+                Rasterizer.forward_batch(self.g, [self.cameras[u] for u in views], self.ctxs,
+                                         config=self.cfg, images=self.images[:len(views)])
+            k = self._slot[v]
+            ctx = self.last_ctx = self.ctxs[k]
+            image = self.images[k]
+        else:
+            ctx = self.last_ctx = self.ctxs[0]
+            image = self.image if self.loss_kind == "combined" else None
+            Rasterizer.forward(self.g, cam, context=ctx, config=self.cfg, out=image)
         if self.loss_kind == "combined":
-            Rasterizer.forward(self.g, cam, context=ctx, config=self.cfg, out=self.image)
-            combined_with_grad(self.image, target, self.lambda_ssim, out=self.loss_terms,
-                               grad=self.dimage)
+            combined_with_grad(image, target, self.lambda_ssim, out=self.loss_terms, grad=self.dimage)
             self.loss += self.loss_terms[0]
             Rasterizer.backward(self.dimage, self.g, cam, ctx, grads=self.grads, config=self.cfg,
                                 defer=defer)
         else:
-            Rasterizer.forward(self.g, cam, context=ctx, config=self.cfg)
             Rasterizer.backward(None, self.g, cam, ctx, grads=self.grads, target=target,
                                 l1_scale=1.0 / target.numel(), loss_sum=self.loss, config=self.cfg,
                                 defer=defer)
         if defer:
             self._pending.append(v)
-            if len(self._pending) == self.batch:
+            if len(self._pending) == len(self._slot):
                 self.flush()
 
     def flush(self):
         """Preprocess backward of the views whose compositing backward is done."""
         if not self._pending:
+            self._slot = {}
             return
-        k = len(self._pending)
-        Rasterizer.backward_batch(self.ctxs[:k], self.g, [self.cameras[v] for v in self._pending],
-                                  self.grads, config=self.cfg)
+        Rasterizer.backward_batch([self.ctxs[self._slot[v]] for v in self._pending], self.g,
+                                  [self.cameras[v] for v in self._pending], self.grads, config=self.cfg)
         self._pending = []
+        self._slot = {}
 
     def _setup_fused(self):
         g = self.g

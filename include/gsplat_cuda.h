@@ -419,6 +419,17 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* frame, const gsc_gaus
                                   const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
                                   uint32_t* n_contrib, float* final_T, int64_t* num_rendered);
 
+/* gsc_rasterize_forward of up to GSC_MAX_BATCH_VIEWS views of one image size
+ * into distinct frames, with one preprocess pass over the Gaussians for all of
+ * them (parameters read once) and one host readback of the pair counts.
+ * images[k] (or images itself) may be NULL: frame k's own image buffer.
+ * num_rendered (host, may be NULL) gets nviews counts. Results are those of
+ * the single-view call, bit for bit. */
+GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams,
+                                        int32_t nviews, const gsc_gaussians* g,
+                                        const gsc_raster_config* cfg, float* const* images,
+                                        int64_t* num_rendered);
+
 /* Largest number of views gsc_rasterize_backward_batch sums in one pass. */
 #define GSC_MAX_BATCH_VIEWS 8
 

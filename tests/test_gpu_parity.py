@@ -386,3 +386,22 @@ def test_backward_batch_equals_per_view_backwards(cuda, mode, k):
     a, b = host(batched.arena), host(single.arena)
     assert np.abs(b).max() > 0
     assert grad_close(a, b) <= GRAD_RTOL
+
+
+@pytest.mark.parametrize("binning", BINNINGS, ids=["reference_lists", "contributing_lists"])
+def test_forward_batch_equals_single_view_forwards(cuda, binning):
+    """gsc_rasterize_forward_batch == gsc_rasterize_forward per view, bit for bit."""
+    n, W, H = 30000, 112, 72
+    arrays, g, _ = make(n, W, H)
+    cams = [gs.make_camera(W, H, tuple(e)) for e in gs.sphere_poses(5, 4.0, seed=3)]
+    cfg = gs.default_config(binning=binning)
+    ctxs = [gs.RasterizerContext() for _ in cams]
+    imgs = gs.Rasterizer.forward_batch(g, cams, ctxs, config=cfg)
+    one = gs.RasterizerContext()
+    for cam, c, im in zip(cams, ctxs, imgs):
+        ref, _ = gs.Rasterizer.forward(g, cam, context=one, config=cfg)
+        assert c.num_rendered == one.num_rendered
+        np.testing.assert_array_equal(host(im), host(ref))
+        for which, dt in ((_abi.GSC_FRAME_VALUES, np.uint32), (_abi.GSC_FRAME_RANGES, np.uint32),
+                          (_abi.GSC_FRAME_FINAL_T, np.float32), (_abi.GSC_FRAME_LAST, np.uint32)):
+            np.testing.assert_array_equal(c.get(which, dt), one.get(which, dt))
