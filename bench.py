@@ -685,9 +685,19 @@ def reference_render(args, cfg):
                     "d2h_bytes_per_step": 0}}
 
 
+def emit_line(res, out_fd):
+    """The one JSON result line, on the process's original standard output."""
+    os.write(out_fd, (json.dumps(res) + "\n").encode())
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    # Everything but the result line (NCCL's version banner, library chatter)
+    # goes to standard error, so standard output carries exactly one line.
+    sys.stdout.flush()
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         if rank == 0:
@@ -697,7 +707,7 @@ def main():
                 res = reference_render(args, cfg)
             else:
                 res = reference_train(args, cfg)
-            print(json.dumps(res), flush=True)
+            emit_line(res, out_fd)
         return
     import torch
     if world > 1:
@@ -711,7 +721,7 @@ def main():
     else:
         res = run_sort(args, cfg, rank, world, local, peaks, peak_kind)
     if rank == 0:
-        print(json.dumps(res), flush=True)
+        emit_line(res, out_fd)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
