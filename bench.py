@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1 gradient exchange: fused NVLink reduce+Adam+broadcast kernel, or NCCL all-reduce")
+    ap.add_argument("--views", type=int, default=None,
+                    help="profiling knob: override the number of views of --config (small ncu cases)")
     ap.add_argument("--binning", default="contributing", choices=["contributing", "reference"],
                     help="tile lists: contributing pairs only (default) or the reference's full lists")
     return ap.parse_args()
@@ -698,7 +700,9 @@ def main():
     sys.stdout.flush()
     out_fd = os.dup(1)
     os.dup2(2, 1)
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.views:
+        cfg["views"] = args.views
     if args.impl == "reference":
         if rank == 0:
             if args.config == "c1":

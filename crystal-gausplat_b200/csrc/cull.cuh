@@ -107,6 +107,55 @@ __device__ __forceinline__ bool tile_culled(float4 g0, float conic_c, float o, f
   return cull_tile(cull_prepare(g0, conic_c, o, alpha_min), rx0, rx1, ry0, ry1);
 }
 
+// Row form of the same test, for contributing-pairs binning. The region that
+// can pass the alpha test is inside the ellipse q(d) <= thr (thr as above).
+// Its intersection with a horizontal strip dy in [y0, y1] is convex, so its x
+// projection is one interval [xl, xr]: xl is the left boundary x(dy) = (-B dy -
+// sqrt(A thr - det dy^2)) / A (convex in dy) at its minimiser clamped into the
+// strip, i.e. the ellipse's leftmost point dy_l = B sqrt(thr / (C det)), and xr
+// likewise at -dy_l. A tile of the row survives iff its pixel-centre span
+// [rx0, rx1] meets [xl, xr]. The interval is widened by 1e-2 px + 2e-3 of the
+// ellipse's half-width sqrt(thr C / det), and the strip's reach by the same
+// share of its half-height, which covers the rounding of this evaluation (the
+// cancellation in A thr - det dy^2 contributes at most sqrt(2 eps thr / A), a
+// sixth of that share); the culled set is therefore a subset of the exact one.
+struct RowCull {
+  float mx, my, A, B, det, thr, dyl, ye, pad;
+  int kind;  // 0: never culled, 1: culled everywhere, 2: test each row
+};
+
+__device__ __forceinline__ RowCull row_cull_prepare(float4 g0, float conic_c, float o, float alpha_min) {
+  const CullGauss c = cull_prepare(g0, conic_c, o, alpha_min);
+  RowCull r;
+  r.kind = c.kind;
+  if (c.kind != 2) return r;
+  r.mx = c.mx; r.my = c.my; r.A = c.A; r.B = c.B; r.thr = c.thr;
+  r.det = c.A * c.C - c.B * c.B;
+  if (!(r.det > 0.0f)) {
+    r.kind = 0;
+    return r;
+  }
+  const float xe = sqrtf(r.thr * c.C / r.det), ye = sqrtf(r.thr * c.A / r.det);
+  r.dyl = c.B * sqrtf(r.thr / (c.C * r.det));
+  r.pad = 1e-2f + 2e-3f * xe;
+  r.ye = ye + 1e-2f + 2e-3f * ye;
+  return r;
+}
+
+// Interval [xl, xr] (relative to the mean, widened) of the strip of pixel-centre
+// rows [ry0, ry1]; false if the strip misses the ellipse.
+__device__ __forceinline__ bool row_extent(const RowCull& r, float ry0, float ry1, float* xl, float* xr) {
+  const float y0 = ry0 - r.my, y1 = ry1 - r.my;
+  if (y0 > r.ye || y1 < -r.ye) return false;
+  const float a = fmaxf(y0, -r.ye), b = fminf(y1, r.ye);
+  const float dl = fminf(fmaxf(r.dyl, a), b), dr = fminf(fmaxf(-r.dyl, a), b);
+  const float Dl = fmaxf(0.0f, r.A * r.thr - r.det * dl * dl);
+  const float Dr = fmaxf(0.0f, r.A * r.thr - r.det * dr * dr);
+  *xl = (-r.B * dl - sqrtf(Dl)) / r.A - r.pad;
+  *xr = (-r.B * dr + sqrtf(Dr)) / r.A + r.pad;
+  return true;
+}
+
 // Pixel-centre rectangle of tile (tx, ty) in a width x height image.
 __device__ __forceinline__ void tile_pixel_rect(int tx, int ty, int width, int height, float* rx0, float* rx1,
                                                 float* ry0, float* ry1) {

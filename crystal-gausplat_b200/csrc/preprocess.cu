@@ -26,11 +26,6 @@ constexpr int kShRow = 13;  // float4 per staged SH row (12 used + 1 pad)
 // view's buffers.
 __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs a) {
   __shared__ float4 s_sh[kPreThreads * kShRow];
-  // contributing-pairs binning: per-thread cull terms, rect {x0, y0, width, 2^16/width rounded up},
-  // number of tile tests and the warp's inclusive scan of it
-  __shared__ CullGauss s_cg[kPreThreads];
-  __shared__ int4 s_rect[kPreThreads];
-  __shared__ uint32_t s_incl[kPreThreads];
   const int64_t base = (int64_t)blockIdx.x * kPreThreads;
   const int64_t i = base + threadIdx.x;
   const int64_t n = a.n;
@@ -69,7 +64,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
     const bool stage_out = a.nviews == 1;  // the per-Gaussian outputs of the stage entry point
     uint32_t tiles = 0;
     float col_b = 0.0f, depth_o = 0.0f, radius_o = 0.0f;
-    uint32_t nt = 0;  // tile tests of this thread's Gaussian (contributing-pairs binning)
+    uint32_t nt = 0;  // contributing tiles of this thread's Gaussian (contributing-pairs binning)
     if (i < n) {
       Projected pr;
       project(p, c3, cam, cfg, &pr);
@@ -97,12 +92,32 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
       }
       const float o_eff = (pr.visible && pr.det > 0.0f) ? o : 0.0f;
       const float4 g0 = make_float4(px, py, pr.A, pr.B);
-      // Contributing-pairs binning: the rect's tiles (<= 64) are tested below by the whole warp.
-      if (a.tile_mask_v[v] && tiles > 0 && tiles <= 64) {
-        s_cg[threadIdx.x] = cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
-        const int w = x1 - x0 + 1;
-        s_rect[threadIdx.x] = make_int4(x0, y0, w, (65536 + w - 1) / w);
-        nt = tiles;
+      // Contributing-pairs binning: the rect's tiles (<= 64) that meet the
+      // ellipse, row by row (bit = row-major position in the rect).
+      if (a.tile_mask_v[v]) {
+        uint64_t mask = ~0ull;
+        if (tiles > 0 && tiles <= 64) {
+          const RowCull rc = row_cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
+          if (rc.kind != 0) {
+            mask = 0ull;
+            int bit = 0;
+            for (int ty = y0; ty <= y1; ty++) {
+              float ry0, ry1, xl = 0.0f, xr = -1.0f, rx0, rx1;
+              tile_pixel_rect(x0, ty, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
+              const bool hit = rc.kind == 2 && row_extent(rc, ry0, ry1, &xl, &xr);
+              for (int tx = x0; tx <= x1; tx++, bit++) {
+                tile_pixel_rect(tx, ty, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
+                if (hit && rx1 - rc.mx >= xl && rx0 - rc.mx <= xr) mask |= 1ull << bit;
+              }
+            }
+          } else {
+            mask = tiles == 64 ? ~0ull : (1ull << tiles) - 1ull;
+          }
+          nt = (uint32_t)__popcll(mask);
+        } else {
+          nt = tiles;
+        }
+        a.tile_mask_v[v][i] = mask;
       }
       float4* sp = reinterpret_cast<float4*>(a.splats_v[v]) + i * 3;
       sp[0] = g0;
@@ -120,50 +135,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
       }
     }
 
-    // Tile tests of the warp's Gaussians, flattened over its lanes so that one
-    // large rectangle does not hold the other 31 lanes: in round `base`, lane l
-    // runs test base + l, which belongs to the first lane whose inclusive count
-    // exceeds it. The round's results come back as one ballot, from which every
-    // lane copies the bits of its own tests into its mask (bit = row-major
-    // position in its rect). The row of test t of a rect of width w is
-    // (t * ceil(2^16 / w)) >> 16, exact for t < 64 <= 2^16 / w.
-    uint32_t emit = tiles;
-    if (a.tile_mask_v[v]) {
-      const int lane = threadIdx.x & 31, wb = threadIdx.x & ~31;
-      uint32_t incl = nt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += t;
-      }
-      const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-      const uint32_t first = incl - nt;  // this lane's tests are [first, incl)
-      s_incl[threadIdx.x] = incl;
-      __syncwarp();
-      uint64_t mask = 0ull;
-      int own = 0;
-      for (uint32_t rb = 0; rb < total; rb += 32) {
-        const uint32_t k = rb + lane;
-        bool keep = false;
-        if (k < total) {
-          while (s_incl[wb + own] <= k) own++;
-          const uint32_t local = k - (own ? s_incl[wb + own - 1] : 0u);
-          const int4 r = s_rect[wb + own];
-          const uint32_t ry = (local * (uint32_t)r.w) >> 16, rx = local - ry * (uint32_t)r.z;
-          float rx0, rx1, ry0, ry1;
-          tile_pixel_rect(r.x + (int)rx, r.y + (int)ry, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
-          keep = !cull_tile(s_cg[wb + own], rx0, rx1, ry0, ry1);
-        }
-        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-        const uint32_t lo = max(first, rb), hi = min(incl, rb + 32);
-        if (lo < hi) mask |= ((uint64_t)(bal >> (lo - rb)) & ((1ull << (hi - lo)) - 1ull)) << (lo - first);
-      }
-      if (i < n) {
-        if (nt) emit = (uint32_t)__popcll(mask);
-        a.tile_mask_v[v][i] = nt ? mask : ~0ull;
-      }
-      __syncwarp();  // the shared rect / cull terms are rewritten by the next view
-    }
+    const uint32_t emit = a.tile_mask_v[v] ? nt : tiles;
     if (i < n) {
       reinterpret_cast<float4*>(a.splats_v[v])[i * 3 + 2] =
           make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));

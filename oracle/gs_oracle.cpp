@@ -770,18 +770,13 @@ static float log_series(float x) {
   return (float)e * 0.69314718f + 2.0f * s * p;
 }
 
-// True if no pixel centre of [rx0, rx1] x [ry0, ry1] can reach alpha_min:
-// the fp32 minimum over the rectangle of the conic's quadratic form against
-// -2 ln(alpha_min / o), with margins (2e-3 relative and absolute, 1e-4 in ln,
-// refused when 1 - |B|/sqrt(AC) < 1e-3) that cover the rounding of this and of
-// the per-pixel evaluation. Per-Gaussian terms first, then the four edge
-// candidates of the rectangle.
-static float cull_form(float A, float B, float C, float dx, float dy) {
-  return A * dx * dx + 2.0f * B * dx * dy + C * dy * dy;
-}
-
-static bool tile_culled(float mx, float my, float A, float B, float C, float o, float rx0,
-                        float rx1, float ry0, float ry1, float alpha_min) {
+// Row form used by contributing-pairs binning: the ellipse q <= thr cut by the
+// tile's row strip projects to one x interval [xl, xr] (from the leftmost and
+// rightmost points of the ellipse clamped into the strip), widened by
+// 1e-2 px + 2e-3 of the half-width (and the strip's reach likewise); the tile
+// survives iff its pixel-centre span meets it.
+static bool row_culled(float mx, float my, float A, float B, float C, float o, float rx0, float rx1,
+                       float ry0, float ry1, float alpha_min) {
   if (!std::isfinite(mx) || !std::isfinite(my)) return false;
   if (!(o > 0.0f)) return o == 0.0f && std::isfinite(A) && std::isfinite(B) && std::isfinite(C);
   if (!(A > 0.0f && C > 0.0f) || !std::isfinite(A) || !std::isfinite(B) || !std::isfinite(C)) return false;
@@ -789,20 +784,22 @@ static bool tile_culled(float mx, float my, float A, float B, float C, float o, 
   if (!(1.0f - rho >= 1e-3f)) return false;
   const float cut = log_series(alpha_min / o) - 1e-4f;
   if (cut >= 0.0f) return true;
-  const float nbc = -B / C, nba = -B / A;
   const float thr = -2.0f * cut * (1.0f + 2e-3f) + 2e-3f;
-  const float x0 = rx0 - mx, x1 = rx1 - mx, y0 = ry0 - my, y1 = ry1 - my;
-  if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return false;
-  float qmin = INFINITY;
-  for (int e = 0; e < 2; e++) {
-    const float dx = e ? x1 : x0;
-    qmin = std::fmin(qmin, cull_form(A, B, C, dx, std::fmin(std::fmax(dx * nbc, y0), y1)));
-  }
-  for (int e = 0; e < 2; e++) {
-    const float dy = e ? y1 : y0;
-    qmin = std::fmin(qmin, cull_form(A, B, C, std::fmin(std::fmax(dy * nba, x0), x1), dy));
-  }
-  return qmin > thr;
+  const float det = A * C - B * B;
+  if (!(det > 0.0f)) return false;
+  const float xe = std::sqrt(thr * C / det), ye0 = std::sqrt(thr * A / det);
+  const float dyl = B * std::sqrt(thr / (C * det));
+  const float pad = 1e-2f + 2e-3f * xe;
+  const float ye = ye0 + 1e-2f + 2e-3f * ye0;
+  const float y0 = ry0 - my, y1 = ry1 - my;
+  if (y0 > ye || y1 < -ye) return true;
+  const float a = std::fmax(y0, -ye), b = std::fmin(y1, ye);
+  const float dl = std::fmin(std::fmax(dyl, a), b), dr = std::fmin(std::fmax(-dyl, a), b);
+  const float Dl = std::fmax(0.0f, A * thr - det * dl * dl);
+  const float Dr = std::fmax(0.0f, A * thr - det * dr * dr);
+  const float xl = (-B * dl - std::sqrt(Dl)) / A - pad;
+  const float xr = (-B * dr + std::sqrt(Dr)) / A + pad;
+  return !(rx1 - mx >= xl && rx0 - mx <= xr);
 }
 
 int64_t gso_contributing_lists(int32_t W, int32_t H, int64_t m, const uint64_t* keys,
@@ -819,8 +816,8 @@ int64_t gso_contributing_lists(int32_t W, int32_t H, int64_t m, const uint64_t* 
       const int tx = (int)(tile % (uint32_t)tiles_x), ty = (int)(tile / (uint32_t)tiles_x);
       const float rx0 = tx * 16 + 0.5f, ry0 = ty * 16 + 0.5f;
       const float rx1 = std::min(tx * 16 + 16, W) - 0.5f, ry1 = std::min(ty * 16 + 16, H) - 0.5f;
-      keep = !tile_culled(mean2d[2 * id], mean2d[2 * id + 1], conic[3 * id], conic[3 * id + 1],
-                          conic[3 * id + 2], opacity[id], rx0, rx1, ry0, ry1, alpha_min);
+      keep = !row_culled(mean2d[2 * id], mean2d[2 * id + 1], conic[3 * id], conic[3 * id + 1],
+                         conic[3 * id + 2], opacity[id], rx0, rx1, ry0, ry1, alpha_min);
     }
     if (keep) {
       out_keys[k] = keys[i];
