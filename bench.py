@@ -267,7 +267,9 @@ def stage_work(stats, n, keys_per_view, pge, tiles, end_bit, batch=1):
         "preprocess": ("hbm", (PARAM_ROW_B / batch + 64) * n, 1.0 / batch),
         "scan": ("hbm", 4 * n + 16 * n, 2),  # order gather + splat word, then the block-sum scan
         "emit": ("hbm", (4 + 32 + 8) * n + 8 * m, 1),  # order, record words, tile mask; packed pairs
-        "sort": ("hbm", packed_sort_bytes(32) * n + packed_sort_bytes(tb) * m, 2),
+        # depth sort: per view (32 bits), or one per batch over view << 32 | depth (36 bits)
+        "sort": ("hbm", packed_sort_bytes(36 if batch > 1 else 32) * n + packed_sort_bytes(tb) * m,
+                 1 + (1.0 / batch if batch > 1 else 1)),
         "ranges": ("hbm", 4 * m + 8 * tiles, 1),
         "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge, 1),
         "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge, 1),

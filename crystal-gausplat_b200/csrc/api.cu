@@ -79,6 +79,7 @@ struct gsc_frame {
   int64_t n = 0, num_keys = 0;
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
   float* image_ptr = nullptr;  // image the last forward wrote (caller's or frame's)
+  const uint32_t* order_ptr = nullptr;  // depth order of the last forward (own buffer or a batch's)
   bool has_forward = false;
   bool has_grad2d = false;  // a backward left grad2d for this forward
 };
@@ -140,6 +141,8 @@ GSC_API int gsc_destroy(gsc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch.ptr) cudaFree(ctx->scratch.ptr);
+  if (ctx->batch_pairs.ptr) cudaFree(ctx->batch_pairs.ptr);
+  if (ctx->batch_order.ptr) cudaFree(ctx->batch_order.ptr);
   if (ctx->err) cudaFree(ctx->err);
   if (ctx->pinned) cudaFreeHost(ctx->pinned);
   delete ctx;
@@ -549,6 +552,7 @@ int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gs
     image = (float*)f->image.ptr;
   }
   f->image_ptr = image;
+  f->order_ptr = (const uint32_t*)f->order.ptr;
   f->keys_valid = false;
   return GSC_OK;
 }
@@ -557,11 +561,12 @@ uint64_t* frame_mask(gsc_frame* f, const gsc_raster_config* cfg) {
   return cfg->binning == GSC_BIN_CONTRIBUTING ? (uint64_t*)f->tile_mask.ptr : nullptr;
 }
 
-int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f) {
+int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true) {
   const int64_t n = f->n;
   // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and
   //    sink); packed (depth << 32 | index) words, split into keys and order
-  if (n > 0) {
+  //    (a batched forward has sorted every view's words together already)
+  if (n > 0 && sort_depth) {
     GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed(n, 32, 64)));
     StageScope sc(ctx, GSC_STAGE_SORT);
     sc.kernels(n > 1 ? 1 + 4 : 1);
@@ -573,7 +578,7 @@ int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f) {
   {
     StageScope sc(ctx, GSC_STAGE_SCAN);
     sc.kernels(1);
-    GS_TRY(launch_block_sums_gather((const float*)f->splats.ptr, (const uint32_t*)f->order.ptr, n,
+    GS_TRY(launch_block_sums_gather((const float*)f->splats.ptr, f->order_ptr, n,
                                     (uint32_t*)f->block_sums.ptr, ctx->stream));
   }
   StageScope sc(ctx, GSC_STAGE_SCAN);
@@ -603,7 +608,7 @@ int forward_finish(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uin
     {
       StageScope sc(ctx, GSC_STAGE_EMIT);
       sc.kernels(1);
-      GS_TRY(launch_emit_tiles(splats, (const uint32_t*)f->order.ptr, n, (const uint64_t*)f->offsets.ptr, tx, ty,
+      GS_TRY(launch_emit_tiles(splats, f->order_ptr, n, (const uint64_t*)f->offsets.ptr, tx, ty,
                                frame_mask(f, cfg), pairs, ctx->stream));
     }
     // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
@@ -641,7 +646,7 @@ int forward_finish(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uin
 
 // One preprocess launch for the frames (all of one image size).
 int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams, int k,
-                       const gsc_gaussians* g, const gsc_raster_config* cfg) {
+                       const gsc_gaussians* g, const gsc_raster_config* cfg, uint64_t* batch_words = nullptr) {
   PreprocessArgs a;
   std::memset(&a, 0, sizeof a);
   a.n = g->count;
@@ -654,9 +659,10 @@ int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera*
   for (int v = 0; v < k; v++) {
     a.cams[v] = cams[v];
     a.splats_v[v] = (float*)frames[v]->splats.ptr;
-    a.depth_pairs_v[v] = (uint64_t*)frames[v]->depth_pairs.ptr;
+    a.depth_pairs_v[v] = batch_words ? batch_words + (size_t)v * g->count : (uint64_t*)frames[v]->depth_pairs.ptr;
     a.tile_mask_v[v] = frame_mask(frames[v], cfg);
   }
+  a.view_key = batch_words != nullptr;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
@@ -690,8 +696,31 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
       GS_REQUIRE(frames[u] != frames[v], "gsc_rasterize_forward_batch: a frame appears twice");
     GS_TRY(forward_prepare(ctx, frames[v], g, &cams[v], cfg, images ? images[v] : nullptr));
   }
-  GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg));
-  for (int v = 0; v < nviews; v++) GS_TRY(forward_sort_scan(ctx, frames[v]));
+  const int64_t n = g->count;
+  if (nviews > 1 && n > 1 && n < (1ll << 28)) {
+    // One depth sort for the whole batch: view << 60 | bits(depth) << 28 |
+    // index words sorted by bits [28, 64), i.e. by view, then depth; view v's
+    // order is the v-th run of n indices.
+    const int64_t total = (int64_t)nviews * n;
+    GS_TRY(ensure(ctx, &ctx->batch_pairs, (size_t)total * 8));
+    GS_TRY(ensure(ctx, &ctx->batch_order, (size_t)total * 4));
+    uint64_t* words = (uint64_t*)ctx->batch_pairs.ptr;
+    uint32_t* order = (uint32_t*)ctx->batch_order.ptr;
+    GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg, words));
+    {
+      GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed(total, 28, 64)));
+      StageScope sc(ctx, GSC_STAGE_SORT);
+      sc.kernels(1 + 5);
+      GS_TRY(launch_sort_packed(ctx, words, total, 28, 64, nullptr, order, scratch_base(ctx), 0x0FFFFFFFu));
+    }
+    for (int v = 0; v < nviews; v++) {
+      frames[v]->order_ptr = order + (size_t)v * n;
+      GS_TRY(forward_sort_scan(ctx, frames[v], false));
+    }
+  } else {
+    GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg));
+    for (int v = 0; v < nviews; v++) GS_TRY(forward_sort_scan(ctx, frames[v]));
+  }
   // one readback of every view's pair count
   uint64_t m[GSC_MAX_BATCH_VIEWS] = {};
   if (g->count) {

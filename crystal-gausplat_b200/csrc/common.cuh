@@ -128,6 +128,8 @@ struct gsc_ctx {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   GsBuf scratch;              // per-call temporary storage (sort double buffer, ...)
+  GsBuf batch_pairs;          // batched forward: every view's packed depth words
+  GsBuf batch_order;          // batched forward: every view's depth order
   uint32_t* err = nullptr;    // device error word
   void* pinned = nullptr;     // 4 KB pinned host staging for small readbacks
   // tracing

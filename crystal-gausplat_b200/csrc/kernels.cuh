@@ -20,8 +20,11 @@ struct PreprocessArgs {
   int nviews;
   gsc_camera cams[kMaxBatchViews];
   float* splats_v[kMaxBatchViews];
-  // bits(depth) (~0 if the Gaussian emits no pair) << 32 | index; may be null
+  // bits(depth) (~0 if the Gaussian emits no pair) << 32 | index; may be null.
+  // With view_key: view << 60 | bits(depth) << 28 | index (index < 2^28), the
+  // words of all views sorted together by bits [28, 64).
   uint64_t* depth_pairs_v[kMaxBatchViews];
+  int view_key;
   // if set: contributing-pairs binning (bit k = k-th tile of the rect, row-major;
   // ~0 = the whole rect) and the record's tile count is the contributing one
   uint64_t* tile_mask_v[kMaxBatchViews];
@@ -135,11 +138,11 @@ int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, i
                       int end_bit, char* scratch);
 size_t sort_scratch_bytes_u32(int64_t n, int begin_bit, int end_bit);
 // Stable sort of packed u64 (key << 32 | value) by bits [begin_bit, end_bit) of
-// the u64 (within the key word); the sorted words go to hi_out / lo_out.
-// `pairs` is overwritten.
+// the u64; the sorted words go to hi_out (may be null) / lo_out (low word &
+// lo_mask). `pairs` is overwritten.
 size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit);
 int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
-                       uint32_t* lo_out, char* scratch);
+                       uint32_t* lo_out, char* scratch, uint32_t lo_mask = 0xFFFFFFFFu);
 int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                           int end_bit, char* scratch);
 int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream);

@@ -139,8 +139,11 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
     if (i < n) {
       reinterpret_cast<float4*>(a.splats_v[v])[i * 3 + 2] =
           make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
-      if (a.depth_pairs_v[v])
-        a.depth_pairs_v[v][i] = ((uint64_t)(emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu) << 32) | (uint64_t)i;
+      if (a.depth_pairs_v[v]) {
+        const uint64_t kb = emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu;
+        a.depth_pairs_v[v][i] = a.view_key ? ((uint64_t)v << 60) | (kb << 28) | (uint64_t)i
+                                           : (kb << 32) | (uint64_t)i;
+      }
     }
   }
 }

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
-    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr) {
+    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu) {
   __shared__ K s_keys[kTileKeys];  // reused for values
   __shared__ uint32_t s_whist[kWarps][256];
   __shared__ uint32_t s_local_excl[256];
@@ -200,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
     if ((int64_t)gpos >= n) {
       atomicOr(err, GS_DEVERR_BOUNDS);
     } else if (MODE == 2) {
-      keys_hi[gpos] = (uint32_t)((uint64_t)key >> 32);
-      vals_out[gpos] = (uint32_t)key;
+      if (keys_hi) keys_hi[gpos] = (uint32_t)((uint64_t)key >> 32);
+      vals_out[gpos] = (uint32_t)key & lo_mask;
     } else {
       keys_out[gpos] = key;
     }
@@ -290,12 +290,13 @@ int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t 
 }
 
 __global__ void __launch_bounds__(256) split_words_kernel(const uint64_t* __restrict__ in, int64_t n,
-                                                          uint32_t* __restrict__ hi, uint32_t* __restrict__ lo) {
+                                                          uint32_t* __restrict__ hi, uint32_t* __restrict__ lo,
+                                                          uint32_t lo_mask) {
   const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
   if (i >= n) return;
   const uint64_t v = in[i];
-  hi[i] = (uint32_t)(v >> 32);
-  lo[i] = (uint32_t)v;
+  if (hi) hi[i] = (uint32_t)(v >> 32);
+  lo[i] = (uint32_t)v & lo_mask;
 }
 
 size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit) {
@@ -303,12 +304,12 @@ size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit) {
 }
 
 int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
-                       uint32_t* lo_out, char* scratch) {
+                       uint32_t* lo_out, char* scratch, uint32_t lo_mask) {
   cudaStream_t stream = ctx->stream;
   if (n <= 0) return GSC_OK;
   const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
   if (n == 1 || npass == 0) {
-    split_words_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(pairs, n, hi_out, lo_out);
+    split_words_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(pairs, n, hi_out, lo_out, lo_mask);
     GS_CK_LAUNCH("split_words_kernel");
     return GSC_OK;
   }
@@ -336,7 +337,7 @@ int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, 
     } else {
       onesweep_kernel<uint64_t, 2><<<(unsigned)parts, kThreads, 0, stream>>>(
           src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + p * 256,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out);
+          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask);
     }
     GS_CK_LAUNCH("onesweep_kernel");
     std::swap(src, dst);

@@ -61,3 +61,4 @@ def test_bench_work_model():
     w8 = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45, batch=8)
     assert w8["preprocess"] == ("hbm", (236 / 8 + 64) * 1000, 1 / 8)
     assert w8["preprocess_bwd"] == ("hbm", (3 * 236 / 8 + 36) * 1000, 1 / 8)
+    assert w8["sort"] == ("hbm", (8 + 16 * 5) * 1000 + (8 + 16 * 2) * 5000, 1 + 1 / 8)
