@@ -9,8 +9,9 @@
 // T > t_stop. The CTA leaves as soon as every pixel is done.
 //
 // Backward replaces rasterize_backward (gaussian.metal:452-567): batches are
-// staged back to front; per Gaussian each thread forms its 9 partials, a warp
-// butterfly reduces them and lane 0 issues the global atomics. The L1 loss
+// staged back to front; per Gaussian each thread forms its 9 partials, the
+// warp sums them through a shared-memory transpose and lanes 0-8 issue the
+// global atomics. The L1 loss
 // gradient (src/ops/loss.cr:33-57) is fused into the per-pixel load.
 //
 // Skip test: a Gaussian with power < power_cut has o*G < alpha_min for every
@@ -144,28 +145,6 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// Sum of 9 per-lane values over the warp by transposed halving: at each of
-// the first four levels a lane keeps half of its slots and receives the
-// partner's sums for them, so 8 + 4 + 2 + 1 + 1 shuffles replace 9 x 5.
-// On return, even lane 2k < 18 holds the warp total of slot k.
-__device__ __forceinline__ float warp_reduce9(const float v[9], int lane) {
-  float a[16];
-#pragma unroll
-  for (int i = 0; i < 16; i++) a[i] = i < 9 ? v[i] : 0.0f;
-#pragma unroll
-  for (int lvl = 0; lvl < 4; lvl++) {
-    const int off = 16 >> lvl, half = 8 >> lvl;
-    const bool up = lane & off;
-#pragma unroll
-    for (int i = 0; i < half; i++) {
-      const float send = up ? a[i] : a[i + half];
-      const float keep = up ? a[i + half] : a[i];
-      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return a[0] + __shfl_xor_sync(0xffffffffu, a[0], 1);
-}
-
 // One pixel's backward state.
 struct BwdPixel {
   bool inside;
@@ -244,6 +223,8 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
   __shared__ uint32_t s_cnt[kBwdWarps];
   __shared__ uint32_t s_hi;
   __shared__ float s_loss[kBwdWarps];
+  // per-warp transpose buffer of the 9 partials (rows padded to 36 floats)
+  __shared__ __align__(16) float s_red[kBwdWarps][9 * 36];
   const int tile = blockIdx.x;
   const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -343,9 +324,21 @@ __global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(Composite
 #pragma unroll
       for (int h = 0; h < kBwdPix; h++) ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
       if (__any_sync(0xffffffffu, ok)) {
-        const float r = warp_reduce9(v, lane);
-        const int k = lane >> 1;
-        if (!(lane & 1) && k < 9 && r != 0.0f) atomicAdd(a.grad2d + (size_t)s_gid[j] * 9 + k, r);
+        float* red = s_red[tid >> 5];
+#pragma unroll
+        for (int k = 0; k < 9; k++) red[k * 36 + lane] = v[k];
+        __syncwarp();
+        if (lane < 9) {
+          const float4* row = reinterpret_cast<const float4*>(red + lane * 36);
+          float r = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const float4 t = row[q];
+            r += (t.x + t.y) + (t.z + t.w);
+          }
+          if (r != 0.0f) atomicAdd(a.grad2d + (size_t)s_gid[j] * 9 + lane, r);
+        }
+        __syncwarp();
       }
     }
   }
