@@ -228,9 +228,11 @@ def pge_count(gs, rctx):
 # ---------------------------------------------------------------------------
 # algorithmic work per stage (bytes, or FP32 ops for compositing)
 # ---------------------------------------------------------------------------
-# DRAM bytes per launch measured by ncu for the config-3 compositing kernels
-# (profiles/composite_traffic_c3.md).
-TRAFFIC_C3 = {"composite_fwd": 83.75e6, "composite_bwd": 146.49e6}
+# DRAM bytes per launch (per view for the sort) measured by ncu on config 3
+# (profiles/binning_sort_preprocess_c3.md).
+TRAFFIC_C3 = {"composite_fwd": 50.3e6, "composite_bwd": 116.2e6,
+              # per view: batched depth sort (1/8 of histogram + 5 passes) + tile sort
+              "sort": 1212e6}
 
 PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
 PARAM_ROW_B = 236  # the 59 floats of one Gaussian
@@ -438,7 +440,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
                              peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind,
                              traffic=TRAFFIC_C3.get(dominant) if args.config == "c3" else None)
             if dominant else None,
-            "roofline_hbm": dict(roof[top_hbm], kernel=top_hbm, peak_kind=peak_kind, traffic=None)
+            "roofline_hbm": dict(roof[top_hbm], kernel=top_hbm, peak_kind=peak_kind,
+                                 traffic=TRAFFIC_C3.get(top_hbm) if args.config == "c3" else None)
             if top_hbm else None,
             "stages": roof,
         }
