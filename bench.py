@@ -264,11 +264,11 @@ def stage_work(stats, n, keys_per_view, pge, tiles, end_bit, batch=1):
     tb = end_bit - 32
     m = keys_per_view
     return {
-        # one launch per `batch` views: parameters read once, per view a 48 B record
-        # + 8 B tile mask + 8 B packed depth word
-        "preprocess": ("hbm", (PARAM_ROW_B / batch + 64) * n, 1.0 / batch),
-        "scan": ("hbm", 4 * n + 16 * n, 2),  # order gather + splat word, then the block-sum scan
-        "emit": ("hbm", (4 + 32 + 8) * n + 8 * m, 1),  # order, record words, tile mask; packed pairs
+        # one launch per `batch` views: parameters read once, per view a 48 B splat
+        # record + 32 B binning record + 8 B packed depth word
+        "preprocess": ("hbm", (PARAM_ROW_B / batch + 88) * n, 1.0 / batch),
+        "scan": ("hbm", 4 * n + 16 * n, 2),  # order + binning-record word gather, then the block-sum scan
+        "emit": ("hbm", (4 + 32) * n + 8 * m, 1),  # order + 32 B binning record; packed pairs
         # depth sort: per view (32 bits), or one per batch over view << 32 | depth (36 bits)
         "sort": ("hbm", packed_sort_bytes(36 if batch > 1 else 32) * n + packed_sort_bytes(tb) * m,
                  1 + (1.0 / batch if batch > 1 else 1)),

@@ -74,7 +74,7 @@ using namespace gs;
 struct gsc_frame {
   gsc_ctx* ctx = nullptr;
   GsBuf splats, depth_pairs, depth_keys, order, pairs, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
-      last, n_contrib, grad2d, tile_mask;
+      last, n_contrib, grad2d, bins;
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
@@ -241,8 +241,7 @@ static int check_view(const gsc_camera* cam, const gsc_raster_config* cfg) {
 
 static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera* cam,
                          const gsc_raster_config* cfg, const gsc_projected* o, uint32_t* block_sums,
-                         uint64_t* depth_pairs = nullptr,
-                         uint64_t* tile_mask = nullptr) {
+                         uint64_t* depth_pairs = nullptr) {
   PreprocessArgs a;
   std::memset(&a, 0, sizeof a);
   a.n = g->count;
@@ -259,7 +258,6 @@ static int do_preprocess(gsc_ctx* ctx, const gsc_gaussians* g, const gsc_camera*
   a.mean2d = o->mean2d; a.cov2d = o->cov2d; a.conic = o->conic; a.depth = o->depth;
   a.radius = o->radius; a.colors = o->colors; a.opacity = o->opacity;
   a.tiles_touched = o->tiles_touched; a.cov3d = o->cov3d;
-  a.tile_mask_v[0] = tile_mask;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
@@ -506,7 +504,7 @@ GSC_API int gsc_frame_destroy(gsc_frame* f) {
   cudaStreamSynchronize(f->ctx->stream);
   GsBuf* bufs[] = {&f->splats, &f->depth_pairs, &f->pairs, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
-                   &f->n_contrib, &f->grad2d, &f->tile_mask};
+                   &f->n_contrib, &f->grad2d, &f->bins};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
   delete f;
@@ -546,7 +544,7 @@ int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gs
   GS_TRY(ensure(ctx, &f->final_T, npix * 4));
   GS_TRY(ensure(ctx, &f->last, npix * 4));
   GS_TRY(ensure(ctx, &f->n_contrib, npix * 4));
-  if (cfg->binning == GSC_BIN_CONTRIBUTING) GS_TRY(ensure(ctx, &f->tile_mask, (size_t)n * 8 + 8));
+  GS_TRY(ensure(ctx, &f->bins, (size_t)n * 32 + 32));
   if (!image) {
     GS_TRY(ensure(ctx, &f->image, npix * 12));
     image = (float*)f->image.ptr;
@@ -557,9 +555,7 @@ int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gs
   return GSC_OK;
 }
 
-uint64_t* frame_mask(gsc_frame* f, const gsc_raster_config* cfg) {
-  return cfg->binning == GSC_BIN_CONTRIBUTING ? (uint64_t*)f->tile_mask.ptr : nullptr;
-}
+const uint4* frame_bins(const gsc_frame* f) { return (const uint4*)f->bins.ptr; }
 
 int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true) {
   const int64_t n = f->n;
@@ -578,7 +574,7 @@ int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true) {
   {
     StageScope sc(ctx, GSC_STAGE_SCAN);
     sc.kernels(1);
-    GS_TRY(launch_block_sums_gather((const float*)f->splats.ptr, f->order_ptr, n,
+    GS_TRY(launch_block_sums_gather(frame_bins(f), f->order_ptr, n,
                                     (uint32_t*)f->block_sums.ptr, ctx->stream));
   }
   StageScope sc(ctx, GSC_STAGE_SCAN);
@@ -608,8 +604,8 @@ int forward_finish(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uin
     {
       StageScope sc(ctx, GSC_STAGE_EMIT);
       sc.kernels(1);
-      GS_TRY(launch_emit_tiles(splats, f->order_ptr, n, (const uint64_t*)f->offsets.ptr, tx, ty,
-                               frame_mask(f, cfg), pairs, ctx->stream));
+      GS_TRY(launch_emit_tiles(frame_bins(f), f->order_ptr, n, (const uint64_t*)f->offsets.ptr, tx, pairs,
+                               ctx->stream));
     }
     // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
     //    only, split into tiles and values
@@ -660,9 +656,10 @@ int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera*
     a.cams[v] = cams[v];
     a.splats_v[v] = (float*)frames[v]->splats.ptr;
     a.depth_pairs_v[v] = batch_words ? batch_words + (size_t)v * g->count : (uint64_t*)frames[v]->depth_pairs.ptr;
-    a.tile_mask_v[v] = frame_mask(frames[v], cfg);
+    a.bin_v[v] = (uint4*)frames[v]->bins.ptr;
   }
   a.view_key = batch_words != nullptr;
+  a.contributing = cfg->binning == GSC_BIN_CONTRIBUTING;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);

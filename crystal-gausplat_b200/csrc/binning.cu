@@ -179,12 +179,14 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 // rebuilt on request (make_keys_kernel).
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(256) block_sums_gather_kernel(const float4* __restrict__ splats,
+// `bins`: the 32-byte binning records of preprocess ({x0, y0, width, count},
+// {mask low, mask high, 0, 0}), gathered in depth order, one sector each.
+__global__ void __launch_bounds__(256) block_sums_gather_kernel(const uint4* __restrict__ bins,
                                                                 const uint32_t* __restrict__ order,
                                                                 int64_t n, uint32_t* __restrict__ sums) {
   __shared__ uint32_t s_warp[8];
   const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  uint32_t t = p < n ? __float_as_uint(splats[(size_t)order[p] * 3 + 2].w) : 0u;
+  uint32_t t = p < n ? bins[(size_t)order[p] * 2].w : 0u;
   uint32_t incl = block_incl_scan_256(t, s_warp);
   if (threadIdx.x == 255) sums[blockIdx.x] = incl;
 }
@@ -204,12 +206,10 @@ __device__ __forceinline__ uint32_t select_bit64(uint64_t m, uint32_t k) {
   return pos;
 }
 
-__global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restrict__ splats,
+__global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict__ bins,
                                                          const uint32_t* __restrict__ order, int64_t n,
                                                          const uint64_t* __restrict__ offsets,
-                                                         int tiles_x, int tiles_y,
-                                                         const uint64_t* __restrict__ tile_mask,
-                                                         uint64_t* __restrict__ pair_out) {
+                                                         int tiles_x, uint64_t* __restrict__ pair_out) {
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
   __shared__ uint32_t s_inv[256];  // ceil(2^16 / width): row of a test < 64 by multiply and shift
@@ -220,17 +220,16 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const float4* __restric
   uint32_t t = 0;
   if (p < n) {
     const uint32_t gid = order[p];
-    const float4 s0 = splats[(size_t)gid * 3], s2 = splats[(size_t)gid * 3 + 2];
-    t = __float_as_uint(s2.w);
+    const uint4 b0 = bins[(size_t)gid * 2];
+    t = b0.w;
     if (t) {
-      int x0, x1, y0, y1;
-      tile_bounds(s0.x, s0.y, s2.z, tiles_x, tiles_y, &x0, &x1, &y0, &y1);
-      s_x0[threadIdx.x] = x0;
-      s_y0[threadIdx.x] = y0;
-      s_wx[threadIdx.x] = x1 - x0 + 1;
-      s_inv[threadIdx.x] = (65536u + (uint32_t)(x1 - x0)) / (uint32_t)(x1 - x0 + 1);
+      const uint4 b1 = bins[(size_t)gid * 2 + 1];
+      s_x0[threadIdx.x] = (int)b0.x;
+      s_y0[threadIdx.x] = (int)b0.y;
+      s_wx[threadIdx.x] = (int)b0.z;
+      s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
       s_id[threadIdx.x] = gid;
-      s_mask[threadIdx.x] = tile_mask ? tile_mask[gid] : ~0ull;
+      s_mask[threadIdx.x] = ((uint64_t)b1.y << 32) | b1.x;
     }
   }
   uint32_t incl = block_incl_scan_256(t, s_warp);
@@ -295,21 +294,18 @@ __global__ void __launch_bounds__(256) make_keys_kernel(const uint32_t* __restri
   keys[i] = ((uint64_t)tiles[i] << 32) | depth_bits;
 }
 
-int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t n, uint32_t* sums,
+int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
                              cudaStream_t stream) {
   if (n == 0) return GSC_OK;
-  block_sums_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const float4*>(splats), order, n, sums);
+  block_sums_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, sums);
   GS_CK_LAUNCH("block_sums_gather_kernel");
   return GSC_OK;
 }
 
-int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint64_t* pair_out,
-                      cudaStream_t stream) {
+int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
+                      int tiles_x, uint64_t* pair_out, cudaStream_t stream) {
   if (n == 0) return GSC_OK;
-  emit_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<const float4*>(splats), order, n, offsets, tiles_x, tiles_y, tile_mask, pair_out);
+  emit_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, offsets, tiles_x, pair_out);
   GS_CK_LAUNCH("emit_tiles_kernel");
   return GSC_OK;
 }

@@ -25,9 +25,14 @@ struct PreprocessArgs {
   // words of all views sorted together by bits [28, 64).
   uint64_t* depth_pairs_v[kMaxBatchViews];
   int view_key;
-  // if set: contributing-pairs binning (bit k = k-th tile of the rect, row-major;
-  // ~0 = the whole rect) and the record's tile count is the contributing one
-  uint64_t* tile_mask_v[kMaxBatchViews];
+  // contributing-pairs binning: the binning record's mask has bit k for the
+  // k-th tile of the rect (row-major) that can contribute (~0 = the whole
+  // rect), and the pair count is theirs
+  int contributing;
+  // if set: the binning record of each Gaussian, 32 B (one sector) that the
+  // depth-ordered gathers of the pair counting and the emission read:
+  // {x0, y0, rect width, pair count}, {mask low, mask high, 0, 0}
+  uint4* bin_v[kMaxBatchViews];
   float* mean2d;
   float* cov2d;
   float* conic;
@@ -124,11 +129,10 @@ int launch_emit_keys(const float* splats, int64_t n, const uint64_t* offsets, in
                      int tiles_y, uint64_t* keys, uint32_t* vals, cudaStream_t stream);
 int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint32_t* ranges,
                        cudaStream_t stream);
-int launch_block_sums_gather(const float* splats, const uint32_t* order, int64_t n, uint32_t* sums,
+int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
                              cudaStream_t stream);
-int launch_emit_tiles(const float* splats, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, int tiles_y, const uint64_t* tile_mask, uint64_t* pair_out,
-                      cudaStream_t stream);
+int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
+                      int tiles_x, uint64_t* pair_out, cudaStream_t stream);
 int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
                            cudaStream_t stream);
 int launch_make_keys(const uint32_t* tiles, const uint32_t* ids, const float* splats, int64_t m,

@@ -65,6 +65,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
     uint32_t tiles = 0;
     float col_b = 0.0f, depth_o = 0.0f, radius_o = 0.0f;
     uint32_t nt = 0;  // contributing tiles of this thread's Gaussian (contributing-pairs binning)
+    uint64_t mask_o = ~0ull;
+    int rx_o = 0, ry_o = 0, rw_o = 1;
     if (i < n) {
       Projected pr;
       project(p, c3, cam, cfg, &pr);
@@ -94,7 +96,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
       const float4 g0 = make_float4(px, py, pr.A, pr.B);
       // Contributing-pairs binning: the rect's tiles (<= 64) that meet the
       // ellipse, row by row (bit = row-major position in the rect).
-      if (a.tile_mask_v[v]) {
+      if (a.contributing) {
         uint64_t mask = ~0ull;
         if (tiles > 0 && tiles <= 64) {
           const RowCull rc = row_cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
@@ -117,7 +119,12 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
         } else {
           nt = tiles;
         }
-        a.tile_mask_v[v][i] = mask;
+        mask_o = mask;
+      }
+      if (tiles) {
+        rx_o = x0;
+        ry_o = y0;
+        rw_o = x1 - x0 + 1;
       }
       float4* sp = reinterpret_cast<float4*>(a.splats_v[v]) + i * 3;
       sp[0] = g0;
@@ -135,10 +142,14 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs 
       }
     }
 
-    const uint32_t emit = a.tile_mask_v[v] ? nt : tiles;
+    const uint32_t emit = a.contributing ? nt : tiles;
     if (i < n) {
       reinterpret_cast<float4*>(a.splats_v[v])[i * 3 + 2] =
           make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
+      if (a.bin_v[v]) {
+        a.bin_v[v][2 * i] = make_uint4((uint32_t)rx_o, (uint32_t)ry_o, (uint32_t)rw_o, emit);
+        a.bin_v[v][2 * i + 1] = make_uint4((uint32_t)mask_o, (uint32_t)(mask_o >> 32), 0u, 0u);
+      }
       if (a.depth_pairs_v[v]) {
         const uint64_t kb = emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu;
         a.depth_pairs_v[v][i] = a.view_key ? ((uint64_t)v << 60) | (kb << 28) | (uint64_t)i

@@ -57,8 +57,8 @@ def test_bench_work_model():
     assert bench.packed_sort_bytes(32) == 8 + 16 * 4 and bench.packed_sort_bytes(13) == 8 + 16 * 2
     w = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45)
     assert w["adam"] == ("hbm", 1652 * 1000, 1)
-    assert w["preprocess"][1] == (236 + 64) * 1000
+    assert w["preprocess"][1] == (236 + 88) * 1000
     w8 = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45, batch=8)
-    assert w8["preprocess"] == ("hbm", (236 / 8 + 64) * 1000, 1 / 8)
+    assert w8["preprocess"] == ("hbm", (236 / 8 + 88) * 1000, 1 / 8)
     assert w8["preprocess_bwd"] == ("hbm", (3 * 236 / 8 + 36) * 1000, 1 / 8)
     assert w8["sort"] == ("hbm", (8 + 16 * 5) * 1000 + (8 + 16 * 2) * 5000, 1 + 1 / 8)
