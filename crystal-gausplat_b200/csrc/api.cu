@@ -143,6 +143,12 @@ GSC_API int gsc_destroy(gsc_ctx* ctx) {
   if (ctx->scratch.ptr) cudaFree(ctx->scratch.ptr);
   if (ctx->batch_pairs.ptr) cudaFree(ctx->batch_pairs.ptr);
   if (ctx->batch_order.ptr) cudaFree(ctx->batch_order.ptr);
+  if (ctx->side) {
+    cudaStreamSynchronize(ctx->side);
+    for (auto& e : ctx->side_ev)
+      if (e) cudaEventDestroy(e);
+    cudaStreamDestroy(ctx->side);
+  }
   if (ctx->err) cudaFree(ctx->err);
   if (ctx->pinned) cudaFreeHost(ctx->pinned);
   delete ctx;
@@ -519,7 +525,8 @@ namespace {
 // preprocess launch and a single host readback of their key counts:
 //   forward_prepare   -- buffers and frame fields (no GPU work)
 //   forward_sort_scan -- depth sort, per-block pair counts, scan (device only)
-//   forward_finish    -- emission, tile sort, ranges, compositing, given the pair count
+//   forward_bin       -- emission, tile sort, ranges, given the pair count
+//   forward_composite -- compositing (on a side stream in a batched forward)
 int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gsc_camera* cam,
                     const gsc_raster_config* cfg, float* image) {
   GS_REQUIRE(ctx && f && f->ctx == ctx, "gsc_rasterize_forward: bad context/frame");
@@ -583,11 +590,10 @@ int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true) {
                                 (uint64_t*)f->total.ptr, ctx->stream);
 }
 
-int forward_finish(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64_t m, uint32_t* n_contrib,
-                   float* final_T) {
+int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64_t m) {
+  (void)cfg;
   const int64_t n = f->n;
-  const int W = f->width, H = f->height, tx = f->tiles_x, ty = f->tiles_y;
-  const size_t npix = (size_t)W * H;
+  const int tx = f->tiles_x, ty = f->tiles_y;
   if (m >= (1ull << 30)) {
     set_error("gsc_rasterize_forward: " + std::to_string(m) + " keys exceed the 2^30 limit");
     return GSC_ERR_CAPACITY;
@@ -620,8 +626,16 @@ int forward_finish(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uin
     sc.kernels(m ? 1 : 0);
     GS_TRY(launch_tile_ranges_u32(tiles, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
   }
+  return GSC_OK;
+}
+
+int forward_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint32_t* n_contrib,
+                      float* final_T) {
+  const int W = f->width, H = f->height;
+  const size_t npix = (size_t)W * H;
   CompositeFwdArgs a;
-  fill_fwd(&a, splats, vals, (const uint32_t*)f->ranges.ptr, W, H, cfg);
+  fill_fwd(&a, (const float*)f->splats.ptr, (const uint32_t*)f->vals.ptr, (const uint32_t*)f->ranges.ptr, W, H,
+           cfg);
   a.image = f->image_ptr;
   a.final_T = (float*)f->final_T.ptr;
   a.last = (uint32_t*)f->last.ptr;
@@ -678,7 +692,8 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   uint64_t m = 0;
   if (f->n) GS_TRY(read_u64(ctx, (const uint64_t*)f->total.ptr, &m));
   if (num_rendered) *num_rendered = (int64_t)m;
-  return forward_finish(ctx, f, cfg, m, n_contrib, final_T);
+  GS_TRY(forward_bin(ctx, f, cfg, m));
+  return forward_composite(ctx, f, cfg, n_contrib, final_T);
 }
 
 GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams,
@@ -727,11 +742,29 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
     GS_CK(cudaStreamSynchronize(ctx->stream));
     std::memcpy(m, ctx->pinned, 8 * (size_t)nviews);
   }
-  for (int v = 0; v < nviews; v++) {
-    if (num_rendered) num_rendered[v] = (int64_t)m[v];
-    GS_TRY(forward_finish(ctx, frames[v], cfg, m[v], nullptr, nullptr));
+  // Binning of view v on the caller's stream, its compositing on the side
+  // stream, so that it overlaps the binning of view v + 1 (every view has its
+  // own frame buffers; the sort scratch is used by the caller's stream only).
+  if (!ctx->side) {
+    GS_CK(cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking));
+    for (auto& e : ctx->side_ev) GS_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
-  return GSC_OK;
+  cudaStream_t main_stream = ctx->stream;
+  int rc = GSC_OK;
+  for (int v = 0; v < nviews && rc == GSC_OK; v++) {
+    if (num_rendered) num_rendered[v] = (int64_t)m[v];
+    rc = forward_bin(ctx, frames[v], cfg, m[v]);
+    if (rc) break;
+    GS_CK(cudaEventRecord(ctx->side_ev[v], main_stream));
+    GS_CK(cudaStreamWaitEvent(ctx->side, ctx->side_ev[v], 0));
+    ctx->stream = ctx->side;
+    rc = forward_composite(ctx, frames[v], cfg, nullptr, nullptr);
+    ctx->stream = main_stream;
+  }
+  // the caller's stream waits for every compositing
+  GS_CK(cudaEventRecord(ctx->side_ev[GSC_MAX_BATCH_VIEWS], ctx->side));
+  GS_CK(cudaStreamWaitEvent(main_stream, ctx->side_ev[GSC_MAX_BATCH_VIEWS], 0));
+  return rc;
 }
 
 GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g,

@@ -130,6 +130,10 @@ struct gsc_ctx {
   GsBuf scratch;              // per-call temporary storage (sort double buffer, ...)
   GsBuf batch_pairs;          // batched forward: every view's packed depth words
   GsBuf batch_order;          // batched forward: every view's depth order
+  // batched forward: compositing of view v on `side` overlaps the binning of
+  // view v + 1 on `stream` (created on first use)
+  cudaStream_t side = nullptr;
+  cudaEvent_t side_ev[GSC_MAX_BATCH_VIEWS + 1] = {};
   uint32_t* err = nullptr;    // device error word
   void* pinned = nullptr;     // 4 KB pinned host staging for small readbacks
   // tracing
