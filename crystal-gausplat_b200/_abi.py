@@ -9,7 +9,8 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libgsplat_cuda.so")
+# GSC_LIBRARY: another build of the same library (e.g. a variant being measured)
+LIB_PATH = os.environ.get("GSC_LIBRARY") or os.path.join(HERE, "libgsplat_cuda.so")
 
 GSC_OK = 0
 GSC_ERR_INVALID = -1

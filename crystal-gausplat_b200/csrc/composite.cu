@@ -45,7 +45,15 @@ __device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* tot
   return keep ? base + __popc(bal & ((1u << lane) - 1u)) : -1;
 }
 
-__global__ void __launch_bounds__(256, 4) composite_fwd_kernel(CompositeFwdArgs a) {
+// Minimum resident CTAs per SM (register budget) of the two kernels.
+#ifndef GS_FWD_MIN_CTAS
+#define GS_FWD_MIN_CTAS 5
+#endif
+#ifndef GS_BWD_MIN_CTAS
+#define GS_BWD_MIN_CTAS 7
+#endif
+
+__global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(CompositeFwdArgs a) {
   __shared__ float4 s0[256];
   __shared__ float4 s1[256];
   __shared__ float s2[256];
@@ -214,7 +222,7 @@ constexpr int kBwdWarps = kBwdThreads / 32;
 constexpr int kBwdRowStep = GS_TILE / kBwdPix;        // rows between a thread's pixels
 
 template <bool FULL, bool L1>
-__global__ void __launch_bounds__(kBwdThreads, 6) composite_bwd_kernel(CompositeBwdArgs a) {
+__global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_kernel(CompositeBwdArgs a) {
   __shared__ float4 s0[kBwdThreads];
   __shared__ float4 s1[kBwdThreads];
   __shared__ float s2[kBwdThreads];
