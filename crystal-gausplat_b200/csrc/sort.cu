@@ -78,8 +78,11 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
 
 // MODE: 0 = (key, value) pairs; 1 = packed u64, written packed; 2 = packed
 // u64, written split (high word to keys_hi, low word to vals_out).
+#ifndef GS_PACKED_MIN_CTAS
+#define GS_PACKED_MIN_CTAS 5
+#endif
 template <typename K, int MODE = 0>
-__global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
+__global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) onesweep_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
@@ -88,7 +91,7 @@ __global__ void __launch_bounds__(kThreads, 4) onesweep_kernel(
   __shared__ uint32_t s_whist[kWarps][256];
   __shared__ uint32_t s_local_excl[256];
   __shared__ uint32_t s_gbase[256];
-  __shared__ uint8_t s_dig[kTileKeys];
+  __shared__ uint8_t s_dig[MODE == 0 ? kTileKeys : 1];  // pair mode only
   __shared__ uint32_t s_warp[kWarps];
   __shared__ uint32_t s_part;
 
