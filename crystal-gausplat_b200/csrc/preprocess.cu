@@ -24,7 +24,10 @@ constexpr int kShRow = 13;  // float4 per staged SH row (12 used + 1 pad)
 // terms (scales, quaternion, 3-D covariance, opacity, the staged SH row) are
 // formed once and every view's record, mask and depth word are written to that
 // view's buffers.
-__global__ void __launch_bounds__(kPreThreads) preprocess_kernel(PreprocessArgs a) {
+#ifndef GS_PRE_MIN_CTAS
+#define GS_PRE_MIN_CTAS 8
+#endif
+__global__ void __launch_bounds__(kPreThreads, GS_PRE_MIN_CTAS) preprocess_kernel(PreprocessArgs a) {
   __shared__ float4 s_sh[kPreThreads * kShRow];
   const int64_t base = (int64_t)blockIdx.x * kPreThreads;
   const int64_t i = base + threadIdx.x;
