@@ -21,6 +21,7 @@ try:
     from . import loss as Loss
     from .densify import (GradientAccumulator, densify_and_prune, densify_apply, densify_plan,
                           reset_opacity)
+    from .trainer import DataParallelTrainer, Trainer, TrainerConfig, TrainStats
 except ImportError:  # torch missing: camera/generator helpers stay usable
     pass
 

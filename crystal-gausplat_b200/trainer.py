@@ -236,3 +236,117 @@ class HostTargetFeeder:
             cur.wait_event(self.ready[slot])
             fn(v, self.bufs[slot])
             self.free[slot].record(cur)
+
+
+# ---- the reference's single-view training loop ------------------------------
+
+class TrainerConfig:
+    """TrainerConfig (src/gaussian_splatting/trainer.cr:15-57), same fields and defaults."""
+
+    def __init__(self, iterations=30000, lr_position=0.00016, lr_scale=0.005, lr_rotation=0.001,
+                 lr_opacity=0.05, lr_sh=0.0025, lambda_ssim=0.2, densify_from=500, densify_until=15000,
+                 densify_interval=100, densify_grad_threshold=0.0002, densify_size_threshold=0.01,
+                 prune_interval=100, opacity_threshold=0.005, max_screen_size=20.0,
+                 opacity_reset_interval=3000):
+        self.iterations = iterations
+        self.lr_position, self.lr_scale, self.lr_rotation = lr_position, lr_scale, lr_rotation
+        self.lr_opacity, self.lr_sh, self.lambda_ssim = lr_opacity, lr_sh, lambda_ssim
+        self.densify_from, self.densify_until = densify_from, densify_until
+        self.densify_interval = densify_interval
+        self.densify_grad_threshold = densify_grad_threshold
+        self.densify_size_threshold = densify_size_threshold
+        self.prune_interval, self.opacity_threshold = prune_interval, opacity_threshold
+        self.max_screen_size = max_screen_size
+        self.opacity_reset_interval = opacity_reset_interval
+
+    def lrs(self):
+        return {"position": self.lr_position, "log_scale": self.lr_scale, "rotation": self.lr_rotation,
+                "logit_opacity": self.lr_opacity, "sh_coeffs": self.lr_sh}
+
+
+class TrainStats:
+    """TrainStats (trainer.cr:61-74)."""
+
+    def __init__(self, iteration=0, loss=0.0, psnr=0.0, num_gaussians=0, lr=0.0):
+        self.iteration, self.loss, self.psnr = iteration, loss, psnr
+        self.num_gaussians, self.lr = num_gaussians, lr
+
+    def __str__(self):
+        return (f"Iter {self.iteration}: loss={self.loss:.4f}, PSNR={self.psnr:.2f}dB, "
+                f"gaussians={self.num_gaussians}")
+
+
+class Trainer:
+    """Trainer (trainer.cr:125-420): one sampled view per step, combined
+    L1 + SSIM loss, screen-space gradient accumulation, densification and
+    pruning every densify_interval steps in [densify_from, densify_until),
+    opacity reset every opacity_reset_interval steps. Every camera carries its
+    device target as `camera.image` ([H, W, 3] fp32).
+
+    The order inside a step is gradients -> Adam -> zero (the reference zeroes
+    before its optimiser step, trainer.cr:202-203, so it never updates); after
+    densification the optimiser state is recreated, as recreate_optimizers!
+    (trainer.cr:412-419) does. Camera sampling uses a seeded generator."""
+
+    def __init__(self, gaussians, cameras, config=None, seed=0, raster_config=None):
+        import numpy as np
+
+        from .densify import GradientAccumulator
+        self.gaussians = gaussians
+        self.cameras = cameras
+        self.config = config or TrainerConfig()
+        self.rcfg = raster_config or _abi.default_config()
+        self.rng = np.random.default_rng(seed)
+        self.iteration = 0
+        self.context = RasterizerContext(gaussians.arena.device)
+        self.grad_accum = GradientAccumulator(gaussians.count, device=gaussians.arena.device)
+        self._recreate()
+
+    def _recreate(self):
+        """recreate_optimizers! (trainer.cr:412-419) and fresh gradient buffers."""
+        self.grads = RasterizerGradients(self.gaussians, screen=True)
+        self.optimizer = Adam.for_gaussians(self.gaussians, self.grads, self.config.lrs())
+
+    def train(self, callback=None):
+        """Trainer#train (trainer.cr:157-180)."""
+        c = self.config
+        for i in range(c.iterations):
+            self.iteration = i
+            stats = self.train_step()
+            if callback is not None:
+                callback(stats)
+            if c.densify_from <= i < c.densify_until and i % c.densify_interval == 0:
+                self.densify_and_prune()
+            if i > 0 and i % c.opacity_reset_interval == 0:
+                self.reset_opacity()
+
+    def train_step(self):
+        """Trainer#train_step (trainer.cr:183-215)."""
+        from .loss import psnr
+        cam = self.cameras.sample(self.rng) if hasattr(self.cameras, "sample") else \
+            self.cameras[int(self.rng.integers(len(self.cameras)))]
+        target = getattr(cam, "image", None)
+        if target is None:
+            raise ValueError("Camera has no target image")
+        rendered, ctx = Rasterizer.forward(self.gaussians, cam, context=self.context, config=self.rcfg)
+        loss, grad_image = combined_with_grad(rendered, target, self.config.lambda_ssim)
+        self.grads.zero_()
+        Rasterizer.backward(grad_image, self.gaussians, cam, ctx, grads=self.grads, config=self.rcfg)
+        self.grad_accum.accumulate(self.grads)
+        self.optimizer.step()
+        return TrainStats(iteration=self.iteration, loss=float(loss), psnr=psnr(rendered, target),
+                          num_gaussians=self.gaussians.count, lr=self.config.lr_position)
+
+    def densify_and_prune(self):
+        """Trainer#densify_and_prune! (trainer.cr:293-330) on the device."""
+        from .densify import densify_and_prune
+        c = self.config
+        self.gaussians = densify_and_prune(self.gaussians, self.grad_accum, c.densify_grad_threshold,
+                                           c.densify_size_threshold, c.opacity_threshold,
+                                           seed=self.iteration)
+        self._recreate()
+
+    def reset_opacity(self):
+        """Trainer#reset_opacity! (trainer.cr:407-410): logit opacity -1."""
+        from .densify import reset_opacity
+        reset_opacity(self.gaussians, -1.0)
