@@ -81,14 +81,22 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
 #ifndef GS_PACKED_MIN_CTAS
 #define GS_PACKED_MIN_CTAS 5
 #endif
+#ifndef GS_PAIR_MIN_CTAS
+#define GS_PAIR_MIN_CTAS 5
+#endif
 template <typename K, int MODE = 0>
-__global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) onesweep_kernel(
+__global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PACKED_MIN_CTAS) onesweep_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
     uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu) {
   __shared__ K s_keys[kTileKeys];  // reused for values
-  __shared__ uint32_t s_whist[kWarps][256];
+  // per-warp digit counters; in pair mode two 16-bit counters per word (a warp
+  // ranks at most 512 keys per digit, a tile 4096), which saves the 4 KB that
+  // the fifth CTA per SM needs
+  constexpr bool kPack16 = MODE == 0;
+  __shared__ uint32_t s_whw[kWarps][kPack16 ? 128 : 256];
+  unsigned short* s_wh16 = reinterpret_cast<unsigned short*>(&s_whw[0][0]);
   __shared__ uint32_t s_local_excl[256];
   __shared__ uint32_t s_gbase[256];
   __shared__ uint8_t s_dig[MODE == 0 ? kTileKeys : 1];  // pair mode only
@@ -97,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) 
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   if (tid == 0) s_part = atomicAdd(ticket, 1u);
-  for (int k = tid; k < kWarps * 256; k += kThreads) (&s_whist[0][0])[k] = 0;
+  for (int k = tid; k < kWarps * (kPack16 ? 128 : 256); k += kThreads) (&s_whw[0][0])[k] = 0;
   __syncthreads();
   const uint32_t part = s_part;
   const int64_t tile_base = (int64_t)part * kTileKeys;
@@ -106,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) 
 
   // Only the packed digits and ranks stay live across the look-back; keys
   // and values are read again (from L2) when the tile is reordered, which
-  // keeps the kernel at four CTAs per SM.
+  // keeps the register count low enough for 4-5 CTAs per SM.
   uint32_t rank[kItems];
   uint32_t dig[kItems / 4];  // four 8-bit digits per register
 #pragma unroll
@@ -137,7 +145,14 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) 
     }
     const int leader = __ffs(peers) - 1;
     uint32_t b = 0;
-    if (lane == leader) b = atomicAdd(&s_whist[w][d], (uint32_t)__popc(peers));
+    if (lane == leader) {
+      if (kPack16) {
+        const uint32_t sh = 16u * (d & 1u);
+        b = (atomicAdd(&s_whw[w][d >> 1], (uint32_t)__popc(peers) << sh) >> sh) & 0xFFFFu;
+      } else {
+        b = atomicAdd(&s_whw[w][d], (uint32_t)__popc(peers));
+      }
+    }
     b = __shfl_sync(0xffffffffu, b, leader);
     rank[i] = (d << 16) | (b + __popc(peers & lt_mask));
   }
@@ -148,9 +163,15 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) 
   uint32_t cnt = 0;
 #pragma unroll
   for (int ww = 0; ww < kWarps; ww++) {
-    const uint32_t c = s_whist[ww][d];
-    s_whist[ww][d] = cnt;
-    cnt += c;
+    if (kPack16) {
+      const uint32_t c = s_wh16[ww * 256 + d];
+      s_wh16[ww * 256 + d] = (unsigned short)cnt;
+      cnt += c;
+    } else {
+      const uint32_t c = s_whw[ww][d];
+      s_whw[ww][d] = cnt;
+      cnt += c;
+    }
   }
   const uint32_t valid_cnt = d == digit_mask ? cnt - (kTileKeys - num_valid) : cnt;
   const uint32_t local_excl = block_excl_scan_256(cnt, s_warp);
@@ -190,7 +211,8 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? 4 : GS_PACKED_MIN_CTAS) 
   for (int i = 0; i < kItems; i++) {
     const int64_t idx = warp_base + i * 32 + lane;
     const uint32_t dd = rank[i] >> 16;
-    const uint32_t pos = s_local_excl[dd] + s_whist[w][dd] + (rank[i] & 0xFFFFu);
+    const uint32_t wbase = kPack16 ? (uint32_t)s_wh16[w * 256 + dd] : s_whw[w][dd];
+    const uint32_t pos = s_local_excl[dd] + wbase + (rank[i] & 0xFFFFu);
     if (idx < n) s_keys[pos] = keys_in[idx];
     rank[i] = pos;
   }
