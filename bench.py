@@ -248,31 +248,38 @@ def sort_bytes_per_pair(end_bit, key_bytes=8):
     return key_bytes + 2 * (key_bytes + 4) * passes
 
 
-def packed_sort_bytes(bits):
-    """Packed (key << 32 | value) u64 words: histogram read + read and write per pass."""
-    return 8 + 16 * ((bits + 7) // 8)
+def packed_sort_bytes(bits, hist=True, hi=False):
+    """Packed (key << 32 | value) u64 words: histogram read (unless the producer
+    counted the digits), read and write per pass; the last pass writes the 4-byte
+    values (and the 4-byte keys with `hi`)."""
+    passes = (bits + 7) // 8
+    return (8 if hist else 0) + 16 * (passes - 1) + 8 + 4 + (4 if hi else 0)
 
 
 def stage_work(stats, n, keys_per_view, pge, tiles, end_bit, batch=1):
     """Algorithmic work of each stage for ONE view: (bound, bytes or flops, stage calls per view).
 
-    Binning of a view = a stable 32-bit depth sort of the N Gaussians (4 passes),
-    a gather-scan and emission of packed (tile << 32 | id) words in depth order,
-    and a stable sort of those words by the tile bits (end_bit - 32 bits). The
+    Binning of a view = a stable depth sort of the N Gaussians (per view: 32 bits,
+    4 passes; batched: one sort of view << 56 | (bits(depth) - bits(near)) << 28 |
+    index words by 28 + ceil(log2(batch)) bits, 4 passes), a gather-scan and
+    emission of packed (tile << 32 | id) words in depth order, which also counts
+    the tile digits, and a stable sort of those words by the tile bits
+    (end_bit - 32 bits) whose last pass writes the ids and the tile ranges. The
     preprocess and its backward run once per `batch` views: parameters read once,
     gradient rows read and written once, one grad2d row per view."""
     tb = end_bit - 32
     m = keys_per_view
+    depth_bits = 28 + max(1, (batch - 1).bit_length()) if batch > 1 else 32
     return {
         # one launch per `batch` views: parameters read once, per view a 48 B splat
         # record + 32 B binning record + 8 B packed depth word
         "preprocess": ("hbm", (PARAM_ROW_B / batch + 88) * n, 1.0 / batch),
         "scan": ("hbm", 4 * n + 16 * n, 2),  # order + binning-record word gather, then the block-sum scan
         "emit": ("hbm", (4 + 32) * n + 8 * m, 1),  # order + 32 B binning record; packed pairs
-        # depth sort: per view (32 bits), or one per batch over view << 32 | depth (36 bits)
-        "sort": ("hbm", packed_sort_bytes(36 if batch > 1 else 32) * n + packed_sort_bytes(tb) * m,
+        # depth sort (per view, or one per batch) + tile sort
+        "sort": ("hbm", packed_sort_bytes(depth_bits, hi=batch == 1) * n + packed_sort_bytes(tb, hist=False) * m,
                  1 + (1.0 / batch if batch > 1 else 1)),
-        "ranges": ("hbm", 4 * m + 8 * tiles, 1),
+        "ranges": ("hbm", 8 * tiles, 1),  # empty ranges {~0, 0} -> {0, 0}
         "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge, 1),
         "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge, 1),
         "preprocess_bwd": ("hbm", (3 * PARAM_ROW_B / batch + GRAD2D_B) * n, 1.0 / batch),

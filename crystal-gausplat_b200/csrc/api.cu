@@ -604,6 +604,35 @@ int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64
   GS_TRY(ensure(ctx, &f->vals, (size_t)m * 4 + 4));
   uint32_t* tiles = (uint32_t*)f->tiles.ptr;
   uint32_t* vals = (uint32_t*)f->vals.ptr;
+  uint32_t* ranges = (uint32_t*)f->ranges.ptr;
+  const int32_t T = tx * ty;
+  const int tb = tile_bits_of(T);
+  if (m > 1 && tb > 0) {
+    // Emission also counts the sort's digits and presets the ranges; the
+    // last sort pass writes the values and the ranges (no tile array).
+    GS_TRY(ensure(ctx, &f->pairs, (size_t)m * 8 + 8));
+    uint64_t* pairs = (uint64_t*)f->pairs.ptr;
+    GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed((int64_t)m, 32, 32 + tb)));
+    char* scratch = scratch_base(ctx);
+    {
+      StageScope sc(ctx, GSC_STAGE_EMIT);
+      sc.kernels(1);
+      GS_TRY(sort_packed_clear(ctx, (int64_t)m, 32, 32 + tb, scratch));
+      GS_TRY(launch_emit_tiles(frame_bins(f), f->order_ptr, n, (const uint64_t*)f->offsets.ptr, tx, pairs,
+                               ctx->stream, sort_packed_hist(scratch, (int64_t)m, 32, 32 + tb), (tb + 7) / 8,
+                               ranges, T, (int64_t)ctx->num_sms * 8));
+    }
+    {
+      // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
+      StageScope sc(ctx, GSC_STAGE_SORT);
+      sc.kernels((tb + 7) / 8);
+      GS_TRY(launch_sort_packed(ctx, pairs, (int64_t)m, 32, 32 + tb, nullptr, vals, scratch, 0xFFFFFFFFu, true,
+                                ranges, (uint32_t)T));
+    }
+    StageScope sc(ctx, GSC_STAGE_RANGES);
+    sc.kernels(1);
+    return launch_ranges_finish(ranges, T, ctx->stream);
+  }
   if (m) {
     GS_TRY(ensure(ctx, &f->pairs, (size_t)m * 8 + 8));
     uint64_t* pairs = (uint64_t*)f->pairs.ptr;
@@ -613,9 +642,7 @@ int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64
       GS_TRY(launch_emit_tiles(frame_bins(f), f->order_ptr, n, (const uint64_t*)f->offsets.ptr, tx, pairs,
                                ctx->stream));
     }
-    // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
-    //    only, split into tiles and values
-    const int tb = tile_bits_of(tx * ty);
+    // 3. a single pair or a single tile: nothing to sort, split the words
     GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed((int64_t)m, 32, 32 + tb)));
     StageScope sc(ctx, GSC_STAGE_SORT);
     sc.kernels(tb > 0 && m > 1 ? 1 + (tb + 7) / 8 : 1);
@@ -624,7 +651,7 @@ int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64
   {
     StageScope sc(ctx, GSC_STAGE_RANGES);
     sc.kernels(m ? 1 : 0);
-    GS_TRY(launch_tile_ranges_u32(tiles, (int64_t)m, tx * ty, (uint32_t*)f->ranges.ptr, ctx->stream));
+    GS_TRY(launch_tile_ranges_u32(tiles, (int64_t)m, T, ranges, ctx->stream));
   }
   return GSC_OK;
 }
@@ -654,6 +681,21 @@ int forward_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, 
   return GSC_OK;
 }
 
+// Compact batched depth keys: an emitted depth z lies in (max(near_z, 0),
+// far_z], so bits(z) - bits(max(near_z, 0)) is in [1, span]; usable when the
+// span leaves 2^28 - 1 free for the Gaussians that emit nothing.
+bool depth_compact_base(const gsc_raster_config* cfg, uint32_t* base) {
+  const float lo = cfg->near_z > 0.0f ? cfg->near_z : 0.0f;
+  const float hi = cfg->far_z;
+  if (!(hi > lo) || !std::isfinite(hi)) return false;
+  uint32_t blo, bhi;
+  std::memcpy(&blo, &lo, 4);
+  std::memcpy(&bhi, &hi, 4);
+  if (bhi - blo >= 0x0FFFFFFFu) return false;
+  *base = blo;
+  return true;
+}
+
 // One preprocess launch for the frames (all of one image size).
 int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams, int k,
                        const gsc_gaussians* g, const gsc_raster_config* cfg, uint64_t* batch_words = nullptr) {
@@ -673,6 +715,7 @@ int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera*
     a.bin_v[v] = (uint4*)frames[v]->bins.ptr;
   }
   a.view_key = batch_words != nullptr;
+  a.depth_compact = a.view_key && depth_compact_base(cfg, &a.depth_base);
   a.contributing = cfg->binning == GSC_BIN_CONTRIBUTING;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
@@ -712,7 +755,9 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
   if (nviews > 1 && n > 1 && n < (1ll << 28)) {
     // One depth sort for the whole batch: view << 60 | bits(depth) << 28 |
     // index words sorted by bits [28, 64), i.e. by view, then depth; view v's
-    // order is the v-th run of n indices.
+    // order is the v-th run of n indices. With the compact depth keys the
+    // words are view << 56 | (bits(depth) - bits(near)) << 28 | index and the
+    // sort takes 4 passes instead of 5.
     const int64_t total = (int64_t)nviews * n;
     GS_TRY(ensure(ctx, &ctx->batch_pairs, (size_t)total * 8));
     GS_TRY(ensure(ctx, &ctx->batch_order, (size_t)total * 4));
@@ -720,10 +765,17 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
     uint32_t* order = (uint32_t*)ctx->batch_order.ptr;
     GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg, words));
     {
-      GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed(total, 28, 64)));
+      uint32_t base;
+      int end_bit = 64;
+      if (depth_compact_base(cfg, &base)) {
+        int vb = 0;
+        while ((1 << vb) < nviews) vb++;
+        end_bit = 56 + vb;
+      }
+      GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed(total, 28, end_bit)));
       StageScope sc(ctx, GSC_STAGE_SORT);
-      sc.kernels(1 + 5);
-      GS_TRY(launch_sort_packed(ctx, words, total, 28, 64, nullptr, order, scratch_base(ctx), 0x0FFFFFFFu));
+      sc.kernels(1 + (end_bit - 28 + 7) / 8);
+      GS_TRY(launch_sort_packed(ctx, words, total, 28, end_bit, nullptr, order, scratch_base(ctx), 0x0FFFFFFFu));
     }
     for (int v = 0; v < nviews; v++) {
       frames[v]->order_ptr = order + (size_t)v * n;
@@ -855,9 +907,9 @@ GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {
     case GSC_FRAME_KEYS:
       if (!f->keys_valid) {
         GS_TRY(ensure(f->ctx, &f->keys, (size_t)f->num_keys * 8 + 8));
-        GS_TRY(launch_make_keys((const uint32_t*)f->tiles.ptr, (const uint32_t*)f->vals.ptr,
-                                (const float*)f->splats.ptr, f->num_keys, (uint64_t*)f->keys.ptr,
-                                f->ctx->stream));
+        GS_TRY(launch_make_keys_ranges((const uint32_t*)f->ranges.ptr, f->tiles_x * f->tiles_y,
+                                       (const uint32_t*)f->vals.ptr, (const float*)f->splats.ptr,
+                                       (uint64_t*)f->keys.ptr, f->ctx->stream));
         f->keys_valid = true;
       }
       p = f->keys.ptr;

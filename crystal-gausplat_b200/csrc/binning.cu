@@ -10,6 +10,8 @@
 // [offset[b], offset[b] + sum[b]) and fills it with coalesced stores, every
 // thread locating the Gaussian of its output slot by binary search over the
 // block's inclusive scan. Canonical order: Gaussian id, then ty, then tx.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -176,7 +178,7 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 //   3. a stable sort of those pairs by the tile bits only,
 // which moves 8-byte pairs through ceil(tile_bits / 8) passes instead of
 // 12-byte pairs through ceil((32 + tile_bits) / 8) passes. The 64-bit keys are
-// rebuilt on request (make_keys_kernel).
+// rebuilt on request from the tile ranges (make_keys_ranges_kernel).
 // ---------------------------------------------------------------------------
 
 // `bins`: the 32-byte binning records of preprocess ({x0, y0, width, count},
@@ -190,6 +192,8 @@ __global__ void __launch_bounds__(256) block_sums_gather_kernel(const uint4* __r
   uint32_t incl = block_incl_scan_256(t, s_warp);
   if (threadIdx.x == 255) sums[blockIdx.x] = incl;
 }
+
+constexpr int kEmitMaxPasses = 4;
 
 // Position of the k-th (0-based) set bit of m; m has more than k set bits.
 __device__ __forceinline__ uint32_t select_bit64(uint64_t m, uint32_t k) {
@@ -209,54 +213,86 @@ __device__ __forceinline__ uint32_t select_bit64(uint64_t m, uint32_t k) {
 __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict__ bins,
                                                          const uint32_t* __restrict__ order, int64_t n,
                                                          const uint64_t* __restrict__ offsets,
-                                                         int tiles_x, uint64_t* __restrict__ pair_out) {
+                                                         int tiles_x, uint64_t* __restrict__ pair_out,
+                                                         uint32_t* __restrict__ hist, int hist_passes,
+                                                         uint32_t* __restrict__ ranges, int32_t num_tiles) {
+  __shared__ uint32_t s_hist[kEmitMaxPasses][256];
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
   __shared__ uint32_t s_inv[256];  // ceil(2^16 / width): row of a test < 64 by multiply and shift
   __shared__ uint32_t s_id[256];
   __shared__ uint64_t s_mask[256];
   __shared__ uint32_t s_warp[8];
-  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  uint32_t t = 0;
-  if (p < n) {
-    const uint32_t gid = order[p];
-    const uint4 b0 = bins[(size_t)gid * 2];
-    t = b0.w;
-    if (t) {
-      const uint4 b1 = bins[(size_t)gid * 2 + 1];
-      s_x0[threadIdx.x] = (int)b0.x;
-      s_y0[threadIdx.x] = (int)b0.y;
-      s_wx[threadIdx.x] = (int)b0.z;
-      s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
-      s_id[threadIdx.x] = gid;
-      s_mask[threadIdx.x] = ((uint64_t)b1.y << 32) | b1.x;
+  if (ranges)
+    for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < num_tiles; r += (int64_t)gridDim.x * 256) {
+      ranges[2 * r] = 0xFFFFFFFFu;
+      ranges[2 * r + 1] = 0u;
     }
+  for (int k = threadIdx.x; k < hist_passes * 256; k += 256) (&s_hist[0][0])[k] = 0u;
+  // A block takes chunks of 256 Gaussians (in depth order) in turn, so that
+  // its digit counts reach global memory once per block, not per chunk.
+  const int64_t nchunks = (n + 255) / 256;
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    const int64_t p = chunk * 256 + threadIdx.x;
+    uint32_t t = 0;
+    if (p < n) {
+      const uint32_t gid = order[p];
+      const uint4 b0 = bins[(size_t)gid * 2];
+      t = b0.w;
+      if (t) {
+        const uint4 b1 = bins[(size_t)gid * 2 + 1];
+        s_x0[threadIdx.x] = (int)b0.x;
+        s_y0[threadIdx.x] = (int)b0.y;
+        s_wx[threadIdx.x] = (int)b0.z;
+        s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
+        s_id[threadIdx.x] = gid;
+        s_mask[threadIdx.x] = ((uint64_t)b1.y << 32) | b1.x;
+      }
+    }
+    uint32_t incl = block_incl_scan_256(t, s_warp);
+    s_incl[threadIdx.x] = incl;
+    __syncthreads();
+    // Each warp writes the contiguous output range of its 32 Gaussians; a
+    // lane's output index grows by 32 per round, so the Gaussian that owns it
+    // is found by advancing a pointer instead of searching.
+    const uint64_t out = offsets[chunk];
+    const int wb = threadIdx.x & ~31;
+    const uint32_t wend = s_incl[wb + 31];
+    int own = wb;
+    const uint32_t wbeg = wb ? s_incl[wb - 1] : 0u;
+    for (uint32_t k0 = wbeg; k0 < wend; k0 += 32) {
+      const uint32_t k = k0 + (threadIdx.x & 31);
+      const bool valid = k < wend;
+      uint32_t tile = 0xFFFFFFFFu;
+      if (valid) {
+        while (s_incl[own] <= k) own++;
+        uint32_t local = k - (own ? s_incl[own - 1] : 0u);
+        const uint64_t mk = s_mask[own];
+        const uint32_t wx = (uint32_t)s_wx[own];
+        uint32_t ry;
+        if (mk != ~0ull) {
+          local = select_bit64(mk, local);  // local-th contributing tile of the rect (< 64)
+          ry = (local * s_inv[own]) >> 16;
+        } else {
+          ry = local / wx;
+        }
+        const int ty = s_y0[own] + (int)ry;
+        const int tx = s_x0[own] + (int)(local - ry * wx);
+        tile = (uint32_t)(ty * tiles_x + tx);
+        pair_out[out + k] = ((uint64_t)tile << 32) | (uint64_t)s_id[own];
+      }
+      // digit counts of the tile sort
+      if (valid)
+        for (int q = 0; q < hist_passes; q++) atomicAdd(&s_hist[q][(tile >> (8 * q)) & 255u], 1u);
+    }
+    __syncthreads();  // the chunk's shared records are replaced next
   }
-  uint32_t incl = block_incl_scan_256(t, s_warp);
-  s_incl[threadIdx.x] = incl;
-  __syncthreads();
-  // Each warp writes the contiguous output range of its 32 Gaussians; a
-  // lane's output index grows by 32 per round, so the Gaussian that owns it
-  // is found by advancing a pointer instead of searching.
-  const uint64_t out = offsets[blockIdx.x];
-  const int wb = threadIdx.x & ~31;
-  const uint32_t wend = s_incl[wb + 31];
-  int own = wb;
-  for (uint32_t k = (wb ? s_incl[wb - 1] : 0u) + (threadIdx.x & 31); k < wend; k += 32) {
-    while (s_incl[own] <= k) own++;
-    uint32_t local = k - (own ? s_incl[own - 1] : 0u);
-    const uint64_t mk = s_mask[own];
-    const uint32_t wx = (uint32_t)s_wx[own];
-    uint32_t ry;
-    if (mk != ~0ull) {
-      local = select_bit64(mk, local);  // local-th contributing tile of the rect (< 64)
-      ry = (local * s_inv[own]) >> 16;
-    } else {
-      ry = local / wx;
-    }
-    const int ty = s_y0[own] + (int)ry;
-    const int tx = s_x0[own] + (int)(local - ry * wx);
-    pair_out[out + k] = ((uint64_t)(uint32_t)(ty * tiles_x + tx) << 32) | (uint64_t)s_id[own];
+  if (hist_passes == 0) return;
+  // one counter per 128-byte line (stride kHistStride), so that the blocks'
+  // adds spread over the L2 slices
+  for (int k = threadIdx.x; k < hist_passes * 256; k += 256) {
+    const uint32_t c = (&s_hist[0][0])[k];
+    if (c) atomicAdd(&hist[(size_t)k * kHistStride], c);
   }
 }
 
@@ -284,16 +320,6 @@ __global__ void __launch_bounds__(256) tile_ranges_u32_kernel(const uint32_t* __
   }
 }
 
-__global__ void __launch_bounds__(256) make_keys_kernel(const uint32_t* __restrict__ tiles,
-                                                        const uint32_t* __restrict__ ids,
-                                                        const float4* __restrict__ splats, int64_t m,
-                                                        uint64_t* __restrict__ keys) {
-  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  if (i >= m) return;
-  const uint32_t depth_bits = __float_as_uint(splats[(size_t)ids[i] * 3 + 2].y);
-  keys[i] = ((uint64_t)tiles[i] << 32) | depth_bits;
-}
-
 int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
                              cudaStream_t stream) {
   if (n == 0) return GSC_OK;
@@ -303,10 +329,55 @@ int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n
 }
 
 int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, uint64_t* pair_out, cudaStream_t stream) {
+                      int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist, int hist_passes,
+                      uint32_t* ranges, int32_t num_tiles, int64_t grid_cap) {
   if (n == 0) return GSC_OK;
-  emit_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, offsets, tiles_x, pair_out);
+  if (hist_passes < 0 || hist_passes > kEmitMaxPasses || (hist_passes > 0 && !hist)) {
+    set_error("emit_tiles: bad histogram arguments");
+    return GSC_ERR_INVALID;
+  }
+  const int64_t chunks = (n + 255) / 256;
+  const int64_t grid = grid_cap > 0 ? std::min<int64_t>(chunks, grid_cap) : chunks;
+  emit_tiles_kernel<<<(unsigned)grid, 256, 0, stream>>>(bins, order, n, offsets, tiles_x, pair_out, hist,
+                                                        hist_passes, ranges, num_tiles);
   GS_CK_LAUNCH("emit_tiles_kernel");
+  return GSC_OK;
+}
+
+__global__ void __launch_bounds__(256) ranges_finish_kernel(uint32_t* __restrict__ ranges, int32_t num_tiles) {
+  const int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (t >= num_tiles) return;
+  if (ranges[2 * t] == 0xFFFFFFFFu) ranges[2 * t] = 0u;
+}
+
+int launch_ranges_finish(uint32_t* ranges, int32_t num_tiles, cudaStream_t stream) {
+  if (num_tiles <= 0) return GSC_OK;
+  ranges_finish_kernel<<<(unsigned)((num_tiles + 255) / 256), 256, 0, stream>>>(ranges, num_tiles);
+  GS_CK_LAUNCH("ranges_finish_kernel");
+  return GSC_OK;
+}
+
+// One warp per tile writes the keys of the tile's range.
+__global__ void __launch_bounds__(256) make_keys_ranges_kernel(const uint32_t* __restrict__ ranges,
+                                                               int32_t num_tiles,
+                                                               const uint32_t* __restrict__ ids,
+                                                               const float4* __restrict__ splats,
+                                                               uint64_t* __restrict__ keys) {
+  const int64_t t = ((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5;
+  if (t >= num_tiles) return;
+  const uint32_t b = ranges[2 * t], e = ranges[2 * t + 1];
+  for (uint32_t i = b + (threadIdx.x & 31); i < e; i += 32) {
+    const uint32_t depth_bits = __float_as_uint(splats[(size_t)ids[i] * 3 + 2].y);
+    keys[i] = ((uint64_t)t << 32) | depth_bits;
+  }
+}
+
+int launch_make_keys_ranges(const uint32_t* ranges, int32_t num_tiles, const uint32_t* ids, const float* splats,
+                            uint64_t* keys, cudaStream_t stream) {
+  if (num_tiles <= 0) return GSC_OK;
+  make_keys_ranges_kernel<<<(unsigned)(((int64_t)num_tiles * 32 + 255) / 256), 256, 0, stream>>>(
+      ranges, num_tiles, ids, reinterpret_cast<const float4*>(splats), keys);
+  GS_CK_LAUNCH("make_keys_ranges_kernel");
   return GSC_OK;
 }
 
@@ -319,13 +390,5 @@ int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, 
   return GSC_OK;
 }
 
-int launch_make_keys(const uint32_t* tiles, const uint32_t* ids, const float* splats, int64_t m,
-                     uint64_t* keys, cudaStream_t stream) {
-  if (m == 0) return GSC_OK;
-  make_keys_kernel<<<(unsigned)((m + 255) / 256), 256, 0, stream>>>(
-      tiles, ids, reinterpret_cast<const float4*>(splats), m, keys);
-  GS_CK_LAUNCH("make_keys_kernel");
-  return GSC_OK;
-}
 
 }  // namespace gs

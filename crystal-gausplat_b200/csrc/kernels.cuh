@@ -25,6 +25,12 @@ struct PreprocessArgs {
   // words of all views sorted together by bits [28, 64).
   uint64_t* depth_pairs_v[kMaxBatchViews];
   int view_key;
+  // with view_key and depth_compact: view << 56 | (bits(depth) - depth_base,
+  // 2^28 - 1 if no pair) << 28 | index, sorted by bits [28, 56 + view bits);
+  // the host sets it only when every emitted depth (near_z, far_z] maps below
+  // 2^28 - 1
+  int depth_compact;
+  uint32_t depth_base;
   // contributing-pairs binning: the binning record's mask has bit k for the
   // k-th tile of the rect (row-major) that can contribute (~0 = the whole
   // rect), and the pair count is theirs
@@ -131,12 +137,21 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
                        cudaStream_t stream);
 int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
                              cudaStream_t stream);
+// hist (may be null): the tile sort's digit counts of the tile bits, digit d of
+// pass q at hist[(q * 256 + d) * kHistStride]; ranges (may be null): preset to
+// {0xFFFFFFFF, 0} for num_tiles tiles; grid_cap (> 0): at most that many blocks.
+constexpr int kHistStride = 32;
 int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
-                      int tiles_x, uint64_t* pair_out, cudaStream_t stream);
+                      int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist = nullptr,
+                      int hist_passes = 0, uint32_t* ranges = nullptr, int32_t num_tiles = 0,
+                      int64_t grid_cap = 0);
+// empty ranges {0xFFFFFFFF, 0} -> {0, 0}
+int launch_ranges_finish(uint32_t* ranges, int32_t num_tiles, cudaStream_t stream);
+// 64-bit keys (tile << 32 | bits(depth)) from the tile ranges and the ids
+int launch_make_keys_ranges(const uint32_t* ranges, int32_t num_tiles, const uint32_t* ids, const float* splats,
+                            uint64_t* keys, cudaStream_t stream);
 int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
                            cudaStream_t stream);
-int launch_make_keys(const uint32_t* tiles, const uint32_t* ids, const float* splats, int64_t m,
-                     uint64_t* keys, cudaStream_t stream);
 size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit);
 int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                       int end_bit, char* scratch);
@@ -145,8 +160,16 @@ size_t sort_scratch_bytes_u32(int64_t n, int begin_bit, int end_bit);
 // the u64; the sorted words go to hi_out (may be null) / lo_out (low word &
 // lo_mask). `pairs` is overwritten.
 size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit);
+// With hist_ready the digit histograms are already in the scratch (zeroed by
+// sort_packed_clear, filled by the producer of `pairs`, e.g. emit_tiles, at
+// stride kHistStride: sort_packed_hist). With
+// `ranges` (begin_bit 32, every tile bit sorted, ranges preset to
+// {0xFFFFFFFF, 0} per tile) the last pass also writes each tile's range.
 int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
-                       uint32_t* lo_out, char* scratch, uint32_t lo_mask = 0xFFFFFFFFu);
+                       uint32_t* lo_out, char* scratch, uint32_t lo_mask = 0xFFFFFFFFu, bool hist_ready = false,
+                       uint32_t* ranges = nullptr, uint32_t ntiles = 0);
+uint32_t* sort_packed_hist(char* scratch, int64_t n, int begin_bit, int end_bit);  // wide digit counts
+int sort_packed_clear(gsc_ctx* ctx, int64_t n, int begin_bit, int end_bit, char* scratch);
 int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                           int end_bit, char* scratch);
 int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream);

@@ -154,9 +154,15 @@ __global__ void __launch_bounds__(kPreThreads, GS_PRE_MIN_CTAS) preprocess_kerne
         a.bin_v[v][2 * i + 1] = make_uint4((uint32_t)mask_o, (uint32_t)(mask_o >> 32), 0u, 0u);
       }
       if (a.depth_pairs_v[v]) {
-        const uint64_t kb = emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu;
-        a.depth_pairs_v[v][i] = a.view_key ? ((uint64_t)v << 60) | (kb << 28) | (uint64_t)i
-                                           : (kb << 32) | (uint64_t)i;
+        uint64_t word;
+        if (a.view_key && a.depth_compact) {
+          const uint64_t kb = emit ? __float_as_uint(depth_o) - a.depth_base : 0x0FFFFFFFu;
+          word = ((uint64_t)v << 56) | (kb << 28) | (uint64_t)i;
+        } else {
+          const uint64_t kb = emit ? __float_as_uint(depth_o) : 0xFFFFFFFFu;
+          word = a.view_key ? ((uint64_t)v << 60) | (kb << 28) | (uint64_t)i : (kb << 32) | (uint64_t)i;
+        }
+        a.depth_pairs_v[v][i] = word;
       }
     }
   }

@@ -89,7 +89,8 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
     uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
-    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu) {
+    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu,
+    uint32_t* __restrict__ ranges = nullptr, uint32_t ntiles = 0, int hstride = 1) {
   __shared__ K s_keys[kTileKeys];  // reused for values
   // per-warp digit counters; in pair mode two 16-bit counters per word (a warp
   // ranks at most 512 keys per digit, a tile 4096), which saves the 4 KB that
@@ -175,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   }
   const uint32_t valid_cnt = d == digit_mask ? cnt - (kTileKeys - num_valid) : cnt;
   const uint32_t local_excl = block_excl_scan_256(cnt, s_warp);
-  const uint32_t gexcl = block_excl_scan_256(hist[d], s_warp);
+  const uint32_t gexcl = block_excl_scan_256(hist[(size_t)d * hstride], s_warp);
   s_local_excl[d] = local_excl;
 
   // Decoupled look-back.
@@ -225,8 +226,18 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
     if ((int64_t)gpos >= n) {
       atomicOr(err, GS_DEVERR_BOUNDS);
     } else if (MODE == 2) {
-      if (keys_hi) keys_hi[gpos] = (uint32_t)((uint64_t)key >> 32);
+      const uint32_t hi = (uint32_t)((uint64_t)key >> 32);
+      if (keys_hi) keys_hi[gpos] = hi;
       vals_out[gpos] = (uint32_t)key & lo_mask;
+      if (ranges && hi < ntiles) {
+        // Last pass of a sort by the whole high word (the tile): equal tiles
+        // share the digit, so a run of one tile in this tile-local order is a
+        // run of consecutive output positions; its ends bound the tile's
+        // range, and the runs of all partitions merge by min / max.
+        if (j == 0 || (uint32_t)((uint64_t)s_keys[j - 1] >> 32) != hi) atomicMin(&ranges[2 * (size_t)hi], gpos);
+        if (j + 1 == num_valid || (uint32_t)((uint64_t)s_keys[j + 1] >> 32) != hi)
+          atomicMax(&ranges[2 * (size_t)hi + 1], gpos + 1);
+      }
     } else {
       keys_out[gpos] = key;
     }
@@ -324,12 +335,40 @@ __global__ void __launch_bounds__(256) split_words_kernel(const uint64_t* __rest
   lo[i] = (uint32_t)v & lo_mask;
 }
 
+// Packed-sort scratch: the pair-sort layout (alternate words, status words,
+// compact histograms, tickets), then the wide histograms that a producer of
+// the words fills (one counter per 128-byte line, kHistStride apart).
+static size_t wide_hist_bytes(int begin_bit, int end_bit) {
+  const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
+  return align256((size_t)npass * 256 * kHistStride * 4);
+}
+
 size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit) {
-  return sort_scratch_bytes_t<uint64_t>(n, begin_bit, end_bit);
+  return sort_scratch_bytes_t<uint64_t>(n, begin_bit, end_bit) + wide_hist_bytes(begin_bit, end_bit);
+}
+
+static uint32_t* compact_hist(char* scratch, int64_t n) {
+  return reinterpret_cast<uint32_t*>(scratch + align256((size_t)n * 8) + align256((size_t)n * 4));
+}
+
+uint32_t* sort_packed_hist(char* scratch, int64_t n, int begin_bit, int end_bit) {
+  return reinterpret_cast<uint32_t*>(scratch + sort_scratch_bytes_t<uint64_t>(n, begin_bit, end_bit));
+}
+
+int sort_packed_clear(gsc_ctx* ctx, int64_t n, int begin_bit, int end_bit, char* scratch) {
+  const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
+  if (n <= 1 || npass == 0) return GSC_OK;
+  // compact histograms, status words and tickets, through the wide histograms
+  char* from = reinterpret_cast<char*>(compact_hist(scratch, n));
+  char* to = reinterpret_cast<char*>(sort_packed_hist(scratch, n, begin_bit, end_bit)) +
+             wide_hist_bytes(begin_bit, end_bit);
+  GS_CK(cudaMemsetAsync(from, 0, (size_t)(to - from), ctx->stream));
+  return GSC_OK;
 }
 
 int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
-                       uint32_t* lo_out, char* scratch, uint32_t lo_mask) {
+                       uint32_t* lo_out, char* scratch, uint32_t lo_mask, bool hist_ready, uint32_t* ranges,
+                       uint32_t ntiles) {
   cudaStream_t stream = ctx->stream;
   if (n <= 0) return GSC_OK;
   const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
@@ -340,16 +379,20 @@ int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, 
   }
   const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
   uint64_t* alt = reinterpret_cast<uint64_t*>(scratch);
-  scratch += align256((size_t)n * 8) + align256((size_t)n * 4);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(scratch);
+  uint32_t* hist = compact_hist(scratch, n);
   uint32_t* status = hist + npass * 256;
   uint32_t* tickets = status + (size_t)npass * parts * 256;
-  const size_t meta = (size_t)npass * 256 * 4 + (size_t)npass * parts * 256 * 4 + (size_t)npass * 4;
-  GS_CK(cudaMemsetAsync(hist, 0, meta, stream));
-  const int64_t hblocks = min((int64_t)ctx->num_sms * 8, (n + 4095) / 4096);
-  histogram_kernel<uint64_t><<<(unsigned)max((int64_t)1, hblocks), 256, 0, stream>>>(pairs, n, begin_bit, end_bit,
-                                                                                    npass, hist);
-  GS_CK_LAUNCH("histogram_kernel");
+  const int hstride = hist_ready ? kHistStride : 1;
+  if (hist_ready) {
+    hist = sort_packed_hist(scratch, n, begin_bit, end_bit);
+  } else {
+    const int rc = sort_packed_clear(ctx, n, begin_bit, end_bit, scratch);
+    if (rc != GSC_OK) return rc;
+    const int64_t hblocks = min((int64_t)ctx->num_sms * 8, (n + 4095) / 4096);
+    histogram_kernel<uint64_t><<<(unsigned)max((int64_t)1, hblocks), 256, 0, stream>>>(pairs, n, begin_bit,
+                                                                                      end_bit, npass, hist);
+    GS_CK_LAUNCH("histogram_kernel");
+  }
   uint64_t* src = pairs;
   uint64_t* dst = alt;
   for (int p = 0; p < npass; p++) {
@@ -357,12 +400,12 @@ int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, 
     const int bits = min(8, end_bit - shift);
     if (p + 1 < npass) {
       onesweep_kernel<uint64_t, 1><<<(unsigned)parts, kThreads, 0, stream>>>(
-          src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + p * 256,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err);
+          src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
+          status + (size_t)p * parts * 256, tickets + p, ctx->err, nullptr, 0xFFFFFFFFu, nullptr, 0, hstride);
     } else {
       onesweep_kernel<uint64_t, 2><<<(unsigned)parts, kThreads, 0, stream>>>(
-          src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + p * 256,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask);
+          src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
+          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask, ranges, ntiles, hstride);
     }
     GS_CK_LAUNCH("onesweep_kernel");
     std::swap(src, dst);

@@ -403,5 +403,51 @@ def test_forward_batch_equals_single_view_forwards(cuda, binning):
         assert c.num_rendered == one.num_rendered
         np.testing.assert_array_equal(host(im), host(ref))
         for which, dt in ((_abi.GSC_FRAME_VALUES, np.uint32), (_abi.GSC_FRAME_RANGES, np.uint32),
+                          (_abi.GSC_FRAME_KEYS, np.uint64),
                           (_abi.GSC_FRAME_FINAL_T, np.float32), (_abi.GSC_FRAME_LAST, np.uint32)):
             np.testing.assert_array_equal(c.get(which, dt), one.get(which, dt))
+
+
+@pytest.mark.parametrize("near_far", [(0.01, 1000.0), (0.5, 6.0), (-1.0, 1000.0), (0.01, float("inf"))],
+                         ids=["default", "narrow", "negative_near", "infinite_far"])
+def test_forward_batch_depth_words(cuda, oracle, near_far):
+    """The batched depth sort (compact view/depth words where the near..far
+    span allows, 36-bit words otherwise) gives the oracle's lists per view."""
+    n, W, H = 6000, 80, 64
+    arrays, g, _ = make(n, W, H, seed=12)
+    cams = [gs.make_camera(W, H, tuple(e)) for e in gs.sphere_poses(3, 4.0, seed=5)]
+    cfg = gs.default_config()
+    cfg.near_z, cfg.far_z = near_far
+    ctxs = [gs.RasterizerContext() for _ in cams]
+    imgs = gs.Rasterizer.forward_batch(g, cams, ctxs, config=cfg)
+    for cam, c, im in zip(cams, ctxs, imgs):
+        ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
+        assert c.num_rendered == ref["sorted_keys"].size
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
+        np.testing.assert_array_equal(host(im), ref["image"])
+
+
+@pytest.mark.parametrize("n,W,H", [(300, 16, 16), (300, 13, 9), (1, 48, 48), (2, 48, 48)],
+                         ids=["one_tile", "one_ragged_tile", "one_gaussian", "two_gaussians"])
+def test_forward_tiny_lists(cuda, oracle, n, W, H):
+    """One tile (no tile bits to sort) and lists of one or two pairs."""
+    arrays = scene(n, 4)
+    if n <= 2:
+        arrays["position"][:] = 0.0
+        arrays["log_scale"][:] = -5.0
+    g = gs.Gaussian3D(arrays)
+    cam = gs.make_camera(W, H, (0.0, 0.0, 4.0))
+    cfg = gs.default_config()
+    for views in (1, 2):
+        cams = [cam] * views
+        ctxs = [gs.RasterizerContext() for _ in cams]
+        imgs = gs.Rasterizer.forward_batch(g, cams, ctxs, config=cfg)
+        ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
+        for c, im in zip(ctxs, imgs):
+            assert c.num_rendered == ref["sorted_keys"].size
+            np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
+            np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
+            np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
+            np.testing.assert_array_equal(host(im), ref["image"])

@@ -54,11 +54,15 @@ def test_bench_work_model():
     import bench
     assert bench.sort_bytes_per_pair(45) == 8 + 24 * 6
     assert bench.sort_bytes_per_pair(13, 4) == 4 + 16 * 2
-    assert bench.packed_sort_bytes(32) == 8 + 16 * 4 and bench.packed_sort_bytes(13) == 8 + 16 * 2
+    # histogram read, 16 B per pass, the last pass writing 4 B ids (+ 4 B keys)
+    assert bench.packed_sort_bytes(32, hi=True) == 8 + 16 * 4
+    assert bench.packed_sort_bytes(13, hist=False) == 16 + 12
     w = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45)
     assert w["adam"] == ("hbm", 1652 * 1000, 1)
     assert w["preprocess"][1] == (236 + 88) * 1000
     w8 = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45, batch=8)
     assert w8["preprocess"] == ("hbm", (236 / 8 + 88) * 1000, 1 / 8)
     assert w8["preprocess_bwd"] == ("hbm", (3 * 236 / 8 + 36) * 1000, 1 / 8)
-    assert w8["sort"] == ("hbm", (8 + 16 * 5) * 1000 + (8 + 16 * 2) * 5000, 1 + 1 / 8)
+    # batched depth words: 28 + 3 bits (4 passes); tile sort: digits counted by emission
+    assert w8["sort"] == ("hbm", (8 + 16 * 3 + 12) * 1000 + (16 + 12) * 5000, 1 + 1 / 8)
+    assert w8["ranges"] == ("hbm", 8 * 8160, 1)
