@@ -620,7 +620,7 @@ int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64
       GS_TRY(sort_packed_clear(ctx, (int64_t)m, 32, 32 + tb, scratch));
       GS_TRY(launch_emit_tiles(frame_bins(f), f->order_ptr, n, (const uint64_t*)f->offsets.ptr, tx, pairs,
                                ctx->stream, sort_packed_hist(scratch, (int64_t)m, 32, 32 + tb), (tb + 7) / 8,
-                               ranges, T, (int64_t)ctx->num_sms * 8));
+                               ranges, T, (int64_t)ctx->num_sms * 32));
     }
     {
       // 3. stable sort of the packed (tile << 32 | id) words by the tile bits
