@@ -230,9 +230,9 @@ def pge_count(gs, rctx):
 # ---------------------------------------------------------------------------
 # DRAM bytes per launch (per view for the sort) measured by ncu on config 3
 # (profiles/binning_sort_preprocess_c3.md).
-TRAFFIC_C3 = {"composite_fwd": 50.3e6, "composite_bwd": 116.2e6,
-              # per view: batched depth sort (1/8 of histogram + 5 passes) + tile sort
-              "sort": 1212e6}
+TRAFFIC_C3 = {"composite_fwd": 49.0e6, "composite_bwd": 114.8e6,
+              # per view: batched depth sort (1/8 of histogram + 4 passes) + tile sort (2 passes)
+              "sort": 873e6}
 
 PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
 PARAM_ROW_B = 236  # the 59 floats of one Gaussian
