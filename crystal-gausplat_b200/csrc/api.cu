@@ -74,7 +74,7 @@ using namespace gs;
 struct gsc_frame {
   gsc_ctx* ctx = nullptr;
   GsBuf splats, depth_pairs, depth_keys, order, pairs, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
-      last, n_contrib, grad2d, bins;
+      last, n_contrib, grad2d, bins, tile_order, tile_work;
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
@@ -510,7 +510,7 @@ GSC_API int gsc_frame_destroy(gsc_frame* f) {
   cudaStreamSynchronize(f->ctx->stream);
   GsBuf* bufs[] = {&f->splats, &f->depth_pairs, &f->pairs, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
-                   &f->n_contrib, &f->grad2d, &f->bins};
+                   &f->n_contrib, &f->grad2d, &f->bins, &f->tile_order, &f->tile_work};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
   delete f;
@@ -668,10 +668,22 @@ int forward_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, 
   a.last = (uint32_t*)f->last.ptr;
   a.n_contrib = (uint32_t*)f->n_contrib.ptr;
   if (ctx->profiling) a.pge = reinterpret_cast<unsigned long long*>(ctx->err + 2);
+  const int32_t T = f->tiles_x * f->tiles_y;
+  GS_TRY(ensure(ctx, &f->tile_work, (size_t)T * 4 + 4));
+  a.tile_work = (uint32_t*)f->tile_work.ptr;
   {
+    // The forward keeps the row-major tile order (its last wave overlaps the
+    // next view's binning in a batched forward). It leaves the backward's
+    // order: longest backward lists first, so that the backward's last wave
+    // holds the short ones; the length is the tile's max of `last` (the full
+    // mode's backward starts there), the whole list in the reference mode.
     StageScope sc(ctx, GSC_STAGE_COMPOSITE_FWD);
-    sc.kernels(1);
+    sc.kernels(2);
     GS_TRY(launch_composite_fwd(a, ctx->stream));
+    const bool full = cfg->mode == GSC_MODE_FULL;
+    GS_TRY(ensure(ctx, &f->tile_order, (size_t)T * 4 + 4));
+    GS_TRY(launch_tile_order(full ? nullptr : (const uint32_t*)f->ranges.ptr, full ? a.tile_work : nullptr, T,
+                             (uint32_t*)f->tile_order.ptr, ctx->stream));
   }
   if (n_contrib)
     GS_CK(cudaMemcpyAsync(n_contrib, f->n_contrib.ptr, npix * 4, cudaMemcpyDeviceToDevice, ctx->stream));
@@ -850,6 +862,7 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussia
   a.loss_sum = loss_sum;
   {
     StageScope sc(ctx, GSC_STAGE_COMPOSITE_BWD);
+    a.tile_order = (const uint32_t*)f->tile_order.ptr;  // the forward's work order
     sc.kernels(1);
     GS_TRY(launch_composite_bwd(a, cfg->mode == GSC_MODE_FULL, ctx->stream));
   }

@@ -344,6 +344,43 @@ int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const
   return GSC_OK;
 }
 
+constexpr int kOrderBuckets = 132;  // 0: no work; 1 + 4 * msb + next two bits
+
+__global__ void __launch_bounds__(1024) tile_order_kernel(const uint32_t* __restrict__ ranges,
+                                                          const uint32_t* __restrict__ tile_work,
+                                                          int32_t num_tiles, uint32_t* __restrict__ order) {
+  __shared__ uint32_t s_off[kOrderBuckets];
+  for (int k = threadIdx.x; k < kOrderBuckets; k += 1024) s_off[k] = 0u;
+  __syncthreads();
+  auto bucket = [&](int32_t t) -> int {
+    const uint32_t w = ranges ? ranges[2 * t + 1] - ranges[2 * t] : tile_work[t];
+    if (w == 0) return kOrderBuckets - 1;  // last
+    const int msb = 31 - __clz(w);
+    const uint32_t frac = msb >= 2 ? (w >> (msb - 2)) & 3u : (w << (2 - msb)) & 3u;
+    return kOrderBuckets - 2 - (4 * msb + (int)frac);  // larger work first
+  };
+  for (int32_t t = threadIdx.x; t < num_tiles; t += 1024) atomicAdd(&s_off[bucket(t)], 1u);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t run = 0;
+    for (int k = 0; k < kOrderBuckets; k++) {
+      const uint32_t c = s_off[k];
+      s_off[k] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int32_t t = threadIdx.x; t < num_tiles; t += 1024) order[atomicAdd(&s_off[bucket(t)], 1u)] = (uint32_t)t;
+}
+
+int launch_tile_order(const uint32_t* ranges, const uint32_t* tile_work, int32_t num_tiles, uint32_t* order,
+                      cudaStream_t stream) {
+  if (num_tiles <= 0) return GSC_OK;
+  tile_order_kernel<<<1, 1024, 0, stream>>>(ranges, tile_work, num_tiles, order);
+  GS_CK_LAUNCH("tile_order_kernel");
+  return GSC_OK;
+}
+
 __global__ void __launch_bounds__(256) ranges_finish_kernel(uint32_t* __restrict__ ranges, int32_t num_tiles) {
   const int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x;
   if (t >= num_tiles) return;

@@ -137,6 +137,17 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     __syncthreads();
     if (tid == 0) atomicAdd(a.pge, s_pge);
   }
+  if (a.tile_work) {  // the backward's list length for this tile: max over pixels of `last`
+    __shared__ uint32_t s_work;
+    if (tid == 0) s_work = 0u;
+    __syncthreads();
+    uint32_t v = inside ? lst : 0u;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if ((tid & 31) == 0 && v) atomicMax(&s_work, v);
+    __syncthreads();
+    if (tid == 0) a.tile_work[tile] = s_work;
+  }
   if (!inside) return;
   const size_t pix = (size_t)y * a.width + x;
   a.image[pix * 3 + 0] = fmaf(T, a.bg[0], C0);
@@ -233,7 +244,7 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
   __shared__ float s_loss[kBwdWarps];
   // per-warp transpose buffer of the 9 partials (rows padded to 36 floats)
   __shared__ __align__(16) float s_red[kBwdWarps][9 * 36];
-  const int tile = blockIdx.x;
+  const int tile = a.tile_order ? (int)a.tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
   const int tid = threadIdx.x, lane = tid & 31;
   const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];

@@ -62,6 +62,7 @@ struct CompositeFwdArgs {
   float* final_T;
   uint32_t* last;
   unsigned long long* pge;  // if set: += pixel-Gaussian evaluations (tile-list entries visited)
+  uint32_t* tile_work;         // if set: per tile, the largest per-pixel `last` (backward list length)
 };
 
 struct CompositeBwdArgs {
@@ -79,6 +80,7 @@ struct CompositeBwdArgs {
   const uint32_t* last;
   float* grad2d;
   float* loss_sum;
+  const uint32_t* tile_order;  // if set: block b composites tile tile_order[b]
 };
 
 struct PreprocessBwdArgs {
@@ -145,6 +147,11 @@ int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const
                       int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist = nullptr,
                       int hist_passes = 0, uint32_t* ranges = nullptr, int32_t num_tiles = 0,
                       int64_t grid_cap = 0);
+// Tiles in decreasing order of their work (log-spaced buckets, 4 per
+// octave), so that the compositing's last wave holds the short tiles: work
+// = range length (ranges given) or tile_work[t].
+int launch_tile_order(const uint32_t* ranges, const uint32_t* tile_work, int32_t num_tiles, uint32_t* order,
+                      cudaStream_t stream);
 // empty ranges {0xFFFFFFFF, 0} -> {0, 0}
 int launch_ranges_finish(uint32_t* ranges, int32_t num_tiles, cudaStream_t stream);
 // 64-bit keys (tile << 32 | bits(depth)) from the tile ranges and the ids
