@@ -79,7 +79,11 @@ __device__ __forceinline__ void unstage_rows(const float4* s4, float* g, int64_t
 // the SH gradient goes straight into the staged gradient row, and every
 // gradient row is read and written once per launch. Dynamic shared memory:
 // the SH rows and the SH-gradient rows of the block.
-__global__ void __launch_bounds__(kPbThreads) preprocess_bwd_full_kernel(PreprocessBwdArgs a) {
+// 4 CTAs per SM (its shared memory allows no more): at most 128 registers.
+// Reading the SH rows from global memory instead of staging them (half the
+// shared memory) measured slower at 4 and 5 CTAs per SM (0.297 / 0.295 vs
+// 0.279 ms per view), and at 6 CTAs the registers spill.
+__global__ void __launch_bounds__(kPbThreads, 4) preprocess_bwd_full_kernel(PreprocessBwdArgs a) {
   extern __shared__ float4 s_dyn[];
   float4* s_par = s_dyn;                         // SH rows
   float4* s_grd = s_dyn + kPbThreads * kRowF4;   // SH-gradient rows
