@@ -98,7 +98,6 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   constexpr bool kPack16 = MODE == 0;
   __shared__ uint32_t s_whw[kWarps][kPack16 ? 128 : 256];
   unsigned short* s_wh16 = reinterpret_cast<unsigned short*>(&s_whw[0][0]);
-  __shared__ uint32_t s_local_excl[256];
   __shared__ uint32_t s_gbase[256];
   __shared__ uint8_t s_dig[MODE == 0 ? kTileKeys : 1];  // pair mode only
   __shared__ uint32_t s_warp[kWarps];
@@ -120,12 +119,15 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   uint32_t dig[kItems / 4];  // four 8-bit digits per register
 #pragma unroll
   for (int i = 0; i < kItems / 4; i++) dig[i] = 0;
+  // partition-local 32-bit indices: the warp's keys start at wkeys
+  const K* __restrict__ wkeys = keys_in + warp_base;
+  const int wvalid = (int)max((int64_t)0, min((int64_t)kWarpKeys, n - warp_base));
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
-    const int64_t idx = warp_base + i * 32 + lane;
+    const int li = i * 32 + lane;
     // Pairs past the end take the largest digit (and come last in index
     // order), so they sort behind every valid pair of the tile.
-    const uint32_t d = idx < n ? ((uint32_t)(keys_in[idx] >> shift) & digit_mask) : digit_mask;
+    const uint32_t d = li < wvalid ? ((uint32_t)(wkeys[li] >> shift) & digit_mask) : digit_mask;
     dig[i / 4] |= d << (8 * (i % 4));
   }
   const uint32_t lt_mask = (1u << lane) - 1u;
@@ -139,9 +141,9 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
 #pragma unroll
     for (int b = 0; b < 8; b++) {
       if (b < nbits) {
-        const bool bit = (d >> b) & 1u;
+        const uint32_t bit = (d >> b) & 1u;
         const uint32_t bal = __ballot_sync(0xffffffffu, bit);
-        peers &= bit ? bal : ~bal;
+        peers &= ~(bal ^ (0u - bit));  // bal where the bit is set, ~bal where clear
       }
     }
     const int leader = __ffs(peers) - 1;
@@ -176,8 +178,13 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   }
   const uint32_t valid_cnt = d == digit_mask ? cnt - (kTileKeys - num_valid) : cnt;
   const uint32_t local_excl = block_excl_scan_256(cnt, s_warp);
+  // each warp's start within the digit becomes its start within the tile
+#pragma unroll
+  for (int ww = 0; ww < kWarps; ww++) {
+    if (kPack16) s_wh16[ww * 256 + d] = (unsigned short)(s_wh16[ww * 256 + d] + local_excl);
+    else s_whw[ww][d] += local_excl;
+  }
   const uint32_t gexcl = block_excl_scan_256(hist[(size_t)d * hstride], s_warp);
-  s_local_excl[d] = local_excl;
 
   // Decoupled look-back.
   uint32_t* my = status + (size_t)part * 256 + d;
@@ -210,11 +217,11 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
 
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
-    const int64_t idx = warp_base + i * 32 + lane;
+    const int li = i * 32 + lane;
     const uint32_t dd = rank[i] >> 16;
     const uint32_t wbase = kPack16 ? (uint32_t)s_wh16[w * 256 + dd] : s_whw[w][dd];
-    const uint32_t pos = s_local_excl[dd] + wbase + (rank[i] & 0xFFFFu);
-    if (idx < n) s_keys[pos] = keys_in[idx];
+    const uint32_t pos = wbase + (rank[i] & 0xFFFFu);
+    if (li < wvalid) s_keys[pos] = wkeys[li];
     rank[i] = pos;
   }
   __syncthreads();
@@ -247,8 +254,8 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys);
 #pragma unroll
   for (int i = 0; i < kItems; i++) {
-    const int64_t idx = warp_base + i * 32 + lane;
-    if (idx < n) s_vals[rank[i]] = vals_in[idx];
+    const int li = i * 32 + lane;
+    if (li < wvalid) s_vals[rank[i]] = vals_in[warp_base + li];
   }
   __syncthreads();
   for (uint32_t j = tid; j < num_valid; j += kThreads) {
