@@ -167,7 +167,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // One pixel's backward state.
 struct BwdPixel {
   bool inside;
-  float pxf, pyf;
+  float pyf;
   float g[3];
   float T;
   float ag;  // (colour behind this Gaussian, incl. background) . g -- the only use of it
@@ -178,10 +178,12 @@ struct BwdPixel {
 // adds the conic gradient, the alpha clamp and the corrected running colour).
 template <bool FULL>
 __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, float4 g1, float g2,
-                                          float amin, float amax, float cut, bool short_exp, float v[9]) {
+                                          float amin, float amax, float cut, bool short_exp, float dx, float dxxa,
+                                          float v[9]) {
   if (!(P.inside && idx < P.hi)) return false;
-  const float dx = P.pxf - g0.x, dy = P.pyf - g0.y;
-  const float power = fmaf(dy * dy, g1.x, fmaf(dx * dy, g0.w, dx * dx * g0.z));  // == forward's power
+  // dx and dx dx (-A/2) are shared by the thread's pixels (one column)
+  const float dy = P.pyf - g0.y;
+  const float power = fmaf(dy * dy, g1.x, fmaf(dx * dy, g0.w, dxxa));  // == forward's power
   if (power > 0.0f || power < cut) return false;
   // Same exponential and tests as the forward, so the accepted set matches it.
   const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
@@ -253,13 +255,13 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
   const bool short_exp = cut >= -103.0f;
 
   BwdPixel P[kBwdPix];
+  const float pxf = (float)(tx * GS_TILE + (tid & 15)) + 0.5f;  // the thread's pixel column
   float loss = 0.0f;
 #pragma unroll
   for (int h = 0; h < kBwdPix; h++) {
     const int x = tx * GS_TILE + (tid & 15), y = ty * GS_TILE + (tid >> 4) + kBwdRowStep * h;
     BwdPixel& Q = P[h];
     Q.inside = x < a.width && y < a.height;
-    Q.pxf = (float)x + 0.5f;
     Q.pyf = (float)y + 0.5f;
     Q.T = 1.0f;
     Q.hi = start;
@@ -306,6 +308,7 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
   const float rx0 = tx * GS_TILE + 0.5f, ry0 = ty * GS_TILE + 0.5f;
   const float rx1 = min(tx * GS_TILE + GS_TILE, a.width) - 0.5f;
   const float ry1 = min(ty * GS_TILE + GS_TILE, a.height) - 0.5f;
+  const int red_row = lane / 3, red_part = lane - 3 * (lane / 3);  // reduction roles
   for (int64_t bend = hi; bend > (int64_t)start; bend -= kBwdThreads) {
     const int64_t bstart = max((int64_t)start, bend - kBwdThreads);
     const int mb = (int)(bend - bstart);
@@ -340,22 +343,33 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
 #pragma unroll
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
       bool ok = false;
+      const float dx = pxf - g0.x, dxxa = dx * dx * g0.z;
 #pragma unroll
-      for (int h = 0; h < kBwdPix; h++) ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2, amin, amax, cut, short_exp, v);
+      for (int h = 0; h < kBwdPix; h++)
+        ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2, amin, amax, cut, short_exp, dx, dxxa, v);
       if (__any_sync(0xffffffffu, ok)) {
         float* red = s_red[tid >> 5];
 #pragma unroll
         for (int k = 0; k < 9; k++) red[k * 36 + lane] = v[k];
         __syncwarp();
-        if (lane < 9) {
-          const float4* row = reinterpret_cast<const float4*>(red + lane * 36);
-          float r = 0.0f;
-#pragma unroll
-          for (int q = 0; q < 8; q++) {
-            const float4 t = row[q];
-            r += (t.x + t.y) + (t.z + t.w);
+        // row k (32 lanes' partials of field k) is summed by lanes 3k..3k+2,
+        // three, three and two float4 each (conflict-free: the 8 lanes of a
+        // quarter-warp cover 32 distinct banks), then folded into lane 3k
+        float r = 0.0f;
+        if (lane < 27) {
+          const float4* row = reinterpret_cast<const float4*>(red + red_row * 36) + red_part * 3;
+          const float4 t0 = row[0], t1 = row[1];
+          r = ((t0.x + t0.y) + (t0.z + t0.w)) + ((t1.x + t1.y) + (t1.z + t1.w));
+          if (red_part < 2) {
+            const float4 t2 = row[2];
+            r += (t2.x + t2.y) + (t2.z + t2.w);
           }
-          if (r != 0.0f) atomicAdd(a.grad2d + (size_t)s_gid[j] * 9 + lane, r);
+        }
+        const float r1 = __shfl_down_sync(0xffffffffu, r, 1);
+        const float r2 = __shfl_down_sync(0xffffffffu, r, 2);
+        if (lane < 27 && red_part == 0) {
+          r = (r + r1) + r2;
+          if (r != 0.0f) atomicAdd(a.grad2d + (size_t)s_gid[j] * 9 + red_row, r);
         }
         __syncwarp();
       }
