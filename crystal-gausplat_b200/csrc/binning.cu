@@ -177,8 +177,13 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 //   2. emission of (tile, id) pairs in that depth order,
 //   3. a stable sort of those pairs by the tile bits only,
 // which moves 8-byte pairs through ceil(tile_bits / 8) passes instead of
-// 12-byte pairs through ceil((32 + tile_bits) / 8) passes. The 64-bit keys are
-// rebuilt on request from the tile ranges (make_keys_ranges_kernel).
+// 12-byte pairs through ceil((32 + tile_bits) / 8) passes. The emission also
+// counts the tile sort's digits (so the sort needs no histogram pass) and
+// presets every tile's range to {~0, 0}; the sort's last pass writes the ids
+// and the ranges (runs of one tile), ranges_finish_kernel turns the untouched
+// {~0, 0} into the reference's empty {0, 0}, and no tile array is kept. The
+// 64-bit keys are rebuilt on request from the tile ranges
+// (make_keys_ranges_kernel).
 // ---------------------------------------------------------------------------
 
 // `bins`: the 32-byte binning records of preprocess ({x0, y0, width, count},
@@ -344,7 +349,12 @@ int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const
   return GSC_OK;
 }
 
-constexpr int kOrderBuckets = 132;  // 0: no work; 1 + 4 * msb + next two bits
+// Tile order for the backward compositing: a counting sort of the tiles by
+// work in buckets of a quarter octave (the work's leading bit and the two
+// below it), largest first, tiles without work last. One block; the order
+// within a bucket is whatever the shared-memory atomics give (every tile is
+// composited independently, so it does not change any result).
+constexpr int kOrderBuckets = 132;
 
 __global__ void __launch_bounds__(1024) tile_order_kernel(const uint32_t* __restrict__ ranges,
                                                           const uint32_t* __restrict__ tile_work,
