@@ -11,13 +11,22 @@
 //
 // Limits and rules:
 //  - The scratch is a file-scope __device__ array of kStaticScratchBytes
-//    (about 3.7 MB). Every GPU that loads this library holds it until the
-//    process exits.
+//    (about 3.7 MB). Every GPU on which the library's device code is loaded
+//    holds it until the process exits. With CUDA's lazy module loading (the
+//    default since CUDA 12.2) that load, and so the reservation of the
+//    array, may happen only at the first call on a device: make that first
+//    call during initialisation, outside real-time threads and outside any
+//    stream capture.
 //  - n may be at most GSC_STATIC_SORT_MAX_PAIRS (262144); larger sizes are
 //    rejected with GSC_ERR_INVALID before any GPU work is queued.
 //  - The first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture.
+//    cudaGetSymbolAddress (with that device current) and caches it for the
+//    life of the process, so cudaDeviceReset (or destroying the primary
+//    context) is not supported while the library is in use.
+//  - Device-side errors (a look-back wait that gave up, a bounds check) land
+//    in an error word at the end of the array; the next call clears it.
+//    gsc_sort_pairs_u64_static_status(stream) waits for the stream, reads
+//    and clears the word and reports it, without allocating.
 //  - All calls share the one array, and each call clears the parts that must
 //    start at zero (histograms, look-back flags, tickets) on its stream.
 //    Calls whose GPU work overlaps -- on two streams, or from two threads --
@@ -100,4 +109,28 @@ extern "C" GSC_API int gsc_sort_pairs_u64_static(uint64_t* keys, uint32_t* value
   c.err = reinterpret_cast<uint32_t*>(static_cast<char*>(base) + kSortBytes);
   GS_CK(cudaMemsetAsync(c.err, 0, 4, c.stream));
   return launch_sort_pairs(&c, keys, values, n, begin_bit, end_bit, static_cast<char*>(base));
+}
+
+extern "C" GSC_API int gsc_sort_pairs_u64_static_status(void* stream) {
+  int device = 0;
+  GS_CK(cudaGetDevice(&device));
+  GS_REQUIRE(device >= 0 && device < kMaxDevices, "gsc_sort_pairs_u64_static_status: device index too large");
+  void* base = nullptr;
+  int rc = scratch_address(device, &base);
+  if (rc != GSC_OK) return rc;
+  uint32_t* err = reinterpret_cast<uint32_t*>(static_cast<char*>(base) + kSortBytes);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint32_t flags = 0;  // pageable host word: the copy completes before the call returns
+  GS_CK(cudaStreamSynchronize(s));
+  GS_CK(cudaMemcpyAsync(&flags, err, 4, cudaMemcpyDeviceToHost, s));
+  GS_CK(cudaStreamSynchronize(s));
+  if (!flags) return GSC_OK;
+  GS_CK(cudaMemsetAsync(err, 0, 4, s));
+  GS_CK(cudaStreamSynchronize(s));
+  if (flags & GS_DEVERR_TIMEOUT) {
+    set_error("gsc_sort_pairs_u64_static: a bounded look-back wait gave up; the output is not sorted");
+    return GSC_ERR_TIMEOUT;
+  }
+  set_error("gsc_sort_pairs_u64_static: a device-side bounds check failed; the output is not sorted");
+  return GSC_ERR_CUDA;
 }

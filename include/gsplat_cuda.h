@@ -223,14 +223,23 @@ GSC_API int gsc_sort_pairs_u64(gsc_ctx* ctx, uint64_t* keys, uint32_t* values, i
  * pool owns all device memory, a thread that must not take the driver's
  * allocation locks, a caller without a gsc_ctx): same stable sort and
  * arguments, but the scratch is a fixed device array inside the library
- * (about 3.7 MB, held on every GPU that loads the library until exit), so
- * n <= GSC_STATIC_SORT_MAX_PAIRS; larger n returns GSC_ERR_INVALID. Work is
- * queued on `stream` (a cudaStream_t, NULL = legacy default). The first call
- * on a device looks up the array's address; make it before any stream
- * capture. All calls share the array: calls whose GPU work overlaps race. */
+ * (about 3.7 MB per GPU, held until exit), so n <= GSC_STATIC_SORT_MAX_PAIRS;
+ * larger n returns GSC_ERR_INVALID. Work is queued on `stream` (a
+ * cudaStream_t, NULL = legacy default). The first call on a device may load
+ * the library's device code (CUDA lazy loading), which reserves the array,
+ * and looks up its address once: make it during initialisation, outside
+ * real-time threads and before any stream capture. cudaDeviceReset is not
+ * supported while the library is in use. All calls share the array: calls
+ * whose GPU work overlaps race. */
 #define GSC_STATIC_SORT_MAX_PAIRS 262144
 GSC_API int gsc_sort_pairs_u64_static(uint64_t* keys, uint32_t* values, int64_t n, int begin_bit,
                                       int end_bit, void* stream);
+/* Device-side status of the last gsc_sort_pairs_u64_static on this device
+ * (no reference counterpart, no allocation): waits for `stream`, then returns
+ * GSC_OK, GSC_ERR_TIMEOUT (a bounded look-back wait gave up) or GSC_ERR_CUDA
+ * (a bounds check failed), and clears the status. The output of a sort whose
+ * status is not GSC_OK is not sorted. */
+GSC_API int gsc_sort_pairs_u64_static_status(void* stream);
 
 /* GPURadixSort.compute_tile_ranges! (gpu_radix_sort.cr:204-233,
  * radix_sort.metal:288-324): ranges[t] = [first, last+1) of tile t in the
