@@ -21,6 +21,7 @@ import math
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -58,11 +59,36 @@ def parse():
                     help="profiling knob: override the number of views of --config (small ncu cases)")
     ap.add_argument("--binning", default="contributing", choices=["contributing", "reference"],
                     help="tile lists: contributing pairs only (default) or the reference's full lists")
+    ap.add_argument("--t-stop", type=float, default=None,
+                    help="transmittance stop (default: the reference's 1e-3; the north star names 1e-4)")
     return ap.parse_args()
 
 
 def binning_of(gs, args):
     return gs._abi.GSC_BIN_CONTRIBUTING if args.binning == "contributing" else gs._abi.GSC_BIN_REFERENCE
+
+
+def t_stop_of(args):
+    return 1e-3 if args.t_stop is None else args.t_stop
+
+
+def workload_config(args, cfg, world):
+    """The `config` object of both arms' lines: the workload only (what the
+    run measured lives in `workload_stats`), so the two arms' configs are equal."""
+    if args.config in ("c3", "c2"):
+        return {"workload": f"{args.config}: train step, {cfg['n']} Gaussians SH3, {cfg['views']} views "
+                            f"{cfg['W']}x{cfg['H']}, L1, gradient exchange + fused Adam",
+                "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
+                "binning": args.binning, "t_stop": t_stop_of(args),
+                "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush"}
+    if args.config == "c4":
+        return {"workload": f"c4: render-only, {cfg['n']} Gaussians, {cfg['views']} views "
+                            f"{cfg['W']}x{cfg['H']}", "parallelism": f"views/{world}",
+                "binning": args.binning, "t_stop": t_stop_of(args),
+                "l2": "inputs larger than L2, no flush"}
+    end_bit = 32 + int(math.ceil(math.log2(cfg["tiles"])))
+    return {"workload": f"c1: stable sort of {cfg['pairs']} pairs by bits [0,{end_bit})",
+            "parallelism": f"independent sorts/{world}", "l2": "inputs (360 MB) larger than L2, no flush"}
 
 
 def load_peaks():
@@ -86,12 +112,12 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        self.path = None
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix=f"bench_clocks_gpu{self.gpu}_", suffix=".csv")
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
@@ -128,6 +154,10 @@ class ClockSampler:
                     if val.lower().startswith("active"):
                         reasons.add(name)
         med = float(np.median(sm)) if sm else None
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
         return {"sm_mhz": med, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -228,8 +258,7 @@ def pge_count(gs, rctx):
 # ---------------------------------------------------------------------------
 # algorithmic work per stage (bytes, or FP32 ops for compositing)
 # ---------------------------------------------------------------------------
-# DRAM bytes per launch (per view for the sort) measured by ncu on config 3
-# (profiles/binning_sort_preprocess_c3.md).
+# DRAM bytes per launch (per view for the sort) measured by ncu on config 3.
 TRAFFIC_C3 = {"composite_fwd": 49.0e6, "composite_bwd": 114.8e6,
               # per view: batched depth sort (1/8 of histogram + 4 passes) + tile sort (2 passes)
               "sort": 873e6}
@@ -365,7 +394,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     g = gs.Gaussian3D(arrays, device=dev)
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config(binning=binning_of(gs, args))
+    rcfg = gs.default_config(binning=binning_of(gs, args), t_stop=args.t_stop)
     tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg, exchange=args.exchange)
     host_t = make_targets(cfg, tr.lo, tr.hi)
     dev_t = host_t.to(dev)
@@ -378,25 +407,38 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     for _ in range(args.warmup):
         tr.step(targets)
     torch.cuda.synchronize()
-    profile_read(gs, ctx, reset=True)
-    profile_pge(gs, ctx, reset=True)
+
+    def one_step(counts):
+        tr.zero()
+        for v in tr.my_views:
+            tr.view_fwd_bwd(v, targets(v))
+            counts[0] += tr.last_ctx.num_rendered
+        tr.reduce_and_step()
+
+    # timed region: tracing off
     k0 = lib.gsc_kernel_count(ctx)
-    keys_total = 0
-    lib.gsc_profile_enable(ctx, 1)
+    keys_total = [0]
     with ClockSampler(local) as clk:
         with Timer(torch, world) as tm:
             for _ in range(args.steps):
-                tr.zero()
-                for v in tr.my_views:
-                    tr.view_fwd_bwd(v, targets(v))
-                    keys_total += tr.last_ctx.num_rendered
-                tr.reduce_and_step()
-    lib.gsc_profile_enable(ctx, 0)
+                one_step(keys_total)
     ms = tm.max_over_ranks()
-    stats = profile_read(gs, ctx, reset=True)
     launches = int(lib.gsc_kernel_count(ctx) - k0)
+    keys_total = keys_total[0]
     views_done = args.steps * cfg["views"]
     value = views_done / (ms / 1e3)
+
+    # a second pass of the same steps with the library's per-stage CUDA events
+    # (stage times, pixel-Gaussian evaluations): the roofline's kernel times
+    profile_read(gs, ctx, reset=True)
+    profile_pge(gs, ctx, reset=True)
+    lib.gsc_profile_enable(ctx, 1)
+    with Timer(torch, world) as tm_traced:
+        for _ in range(args.steps):
+            one_step([0])
+    lib.gsc_profile_enable(ctx, 0)
+    ms_traced = tm_traced.max_over_ranks()
+    stats = profile_read(gs, ctx, reset=True)
 
     my_views = max(1, tr.hi - tr.lo)
     pge = profile_pge(gs, ctx) / (args.steps * my_views)  # exact mean over this rank's views
@@ -433,13 +475,12 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Gaussians, poses and U[0,1] targets per BASELINE.json)",
-            "config": {"workload": f"{args.config}: train step, {cfg['n']} Gaussians SH3, {cfg['views']} views "
-                                   f"{cfg['W']}x{cfg['H']}, L1, all-reduce + fused Adam",
-                       "global_batch_views": cfg["views"], "parallelism": f"dp{world} (views)",
-                       "exchange": tr.exchange, "binning": args.binning,
-                       "backward_batch_views": tr.batch,
-                       "l2": "inputs larger than L2 (708 MB params + 1.6 GB targets), no flush",
-                       "keys_per_view": round(keys_per_view), "pge_per_view": round(pge)},
+            "config": workload_config(args, cfg, world),
+            "workload_stats": {"exchange": tr.exchange, "backward_batch_views": tr.batch,
+                               "keys_per_view": round(keys_per_view), "pge_per_view": round(pge),
+                               "traced_pass_ms_per_step": round(ms_traced / args.steps, 3),
+                               "stage_times": "per-stage CUDA events of a second, traced pass of "
+                                              "the same steps (the timed region runs untraced)"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "e2e": e2e,
@@ -453,18 +494,22 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "stages": roof,
         }
         if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as O
             result["cpu_baseline"] = cpu_baseline_train(
-                gs, cfg, arrays, cams, gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE), host_t,
-                os.cpu_count())
+                gs, cfg, arrays, cams, O.default_config(binning=gs._abi.GSC_BIN_REFERENCE, t_stop=args.t_stop),
+                host_t, os.cpu_count())
     return result
 
 
-def reference_train(args, cfg):
-    """--impl reference: the oracle port on all host threads, one view per step."""
+def reference_train(args, cfg, world):
+    """--impl reference: the oracle port on all host threads, one view per step.
+    Nothing here loads the CUDA library: the configuration comes from the
+    oracle, the scene and cameras from the package's host-only helpers."""
+    from oracle import oracle as O
     gs = importlib.import_module("crystal-gausplat_b200")
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE)  # the reference's CPU path
+    rcfg = O.default_config(binning=gs._abi.GSC_BIN_REFERENCE, t_stop=args.t_stop)  # the reference's lists
     threads = os.cpu_count()
     H, W = cfg["H"], cfg["W"]
     ta = cpu_adam_seconds(cfg["n"], threads)
@@ -481,11 +526,12 @@ def reference_train(args, cfg):
             "value": round(value, 4), "unit": "views/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(per_view * 1e3, 1), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.config}: one view fwd+bwd per step + Adam/views"},
+            "config": workload_config(args, cfg, world),
             "cpu_baseline": {"value": round(value, 4), "unit": "views/s", "cores": threads, "kind": "port",
-                             "sample": "one view per step (fwd+bwd+L1) + Adam over all parameters / views; "
-                                       "the reference (Crystal + Metal) cannot build here, so the C++ "
-                                       "oracle restating it runs"},
+                             "sample": "one view of the workload per step (fwd+bwd+L1, the reference's "
+                                       "full tile lists) + Adam over all parameters / views; the reference "
+                                       "(Crystal + Metal) cannot build here, so the C++ oracle restating "
+                                       "it runs"},
             "e2e": {"value": round(value, 4), "unit": "views/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -502,7 +548,7 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     g = gs.Gaussian3D(arrays, device=dev)
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config(binning=binning_of(gs, args))
+    rcfg = gs.default_config(binning=binning_of(gs, args), t_stop=args.t_stop)
     lo, hi = trainer_mod.shard(len(cams), rank, world)
     kb = gs._abi.GSC_MAX_BATCH_VIEWS  # views per Rasterizer.forward_batch (one preprocess pass)
     rctxs = [gs.RasterizerContext(dev) for _ in range(kb)]
@@ -525,19 +571,22 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     for _ in range(args.warmup):
         render_all()
     torch.cuda.synchronize()
-    profile_read(gs, ctx, reset=True)
-    profile_pge(gs, ctx, reset=True)
     k0 = lib.gsc_kernel_count(ctx)
     keys_total = 0
-    lib.gsc_profile_enable(ctx, 1)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk:  # timed region: tracing off
         with Timer(torch, world) as tm:
             for _ in range(args.steps):
                 keys_total += render_all()
-    lib.gsc_profile_enable(ctx, 0)
     ms = tm.max_over_ranks()
-    stats = profile_read(gs, ctx, reset=True)
     launches = int(lib.gsc_kernel_count(ctx) - k0)
+    # the same steps again with the library's per-stage events (stage times, PGE)
+    profile_read(gs, ctx, reset=True)
+    profile_pge(gs, ctx, reset=True)
+    lib.gsc_profile_enable(ctx, 1)
+    for _ in range(args.steps):
+        render_all()
+    lib.gsc_profile_enable(ctx, 0)
+    stats = profile_read(gs, ctx, reset=True)
     pix = args.steps * cfg["views"] * cfg["W"] * cfg["H"]
     value = pix / 1e6 / (ms / 1e3)
     pge = profile_pge(gs, ctx) / max(1, args.steps * (hi - lo))
@@ -563,16 +612,16 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": f"c4: render-only, {cfg['n']} Gaussians, {cfg['views']} views "
-                                  f"{cfg['W']}x{cfg['H']}", "parallelism": f"views/{world}",
-                      "l2": "inputs larger than L2, no flush", "keys_per_view": round(kpv),
-                      "binning": args.binning},
+           "config": workload_config(args, cfg, world),
+           "workload_stats": {"keys_per_view": round(kpv), "pge_per_view": round(pge)},
            "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
            "roofline": dict(roof[dominant], kernel=dominant, traffic=None,
                             peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind),
            "stages": roof}
     if world == 1 and not args.no_cpu_baseline:
-        t = cpu_view_seconds(gs, arrays, cams[0], gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE), None, os.cpu_count(), with_backward=False)
+        from oracle import oracle as O
+        t = cpu_view_seconds(gs, arrays, cams[0], O.default_config(binning=gs._abi.GSC_BIN_REFERENCE, t_stop=args.t_stop),
+                             None, os.cpu_count(), with_backward=False)
         res["cpu_baseline"] = {"value": round(cfg["W"] * cfg["H"] / 1e6 / t, 3), "unit": "MPix/s",
                                "cores": os.cpu_count(), "kind": "port",
                                "sample": f"1 view (view 0) forward, {t:.2f} s, CPU oracle (OpenMP)"}
@@ -641,8 +690,7 @@ def run_sort(args, cfg, rank, world, local, peaks, peak_kind):
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
            "data": "synthetic (tile in [0,8160) << 32 | fp32 depth bits, depth U[0.5,10])",
-           "config": {"workload": f"c1: stable sort of {n} pairs by bits [0,{end_bit})",
-                      "l2": "inputs (360 MB) larger than L2, no flush"},
+           "config": workload_config(args, cfg, world),
            "gpu_launches": int(lib.gsc_kernel_count(ctx) - k0), "clocks": clk.summary(), "e2e": e2e,
            "roofline": {"kernel": "sort", "bound": "hbm", "achieved": round(ach, 1),
                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 4),
@@ -653,7 +701,7 @@ def run_sort(args, cfg, rank, world, local, peaks, peak_kind):
     return res
 
 
-def reference_sort(args, cfg, bounded=False):
+def reference_sort(args, cfg, bounded=False, world=1):
     from oracle import oracle as O
     n = 3_000_000
     keys, vals = sort_input(cfg, n)
@@ -669,19 +717,20 @@ def reference_sort(args, cfg, bounded=False):
             "unit": "Mkey/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(per * 1e3, 1), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": "c1 sample: 3M of the 30M pairs per step"},
+            "config": workload_config(args, cfg, world),
             "cpu_baseline": {"value": round(v, 2), "unit": "Mkey/s", "cores": 1, "kind": "port",
-                             "sample": "3M pairs per step, std::stable_sort (the reference's CPU key "
+                             "sample": "3M of the 30M pairs per step, std::stable_sort (the reference's CPU key "
                                        "sort, rasterizer.cr:250-255, is a comparison sort)"},
             "e2e": {"value": round(v, 2), "unit": "Mkey/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
 
-def reference_render(args, cfg):
+def reference_render(args, cfg, world):
+    from oracle import oracle as O
     gs = importlib.import_module("crystal-gausplat_b200")
     arrays = gs.synthetic_arrays(cfg["n"], cfg["seed"], cfg["extent"])
     cams = make_cameras(gs, cfg)
-    rcfg = gs.default_config(binning=gs._abi.GSC_BIN_REFERENCE)  # the reference's CPU path
+    rcfg = O.default_config(binning=gs._abi.GSC_BIN_REFERENCE, t_stop=args.t_stop)  # the reference's lists
     times = []
     for i in range(args.warmup + args.steps):
         t = cpu_view_seconds(gs, arrays, cams[i % len(cams)], rcfg, None, os.cpu_count(), False)
@@ -692,7 +741,7 @@ def reference_render(args, cfg):
             "unit": "MPix/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(float(np.mean(times)) * 1e3, 1), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "c4 sample: one 4K view forward per step"},
+            "config": workload_config(args, cfg, world),
             "cpu_baseline": {"value": round(v, 3), "unit": "MPix/s", "cores": os.cpu_count(),
                              "kind": "port", "sample": "one view per step, CPU oracle (OpenMP)"},
             "e2e": {"value": round(v, 3), "unit": "MPix/s", "h2d_bytes_per_step": 0,
@@ -718,11 +767,11 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             if args.config == "c1":
-                res = reference_sort(args, cfg)
+                res = reference_sort(args, cfg, world=world)
             elif args.config == "c4":
-                res = reference_render(args, cfg)
+                res = reference_render(args, cfg, world)
             else:
-                res = reference_train(args, cfg)
+                res = reference_train(args, cfg, world)
             emit_line(res, out_fd)
         return
     import torch

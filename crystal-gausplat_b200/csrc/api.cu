@@ -470,9 +470,9 @@ GSC_API int gsc_adam_step(gsc_ctx* ctx, const gsc_adam_group* groups, int32_t ng
   std::memset(&a, 0, sizeof a);
   a.ngroups = ngroups;
   a.beta1 = beta1; a.beta2 = beta2; a.eps = eps; a.grad_scale = grad_scale;
-  // 1 - beta^t evaluated in double and rounded once.
-  a.bc1 = (float)(1.0 - std::pow((double)beta1, (double)step));
-  a.bc2 = (float)(1.0 - std::pow((double)beta2, (double)step));
+  // 1 - beta^t in fp32 as the reference (adam.cr:129-130)
+  a.bc1 = 1.0f - powi_f32(beta1, step);
+  a.bc2 = 1.0f - powi_f32(beta2, step);
   int64_t run = 0;
   for (int i = 0; i < ngroups; i++) {
     const gsc_adam_group& G = groups[i];

@@ -43,6 +43,24 @@ __device__ __forceinline__ ShConsts sh_consts() {
   return k;
 }
 
+// beta^step of Adam's bias correction as the reference evaluates it:
+// `@beta1 ** state.step` (src/optim/adam.cr:129-130) is Float32#**(Int32),
+// which Crystal lowers to LLVM's powi intrinsic; with a run-time exponent
+// that is compiler-rt's __powisf2, binary exponentiation in fp32 (the
+// result is multiplied by the running square for each set bit of the
+// exponent, lowest bit first, and the square is updated after each bit).
+inline float powi_f32(float a, int b) {
+  const bool recip = b < 0;
+  float r = 1.0f;
+  for (;;) {
+    if (b & 1) r *= a;
+    b /= 2;
+    if (b == 0) break;
+    a *= a;
+  }
+  return recip ? 1.0f / r : r;
+}
+
 __device__ __forceinline__ float pow2i(int j) { return __int_as_float((j + 127) << 23); }
 
 // exp(x) in fp32: Cody & Waite (1980) reduction x = k ln2 + r with ln 2

@@ -119,8 +119,8 @@ extern "C" GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* in
     a.chunk_end[i] = run;
   }
   a.beta1 = in->beta1; a.beta2 = in->beta2; a.eps = in->eps; a.grad_scale = in->grad_scale;
-  a.bc1 = (float)(1.0 - std::pow((double)in->beta1, (double)in->step));
-  a.bc2 = (float)(1.0 - std::pow((double)in->beta2, (double)in->step));
+  a.bc1 = 1.0f - powi_f32(in->beta1, in->step);  // fp32, as adam.cr:129-130
+  a.bc2 = 1.0f - powi_f32(in->beta2, in->step);
   a.chunk_lo = run * in->rank / in->nranks;
   a.chunk_hi = run * (in->rank + 1) / in->nranks;
   const int64_t n = a.chunk_hi - a.chunk_lo;

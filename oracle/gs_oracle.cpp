@@ -264,6 +264,24 @@ inline void tile_bounds(float px, float py, float r, int tiles_x, int tiles_y, i
 
 extern "C" {
 
+// The reference's rasterizer constants (gaussian.metal:160,174,227-228,
+// 400,425-426; trainer.cr:186), as gsc_raster_config_default fills them, so
+// that a CPU-only caller (the benchmark's reference arm) needs nothing from
+// the CUDA library.
+void gso_raster_config_default(gsc_raster_config* cfg) {
+  cfg->mode = GSC_MODE_FULL;
+  cfg->sh_degree = 3;
+  cfg->t_stop = 1e-3f;
+  cfg->alpha_min = 1.0f / 255.0f;
+  cfg->alpha_max = 0.99f;
+  cfg->lowpass = 0.3f;
+  cfg->fov_cull = 1.3f;
+  cfg->near_z = 0.01f;
+  cfg->far_z = 1000.0f;
+  cfg->background[0] = cfg->background[1] = cfg->background[2] = 0.0f;
+  cfg->binning = GSC_BIN_CONTRIBUTING;
+}
+
 float gso_expf(float x) {
   if (x != x) return x;
   if (x > 88.72283935546875f) return INFINITY;
@@ -471,6 +489,63 @@ void gso_composite_forward(int32_t width, int32_t height, const uint32_t* ranges
         if (n_contrib) n_contrib[pix] = cnt;
         if (final_T) final_T[pix] = T;
         if (last) last[pix] = lst;
+      }
+  }
+}
+
+// rasterize_tile (gaussian.metal:364-445) with the reference's own
+// expression forms, for bounding the fused forms above against it: the
+// inverse covariance recomputed per pixel, power = -0.5 (dx dx inv_xx +
+// 2 dx dy inv_xy + dy dy inv_yy) summed left to right (gaussian.metal:421),
+// colour += (T alpha) c and colour += T background without fused
+// multiply-adds (gaussian.metal:430, 436). The exponential is this project's
+// (the reference's fast-math Metal exp is not specified to the bit).
+void gso_composite_forward_literal(int32_t width, int32_t height, const uint32_t* ranges,
+                                   const uint32_t* vals, const float* mean2d, const float* cov2d,
+                                   const float* opacity, const float* colors,
+                                   const gsc_raster_config* cfg, float* image, uint32_t* n_contrib,
+                                   float* final_T) {
+  const int tiles_x = (width + TILE - 1) / TILE, tiles_y = (height + TILE - 1) / TILE;
+#pragma omp parallel for num_threads(g_threads) schedule(dynamic, 4)
+  for (int t = 0; t < tiles_x * tiles_y; t++) {
+    const int tx = t % tiles_x, ty = t / tiles_x;
+    const uint32_t start = ranges[t * 2], end = ranges[t * 2 + 1];
+    for (int ly = 0; ly < TILE; ly++)
+      for (int lx = 0; lx < TILE; lx++) {
+        const int x = tx * TILE + lx, y = ty * TILE + ly;
+        if (x >= width || y >= height) continue;
+        const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+        float col[3] = {0.0f, 0.0f, 0.0f};
+        float T = 1.0f;
+        uint32_t cnt = 0;
+        for (uint32_t i = start; i < end && T > cfg->t_stop; i++) {
+          const uint32_t gid = vals[i];
+          const float dx = px - mean2d[gid * 2], dy = py - mean2d[gid * 2 + 1];
+          const float cxx = cov2d[gid * 3], cxy = cov2d[gid * 3 + 1], cyy = cov2d[gid * 3 + 2];
+          const float det = cxx * cyy - cxy * cxy;
+          if (det <= 0.0f) continue;
+          const float inv_det = 1.0f / det;
+          const float inv_xx = cyy * inv_det, inv_xy = -cxy * inv_det, inv_yy = cxx * inv_det;
+          const float q = dx * dx * inv_xx + 2.0f * dx * dy * inv_xy + dy * dy * inv_yy;
+          const float power = -0.5f * q;
+          if (power > 0.0f) continue;
+          const float alpha = std::fmin(cfg->alpha_max, opacity[gid] * gso_expf(power));
+          if (alpha < cfg->alpha_min) continue;
+          const float w = T * alpha;
+          for (int c = 0; c < 3; c++) {
+            const float term = w * colors[gid * 3 + c];
+            col[c] = col[c] + term;
+          }
+          T *= (1.0f - alpha);
+          cnt++;
+        }
+        const size_t pix = (size_t)y * width + x;
+        for (int c = 0; c < 3; c++) {
+          const float bg = T * cfg->background[c];
+          image[pix * 3 + c] = col[c] + bg;
+        }
+        if (n_contrib) n_contrib[pix] = cnt;
+        if (final_T) final_T[pix] = T;
       }
   }
 }
@@ -1105,12 +1180,36 @@ void gso_densify_apply(const gsc_gaussians* g, const uint8_t* flags, const gsc_g
   }
 }
 
+}  // extern "C"
+
+namespace {
+// Float32#**(Int32) of the reference's Crystal host (adam.cr:129-130): the
+// LLVM powi intrinsic, at run time compiler-rt's __powisf2 -- binary
+// exponentiation in fp32, lowest exponent bit first.
+float powi_f32(float a, int b) {
+  const bool recip = b < 0;
+  float r = 1.0f;
+  for (;;) {
+    if (b & 1) r *= a;
+    b /= 2;
+    if (b == 0) break;
+    a *= a;
+  }
+  return recip ? 1.0f / r : r;
+}
+}  // namespace
+
+extern "C" {
+
+float gso_powi_f32(float a, int32_t b) { return powi_f32(a, b); }
+
 void gso_adam_step(const gsc_adam_group* groups, int32_t ngroups, float beta1, float beta2,
                    float eps, int32_t step, float grad_scale) {
   // Adam#step / update_adam! / apply_weight_decay!, src/optim/adam.cr:86-176.
-  // Bias corrections 1 - beta^t evaluated in double and rounded once.
-  const float bc1 = (float)(1.0 - std::pow((double)beta1, (double)step));
-  const float bc2 = (float)(1.0 - std::pow((double)beta2, (double)step));
+  // Bias corrections 1 - beta^t in fp32, with beta^t as Float32#**(Int32)
+  // evaluates it (adam.cr:129-130; see powi_f32).
+  const float bc1 = 1.0f - powi_f32(beta1, step);
+  const float bc2 = 1.0f - powi_f32(beta2, step);
   for (int gi = 0; gi < ngroups; gi++) {
     const gsc_adam_group& G = groups[gi];
     const float decay = 1.0f - G.lr * G.weight_decay;

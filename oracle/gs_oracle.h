@@ -29,6 +29,9 @@ extern "C" {
  * Taylor polynomial in Horner form with fused multiply-adds, scale by 2^k. */
 float gso_expf(float x);
 
+/* The reference's rasterizer constants (same values as gsc_raster_config_default). */
+void gso_raster_config_default(gsc_raster_config* cfg);
+
 void gso_set_threads(int nthreads);
 
 /* Fused preprocess. Any output may be NULL. */
@@ -62,6 +65,15 @@ void gso_composite_forward(int32_t width, int32_t height, const uint32_t* ranges
                            const gsc_raster_config* cfg, float* image, uint32_t* n_contrib,
                            float* final_T, uint32_t* last);
 
+/* rasterize_tile with the reference's literal expression forms (unfused
+ * power and colour sums); the same arguments as gso_composite_forward
+ * without `last`. */
+void gso_composite_forward_literal(int32_t width, int32_t height, const uint32_t* ranges,
+                                   const uint32_t* vals, const float* mean2d, const float* cov2d,
+                                   const float* opacity, const float* colors,
+                                   const gsc_raster_config* cfg, float* image, uint32_t* n_contrib,
+                                   float* final_T);
+
 /* grad2d [N,9] accumulated (+=). dL_dimage or (image, target, l1_scale). */
 void gso_composite_backward(int32_t width, int32_t height, const uint32_t* ranges,
                             const uint32_t* vals, const float* mean2d, const float* cov2d,
@@ -79,6 +91,8 @@ void gso_preprocess_backward(const gsc_gaussians* g, const gsc_camera* cam,
 void gso_l1_loss_grad(int64_t numel, const float* pred, const float* target, float scale,
                       float* grad, double* loss_sum);
 
+/* beta^b as the reference's Float32#**(Int32) (binary exponentiation in fp32). */
+float gso_powi_f32(float a, int32_t b);
 void gso_adam_step(const gsc_adam_group* groups, int32_t ngroups, float beta1, float beta2,
                    float eps, int32_t step, float grad_scale);
 

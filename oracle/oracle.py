@@ -40,10 +40,33 @@ def lib():
         L = C.CDLL(LIB_PATH)
         L.gso_expf.restype = C.c_float
         L.gso_expf.argtypes = [C.c_float]
+        L.gso_powi_f32.restype = C.c_float
+        L.gso_powi_f32.argtypes = [C.c_float, C.c_int32]
         L.gso_emit_keys.restype = C.c_int64
         L.gso_render_view.restype = C.c_int64
         _lib = L
     return _lib
+
+
+def default_config(mode=_abi.GSC_MODE_FULL, sh_degree=3, background=(0.0, 0.0, 0.0), t_stop=None,
+                   binning=None):
+    """The reference's rasterizer constants from the oracle library (no CUDA
+    library is loaded), with the overrides of the product's default_config."""
+    cfg = _abi.RasterConfig()
+    lib().gso_raster_config_default(C.byref(cfg))
+    if binning is not None:
+        cfg.binning = binning
+    cfg.mode = mode
+    cfg.sh_degree = sh_degree
+    for i in range(3):
+        cfg.background[i] = background[i]
+    if t_stop is not None:
+        cfg.t_stop = t_stop
+    return cfg
+
+
+def powi_f32(a, b):
+    return np.float32(lib().gso_powi_f32(C.c_float(a), int(b)))
 
 
 def set_threads(n):
@@ -140,6 +163,17 @@ def composite_forward(W, H, ranges, vals, pre, cfg):
                                 _p(pre["opacity"]), _p(pre["colors"]), C.byref(cfg), _p(img),
                                 _p(nc), _p(fT), _p(last))
     return img, nc, fT, last
+
+
+def composite_forward_literal(W, H, ranges, vals, pre, cfg):
+    """rasterize_tile with the reference's unfused expression forms."""
+    img = np.zeros((H, W, 3), np.float32)
+    nc = np.zeros((H, W), np.uint32)
+    fT = np.zeros((H, W), np.float32)
+    lib().gso_composite_forward_literal(W, H, _p(ranges), _p(vals), _p(pre["mean2d"]), _p(pre["cov2d"]),
+                                        _p(pre["opacity"]), _p(pre["colors"]), C.byref(cfg), _p(img),
+                                        _p(nc), _p(fT))
+    return img, nc, fT
 
 
 def composite_backward(W, H, ranges, vals, pre, cfg, final_T, last, dL_dimage=None, image=None,

@@ -151,11 +151,40 @@ def test_adam_closed_form_and_float32_order(oracle):
         gr = g * f(0.5)
         m = f(0.9) * m + (f(1) - f(0.9)) * gr
         v = f(0.999) * v + (f(1) - f(0.999)) * gr * gr
-        bc1 = f(1 - np.float64(f(0.9)) ** step)  # beta^t in double from the fp32 beta
-        bc2 = f(1 - np.float64(f(0.999)) ** step)
+        bc1 = f(1) - powi_f32(f(0.9), step)  # beta^t as Float32#**(Int32)
+        bc2 = f(1) - powi_f32(f(0.999), step)
         p = p - f(1e-2) * (m / bc1) / (np.sqrt(v / bc2) + f(1e-8))
         np.testing.assert_array_equal(grp["param"], p)
         np.testing.assert_array_equal(grp["m"], m)
+
+
+def powi_f32(a, b):
+    """Binary exponentiation in float32, lowest exponent bit first: what
+    Float32#**(Int32) runs in the reference's Adam (adam.cr:129-130)."""
+    a, r = np.float32(a), np.float32(1)
+    while True:
+        if b & 1:
+            r = np.float32(r * a)
+        b //= 2
+        if b == 0:
+            return r
+        a = np.float32(a * a)
+
+
+def test_powi_f32_is_the_references_fp32_power(oracle):
+    f = np.float32
+    for beta in (f(0.9), f(0.999)):
+        assert oracle.powi_f32(beta, 1) == beta
+        assert oracle.powi_f32(beta, 2) == f(beta * beta)
+        assert oracle.powi_f32(beta, 3) == f(f(beta) * f(beta * beta))  # r = a, then a^2 * r
+        for t in list(range(1, 200)) + [1000, 4095, 4096, 30000]:
+            got = oracle.powi_f32(beta, t)
+            assert got == powi_f32(beta, t), (beta, t)
+            # each squaring doubles the relative error it inherits, so the
+            # relative error of the fp32 power stays below t * 2^-23
+            exact = np.float64(beta) ** t
+            if exact > 1e-30:
+                assert abs(float(got) / exact - 1.0) <= t * 2.0 ** -23, (beta, t)
 
 
 def test_l1_loss_grad(oracle):
