@@ -124,6 +124,7 @@ _SIGS = {
     "gsc_sort_pairs_u64": (C.c_int, [P, P, P, C.c_int64, C.c_int, C.c_int]),
     "gsc_sort_pairs_u64_static": (C.c_int, [P, P, C.c_int64, C.c_int, C.c_int, P]),
     "gsc_sort_pairs_u64_static_status": (C.c_int, [P]),
+    "gsc_selftest_wait_timeout": (C.c_int, [P, C.c_int32]),
     "gsc_tile_ranges": (C.c_int, [P, P, C.c_int64, C.c_int32, P]),
     "gsc_composite_forward": (C.c_int, [P, P, P, P, C.c_int32, C.c_int32, C.POINTER(RasterConfig),
                                         P, P, P, P]),

@@ -163,6 +163,7 @@ lib GSCuda
   fun destroy = gsc_destroy(ctx : Ctx) : Int32
   fun set_stream = gsc_set_stream(ctx : Ctx, stream : Void*) : Int32
   fun sync = gsc_sync(ctx : Ctx) : Int32
+  fun selftest_wait_timeout = gsc_selftest_wait_timeout(ctx : Ctx, spin_limit : Int32) : Int32
 
   # memory (gs_create_buffer / gs_buffer_*, bridge.mm:131-146)
   fun alloc = gsc_alloc(ctx : Ctx, bytes : LibC::SizeT, out : Void**) : Int32

@@ -181,6 +181,14 @@ GSC_API int gsc_sync(gsc_ctx* ctx) {
   return GSC_OK;
 }
 
+GSC_API int gsc_selftest_wait_timeout(gsc_ctx* ctx, int32_t spin_limit) {
+  GS_REQUIRE(ctx, "gsc_selftest_wait_timeout: null context");
+  GS_REQUIRE(spin_limit >= 1 && spin_limit <= 100000, "gsc_selftest_wait_timeout: spin_limit must be 1..100000");
+  const int rc = scratch_reserve(ctx, 2 * 256 * 4);
+  if (rc != GSC_OK) return rc;
+  return launch_lookback_selftest(ctx, (uint32_t)spin_limit, scratch_base(ctx));
+}
+
 GSC_API int gsc_alloc(gsc_ctx* ctx, size_t bytes, void** out) {
   GS_REQUIRE(ctx && out, "gsc_alloc: null argument");
   *out = nullptr;

@@ -160,6 +160,9 @@ int launch_make_keys_ranges(const uint32_t* ranges, int32_t num_tiles, const uin
 int launch_tile_ranges_u32(const uint32_t* tiles, int64_t n, int32_t num_tiles, uint32_t* ranges,
                            cudaStream_t stream);
 size_t sort_scratch_bytes(int64_t n, int begin_bit, int end_bit);
+// The sort's look-back wait against a predecessor that never publishes (needs
+// 2 KB of zeroable scratch); it gives up after spin_limit re-reads.
+int launch_lookback_selftest(gsc_ctx* ctx, uint32_t spin_limit, char* scratch);
 int launch_sort_pairs(gsc_ctx* ctx, uint64_t* keys, uint32_t* vals, int64_t n, int begin_bit,
                       int end_bit, char* scratch);
 size_t sort_scratch_bytes_u32(int64_t n, int begin_bit, int end_bit);

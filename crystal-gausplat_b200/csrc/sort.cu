@@ -36,6 +36,51 @@ constexpr uint32_t kValMask = (1u << 30) - 1u;
 constexpr uint32_t kSpinLimit = 1u << 21;
 }  // namespace
 
+
+// Decoupled look-back of partition `part` for digit d: walks the earlier
+// partitions' status words back to the nearest inclusive prefix, adding the
+// aggregates on the way. A word still 0 (nothing published) is re-read after
+// a short sleep, at most spin_limit times; then the wait gives up, sets
+// GS_DEVERR_TIMEOUT in *err (read back by gsc_sync) and returns what it has,
+// so the kernel always finishes.
+__device__ __forceinline__ uint32_t lookback_exclusive(const uint32_t* status, int64_t part, uint32_t d,
+                                                       uint32_t spin_limit, uint32_t* err) {
+  uint32_t excl = 0, spins = 0;
+  int64_t j = part - 1;
+  while (j >= 0) {
+    const uint32_t s = *(volatile const uint32_t*)(status + (size_t)j * 256 + d);
+    const uint32_t flag = s & ~kValMask;
+    if (flag == 0) {
+      if (++spins > spin_limit) {
+        atomicOr(err, GS_DEVERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(32);
+      continue;
+    }
+    excl += s & kValMask;
+    if (flag == kFlagInc) break;
+    j--;
+  }
+  return excl;
+}
+
+// The look-back wait on a status array whose partition 0 never publishes:
+// partition 1's wait must give up after spin_limit re-reads (failure-path
+// self-test of gsc_selftest_wait_timeout).
+__global__ void __launch_bounds__(256) lookback_selftest_kernel(const uint32_t* status, uint32_t spin_limit,
+                                                                uint32_t* err) {
+  lookback_exclusive(status, 1, threadIdx.x, spin_limit, err);
+}
+
+int launch_lookback_selftest(gsc_ctx* ctx, uint32_t spin_limit, char* scratch) {
+  GS_CK(cudaMemsetAsync(scratch, 0, 2 * 256 * 4, ctx->stream));
+  lookback_selftest_kernel<<<1, 256, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(scratch), spin_limit,
+                                                      ctx->err);
+  GS_CK_LAUNCH("lookback_selftest_kernel");
+  return GSC_OK;
+}
+
 template <typename K>
 __global__ void __launch_bounds__(256) histogram_kernel(const K* __restrict__ keys, int64_t n,
                                                         int begin_bit, int end_bit, int npass,
@@ -193,23 +238,7 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
     *(volatile uint32_t*)my = kFlagInc | valid_cnt;
   } else {
     *(volatile uint32_t*)my = kFlagAgg | valid_cnt;
-    int64_t j = (int64_t)part - 1;
-    uint32_t spins = 0;
-    while (j >= 0) {
-      const uint32_t s = *(volatile const uint32_t*)(status + (size_t)j * 256 + d);
-      const uint32_t flag = s & ~kValMask;
-      if (flag == 0) {
-        if (++spins > kSpinLimit) {
-          atomicOr(err, GS_DEVERR_TIMEOUT);
-          break;
-        }
-        __nanosleep(32);
-        continue;
-      }
-      excl += s & kValMask;
-      if (flag == kFlagInc) break;
-      j--;
-    }
+    excl = lookback_exclusive(status, part, d, kSpinLimit, err);
     *(volatile uint32_t*)my = kFlagInc | ((excl + valid_cnt) & kValMask);
   }
   s_gbase[d] = gexcl + excl - local_excl;  // global position = s_gbase[d] + tile position

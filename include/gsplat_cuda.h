@@ -189,6 +189,14 @@ GSC_API int gsc_set_stream(gsc_ctx* ctx, void* stream);
 /* Wait for the stream; returns GSC_ERR_TIMEOUT if a device wait gave up. */
 GSC_API int gsc_sync(gsc_ctx* ctx);
 
+/* Failure-path self-test, with no counterpart in the reference: runs the
+ * sort's bounded look-back wait (the only device-side wait on the
+ * single-GPU path) against a predecessor that never publishes, so the wait
+ * gives up after spin_limit (1..100000) re-reads and the kernel finishes;
+ * the next gsc_sync returns GSC_ERR_TIMEOUT and clears the flag, and the
+ * context stays usable. */
+GSC_API int gsc_selftest_wait_timeout(gsc_ctx* ctx, int32_t spin_limit);
+
 /* ---- memory (replaces gs_create_buffer / gs_buffer_* , bridge.mm:131-146) */
 GSC_API int gsc_alloc(gsc_ctx* ctx, size_t bytes, void** out);
 GSC_API int gsc_free(gsc_ctx* ctx, void* ptr);

@@ -389,15 +389,38 @@ int64_t gso_emit_keys(int64_t n, const float* mean2d, const float* depth, const 
 }
 
 void gso_sort_pairs(int64_t n, uint64_t* keys, uint32_t* vals, int begin_bit, int end_bit) {
-  uint64_t mask = (end_bit - begin_bit >= 64) ? ~0ull : (((1ull << (end_bit - begin_bit)) - 1ull));
-  std::vector<int64_t> idx(n);
-  std::iota(idx.begin(), idx.end(), 0);
-  std::stable_sort(idx.begin(), idx.end(), [&](int64_t a, int64_t b) {
-    return ((keys[a] >> begin_bit) & mask) < ((keys[b] >> begin_bit) & mask);
-  });
+  // A stable comparison sort by the key bits [begin_bit, end_bit): the
+  // (masked key, original position) records are ordered lexicographically,
+  // which is the stable order. Chunks are sorted on the OpenMP threads and
+  // merged pairwise (std::merge keeps the left run first on ties, and the
+  // positions make every record distinct anyway).
+  const uint64_t mask = (end_bit - begin_bit >= 64) ? ~0ull : (((1ull << (end_bit - begin_bit)) - 1ull));
+  struct Rec {
+    uint64_t k;
+    int64_t i;
+    bool operator<(const Rec& o) const { return k < o.k || (k == o.k && i < o.i); }
+  };
+  std::vector<Rec> a(n), b(n);
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+  for (int64_t i = 0; i < n; i++) a[i] = Rec{(keys[i] >> begin_bit) & mask, i};
+  int parts = 1;
+  while (parts < g_threads && parts < 64 && (int64_t)parts * 65536 < n) parts *= 2;
+  std::vector<int64_t> cut(parts + 1);
+  for (int p = 0; p <= parts; p++) cut[p] = n * p / parts;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+  for (int p = 0; p < parts; p++) std::sort(a.begin() + cut[p], a.begin() + cut[p + 1]);
+  for (int w = 1; w < parts; w *= 2) {
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int p = 0; p < parts; p += 2 * w) {
+      const int64_t lo = cut[p], mid = cut[std::min(p + w, parts)], hi = cut[std::min(p + 2 * w, parts)];
+      std::merge(a.begin() + lo, a.begin() + mid, a.begin() + mid, a.begin() + hi, b.begin() + lo);
+    }
+    std::swap(a, b);
+  }
   std::vector<uint64_t> k2(n);
   std::vector<uint32_t> v2(n);
-  for (int64_t i = 0; i < n; i++) { k2[i] = keys[idx[i]]; v2[i] = vals[idx[i]]; }
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+  for (int64_t i = 0; i < n; i++) { k2[i] = keys[a[i].i]; v2[i] = vals[a[i].i]; }
   std::memcpy(keys, k2.data(), n * 8);
   std::memcpy(vals, v2.data(), n * 4);
 }
@@ -882,7 +905,9 @@ int64_t gso_contributing_lists(int32_t W, int32_t H, int64_t m, const uint64_t* 
                                const float* opacity, const uint32_t* tiles_touched,
                                float alpha_min, uint64_t* out_keys, uint32_t* out_vals) {
   const int tiles_x = (W + 15) / 16;
-  int64_t k = 0;
+  // keep flags on the OpenMP threads, then an ordered compaction
+  std::vector<uint8_t> keep_flag(m);
+#pragma omp parallel for num_threads(g_threads) schedule(dynamic, 65536)
   for (int64_t i = 0; i < m; i++) {
     const uint32_t id = vals[i];
     const uint32_t tile = (uint32_t)(keys[i] >> 32);
@@ -894,9 +919,13 @@ int64_t gso_contributing_lists(int32_t W, int32_t H, int64_t m, const uint64_t* 
       keep = !row_culled(mean2d[2 * id], mean2d[2 * id + 1], conic[3 * id], conic[3 * id + 1],
                          conic[3 * id + 2], opacity[id], rx0, rx1, ry0, ry1, alpha_min);
     }
-    if (keep) {
+    keep_flag[i] = keep;
+  }
+  int64_t k = 0;
+  for (int64_t i = 0; i < m; i++) {
+    if (keep_flag[i]) {
       out_keys[k] = keys[i];
-      out_vals[k] = id;
+      out_vals[k] = vals[i];
       k++;
     }
   }

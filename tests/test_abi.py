@@ -76,3 +76,8 @@ def test_init_without_a_device_reports_nodevice():
     assert h.value is None
     with pytest.raises(_abi.GscError):
         _abi.check(rc, "gsc_init")
+
+
+def test_selftest_argument_checks():
+    lib = _abi.lib()
+    assert lib.gsc_selftest_wait_timeout(None, 10) == _abi.GSC_ERR_INVALID

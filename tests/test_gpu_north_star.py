@@ -1,0 +1,235 @@
+"""Parity at the benchmark's own configurations (2 and the
+config-3 training path), CUDA path through the C ABI against the CPU oracle.
+
+Bars: bit-exact for sorted keys, values, tile ranges and per-tile lists;
+images within 1e-5 relative (bit-exact in practice: the kernels and the
+oracle share the fp32 operation order, asserted); gradients within 1e-4
+relative (max of the norm-wise error and the element-wise error floored at
+1e-2 of the largest magnitude; float atomics reorder the screen-space sums).
+
+- config 0: 100k Gaussians, one 256x256 camera at (0,0,4): both tile-list
+  kinds, both arithmetic modes, both transmittance stops (the reference's
+  1e-3, gaussian.metal:400, and the north star's 1e-4).
+- config 2: 1M Gaussians, one 1920x1080 camera on the radius-4 sphere, L1
+  against a seeded target: the reference's sorted lists and ranges, the image
+  and all 59 parameter gradients, at both stops.
+- config 3 path: 3M Gaussians at 1920x1080, three views through the
+  benchmark's own training path (DataParallelTrainer: one batched forward with
+  contributing-pairs lists and batched depth words, deferred compositing
+  backwards, one batched preprocess backward). Per view the lists equal the
+  oracle's contributing lists and are an order-preserving subset of the
+  reference's sorted lists; images, contributor counts and final
+  transmittance equal the oracle's over the reference lists; the summed
+  gradients of the three views are within 1e-4.
+"""
+import importlib
+import os
+
+import numpy as np
+import pytest
+
+from helpers import R, _abi, gs, host, rel_err, to_dev
+
+pytestmark = pytest.mark.gpu
+
+GRAD_RTOL = 1e-4
+IMG_RTOL = 1e-5
+C0_SEED = 0x6A5D0000
+C2_SEED = 0x6A5D0002
+C3_SEED = 0x6A5D0003
+
+
+def grad_close(a, b):
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    nb = float(np.linalg.norm(b))
+    if nb == 0.0:
+        return float(np.abs(a).max()) if a.size else 0.0
+    return max(float(np.linalg.norm(a - b)) / nb,
+               float(np.max(np.abs(a - b) / (np.abs(b) + 1e-2 * float(np.abs(b).max())))))
+
+
+@pytest.fixture
+def par_oracle(oracle):
+    """The oracle on every host thread for the large cases."""
+    oracle.set_threads(os.cpu_count() or 1)
+    yield oracle
+    oracle.set_threads(1)
+
+
+def sphere_camera(seed, W, H, k=0, views=1):
+    eyes = gs.sphere_poses(views, 4.0, seed + 101)
+    return gs.make_camera(W, H, tuple(eyes[k]))
+
+
+def target_of(seed, v, H, W):
+    return np.random.default_rng(seed * 1000 + v).random((H, W, 3), dtype=np.float32)
+
+
+def check_forward(ctx, img, ref, W, H):
+    assert ctx.num_rendered == ref["sorted_keys"].size
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
+    im = host(img)
+    assert rel_err(im, ref["image"], 1e-6) <= IMG_RTOL
+    np.testing.assert_array_equal(im, ref["image"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_N_CONTRIB, np.uint32).reshape(H, W), ref["n_contrib"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_FINAL_T, np.float32).reshape(H, W), ref["final_T"])
+    np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_LAST, np.uint32).reshape(H, W), ref["last"])
+
+
+def check_backward(o, sc, cs, cfg, ref, grads, loss, target, W, H):
+    scale = 1.0 / target.size
+    g2d, rloss = o.composite_backward(W, H, ref["ranges"], ref["sorted_vals"], ref["pre"], cfg,
+                                      ref["final_T"], ref["last"], image=ref["image"], target=target,
+                                      l1_scale=scale)
+    rg, views = o.preprocess_backward(sc, cs, cfg, g2d)
+    assert abs(float(loss.item()) - rloss) <= 1e-5 * abs(rloss)
+    pairs = {"mean2d": (grads.dL_dmean2d, views["mean2d"]), "opacity": (grads.dL_dopacity, views["opacity"]),
+             "colors": (grads.dL_dcolors, views["colors"]), "cov2d": (grads.dL_dcov2d, views["cov2d"]),
+             "position": (grads.dL_dposition, rg["position"]), "log_scale": (grads.dL_dlog_scale, rg["log_scale"]),
+             "rotation": (grads.dL_drotation, rg["rotation"]),
+             "logit": (grads.dL_dlogit_opacity, rg["logit_opacity"]), "sh": (grads.dL_dsh, rg["sh_coeffs"])}
+    for name, (a, b) in pairs.items():
+        if cfg.mode == _abi.GSC_MODE_REF and name == "cov2d":
+            continue  # the reference never writes it (zero on both sides)
+        e = grad_close(host(a), b)
+        assert e <= GRAD_RTOL, f"{name}: {e}"
+
+
+# ---- config 0 ------------------------------------------------------------------
+
+@pytest.mark.parametrize("t_stop", [1e-3, 1e-4], ids=["T1e-3", "T1e-4"])
+@pytest.mark.parametrize("binning", [_abi.GSC_BIN_REFERENCE, _abi.GSC_BIN_CONTRIBUTING],
+                         ids=["reference_lists", "contributing_lists"])
+@pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF], ids=["full", "ref"])
+def test_c0_forward_backward(cuda, par_oracle, mode, binning, t_stop):
+    W = H = 256
+    arrays = gs.synthetic_arrays(100_000, C0_SEED)
+    g = gs.Gaussian3D(arrays)
+    cam = gs.make_camera(W, H, (0.0, 0.0, 4.0))
+    cfg = gs.default_config(mode=mode, binning=binning, t_stop=t_stop)
+    img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+    target = target_of(C0_SEED, 0, H, W)
+    loss = cuda.zeros(1, device="cuda")
+    grads = gs.Rasterizer.backward(None, g, cam, ctx, target=to_dev(target), loss_sum=loss)
+    R.sync()
+    sc = par_oracle.Scene(arrays)
+    cs = cam.to_struct()
+    ref = par_oracle.forward_pipeline(sc, cs, cfg)
+    assert ref["sorted_keys"].size > 100_000
+    check_forward(ctx, img, ref, W, H)
+    check_backward(par_oracle, sc, cs, cfg, ref, grads, loss, target, W, H)
+
+
+# ---- config 2 ------------------------------------------------------------------
+
+@pytest.mark.parametrize("t_stop", [1e-3, 1e-4], ids=["T1e-3", "T1e-4"])
+def test_c2_single_view_forward_backward(cuda, par_oracle, t_stop):
+    W, H = 1920, 1080
+    arrays = gs.synthetic_arrays(1_000_000, C2_SEED)
+    g = gs.Gaussian3D(arrays)
+    cam = sphere_camera(C2_SEED, W, H)
+    cfg = gs.default_config(binning=_abi.GSC_BIN_REFERENCE, t_stop=t_stop)
+    img, ctx = gs.Rasterizer.forward(g, cam, config=cfg)
+    target = target_of(C2_SEED, 0, H, W)
+    loss = cuda.zeros(1, device="cuda")
+    grads = gs.Rasterizer.backward(None, g, cam, ctx, target=to_dev(target), loss_sum=loss)
+    R.sync()
+    sc = par_oracle.Scene(arrays)
+    cs = cam.to_struct()
+    ref = par_oracle.forward_pipeline(sc, cs, cfg)
+    assert ref["sorted_keys"].size > 5_000_000
+    check_forward(ctx, img, ref, W, H)
+    check_backward(par_oracle, sc, cs, cfg, ref, grads, loss, target, W, H)
+
+
+# ---- config 3 training path ------------------------------------------------------
+
+def test_c3_training_path_three_views(cuda, par_oracle):
+    O = par_oracle
+    trainer_mod = importlib.import_module("crystal-gausplat_b200.trainer")
+    W, H, views = 1920, 1080, 3
+    arrays = gs.synthetic_arrays(3_000_000, C3_SEED)
+    g = gs.Gaussian3D(arrays)
+    eyes = gs.sphere_poses(64, 4.0, C3_SEED + 101)[:views]  # the benchmark's first three poses
+    cams = [gs.make_camera(W, H, tuple(e)) for e in eyes]
+    cfg = gs.default_config()  # contributing-pairs lists, as the benchmark
+    assert cfg.binning == _abi.GSC_BIN_CONTRIBUTING
+    tr = trainer_mod.DataParallelTrainer(g, cams, cfg)
+    targets = [target_of(C3_SEED, v, H, W) for v in range(views)]
+    dev_t = [to_dev(t) for t in targets]
+    tr.zero()
+    for v in range(views):
+        tr.view_fwd_bwd(v, dev_t[v])
+    tr.flush()
+    R.sync()
+    got = {v: {"keys": tr.ctxs[v].get(_abi.GSC_FRAME_KEYS, np.uint64),
+               "vals": tr.ctxs[v].get(_abi.GSC_FRAME_VALUES, np.uint32),
+               "ranges": tr.ctxs[v].get(_abi.GSC_FRAME_RANGES, np.uint32),
+               "n_contrib": tr.ctxs[v].get(_abi.GSC_FRAME_N_CONTRIB, np.uint32).reshape(H, W),
+               "final_T": tr.ctxs[v].get(_abi.GSC_FRAME_FINAL_T, np.float32).reshape(H, W),
+               "image": host(tr.images[v])} for v in range(views)}
+    gpu_grads = host(tr.grads.arena).copy()
+    gpu_loss = float(tr.loss.item())
+    del tr
+
+    sc = O.Scene(arrays)
+    ref_cfg = O.default_config(binning=_abi.GSC_BIN_REFERENCE)
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    end_bit = 32 + int(np.ceil(np.log2(tx * ty)))
+    ref_grads = None
+    ref_loss = 0.0
+    for v in range(views):
+        cs = cams[v].to_struct()
+        pre = O.preprocess(sc, cs, ref_cfg)
+        keys, vals = O.emit_keys(pre, tx, ty)
+        sk, sv = O.sort_pairs(keys, vals, 0, end_bit)
+        del keys, vals
+        ck, cv = O.contributing_lists(W, H, sk, sv, pre, ref_cfg.alpha_min)
+        # the GPU's lists are the oracle's contributing lists, bit for bit
+        np.testing.assert_array_equal(got[v]["keys"], ck)
+        np.testing.assert_array_equal(got[v]["vals"], cv)
+        np.testing.assert_array_equal(got[v]["ranges"], O.tile_ranges(ck, tx * ty))
+        # ... which are an order-preserving subset of the reference's sorted lists
+        assert ck.size < sk.size
+        # (tile, id) pairs are unique: locate each contributing pair in the
+        # reference list; the positions must rise (order preserved)
+        pr = (sk >> np.uint64(32) << np.uint64(32)) | sv.astype(np.uint64)
+        pc = (ck >> np.uint64(32) << np.uint64(32)) | cv.astype(np.uint64)
+        o = np.argsort(pr, kind="stable")
+        pos = o[np.searchsorted(pr[o], pc)]
+        np.testing.assert_array_equal(pr[pos], pc)
+        assert np.all(np.diff(pos) > 0)
+        np.testing.assert_array_equal(sk[pos], ck)
+        del pr, pc, o, pos
+        # the image over the reference lists equals the GPU's over the contributing lists
+        ranges = O.tile_ranges(sk, tx * ty)
+        img, nc, fT, last = O.composite_forward(W, H, ranges, sv, pre, ref_cfg)
+        np.testing.assert_array_equal(got[v]["image"], img)
+        np.testing.assert_array_equal(got[v]["n_contrib"], nc)
+        np.testing.assert_array_equal(got[v]["final_T"], fT)
+        g2d, lv = O.composite_backward(W, H, ranges, sv, pre, ref_cfg, fT, last, image=img,
+                                       target=targets[v], l1_scale=1.0 / targets[v].size)
+        ref_loss += lv
+        rg, _ = O.preprocess_backward(sc, cs, ref_cfg, g2d)
+        flat = np.concatenate([rg[k].reshape(-1).astype(np.float64)
+                               for k in ("position", "log_scale", "rotation", "logit_opacity", "sh_coeffs")])
+        ref_grads = flat if ref_grads is None else ref_grads + flat
+        del sk, sv, ck, cv, g2d, rg
+    assert abs(gpu_loss - ref_loss) <= 1e-5 * abs(ref_loss)
+    # the arena holds the five gradient fields in the same order, each block
+    # padded to a 16-byte boundary
+    n = 3_000_000
+    parts = []
+    gsmod = importlib.import_module("crystal-gausplat_b200.gaussian")
+    offs, _ = gsmod.field_offsets(n)
+    for name, w in gsmod.FIELDS:
+        parts.append(gpu_grads[offs[name]: offs[name] + n * w].astype(np.float64))
+    got_flat = np.concatenate(parts)
+    start = 0
+    for name, w in gsmod.FIELDS:
+        e = grad_close(got_flat[start: start + n * w], ref_grads[start: start + n * w])
+        assert e <= GRAD_RTOL, f"{name}: {e}"
+        start += n * w

@@ -243,3 +243,22 @@ def test_oracle_contributing_lists_adversarial(oracle):
     assert con["sorted_keys"].size < ref["sorted_keys"].size
     for k in ("image", "n_contrib", "final_T"):
         np.testing.assert_array_equal(con[k], ref[k], err_msg=k)
+
+
+@pytest.mark.parametrize("n,begin,end", [(1, 0, 64), (1000, 0, 64), (300_001, 0, 45), (1 << 20, 8, 40)])
+def test_oracle_sort_is_numpys_stable_sort(oracle, n, begin, end):
+    """The oracle's pair sort (parallel chunks + stable merges) against
+    numpy's stable argsort of the same key bits, duplicates included."""
+    rng = np.random.default_rng(n)
+    keys = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, n, dtype=np.uint64)
+    keys[: n // 3] = keys[n // 3: 2 * (n // 3)]
+    vals = np.arange(n, dtype=np.uint32)
+    oracle.set_threads(8)
+    try:
+        k, v = oracle.sort_pairs(keys, vals, begin, end)
+    finally:
+        oracle.set_threads(1)
+    sel = (keys >> np.uint64(begin)) & np.uint64((1 << (end - begin)) - 1 if end - begin < 64 else 2**64 - 1)
+    order = np.argsort(sel, kind="stable")
+    np.testing.assert_array_equal(v, vals[order])
+    np.testing.assert_array_equal(k, keys[order])
