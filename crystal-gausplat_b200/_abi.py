@@ -102,6 +102,11 @@ class DpAdamArgs(C.Structure):
                 ("grad_scale", C.c_float)]
 
 
+class DpBarrierArgs(C.Structure):
+    _fields_ = [("nranks", C.c_int32), ("rank", C.c_int32), ("peer_flags", P * 8),
+                ("epoch", C.c_uint32), ("timeout_us", C.c_int32)]
+
+
 assert C.sizeof(Camera) == 176, C.sizeof(Camera)
 
 _SIGS = {
@@ -137,6 +142,7 @@ _SIGS = {
     "gsc_adam_step": (C.c_int, [P, C.POINTER(AdamGroup), C.c_int32, C.c_float, C.c_float,
                                 C.c_float, C.c_int32, C.c_float]),
     "gsc_dp_adam_step": (C.c_int, [P, C.POINTER(DpAdamArgs)]),
+    "gsc_dp_barrier": (C.c_int, [P, C.POINTER(DpBarrierArgs)]),
     "gsc_ssim_loss_grad": (C.c_int, [P, P, P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                      P, P, P]),
     "gsc_combined_loss_grad": (C.c_int, [P, P, P, C.c_int32, C.c_int32, C.c_int32, C.c_float,

@@ -144,6 +144,14 @@ lib GSCuda
     grad_scale : Float32
   end
 
+  struct DpBarrierArgs
+    nranks : Int32
+    rank : Int32
+    peer_flags : StaticArray(UInt32*, 8)
+    epoch : UInt32
+    timeout_us : Int32
+  end
+
   struct GaussiansOut
     position : Float32*
     log_scale : Float32*
@@ -206,6 +214,7 @@ lib GSCuda
                                 beta2 : Float32, eps : Float32, step : Int32,
                                 grad_scale : Float32) : Int32
   fun dp_adam_step = gsc_dp_adam_step(ctx : Ctx, args : DpAdamArgs*) : Int32
+  fun dp_barrier = gsc_dp_barrier(ctx : Ctx, args : DpBarrierArgs*) : Int32
 
   # losses (loss.cr:59-296)
   fun ssim_loss_grad = gsc_ssim_loss_grad(ctx : Ctx, pred : Float32*, target : Float32*,

@@ -17,6 +17,13 @@
 
 namespace gs {
 
+struct DpBarrierDev {
+  int nranks, rank;
+  uint32_t* flags[GSC_DP_MAX_RANKS];
+  uint32_t epoch;
+  uint64_t timeout_ns;
+};
+
 struct DpArgsDev {
   int nranks, rank;
   float* peer_grads[GSC_DP_MAX_RANKS];
@@ -30,6 +37,7 @@ struct DpArgsDev {
   float lr[8], weight_decay[8], decay[8];
   float beta1, beta2, eps, bc1, bc2, grad_scale;
   int64_t chunk_lo, chunk_hi;  // this rank's shard
+  const uint32_t* err;         // the context's error word: skip all work after a failed barrier
 };
 
 __device__ __forceinline__ float dp_adam(float p, float g, float& m, float& v, const DpArgsDev& a, int gi) {
@@ -45,6 +53,9 @@ __device__ __forceinline__ float dp_adam(float p, float g, float& m, float& v, c
 __global__ void __launch_bounds__(256) dp_adam_kernel(DpArgsDev a) {
   const int64_t chunk = a.chunk_lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (chunk >= a.chunk_hi) return;
+  // a cross-rank barrier before this launch gave up: the peers' gradients
+  // may be incomplete, so touch no peer memory (the host reads the error)
+  if (*(volatile const uint32_t*)a.err & GS_DEVERR_TIMEOUT) return;
   int gi = 0;
   while (chunk >= a.chunk_end[gi]) gi++;
   const int64_t first = (chunk - (gi ? a.chunk_end[gi - 1] : 0)) * 4;
@@ -79,9 +90,62 @@ __global__ void __launch_bounds__(256) dp_adam_kernel(DpArgsDev a) {
   }
 }
 
+// Cross-rank barrier over peer-addressable flag arrays: rank r stores
+// `epoch` into slot r of every peer's array (release, system scope, after a
+// system fence so that this rank's earlier writes -- its gradients, or the
+// parameter shards it stored into the peers -- are visible first), then waits
+// until every peer's slot of its own array has reached `epoch` (acquire). The
+// wait is bounded by timeout_ns of the GPU's global timer; on expiry the
+// kernel sets GS_DEVERR_TIMEOUT in the context's error word and returns.
+__global__ void dp_barrier_kernel(DpBarrierDev b, uint32_t* err) {
+  const int p = threadIdx.x;
+  if (p >= b.nranks || p == b.rank) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(b.flags[p] + b.rank), "r"(b.epoch) : "memory");
+  const uint32_t* mine = b.flags[b.rank] + p;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if ((int32_t)(v - b.epoch) >= 0) return;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > b.timeout_ns) {
+      atomicOr(err, GS_DEVERR_TIMEOUT);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 }  // namespace gs
 
 using namespace gs;
+
+extern "C" GSC_API int gsc_dp_barrier(gsc_ctx* ctx, const gsc_dp_barrier_args* in) {
+  GS_REQUIRE(ctx && in, "gsc_dp_barrier: null argument");
+  GS_REQUIRE(in->nranks >= 1 && in->nranks <= GSC_DP_MAX_RANKS && in->rank >= 0 && in->rank < in->nranks,
+             "gsc_dp_barrier: bad nranks/rank");
+  GS_REQUIRE(in->timeout_us >= 1 && in->timeout_us <= 600000000, "gsc_dp_barrier: timeout_us must be 1 us .. 600 s");
+  if (in->nranks == 1) return GSC_OK;
+  DpBarrierDev b;
+  std::memset(&b, 0, sizeof b);
+  b.nranks = in->nranks;
+  b.rank = in->rank;
+  for (int p = 0; p < in->nranks; p++) {
+    GS_REQUIRE(in->peer_flags[p] && ((uintptr_t)in->peer_flags[p] & 3u) == 0,
+               "gsc_dp_barrier: null or misaligned flag array");
+    b.flags[p] = in->peer_flags[p];
+  }
+  b.epoch = in->epoch;
+  b.timeout_ns = (uint64_t)in->timeout_us * 1000ull;
+  StageScope sc(ctx, GSC_STAGE_ADAM);  // part of the exchange + optimiser step
+  sc.kernels(1);
+  dp_barrier_kernel<<<1, 32, 0, ctx->stream>>>(b, ctx->err);
+  GS_CK_LAUNCH("dp_barrier_kernel");
+  return GSC_OK;
+}
 
 extern "C" GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* in) {
   GS_REQUIRE(ctx && in, "gsc_dp_adam_step: null argument");
@@ -123,6 +187,7 @@ extern "C" GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* in
   a.bc2 = 1.0f - powi_f32(in->beta2, in->step);
   a.chunk_lo = run * in->rank / in->nranks;
   a.chunk_hi = run * (in->rank + 1) / in->nranks;
+  a.err = ctx->err;
   const int64_t n = a.chunk_hi - a.chunk_lo;
   if (n <= 0) return GSC_OK;
   StageScope sc(ctx, GSC_STAGE_ADAM);

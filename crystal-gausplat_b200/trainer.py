@@ -54,7 +54,8 @@ class DataParallelTrainer:
     the rendered image by gsc_combined_loss_grad and fed back as dL/dimage."""
 
     def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl",
-                 loss="l1", lambda_ssim=0.2, batch_views=_abi.GSC_MAX_BATCH_VIEWS):
+                 loss="l1", lambda_ssim=0.2, batch_views=_abi.GSC_MAX_BATCH_VIEWS,
+                 barrier_timeout_s=60.0):
         self.g = gaussians
         self.cameras = cameras
         self.cfg = config
@@ -70,6 +71,7 @@ class DataParallelTrainer:
             grad_arena, self.hdl_grads = _symmetric_copy(torch.zeros_like(arena), process_group)
         self.grads = RasterizerGradients(gaussians, arena=grad_arena, screen=False)
         self.opt = Adam.for_gaussians(gaussians, self.grads, lrs)
+        self.barrier_timeout_s = barrier_timeout_s
         if self.exchange == "fused":
             self._setup_fused()
         # batch_views > 1: compositing backward per view, then one preprocess
@@ -168,6 +170,29 @@ class DataParallelTrainer:
         a.beta1, a.beta2, a.eps = self.opt.beta1, self.opt.beta2, self.opt.eps
         a.grad_scale = 1.0 / len(self.cameras)
         self.dp_args = a
+        # bounded cross-rank barrier (gsc_dp_barrier) over one flag word per
+        # rank in symmetric memory; every barrier call uses the next epoch
+        self.flags, self.hdl_flags = _symmetric_copy(
+            torch.zeros(self.world, dtype=torch.int32, device=g.arena.device), self.pg)
+        b = _abi.DpBarrierArgs()
+        b.nranks, b.rank = self.world, self.rank
+        for p, fp in enumerate(_peer_ptrs(self.flags, self.hdl_flags)):
+            b.peer_flags[p] = fp
+        b.timeout_us = int(self.barrier_timeout_s * 1e6)
+        self.barrier_args = b
+        self.epoch = 0
+        self.hdl_flags.barrier(channel=0)  # every rank's zeroed flags exist before the first signal
+
+    def _barrier(self):
+        self.epoch += 1
+        self.barrier_args.epoch = self.epoch
+        check(lib().gsc_dp_barrier(context(self.g.arena.device), C.byref(self.barrier_args)),
+              "gsc_dp_barrier")
+
+    def check(self):
+        """Wait for the queued work and raise GscError if a cross-rank wait
+        gave up (a peer that never arrived) or a device check failed."""
+        check(lib().gsc_sync(context(self.g.arena.device)), "gsc_sync")
 
     def reduce_and_step(self):
         self.flush()
@@ -175,10 +200,10 @@ class DataParallelTrainer:
             torch.distributed.all_reduce(self.loss, group=self.pg)
             self.opt.step_count += 1
             self.dp_args.step = self.opt.step_count
-            self.hdl_grads.barrier(channel=0)   # every rank's gradients are complete
+            self._barrier()  # every rank's gradients are complete
             check(lib().gsc_dp_adam_step(context(self.g.arena.device), C.byref(self.dp_args)),
                   "gsc_dp_adam_step")
-            self.hdl_params.barrier(channel=1)  # every shard's parameters have landed
+            self._barrier()  # every shard's parameters have landed
             return
         if self.world > 1:
             torch.distributed.all_reduce(self.grads.arena, group=self.pg)

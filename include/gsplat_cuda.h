@@ -329,6 +329,26 @@ typedef struct gsc_dp_adam_args {
 } gsc_dp_adam_args;
 GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* args);
 
+/* Cross-rank barrier for the fused exchange (no reference counterpart; it
+ * replaces an unbounded device barrier). peer_flags[p] is rank p's array of
+ * nranks uint32 words in peer-addressable memory (CUDA IPC or symmetric
+ * memory), zero-initialised once. Rank `rank` publishes `epoch` into slot
+ * `rank` of every peer's array after a system-scope fence (its earlier writes
+ * become visible to the peers first), then waits until every peer's slot of
+ * its own array has reached `epoch`. Every rank passes the same epoch, one
+ * greater on each call. The wait is bounded by timeout_us (1 .. 600e6): on
+ * expiry the kernel sets the context's timeout flag and returns, a
+ * following gsc_dp_adam_step skips its work (no peer memory is touched), and
+ * gsc_sync returns GSC_ERR_TIMEOUT. nranks == 1 is a no-op. */
+typedef struct gsc_dp_barrier_args {
+  int32_t nranks;
+  int32_t rank;
+  uint32_t* peer_flags[GSC_DP_MAX_RANKS];
+  uint32_t epoch;
+  int32_t timeout_us;
+} gsc_dp_barrier_args;
+GSC_API int gsc_dp_barrier(gsc_ctx* ctx, const gsc_dp_barrier_args* args);
+
 /* ---- losses beyond L1 (src/ops/loss.cr:59-249) --------------------------
  * Images are [height, width, channels] fp32 row-major, 1 <= channels <= 4.
  * `out` is a DEVICE array of 3 floats: {loss, mean |pred - target|, SSIM}.

@@ -31,6 +31,7 @@ const float SH_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.45704579946
 const int TILE = 16;  // gaussian.metal:31
 
 int g_threads = 1;
+int g_exact_sums = 1;  // screen-space gradient sums in double (see gso_composite_backward)
 
 inline float bits_to_float(uint32_t u) {
   float f;
@@ -306,6 +307,7 @@ float gso_expf(float x) {
 }
 
 void gso_set_threads(int nthreads) { g_threads = nthreads < 1 ? 1 : nthreads; }
+void gso_set_exact_sums(int on) { g_exact_sums = on ? 1 : 0; }
 
 void gso_preprocess(const gsc_gaussians* g, const gsc_camera* cam, const gsc_raster_config* cfg,
                     float* mean2d, float* cov2d, float* conic, float* depth, float* radius,
@@ -582,6 +584,17 @@ void gso_composite_backward(int32_t width, int32_t height, const uint32_t* range
                             double* loss_sum) {
   const int tiles_x = (width + TILE - 1) / TILE, tiles_y = (height + TILE - 1) / TILE;
   const bool full = cfg->mode == GSC_MODE_FULL;
+  // The per-pixel terms are fp32 (the reference's per-thread arithmetic).
+  // By default (gso_set_exact_sums(1)) their sum per Gaussian and field is
+  // accumulated in double and rounded once: the exact sum of those terms,
+  // independent of the order in which threads add. With 0 they are added in
+  // fp32 as they come, like the reference's fp32 atomics in an unspecified
+  // order (gaussian.metal:503-566); that spread of fp32 summation orders is
+  // what the parity tests compare the kernels' own spread with.
+  int64_t n_gauss = 0;
+  for (int t = 0; g_exact_sums && t < tiles_x * tiles_y; t++)
+    for (uint32_t i = ranges[t * 2]; i < ranges[t * 2 + 1]; i++) n_gauss = std::max<int64_t>(n_gauss, vals[i] + 1);
+  std::vector<double> acc2d((size_t)n_gauss * 9, 0.0);
   double loss = 0.0;
 #pragma omp parallel for num_threads(g_threads) schedule(dynamic, 4) reduction(+ : loss)
   for (int t = 0; t < tiles_x * tiles_y; t++) {
@@ -639,10 +652,18 @@ void gso_composite_backward(int32_t width, int32_t height, const uint32_t* range
             vals9[3] = dL_dpower * (-e.dx * e.dy);
             vals9[4] = dL_dpower * (-0.5f * e.dy * e.dy);
           }
-          float* gd = grad2d + (size_t)gid * 9;
-          for (int k = 0; k < 9; k++) {
+          if (g_exact_sums) {
+            double* gd = acc2d.data() + (size_t)gid * 9;
+            for (int k = 0; k < 9; k++) {
 #pragma omp atomic
-            gd[k] += vals9[k];
+              gd[k] += (double)vals9[k];
+            }
+          } else {
+            float* gf = grad2d + (size_t)gid * 9;
+            for (int k = 0; k < 9; k++) {
+#pragma omp atomic
+              gf[k] += vals9[k];
+            }
           }
           T = T_before;
           for (int k = 0; k < 3; k++) {
@@ -652,6 +673,7 @@ void gso_composite_backward(int32_t width, int32_t height, const uint32_t* range
         }
       }
   }
+  for (size_t i = 0; i < acc2d.size(); i++) grad2d[i] += (float)acc2d[i];
   if (loss_sum) *loss_sum += loss;
 }
 

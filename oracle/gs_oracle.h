@@ -33,6 +33,9 @@ float gso_expf(float x);
 void gso_raster_config_default(gsc_raster_config* cfg);
 
 void gso_set_threads(int nthreads);
+/* 1 (default): composite-backward sums accumulated in double, rounded once;
+ * 0: added in fp32 as they come (the reference's atomics, some order). */
+void gso_set_exact_sums(int on);
 
 /* Fused preprocess. Any output may be NULL. */
 void gso_preprocess(const gsc_gaussians* g, const gsc_camera* cam, const gsc_raster_config* cfg,

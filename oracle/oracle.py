@@ -73,6 +73,11 @@ def set_threads(n):
     lib().gso_set_threads(int(n))
 
 
+def set_exact_sums(on):
+    """Composite-backward sums in double (default) or in fp32 as they come."""
+    lib().gso_set_exact_sums(1 if on else 0)
+
+
 def _p(a):
     return None if a is None else a.ctypes.data_as(P)
 

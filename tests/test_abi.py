@@ -81,3 +81,10 @@ def test_init_without_a_device_reports_nodevice():
 def test_selftest_argument_checks():
     lib = _abi.lib()
     assert lib.gsc_selftest_wait_timeout(None, 10) == _abi.GSC_ERR_INVALID
+
+
+def test_dp_barrier_argument_checks():
+    lib = _abi.lib()
+    b = _abi.DpBarrierArgs()
+    b.nranks, b.rank, b.timeout_us = 2, 0, 0
+    assert lib.gsc_dp_barrier(None, C.byref(b)) == _abi.GSC_ERR_INVALID

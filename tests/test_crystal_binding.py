@@ -19,7 +19,8 @@ SCALARS = {"int": "Int32", "int32_t": "Int32", "int64_t": "Int64", "uint64_t": "
 STRUCTS = {"gsc_camera": "Camera", "gsc_raster_config": "RasterConfig", "gsc_gaussians": "Gaussians",
            "gsc_gaussian_grads": "GaussianGrads", "gsc_projected": "Projected",
            "gsc_grads2d": "Grads2D", "gsc_adam_group": "AdamGroup",
-           "gsc_dp_adam_args": "DpAdamArgs", "gsc_gaussians_out": "GaussiansOut"}
+           "gsc_dp_adam_args": "DpAdamArgs", "gsc_gaussians_out": "GaussiansOut",
+           "gsc_dp_barrier_args": "DpBarrierArgs"}
 OPAQUE = {"gsc_ctx": "Ctx", "gsc_frame": "Frame"}  # Crystal `type X = Void*`
 
 

@@ -3,9 +3,10 @@ config-3 training path), CUDA path through the C ABI against the CPU oracle.
 
 Bars: bit-exact for sorted keys, values, tile ranges and per-tile lists;
 images within 1e-5 relative (bit-exact in practice: the kernels and the
-oracle share the fp32 operation order, asserted); gradients within 1e-4
-relative (max of the norm-wise error and the element-wise error floored at
-1e-2 of the largest magnitude; float atomics reorder the screen-space sums).
+oracle share the fp32 operation order, asserted); gradients against the
+oracle with exact (double) per-Gaussian sums: norm-wise relative error
+<= 1e-4 per tensor, element-wise within 1e-4 or within 3x the spread of
+fp32 summation orders (see `gate`).
 
 - config 0: 100k Gaussians, one 256x256 camera at (0,0,4): both tile-list
   kinds, both arithmetic modes, both transmittance stops (the reference's
@@ -39,16 +40,6 @@ C2_SEED = 0x6A5D0002
 C3_SEED = 0x6A5D0003
 
 
-def grad_close(a, b):
-    a = np.asarray(a, np.float64).reshape(-1)
-    b = np.asarray(b, np.float64).reshape(-1)
-    nb = float(np.linalg.norm(b))
-    if nb == 0.0:
-        return float(np.abs(a).max()) if a.size else 0.0
-    return max(float(np.linalg.norm(a - b)) / nb,
-               float(np.max(np.abs(a - b) / (np.abs(b) + 1e-2 * float(np.abs(b).max())))))
-
-
 @pytest.fixture
 def par_oracle(oracle):
     """The oracle on every host thread for the large cases."""
@@ -79,23 +70,62 @@ def check_forward(ctx, img, ref, W, H):
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_LAST, np.uint32).reshape(H, W), ref["last"])
 
 
-def check_backward(o, sc, cs, cfg, ref, grads, loss, target, W, H):
-    scale = 1.0 / target.size
-    g2d, rloss = o.composite_backward(W, H, ref["ranges"], ref["sorted_vals"], ref["pre"], cfg,
-                                      ref["final_T"], ref["last"], image=ref["image"], target=target,
-                                      l1_scale=scale)
+def oracle_backward(o, sc, cs, cfg, ref, target, W, H, exact=True):
+    """The oracle's screen-space and parameter gradients of one view; exact:
+    per-Gaussian sums in double (default), else fp32 in thread order."""
+    o.set_exact_sums(exact)
+    try:
+        g2d, rloss = o.composite_backward(W, H, ref["ranges"], ref["sorted_vals"], ref["pre"], cfg,
+                                          ref["final_T"], ref["last"], image=ref["image"], target=target,
+                                          l1_scale=1.0 / target.size)
+    finally:
+        o.set_exact_sums(True)
     rg, views = o.preprocess_backward(sc, cs, cfg, g2d)
+    out = {k: v for k, v in rg.items()}
+    out.update({"v_" + k: v for k, v in views.items()})
+    return out, rloss
+
+
+def elem_err(a, b):
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    if not b.size or not np.abs(b).max():
+        return float(np.abs(a).max()) if a.size else 0.0
+    return float(np.max(np.abs(a - b) / (np.abs(b) + 1e-2 * float(np.abs(b).max()))))
+
+
+def norm_err(a, b):
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    nb = float(np.linalg.norm(b))
+    return float(np.linalg.norm(a - b)) / nb if nb else float(np.abs(a).max() if a.size else 0.0)
+
+
+def gate(name, got, exact, fp32):
+    """Gradient gate against the exact-sum oracle: norm-wise relative error
+    <= 1e-4 (the north star's bar), and element-wise (floored at 1e-2 of the
+    largest magnitude) <= 1e-4 or, where fp32 summation itself spreads more
+    (ill-conditioned elements: the rotation and scale gradients of nearly
+    isotropic Gaussians, whose terms cancel), <= 3x the spread of the oracle's
+    own fp32 sums (the reference adds with fp32 atomics in an unspecified
+    order, so its results carry that spread from run to run)."""
+    ne = norm_err(got, exact)
+    assert ne <= GRAD_RTOL, f"{name}: norm-wise {ne:.3e}"
+    ee, spread = elem_err(got, exact), elem_err(fp32, exact)
+    assert ee <= max(GRAD_RTOL, 3.0 * spread), f"{name}: element-wise {ee:.3e}, fp32 spread {spread:.3e}"
+
+
+def check_backward(o, sc, cs, cfg, ref, grads, loss, target, W, H):
+    exact, rloss = oracle_backward(o, sc, cs, cfg, ref, target, W, H, exact=True)
+    fp32, _ = oracle_backward(o, sc, cs, cfg, ref, target, W, H, exact=False)
     assert abs(float(loss.item()) - rloss) <= 1e-5 * abs(rloss)
-    pairs = {"mean2d": (grads.dL_dmean2d, views["mean2d"]), "opacity": (grads.dL_dopacity, views["opacity"]),
-             "colors": (grads.dL_dcolors, views["colors"]), "cov2d": (grads.dL_dcov2d, views["cov2d"]),
-             "position": (grads.dL_dposition, rg["position"]), "log_scale": (grads.dL_dlog_scale, rg["log_scale"]),
-             "rotation": (grads.dL_drotation, rg["rotation"]),
-             "logit": (grads.dL_dlogit_opacity, rg["logit_opacity"]), "sh": (grads.dL_dsh, rg["sh_coeffs"])}
-    for name, (a, b) in pairs.items():
-        if cfg.mode == _abi.GSC_MODE_REF and name == "cov2d":
+    got = {"v_mean2d": grads.dL_dmean2d, "v_opacity": grads.dL_dopacity, "v_colors": grads.dL_dcolors,
+           "v_cov2d": grads.dL_dcov2d, "position": grads.dL_dposition, "log_scale": grads.dL_dlog_scale,
+           "rotation": grads.dL_drotation, "logit_opacity": grads.dL_dlogit_opacity, "sh_coeffs": grads.dL_dsh}
+    for name, t in got.items():
+        if cfg.mode == _abi.GSC_MODE_REF and name == "v_cov2d":
             continue  # the reference never writes it (zero on both sides)
-        e = grad_close(host(a), b)
-        assert e <= GRAD_RTOL, f"{name}: {e}"
+        gate(name, host(t), exact[name], fp32[name])
 
 
 # ---- config 0 ------------------------------------------------------------------
@@ -179,7 +209,8 @@ def test_c3_training_path_three_views(cuda, par_oracle):
     ref_cfg = O.default_config(binning=_abi.GSC_BIN_REFERENCE)
     tx, ty = (W + 15) // 16, (H + 15) // 16
     end_bit = 32 + int(np.ceil(np.log2(tx * ty)))
-    ref_grads = None
+    FIELDS = importlib.import_module("crystal-gausplat_b200.gaussian").FIELDS
+    ref_grads = f32_grads = None
     ref_loss = 0.0
     for v in range(views):
         cs = cams[v].to_struct()
@@ -210,14 +241,14 @@ def test_c3_training_path_three_views(cuda, par_oracle):
         np.testing.assert_array_equal(got[v]["image"], img)
         np.testing.assert_array_equal(got[v]["n_contrib"], nc)
         np.testing.assert_array_equal(got[v]["final_T"], fT)
-        g2d, lv = O.composite_backward(W, H, ranges, sv, pre, ref_cfg, fT, last, image=img,
-                                       target=targets[v], l1_scale=1.0 / targets[v].size)
+        view_ref = {"ranges": ranges, "sorted_vals": sv, "pre": pre, "final_T": fT, "last": last, "image": img}
+        ex, lv = oracle_backward(O, sc, cs, ref_cfg, view_ref, targets[v], W, H, exact=True)
+        f32, _ = oracle_backward(O, sc, cs, ref_cfg, view_ref, targets[v], W, H, exact=False)
         ref_loss += lv
-        rg, _ = O.preprocess_backward(sc, cs, ref_cfg, g2d)
-        flat = np.concatenate([rg[k].reshape(-1).astype(np.float64)
-                               for k in ("position", "log_scale", "rotation", "logit_opacity", "sh_coeffs")])
-        ref_grads = flat if ref_grads is None else ref_grads + flat
-        del sk, sv, ck, cv, g2d, rg
+        flat = [np.concatenate([d[k].reshape(-1).astype(np.float64) for k, _ in FIELDS]) for d in (ex, f32)]
+        ref_grads = flat[0] if ref_grads is None else ref_grads + flat[0]
+        f32_grads = flat[1] if f32_grads is None else f32_grads + flat[1]
+        del sk, sv, ck, cv, ex, f32, flat
     assert abs(gpu_loss - ref_loss) <= 1e-5 * abs(ref_loss)
     # the arena holds the five gradient fields in the same order, each block
     # padded to a 16-byte boundary
@@ -230,6 +261,6 @@ def test_c3_training_path_three_views(cuda, par_oracle):
     got_flat = np.concatenate(parts)
     start = 0
     for name, w in gsmod.FIELDS:
-        e = grad_close(got_flat[start: start + n * w], ref_grads[start: start + n * w])
-        assert e <= GRAD_RTOL, f"{name}: {e}"
+        sl = slice(start, start + n * w)
+        gate(name, got_flat[sl], ref_grads[sl], f32_grads[sl])
         start += n * w
