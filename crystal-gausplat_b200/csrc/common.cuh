@@ -109,6 +109,24 @@ __device__ __forceinline__ float gs_expf_nonpos(float x) {
   return p * pow2i(ki);
 }
 
+// gs_expf for x in [-87, 0]: the same operations without the range tests and
+// without the subnormal step (2^k stays normal there), so it returns exactly
+// what gs_expf returns on that range.
+__device__ __forceinline__ float gs_expf_pixel(float x) {
+  float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(-k, 0.693145751953125f, x);
+  r = __fmaf_rn(-k, 1.428606765330187045e-06f, r);
+  float p = 1.98412698412698412698e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666666666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666666666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  return p * pow2i((int)k);
+}
+
 __device__ __forceinline__ float gs_sigmoid(float x) { return 1.0f / (1.0f + gs_expf(-x)); }
 
 // C `int(f)` (truncation toward zero) after saturating to +-1e9, so that

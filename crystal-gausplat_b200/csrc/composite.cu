@@ -4,9 +4,9 @@
 // over EVERY 16x16 tile (the reference's dispatch covers only
 // ceil(tx/16) x ceil(ty/16) of them, rasterizer.cr:332). One CTA of 256
 // threads per tile, one pixel per thread; the tile's sorted Gaussians are
-// staged 256 at a time into shared memory as packed records (two float4 and
-// one float per Gaussian) and every thread walks the batch front to back while
-// T > t_stop. The CTA leaves as soon as every pixel is done.
+// staged 256 at a time into shared memory as packed records (three float4 per
+// Gaussian) and every thread walks the batch front to back while T > t_stop.
+// The CTA leaves as soon as every pixel is done.
 //
 // Backward replaces rasterize_backward (gaussian.metal:452-567): batches are
 // staged back to front; per Gaussian each thread forms its 9 partials, the
@@ -14,10 +14,12 @@
 // global atomics. The L1 loss
 // gradient (src/ops/loss.cr:33-57) is fused into the per-pixel load.
 //
-// Skip test: a Gaussian with power < power_cut has o*G < alpha_min for every
-// opacity <= 1, so it is rejected before the exponential; power_cut is
-// ln(alpha_min) minus a margin far above the exponential's error, so the
-// accepted set is exactly the one the full test gives.
+// Skip test: a pixel whose power lies below its Gaussian's cut has
+// o*G < alpha_min, so it is rejected before the exponential. The cut is
+// ln(alpha_min / o) minus a margin far above the exponential's and the
+// logarithm's error (pixel_power_cut; ln(alpha_min) minus a margin where the
+// whole-tile test has no per-Gaussian threshold), so the accepted set is
+// exactly the one the full test gives.
 #include "common.cuh"
 #include "cull.cuh"
 #include "kernels.cuh"
@@ -54,9 +56,12 @@ __device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* tot
 #endif
 
 __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(CompositeFwdArgs a) {
+  // Staged batch, one record per surviving list entry:
+  //   s0 = {mean.x, mean.y, -A/2, -B}, s1 = {-C/2, opacity, per-Gaussian power cut, -},
+  //   s2 = {r, g, b, -} (read only by accepted pixels)
   __shared__ float4 s0[256];
   __shared__ float4 s1[256];
-  __shared__ float s2[256];
+  __shared__ float4 s2[256];
   const int tile = blockIdx.x;
   const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
   const int tid = threadIdx.x;
@@ -67,7 +72,7 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float t_stop = a.t_stop, amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
   // every power that reaches the exponential lies in [cut, 0]
-  const bool short_exp = cut >= -103.0f;
+  const bool short_exp = cut >= -87.0f;
 
   __shared__ uint32_t s_idx[256];
   __shared__ uint32_t s_cnt[8];
@@ -82,14 +87,16 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     if (__syncthreads_count(done) == 256) break;
     const uint32_t idx = b + tid;
     float4 g0, g1;
-    float g2 = 0.0f;
+    float g2 = 0.0f, pcut = cut;
     bool keep = false;
     if (idx < end) {
       const uint32_t gid = a.vals[idx];
       g0 = splats[(size_t)gid * 3];
       g1 = splats[(size_t)gid * 3 + 1];
       g2 = splats[(size_t)gid * 3 + 2].x;
-      keep = !tile_culled(g0, g1.x, g1.y, rx0, rx1, ry0, ry1, amin);
+      const CullGauss cg = cull_prepare(g0, g1.x, g1.y, amin);
+      keep = !cull_tile(cg, rx0, rx1, ry0, ry1);
+      pcut = pixel_power_cut(cg, cut);
     }
     int m;
     const int slot = compact_slot(keep, s_cnt, &m);
@@ -97,33 +104,36 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
       // conic pre-scaled by powers of two (-A/2, -B, -C/2); the power below is
       // fma(dy dy, -C/2, fma(dx dy, -B, dx dx (-A/2))), the oracle's formula
       s0[slot] = make_float4(g0.x, g0.y, -0.5f * g0.z, -g0.w);
-      s1[slot] = make_float4(-0.5f * g1.x, g1.y, g1.z, g1.w);
-      s2[slot] = g2;
+      s1[slot] = make_float4(-0.5f * g1.x, g1.y, pcut, 0.0f);
+      s2[slot] = make_float4(g1.z, g1.w, g2, 0.0f);
       s_idx[slot] = idx - start;
     }
     __syncthreads();
     if (!done) {
+      int jl = -1;  // slot of the last accepted entry of this batch
       for (int j = 0; j < m; j++) {
         const float4 q0 = s0[j];
         const float dx = pxf - q0.x, dy = pyf - q0.y;
         const float4 q1 = s1[j];
         const float power = fmaf(dy * dy, q1.x, fmaf(dx * dy, q0.w, dx * dx * q0.z));
-        if (power > 0.0f || power < cut) continue;
-        const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
+        if (power > 0.0f || power < q1.z) continue;
+        const float G = short_exp ? gs_expf_pixel(power) : gs_expf(power);
         const float alpha = fminf(amax, q1.y * G);
         if (alpha < amin) continue;
+        const float4 c = s2[j];
         const float w = T * alpha;
-        C0 = fmaf(w, q1.z, C0);
-        C1 = fmaf(w, q1.w, C1);
-        C2 = fmaf(w, s2[j], C2);
+        C0 = fmaf(w, c.x, C0);
+        C1 = fmaf(w, c.y, C1);
+        C2 = fmaf(w, c.z, C2);
         T *= (1.0f - alpha);
         cnt++;
-        lst = s_idx[j] + 1;
+        jl = j;
         if (!(T > t_stop)) {
           done = true;
           break;
         }
       }
+      if (jl >= 0) lst = s_idx[jl] + 1;
     }
   }
   if (a.pge) {  // tracing: entries visited before the stop (whole list if never stopped)
@@ -178,7 +188,7 @@ struct BwdPixel {
 // adds the conic gradient, the alpha clamp and the corrected running colour).
 template <bool FULL>
 __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, float4 g1, float g2,
-                                          float amin, float amax, float cut, bool short_exp, float dx, float dxxa,
+                                          float cut, float amin, float amax, bool short_exp, float dx, float dxxa,
                                           float v[9]) {
   if (!(P.inside && idx < P.hi)) return false;
   // dx and dx dx (-A/2) are shared by the thread's pixels (one column)
@@ -186,7 +196,7 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
   const float power = fmaf(dy * dy, g1.x, fmaf(dx * dy, g0.w, dxxa));  // == forward's power
   if (power > 0.0f || power < cut) return false;
   // Same exponential and tests as the forward, so the accepted set matches it.
-  const float G = short_exp ? gs_expf_nonpos(power) : gs_expf(power);
+  const float G = short_exp ? gs_expf_pixel(power) : gs_expf(power);
   const float alpha = fminf(amax, g1.y * G);
   if (alpha < amin) return false;
   const float o = g1.y;
@@ -233,7 +243,7 @@ __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, 
 // 128 threads per tile, two pixels per thread (rows r and r + 8), so each
 // warp reduction covers 64 pixels.
 constexpr int kBwdPix = 2;                        // pixels per thread
-constexpr int kBwdThreads = GS_TILE_PIXELS / kBwdPix;  // 64
+constexpr int kBwdThreads = GS_TILE_PIXELS / kBwdPix;  // 128
 constexpr int kBwdWarps = kBwdThreads / 32;
 constexpr int kBwdRowStep = GS_TILE / kBwdPix;        // rows between a thread's pixels
 
@@ -241,7 +251,7 @@ template <bool FULL, bool L1>
 __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_kernel(CompositeBwdArgs a) {
   __shared__ float4 s0[kBwdThreads];
   __shared__ float4 s1[kBwdThreads];
-  __shared__ float s2[kBwdThreads];
+  __shared__ float2 s2[kBwdThreads];  // {b, per-Gaussian power cut}
   __shared__ uint32_t s_gid[kBwdThreads];
   __shared__ uint32_t s_idx[kBwdThreads];
   __shared__ uint32_t s_cnt[kBwdWarps];
@@ -255,7 +265,7 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
   const uint32_t start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
-  const bool short_exp = cut >= -103.0f;
+  const bool short_exp = cut >= -87.0f;
 
   BwdPixel P[kBwdPix];
   const float pxf = (float)(tx * GS_TILE + (tid & 15)) + 0.5f;  // the thread's pixel column
@@ -318,14 +328,16 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
     __syncthreads();
     bool keep = false;
     float4 q0, q1;
-    float q2 = 0.0f;
+    float q2 = 0.0f, pcut = cut;
     uint32_t gid = 0;
     if (tid < mb) {
       gid = a.vals[bend - 1 - tid];
       q0 = splats[(size_t)gid * 3];
       q1 = splats[(size_t)gid * 3 + 1];
       q2 = splats[(size_t)gid * 3 + 2].x;
-      keep = !tile_culled(q0, q1.x, q1.y, rx0, rx1, ry0, ry1, amin);
+      const CullGauss cg = cull_prepare(q0, q1.x, q1.y, amin);
+      keep = !cull_tile(cg, rx0, rx1, ry0, ry1);
+      pcut = pixel_power_cut(cg, cut);
     }
     int m;
     const int slot = compact_slot<kBwdWarps>(keep, s_cnt, &m);
@@ -333,7 +345,7 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
       s_gid[slot] = gid;
       s0[slot] = make_float4(q0.x, q0.y, -0.5f * q0.z, -q0.w);
       s1[slot] = make_float4(-0.5f * q1.x, q1.y, q1.z, q1.w);
-      s2[slot] = q2;
+      s2[slot] = make_float2(q2, pcut);
       s_idx[slot] = (uint32_t)(bend - 1 - tid);
     }
     __syncthreads();
@@ -341,7 +353,7 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
       const uint32_t idx = s_idx[j];
       const float4 g0 = s0[j];
       const float4 g1 = s1[j];
-      const float g2 = s2[j];
+      const float2 g2 = s2[j];
       float v[9];
 #pragma unroll
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
@@ -349,7 +361,7 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
       const float dx = pxf - g0.x, dxxa = dx * dx * g0.z;
 #pragma unroll
       for (int h = 0; h < kBwdPix; h++)
-        ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2, amin, amax, cut, short_exp, dx, dxxa, v);
+        ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2.x, g2.y, amin, amax, short_exp, dx, dxxa, v);
       if (__any_sync(0xffffffffu, ok)) {
         float* red = s_red[tid >> 5];
 #pragma unroll

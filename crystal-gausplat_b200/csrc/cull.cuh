@@ -50,6 +50,7 @@ __device__ __forceinline__ float gs_logf_series(float x) {
 // once; cull_tile tests one rectangle with products and clamps.
 struct CullGauss {
   float A, B, C, mx, my, nbc, nba, thr;
+  float cut;  // ln(alpha_min / o) - 1e-4 (kind 2 only)
   int kind;  // 0: never culled, 1: culled everywhere, 2: test each tile
 };
 
@@ -72,6 +73,7 @@ __device__ __forceinline__ CullGauss cull_prepare(float4 g0, float conic_c, floa
   }
   g.A = A; g.B = B; g.C = C;
   g.mx = g0.x; g.my = g0.y;
+  g.cut = cut;
   g.nbc = -B / C;
   g.nba = -B / A;
   g.thr = -2.0f * cut * (1.0f + 2e-3f) + 2e-3f;
@@ -99,6 +101,16 @@ __device__ __forceinline__ bool cull_tile(const CullGauss& g, float rx0, float r
     qmin = fminf(qmin, cull_form(g, fminf(fmaxf(dy * g.nba, x0), x1), dy));
   }
   return qmin > g.thr;
+}
+
+// Per-pixel skip threshold of one Gaussian: a pixel whose power is below it
+// has o * G < alpha_min (G = gs_expf(power) is within 2 ulp of e^power and
+// the threshold sits 1.1e-3 below ln(alpha_min / o), far beyond the few-ulp
+// error of the logarithm), so it is rejected before the exponential with the
+// accepted set unchanged. `fallback` (ln alpha_min minus a margin, valid for
+// every opacity <= 1) is used where the cull has no per-Gaussian threshold.
+__device__ __forceinline__ float pixel_power_cut(const CullGauss& g, float fallback) {
+  return g.kind == 2 ? fmaxf(g.cut - 1e-3f, fallback) : fallback;
 }
 
 // g0 = {mean.x, mean.y, conic.xx, conic.xy}, conic_c = conic.yy, o = opacity.
