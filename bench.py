@@ -57,15 +57,18 @@ def parse():
                     help="N>1 gradient exchange: fused NVLink reduce+Adam+broadcast kernel, or NCCL all-reduce")
     ap.add_argument("--views", type=int, default=None,
                     help="profiling knob: override the number of views of --config (small ncu cases)")
-    ap.add_argument("--binning", default="contributing", choices=["contributing", "reference"],
-                    help="tile lists: contributing pairs only (default) or the reference's full lists")
+    ap.add_argument("--binning", default="occluded", choices=["occluded", "contributing", "reference"],
+                    help="tile lists: contributing pairs binned in depth slices without Gaussians whose "
+                         "tiles are already opaque (default), contributing pairs only, or the reference's "
+                         "full lists")
     ap.add_argument("--t-stop", type=float, default=None,
                     help="transmittance stop (default: the reference's 1e-3; the north star names 1e-4)")
     return ap.parse_args()
 
 
 def binning_of(gs, args):
-    return gs._abi.GSC_BIN_CONTRIBUTING if args.binning == "contributing" else gs._abi.GSC_BIN_REFERENCE
+    return {"occluded": gs._abi.GSC_BIN_OCCLUDED, "contributing": gs._abi.GSC_BIN_CONTRIBUTING,
+            "reference": gs._abi.GSC_BIN_REFERENCE}[args.binning]
 
 
 def t_stop_of(args):

@@ -28,6 +28,7 @@ GSC_MAX_BATCH_VIEWS = 8
 
 GSC_BIN_REFERENCE = 0
 GSC_BIN_CONTRIBUTING = 1
+GSC_BIN_OCCLUDED = 2
 
 GSC_STATIC_SORT_MAX_PAIRS = 262144
 

@@ -29,6 +29,7 @@ lib GSCuda
   MODE_REF         = 1
   BIN_REFERENCE    = 0
   BIN_CONTRIBUTING = 1
+  BIN_OCCLUDED     = 2
   MAX_BATCH_VIEWS  = 8
   DP_MAX_RANKS     = 8
   STATIC_SORT_MAX_PAIRS = 262144

@@ -75,6 +75,9 @@ struct gsc_frame {
   gsc_ctx* ctx = nullptr;
   GsBuf splats, depth_pairs, depth_keys, order, pairs, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
       last, n_contrib, grad2d, bins, tile_order, tile_work;
+  // depth-sliced binning (GSC_BIN_OCCLUDED)
+  GsBuf slice_vals[kMaxSlices], slice_ranges[kMaxSlices], skip_bits, tile_done, tile_base;
+  bool count_pending = false;  // the lists' length is on the device (the final ranges' end)
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
   int width = 0, height = 0, tiles_x = 0, tiles_y = 0;
@@ -249,7 +252,9 @@ static int check_view(const gsc_camera* cam, const gsc_raster_config* cfg) {
              "camera width/height out of range");
   GS_REQUIRE(cfg->mode == GSC_MODE_FULL || cfg->mode == GSC_MODE_REF, "unknown mode");
   GS_REQUIRE(cfg->sh_degree >= 0 && cfg->sh_degree <= 3, "sh_degree must be 0..3");
-  GS_REQUIRE(cfg->binning == GSC_BIN_REFERENCE || cfg->binning == GSC_BIN_CONTRIBUTING, "unknown binning");
+  GS_REQUIRE(cfg->binning == GSC_BIN_REFERENCE || cfg->binning == GSC_BIN_CONTRIBUTING ||
+                 cfg->binning == GSC_BIN_OCCLUDED,
+             "unknown binning");
   return GSC_OK;
 }
 
@@ -518,9 +523,14 @@ GSC_API int gsc_frame_destroy(gsc_frame* f) {
   cudaStreamSynchronize(f->ctx->stream);
   GsBuf* bufs[] = {&f->splats, &f->depth_pairs, &f->pairs, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
-                   &f->n_contrib, &f->grad2d, &f->bins, &f->tile_order, &f->tile_work};
+                   &f->n_contrib, &f->grad2d, &f->bins, &f->tile_order, &f->tile_work,
+                   &f->skip_bits, &f->tile_done, &f->tile_base};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
+  for (int k = 0; k < kMaxSlices; k++) {
+    if (f->slice_vals[k].ptr) cudaFree(f->slice_vals[k].ptr);
+    if (f->slice_ranges[k].ptr) cudaFree(f->slice_ranges[k].ptr);
+  }
   delete f;
   return GSC_OK;
 }
@@ -567,6 +577,7 @@ int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gs
   f->image_ptr = image;
   f->order_ptr = (const uint32_t*)f->order.ptr;
   f->keys_valid = false;
+  f->count_pending = false;
   return GSC_OK;
 }
 
@@ -701,6 +712,221 @@ int forward_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, 
   return GSC_OK;
 }
 
+// ---- depth-sliced binning (GSC_BIN_OCCLUDED) --------------------------------
+//
+// The depth order of a view is cut into slices (positions in multiples of
+// 256). Slice s is binned (pair counts, emission, tile sort) and composited
+// on top of the per-pixel state of slices < s; the compositing marks the
+// tiles whose pixels have all stopped, and the next slice's pair counting
+// and emission drop the Gaussians whose listed tiles are all marked. Within
+// a tile the slices' lists, concatenated in slice order, are the tile's
+// contributing list up to its saturation point (every Gaussian before it
+// kept) and a subset after it, so every pixel sees the same entries in the
+// same order up to its stop and the results equal the unsliced ones bit for
+// bit. The frame keeps, per tile, the first tile_work[t] (the largest `last`)
+// entries, which is all that the backward reads.
+#ifndef GS_OCC_FRAC1
+#define GS_OCC_FRAC1 0.2
+#endif
+#ifndef GS_OCC_FRAC2
+#define GS_OCC_FRAC2 1.0
+#endif
+#ifndef GS_OCC_FRAC3
+#define GS_OCC_FRAC3 1.0
+#endif
+
+// Depth-sliced binning applies to views of more than one tile (the one-tile
+// case has no tile sort to save).
+bool occlusion_binning(const gsc_raster_config* cfg, const gsc_frame* f) {
+  return cfg->binning == GSC_BIN_OCCLUDED && (int64_t)f->tiles_x * f->tiles_y > 1;
+}
+
+// Slice boundaries (depth-order positions) of n Gaussians: [0 = p0 < p1 < ... = n].
+int occlusion_slices(int64_t n, int64_t* p) {
+  const double frac[kMaxSlices - 1] = {GS_OCC_FRAC1, GS_OCC_FRAC2, GS_OCC_FRAC3};
+  int S = 0;
+  p[0] = 0;
+  for (int k = 0; k < kMaxSlices - 1; k++) {
+    int64_t b = (int64_t)(frac[k] * (double)n);
+    b = (b + 255) / 256 * 256;
+    if (b >= n) break;
+    if (b > p[S]) p[++S] = b;
+  }
+  p[++S] = n;
+  return S;
+}
+
+// Binning of slice s of frame f on ctx->stream. Slice 0 uses the whole-view
+// offsets (its pair count `m0` is exact and known on the host); a later slice
+// counts again with the skip test and sorts with a device-side count, its
+// buffers sized by the upper bound `m_up`.
+int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_up) {
+  const int64_t n_s = p[s + 1] - p[s];
+  const int tx = f->tiles_x, ty = f->tiles_y;
+  const int32_t T = tx * ty;
+  const int tb = tile_bits_of(T);
+  const uint32_t* order = f->order_ptr + p[s];
+  GS_TRY(ensure(ctx, &f->slice_vals[s], (size_t)m_up * 4 + 4));
+  GS_TRY(ensure(ctx, &f->slice_ranges[s], (size_t)T * 8));
+  uint32_t* vals = (uint32_t*)f->slice_vals[s].ptr;
+  uint32_t* ranges = (uint32_t*)f->slice_ranges[s].ptr;
+  const uint64_t* offsets = (const uint64_t*)f->offsets.ptr + p[s] / 256;
+  const uint64_t* n_dev = nullptr;
+  const uint32_t* skip = nullptr;
+  if (s > 0 && n_s > 0) {
+    StageScope sc(ctx, GSC_STAGE_SCAN);
+    sc.kernels(2);
+    GS_TRY(launch_block_sums_gather(frame_bins(f), order, n_s, (uint32_t*)f->block_sums.ptr, ctx->stream,
+                                    (const uint8_t*)f->tile_done.ptr, tx, (uint32_t*)f->skip_bits.ptr));
+    GS_TRY(launch_scan_block_sums((const uint32_t*)f->block_sums.ptr, (n_s + 255) / 256, (uint64_t*)f->offsets.ptr,
+                                  (uint64_t*)f->total.ptr, ctx->stream));
+    offsets = (const uint64_t*)f->offsets.ptr;
+    n_dev = (const uint64_t*)f->total.ptr;
+    skip = (const uint32_t*)f->skip_bits.ptr;
+  }
+  if (m_up == 0 || n_s == 0) {
+    GS_CK(cudaMemsetAsync(ranges, 0, (size_t)T * 8, ctx->stream));
+    return GSC_OK;
+  }
+  GS_TRY(ensure(ctx, &f->pairs, (size_t)m_up * 8 + 8));
+  uint64_t* pairs = (uint64_t*)f->pairs.ptr;
+  GS_TRY(scratch_reserve(ctx, sort_scratch_bytes_packed((int64_t)m_up, 32, 32 + tb)));
+  char* scratch = scratch_base(ctx);
+  {
+    StageScope sc(ctx, GSC_STAGE_EMIT);
+    sc.kernels(1);
+    GS_TRY(sort_packed_clear(ctx, (int64_t)m_up, 32, 32 + tb, scratch));
+    GS_TRY(launch_emit_tiles(frame_bins(f), order, n_s, offsets, tx, pairs, ctx->stream,
+                             sort_packed_hist(scratch, (int64_t)m_up, 32, 32 + tb), (tb + 7) / 8, ranges, T,
+                             (int64_t)ctx->num_sms * 32, skip));
+  }
+  {
+    StageScope sc(ctx, GSC_STAGE_SORT);
+    sc.kernels((tb + 7) / 8);
+    GS_TRY(launch_sort_packed(ctx, pairs, (int64_t)m_up, 32, 32 + tb, nullptr, vals, scratch, 0xFFFFFFFFu, true,
+                              ranges, (uint32_t)T, n_dev));
+  }
+  StageScope sc(ctx, GSC_STAGE_RANGES);
+  sc.kernels(1);
+  return launch_ranges_finish(ranges, T, ctx->stream);
+}
+
+// Compositing of slice s of frame f on ctx->stream; the last slice also
+// builds the frame's final lists and the backward's tile order.
+int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, int s, int S) {
+  const int32_t T = f->tiles_x * f->tiles_y;
+  if (s == 0) {
+    GS_CK(cudaMemsetAsync(f->tile_done.ptr, 0, (size_t)T, ctx->stream));
+    GS_CK(cudaMemsetAsync(f->tile_base.ptr, 0, (size_t)T * 4, ctx->stream));
+  }
+  CompositeFwdArgs a;
+  fill_fwd(&a, (const float*)f->splats.ptr, (const uint32_t*)f->slice_vals[s].ptr,
+           (const uint32_t*)f->slice_ranges[s].ptr, f->width, f->height, cfg);
+  a.image = f->image_ptr;
+  a.final_T = (float*)f->final_T.ptr;
+  a.last = (uint32_t*)f->last.ptr;
+  a.n_contrib = (uint32_t*)f->n_contrib.ptr;
+  a.tile_base = (uint32_t*)f->tile_base.ptr;
+  a.tile_done = (uint8_t*)f->tile_done.ptr;
+  a.first_slice = s == 0;
+  a.last_slice = s == S - 1;
+  const bool last = s == S - 1;
+  if (last) {
+    if (ctx->profiling) a.pge = reinterpret_cast<unsigned long long*>(ctx->err + 2);
+    GS_TRY(ensure(ctx, &f->tile_work, (size_t)T * 4 + 4));
+    a.tile_work = (uint32_t*)f->tile_work.ptr;
+  }
+  {
+    StageScope sc(ctx, GSC_STAGE_COMPOSITE_FWD);
+    sc.kernels(1);
+    GS_TRY(launch_composite_fwd(a, ctx->stream));
+  }
+  if (!last) return GSC_OK;
+  // final lists: per tile the entries up to its largest `last`
+  {
+    const uint32_t* sv[kMaxSlices];
+    const uint32_t* sr[kMaxSlices];
+    for (int k = 0; k < S; k++) {
+      sv[k] = (const uint32_t*)f->slice_vals[k].ptr;
+      sr[k] = (const uint32_t*)f->slice_ranges[k].ptr;
+    }
+    StageScope sc(ctx, GSC_STAGE_RANGES);
+    sc.kernels(2);
+    GS_TRY(launch_concat_slices(sv, sr, S, a.tile_work, T, (uint32_t*)f->vals.ptr, (uint32_t*)f->ranges.ptr,
+                                (uint64_t*)f->total.ptr, ctx->stream));
+  }
+  const bool full = cfg->mode == GSC_MODE_FULL;
+  GS_TRY(ensure(ctx, &f->tile_order, (size_t)T * 4 + 4));
+  {
+    StageScope sc(ctx, GSC_STAGE_COMPOSITE_FWD);
+    sc.kernels(1);
+    GS_TRY(launch_tile_order(full ? nullptr : (const uint32_t*)f->ranges.ptr, full ? a.tile_work : nullptr, T,
+                             (uint32_t*)f->tile_order.ptr, ctx->stream));
+  }
+  f->has_forward = true;
+  f->count_pending = true;
+  f->keys_valid = false;
+  return GSC_OK;
+}
+
+// Depth-sliced forward of `nviews` frames whose depth orders and whole-view
+// pair counts (per-chunk offsets; m[v] in total) are ready. up[v][s]: the
+// pair count of slice s before the skip test (exact for s = 0). Binning runs
+// on the caller's stream, compositing on the side stream, slice by slice
+// across the views, so that view v's compositing overlaps the binning of the
+// next views and slice s + 1 of a view waits only for its own slice s.
+int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc_raster_config* cfg,
+                   const int64_t (*p)[kMaxSlices + 1], const int* S, const uint64_t (*up)[kMaxSlices]) {
+  if (!ctx->side) {
+    GS_CK(cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking));
+    for (auto& e : ctx->side_ev) GS_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  if (!ctx->bin_ev[0])
+    for (int v = 0; v < GSC_MAX_BATCH_VIEWS; v++) {
+      GS_CK(cudaEventCreateWithFlags(&ctx->bin_ev[v], cudaEventDisableTiming));
+      GS_CK(cudaEventCreateWithFlags(&ctx->comp_ev[v], cudaEventDisableTiming));
+    }
+  for (int v = 0; v < nviews; v++) {
+    gsc_frame* f = frames[v];
+    const int32_t T = f->tiles_x * f->tiles_y;
+    uint64_t mmax = 0;
+    for (int s = 0; s < S[v]; s++) mmax = std::max(mmax, up[v][s]);
+    GS_TRY(ensure(ctx, &f->tile_done, (size_t)T + 16));
+    GS_TRY(ensure(ctx, &f->tile_base, (size_t)T * 4 + 4));
+    GS_TRY(ensure(ctx, &f->skip_bits, (size_t)(f->n + 31) / 32 * 4 + 4));
+    // the final lists hold at most every pair of the view
+    uint64_t total = 0;
+    for (int s = 0; s < S[v]; s++) total += up[v][s];
+    GS_TRY(ensure(ctx, &f->vals, (size_t)total * 4 + 4));
+    GS_TRY(ensure(ctx, &f->pairs, (size_t)mmax * 8 + 8));
+    f->num_keys = (int64_t)total;
+  }
+  cudaStream_t main_stream = ctx->stream;
+  int Smax = 0;
+  for (int v = 0; v < nviews; v++) Smax = std::max(Smax, S[v]);
+  int rc = GSC_OK;
+  for (int s = 0; s < Smax && rc == GSC_OK; s++) {
+    for (int v = 0; v < nviews && rc == GSC_OK; v++) {
+      if (s >= S[v]) continue;
+      gsc_frame* f = frames[v];
+      if (s > 0) GS_CK(cudaStreamWaitEvent(main_stream, ctx->comp_ev[v], 0));
+      rc = sliced_bin(ctx, f, s, p[v], up[v][s]);
+      if (rc) break;
+      GS_CK(cudaEventRecord(ctx->bin_ev[v], main_stream));
+      GS_CK(cudaStreamWaitEvent(ctx->side, ctx->bin_ev[v], 0));
+      ctx->stream = ctx->side;
+      rc = sliced_composite(ctx, f, cfg, s, S[v]);
+      ctx->stream = main_stream;
+      GS_CK(cudaEventRecord(ctx->comp_ev[v], ctx->side));
+    }
+  }
+  ctx->stream = main_stream;
+  // the caller's stream waits for every compositing
+  GS_CK(cudaEventRecord(ctx->side_ev[GSC_MAX_BATCH_VIEWS], ctx->side));
+  GS_CK(cudaStreamWaitEvent(main_stream, ctx->side_ev[GSC_MAX_BATCH_VIEWS], 0));
+  return rc;
+}
+
 // Compact batched depth keys: an emitted depth z lies in (max(near_z, 0),
 // far_z], so bits(z) - bits(max(near_z, 0)) is in [1, span]; usable when the
 // span leaves 2^28 - 1 free for the Gaussians that emit nothing.
@@ -736,7 +962,7 @@ int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera*
   }
   a.view_key = batch_words != nullptr;
   a.depth_compact = a.view_key && depth_compact_base(cfg, &a.depth_base);
-  a.contributing = cfg->binning == GSC_BIN_CONTRIBUTING;
+  a.contributing = cfg->binning != GSC_BIN_REFERENCE;
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
@@ -750,6 +976,36 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
                                   const gsc_camera* cam, const gsc_raster_config* cfg, float* image,
                                   uint32_t* n_contrib, float* final_T, int64_t* num_rendered) {
   GS_TRY(forward_prepare(ctx, f, g, cam, cfg, image));
+  if (occlusion_binning(cfg, f) && g->count) {
+    // the depth-sliced path of the batched call, with one view
+    GS_TRY(forward_preprocess(ctx, &f, cam, 1, g, cfg));
+    GS_TRY(forward_sort_scan(ctx, f));
+    int S[1];
+    int64_t bounds[1][kMaxSlices + 1];
+    uint64_t up[1][kMaxSlices];
+    S[0] = occlusion_slices(f->n, bounds[0]);
+    uint64_t* pin = (uint64_t*)ctx->pinned;
+    GS_CK(cudaMemcpyAsync(pin, f->total.ptr, 8, cudaMemcpyDeviceToHost, ctx->stream));
+    for (int k = 1; k < S[0]; k++)
+      GS_CK(cudaMemcpyAsync(pin + k, (const uint64_t*)f->offsets.ptr + bounds[0][k] / 256, 8,
+                            cudaMemcpyDeviceToHost, ctx->stream));
+    GS_CK(cudaStreamSynchronize(ctx->stream));
+    uint64_t prev = 0;
+    for (int k = 0; k < S[0]; k++) {
+      const uint64_t at = k + 1 < S[0] ? pin[k + 1] : pin[0];
+      up[0][k] = at - prev;
+      prev = at;
+    }
+    if (num_rendered) *num_rendered = (int64_t)pin[0];
+    GS_TRY(forward_sliced(ctx, &f, 1, cfg, bounds, S, up));
+    if (n_contrib)
+      GS_CK(cudaMemcpyAsync(n_contrib, f->n_contrib.ptr, (size_t)f->width * f->height * 4, cudaMemcpyDeviceToDevice,
+                            ctx->stream));
+    if (final_T)
+      GS_CK(cudaMemcpyAsync(final_T, f->final_T.ptr, (size_t)f->width * f->height * 4, cudaMemcpyDeviceToDevice,
+                            ctx->stream));
+    return GSC_OK;
+  }
   GS_TRY(forward_preprocess(ctx, &f, cam, 1, g, cfg));
   GS_TRY(forward_sort_scan(ctx, f));
   uint64_t m = 0;
@@ -805,14 +1061,40 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
     GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg));
     for (int v = 0; v < nviews; v++) GS_TRY(forward_sort_scan(ctx, frames[v]));
   }
-  // one readback of every view's pair count
+  // one readback of every view's pair count (and, for depth-sliced binning,
+  // of the pair counts before each slice boundary)
   uint64_t m[GSC_MAX_BATCH_VIEWS] = {};
+  const bool occl = occlusion_binning(cfg, frames[0]);
+  int S[GSC_MAX_BATCH_VIEWS] = {};
+  int64_t bounds[GSC_MAX_BATCH_VIEWS][kMaxSlices + 1] = {};
+  uint64_t up[GSC_MAX_BATCH_VIEWS][kMaxSlices] = {};
   if (g->count) {
-    for (int v = 0; v < nviews; v++)
-      GS_CK(cudaMemcpyAsync((char*)ctx->pinned + 8 * v, frames[v]->total.ptr, 8, cudaMemcpyDeviceToHost,
-                            ctx->stream));
+    uint64_t* pin = (uint64_t*)ctx->pinned;
+    for (int v = 0; v < nviews; v++) {
+      GS_CK(cudaMemcpyAsync(pin + v, frames[v]->total.ptr, 8, cudaMemcpyDeviceToHost, ctx->stream));
+      if (occl) {
+        S[v] = occlusion_slices(frames[v]->n, bounds[v]);
+        for (int k = 1; k < S[v]; k++)
+          GS_CK(cudaMemcpyAsync(pin + GSC_MAX_BATCH_VIEWS * k + v,
+                                (const uint64_t*)frames[v]->offsets.ptr + bounds[v][k] / 256, 8,
+                                cudaMemcpyDeviceToHost, ctx->stream));
+      }
+    }
     GS_CK(cudaStreamSynchronize(ctx->stream));
     std::memcpy(m, ctx->pinned, 8 * (size_t)nviews);
+    for (int v = 0; v < nviews && occl; v++) {
+      uint64_t prev = 0;
+      for (int k = 0; k < S[v]; k++) {
+        const uint64_t at = k + 1 < S[v] ? pin[GSC_MAX_BATCH_VIEWS * (k + 1) + v] : m[v];
+        up[v][k] = at - prev;
+        prev = at;
+      }
+    }
+  }
+  if (occl && g->count) {
+    for (int v = 0; v < nviews; v++)
+      if (num_rendered) num_rendered[v] = (int64_t)m[v];
+    return forward_sliced(ctx, frames, nviews, cfg, bounds, S, up);
   }
   // Binning of view v on the caller's stream, its compositing on the side
   // stream, so that it overlaps the binning of view v + 1 (every view has its
@@ -921,6 +1203,13 @@ GSC_API int gsc_rasterize_backward_batch(gsc_ctx* ctx, gsc_frame* const* frames,
 GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {
   GS_REQUIRE(f && ptr, "gsc_frame_get: null argument");
   const int64_t npix = (int64_t)f->width * f->height;
+  if (f->count_pending && (which == GSC_FRAME_KEYS || which == GSC_FRAME_VALUES)) {
+    // the final lists' length, left on the device by the list build
+    uint64_t cnt = 0;
+    GS_TRY(read_u64(f->ctx, (const uint64_t*)f->total.ptr, &cnt));
+    f->num_keys = (int64_t)cnt;
+    f->count_pending = false;
+  }
   void* p = nullptr;
   int64_t c = 0;
   switch (which) {

@@ -11,6 +11,7 @@
 // thread locating the Gaussian of its output slot by binary search over the
 // block's inclusive scan. Canonical order: Gaussian id, then ty, then tx.
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -188,20 +189,68 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 
 // `bins`: the 32-byte binning records of preprocess ({x0, y0, width, count},
 // {mask low, mask high, 0, 0}), gathered in depth order, one sector each.
+// True if every tile the Gaussian's binning record lists is marked done (all
+// its pixels stopped in an earlier depth slice). Rectangles of more than 64
+// tiles are never skipped.
+__device__ __forceinline__ bool all_tiles_done(uint4 b0, uint4 b1, const uint8_t* __restrict__ tile_done,
+                                               int tiles_x) {
+  const uint32_t cnt = b0.w, wx = b0.z;
+  if (cnt > 64) return false;
+  uint64_t mk = ((uint64_t)b1.y << 32) | b1.x;
+  if (mk == ~0ull) mk = cnt == 64 ? ~0ull : (1ull << cnt) - 1ull;  // every tile of the rect
+  while (mk) {
+    const uint32_t pos = (uint32_t)(__ffsll((long long)mk) - 1);
+    mk &= mk - 1ull;
+    const uint32_t ry = pos / wx;
+    const int t = ((int)b0.y + (int)ry) * tiles_x + (int)b0.x + (int)(pos - ry * wx);
+    if (!tile_done[t]) return false;
+  }
+  return true;
+}
+
+// With tile_done (a later depth slice): Gaussians whose tiles are all done
+// count 0 pairs, and their bit is set in skip_bits (one bit per position).
 __global__ void __launch_bounds__(256) block_sums_gather_kernel(const uint4* __restrict__ bins,
                                                                 const uint32_t* __restrict__ order,
-                                                                int64_t n, uint32_t* __restrict__ sums) {
+                                                                int64_t n, uint32_t* __restrict__ sums,
+                                                                const uint8_t* __restrict__ tile_done,
+                                                                int tiles_x, uint32_t* __restrict__ skip_bits) {
   __shared__ uint32_t s_warp[8];
   const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  uint32_t t = p < n ? bins[(size_t)order[p] * 2].w : 0u;
+  uint32_t t = 0;
+  bool skip = false;
+  if (p < n) {
+    const uint32_t gid = order[p];
+    const uint4 b0 = bins[(size_t)gid * 2];
+    t = b0.w;
+    if (tile_done && t) {
+      skip = all_tiles_done(b0, bins[(size_t)gid * 2 + 1], tile_done, tiles_x);
+      if (skip) t = 0;
+    }
+  }
+  if (skip_bits) {
+    const uint32_t bits = __ballot_sync(0xffffffffu, skip);
+    if ((threadIdx.x & 31) == 0 && p < n) skip_bits[p >> 5] = bits;
+  }
   uint32_t incl = block_incl_scan_256(t, s_warp);
   if (threadIdx.x == 255) sums[blockIdx.x] = incl;
 }
 
 constexpr int kEmitMaxPasses = 4;
+#ifndef GS_EMIT_FNS
+#define GS_EMIT_FNS 1
+#endif
+#ifndef GS_EMIT_OWNBUF
+#define GS_EMIT_OWNBUF 1
+#endif
+constexpr int kOwnWin = 1024;  // outputs per warp window (owner lane per output)
 
 // Position of the k-th (0-based) set bit of m; m has more than k set bits.
 __device__ __forceinline__ uint32_t select_bit64(uint64_t m, uint32_t k) {
+#if GS_EMIT_FNS
+  const uint32_t lo = (uint32_t)m, c = (uint32_t)__popc(lo);
+  return k < c ? __fns(lo, 0u, (int)k + 1) : 32u + __fns((uint32_t)(m >> 32), 0u, (int)(k - c) + 1);
+#endif
   uint32_t pos = 0;
 #pragma unroll
   for (int w = 32; w >= 1; w >>= 1) {
@@ -220,7 +269,8 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
                                                          const uint64_t* __restrict__ offsets,
                                                          int tiles_x, uint64_t* __restrict__ pair_out,
                                                          uint32_t* __restrict__ hist, int hist_passes,
-                                                         uint32_t* __restrict__ ranges, int32_t num_tiles) {
+                                                         uint32_t* __restrict__ ranges, int32_t num_tiles,
+                                                         const uint32_t* __restrict__ skip_bits) {
   __shared__ uint32_t s_hist[kEmitMaxPasses][256];
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
@@ -228,6 +278,9 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
   __shared__ uint32_t s_id[256];
   __shared__ uint64_t s_mask[256];
   __shared__ uint32_t s_warp[8];
+#if GS_EMIT_OWNBUF
+  __shared__ uint8_t s_own[8][kOwnWin];
+#endif
   if (ranges)
     for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < num_tiles; r += (int64_t)gridDim.x * 256) {
       ranges[2 * r] = 0xFFFFFFFFu;
@@ -244,6 +297,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
       const uint32_t gid = order[p];
       const uint4 b0 = bins[(size_t)gid * 2];
       t = b0.w;
+      if (skip_bits && ((skip_bits[p >> 5] >> (p & 31)) & 1u)) t = 0;  // every tile already done
       if (t) {
         const uint4 b1 = bins[(size_t)gid * 2 + 1];
         s_x0[threadIdx.x] = (int)b0.x;
@@ -263,8 +317,51 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
     const uint64_t out = offsets[chunk];
     const int wb = threadIdx.x & ~31;
     const uint32_t wend = s_incl[wb + 31];
-    int own = wb;
     const uint32_t wbeg = wb ? s_incl[wb - 1] : 0u;
+#if GS_EMIT_OWNBUF
+    // Each warp writes the contiguous output range of its 32 Gaussians, a
+    // window of kOwnWin outputs at a time: every lane first marks its
+    // Gaussian's outputs of the window with its lane number, then the lanes
+    // take the window's outputs 32 at a time and read their owner back.
+    const int lane = threadIdx.x & 31;
+    uint8_t* own_of = s_own[threadIdx.x >> 5];
+    const uint32_t g_end = s_incl[threadIdx.x], g_beg = g_end - t;
+    for (uint32_t w0 = wbeg; w0 < wend; w0 += kOwnWin) {
+      const uint32_t w1 = min(w0 + (uint32_t)kOwnWin, wend);
+      for (uint32_t k = max(g_beg, w0); k < min(g_end, w1); k++) own_of[k - w0] = (uint8_t)lane;
+      __syncwarp();
+      for (uint32_t k0 = w0; k0 < w1; k0 += 32) {
+        const uint32_t k = k0 + lane;
+        const bool valid = k < w1;
+        uint32_t tile = 0xFFFFFFFFu;
+        if (valid) {
+          const int own = wb + own_of[k - w0];
+          uint32_t local = k - (own ? s_incl[own - 1] : 0u);
+          const uint64_t mk = s_mask[own];
+          const uint32_t wx = (uint32_t)s_wx[own];
+          uint32_t ry;
+          if (mk != ~0ull) {
+            local = select_bit64(mk, local);  // local-th contributing tile of the rect (< 64)
+            ry = (local * s_inv[own]) >> 16;
+          } else {
+            ry = local / wx;
+          }
+          const int ty = s_y0[own] + (int)ry;
+          const int tx = s_x0[own] + (int)(local - ry * wx);
+          tile = (uint32_t)(ty * tiles_x + tx);
+          pair_out[out + k] = ((uint64_t)tile << 32) | (uint64_t)s_id[own];
+        }
+        // digit counts of the tile sort
+        if (valid)
+          for (int q = 0; q < hist_passes; q++) atomicAdd(&s_hist[q][(tile >> (8 * q)) & 255u], 1u);
+      }
+      __syncwarp();
+    }
+#else
+    // Each warp writes the contiguous output range of its 32 Gaussians; a
+    // lane's output index grows by 32 per round, so the Gaussian that owns it
+    // is found by advancing a pointer instead of searching.
+    int own = wb;
     for (uint32_t k0 = wbeg; k0 < wend; k0 += 32) {
       const uint32_t k = k0 + (threadIdx.x & 31);
       const bool valid = k < wend;
@@ -290,6 +387,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
       if (valid)
         for (int q = 0; q < hist_passes; q++) atomicAdd(&s_hist[q][(tile >> (8 * q)) & 255u], 1u);
     }
+#endif
     __syncthreads();  // the chunk's shared records are replaced next
   }
   if (hist_passes == 0) return;
@@ -326,16 +424,106 @@ __global__ void __launch_bounds__(256) tile_ranges_u32_kernel(const uint32_t* __
 }
 
 int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const uint8_t* tile_done, int tiles_x, uint32_t* skip_bits) {
   if (n == 0) return GSC_OK;
-  block_sums_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, sums);
+  block_sums_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, sums, tile_done,
+                                                                            tiles_x, skip_bits);
   GS_CK_LAUNCH("block_sums_gather_kernel");
+  return GSC_OK;
+}
+
+// Final tile lists of depth-sliced binning: tile t keeps the first keep[t]
+// entries of its slices' lists, concatenated in slice order (the entries
+// that the compositing read; the rest lie behind every pixel's stop).
+// keep_scan: one block, exclusive scan of keep into the output ranges.
+__global__ void __launch_bounds__(1024) keep_scan_kernel(const uint32_t* __restrict__ keep, int32_t num_tiles,
+                                                         uint32_t* __restrict__ out_ranges,
+                                                         uint64_t* __restrict__ total) {
+  __shared__ uint32_t s_warp[32];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int chunk = (num_tiles + 1023) / 1024;
+  const int lo = min(num_tiles, tid * chunk), hi = min(num_tiles, lo + chunk);
+  uint32_t mine = 0;
+  for (int t = lo; t < hi; t++) mine += keep[t];
+  uint32_t v = mine;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t u = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += u;
+  }
+  if (lane == 31) s_warp[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    uint32_t x = s_warp[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t u = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += u;
+    }
+    s_warp[lane] = x;
+  }
+  __syncthreads();
+  uint32_t run = (v - mine) + (w > 0 ? s_warp[w - 1] : 0u);
+  for (int t = lo; t < hi; t++) {  // empty tiles get the reference's empty range {0, 0}
+    const uint32_t k = keep[t];
+    out_ranges[2 * (size_t)t] = k ? run : 0u;
+    out_ranges[2 * (size_t)t + 1] = k ? run + k : 0u;
+    run += k;
+  }
+  if (tid == 1023) *total = run;
+}
+
+struct SliceLists {
+  const uint32_t* vals[kMaxSlices];
+  const uint32_t* ranges[kMaxSlices];
+  int n;
+};
+
+// One warp per tile copies its kept entries.
+__global__ void __launch_bounds__(256) concat_slices_kernel(SliceLists sl, const uint32_t* __restrict__ keep,
+                                                            int32_t num_tiles, const uint32_t* __restrict__ out_ranges,
+                                                            uint32_t* __restrict__ out_vals) {
+  const int t = (int)(((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= num_tiles) return;
+  uint32_t left = keep[t];
+  uint32_t dst = out_ranges[2 * (size_t)t];
+  for (int s = 0; s < sl.n && left; s++) {
+    const uint32_t a = sl.ranges[s][2 * (size_t)t], b = sl.ranges[s][2 * (size_t)t + 1];
+    const uint32_t take = min(left, b - a);
+    for (uint32_t k = lane; k < take; k += 32) out_vals[dst + k] = sl.vals[s][a + k];
+    dst += take;
+    left -= take;
+  }
+}
+
+int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* const* slice_ranges, int nslices,
+                         const uint32_t* keep, int32_t num_tiles, uint32_t* out_vals, uint32_t* out_ranges,
+                         uint64_t* total, cudaStream_t stream) {
+  if (nslices < 1 || nslices > kMaxSlices) {
+    set_error("concat_slices: bad slice count");
+    return GSC_ERR_INVALID;
+  }
+  if (num_tiles == 0) return cudaMemsetAsync(total, 0, 8, stream) == cudaSuccess ? GSC_OK : GSC_ERR_CUDA;
+  SliceLists sl;
+  std::memset(&sl, 0, sizeof sl);
+  sl.n = nslices;
+  for (int s = 0; s < nslices; s++) {
+    sl.vals[s] = slice_vals[s];
+    sl.ranges[s] = slice_ranges[s];
+  }
+  keep_scan_kernel<<<1, 1024, 0, stream>>>(keep, num_tiles, out_ranges, total);
+  GS_CK_LAUNCH("keep_scan_kernel");
+  const int64_t threads = (int64_t)num_tiles * 32;
+  concat_slices_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(sl, keep, num_tiles, out_ranges,
+                                                                               out_vals);
+  GS_CK_LAUNCH("concat_slices_kernel");
   return GSC_OK;
 }
 
 int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
                       int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist, int hist_passes,
-                      uint32_t* ranges, int32_t num_tiles, int64_t grid_cap) {
+                      uint32_t* ranges, int32_t num_tiles, int64_t grid_cap, const uint32_t* skip_bits) {
   if (n == 0) return GSC_OK;
   if (hist_passes < 0 || hist_passes > kEmitMaxPasses || (hist_passes > 0 && !hist)) {
     set_error("emit_tiles: bad histogram arguments");
@@ -344,7 +532,7 @@ int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const
   const int64_t chunks = (n + 255) / 256;
   const int64_t grid = grid_cap > 0 ? std::min<int64_t>(chunks, grid_cap) : chunks;
   emit_tiles_kernel<<<(unsigned)grid, 256, 0, stream>>>(bins, order, n, offsets, tiles_x, pair_out, hist,
-                                                        hist_passes, ranges, num_tiles);
+                                                        hist_passes, ranges, num_tiles, skip_bits);
   GS_CK_LAUNCH("emit_tiles_kernel");
   return GSC_OK;
 }

@@ -170,6 +170,10 @@ struct gsc_ctx {
   // view v + 1 on `stream` (created on first use)
   cudaStream_t side = nullptr;
   cudaEvent_t side_ev[GSC_MAX_BATCH_VIEWS + 1] = {};
+  // depth-sliced binning: per view, "slice binned" (stream -> side) and
+  // "slice composited" (side -> stream)
+  cudaEvent_t bin_ev[GSC_MAX_BATCH_VIEWS] = {};
+  cudaEvent_t comp_ev[GSC_MAX_BATCH_VIEWS] = {};
   uint32_t* err = nullptr;    // device error word
   void* pinned = nullptr;     // 4 KB pinned host staging for small readbacks
   // tracing

@@ -54,6 +54,16 @@ __device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* tot
 #ifndef GS_BWD_MIN_CTAS
 #define GS_BWD_MIN_CTAS 7
 #endif
+// Backward: skip, per warp, the entries behind all of its pixels' last
+// contributors; send the partials of a Gaussian that at most GS_BWD_DIRECT
+// lanes of a warp hit straight to global memory instead of through the
+// warp's transpose reduction.
+#ifndef GS_BWD_WARP_HI
+#define GS_BWD_WARP_HI 1
+#endif
+#ifndef GS_BWD_DIRECT
+#define GS_BWD_DIRECT 2
+#endif
 
 __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(CompositeFwdArgs a) {
   // Staged batch, one record per surviving list entry:
@@ -80,10 +90,24 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
   const float rx1 = min(tx * GS_TILE + GS_TILE, a.width) - 0.5f;
   const float ry1 = min(ty * GS_TILE + GS_TILE, a.height) - 0.5f;
 
+  const bool sliced = a.tile_base != nullptr;
+  const bool first = !sliced || a.first_slice, last_slice = !sliced || a.last_slice;
+  const uint32_t base = sliced ? a.tile_base[tile] : 0u;  // list index of this slice's first entry
+  const size_t pix = (size_t)y * a.width + x;
   float T = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f;
   uint32_t cnt = 0, lst = 0;
+  // a tile whose pixels all stopped in an earlier slice has nothing to add
+  const bool tile_skip = sliced && !first && a.tile_done[tile];
+  if (!first && inside && (!tile_skip || last_slice)) {
+    T = a.final_T[pix];
+    C0 = a.image[pix * 3 + 0];
+    C1 = a.image[pix * 3 + 1];
+    C2 = a.image[pix * 3 + 2];
+    cnt = a.n_contrib[pix];
+    lst = a.last[pix];
+  }
   bool done = !inside || !(T > t_stop);
-  for (uint32_t b = start; b < end; b += 256) {
+  for (uint32_t b = start; b < end && !tile_skip; b += 256) {
     if (__syncthreads_count(done) == 256) break;
     const uint32_t idx = b + tid;
     float4 g0, g1;
@@ -133,14 +157,35 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
           break;
         }
       }
-      if (jl >= 0) lst = s_idx[jl] + 1;
+      if (jl >= 0) lst = base + s_idx[jl] + 1;
     }
   }
+  if (!last_slice) {
+    // hand the state to the next slice; mark the tile if every pixel stopped
+    if (tile_skip) {
+      if (tid == 0) a.tile_base[tile] = base + (end - start);
+      return;
+    }
+    const bool all_done = __syncthreads_count(done) == 256;
+    if (tid == 0) {
+      a.tile_base[tile] = base + (end - start);
+      if (all_done) a.tile_done[tile] = 1;
+    }
+    if (!inside) return;
+    a.final_T[pix] = T;
+    a.image[pix * 3 + 0] = C0;
+    a.image[pix * 3 + 1] = C1;
+    a.image[pix * 3 + 2] = C2;
+    a.n_contrib[pix] = cnt;
+    a.last[pix] = lst;
+    return;
+  }
+  const uint32_t list_len = base + (end - start);  // the whole tile list, every slice
   if (a.pge) {  // tracing: entries visited before the stop (whole list if never stopped)
     __shared__ unsigned long long s_pge;
     if (tid == 0) s_pge = 0;
     __syncthreads();
-    uint32_t visited = !inside ? 0u : (!(T > t_stop) ? lst : end - start);
+    uint32_t visited = !inside ? 0u : (!(T > t_stop) ? lst : list_len);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) visited += __shfl_xor_sync(0xffffffffu, visited, off);
     if ((tid & 31) == 0) atomicAdd(&s_pge, (unsigned long long)visited);
@@ -159,7 +204,6 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     if (tid == 0) a.tile_work[tile] = s_work;
   }
   if (!inside) return;
-  const size_t pix = (size_t)y * a.width + x;
   a.image[pix * 3 + 0] = fmaf(T, a.bg[0], C0);
   a.image[pix * 3 + 1] = fmaf(T, a.bg[1], C1);
   a.image[pix * 3 + 2] = fmaf(T, a.bg[2], C2);
@@ -317,6 +361,12 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
   }
   __syncthreads();
   const uint32_t hi = FULL ? s_hi : end;
+#if GS_BWD_WARP_HI
+  // The warp's own list length: entries at or past every one of its pixels'
+  // last contributor are skipped as a block (the per-pixel test stays).
+  uint32_t whi = end;
+  if (FULL) whi = __reduce_max_sync(0xffffffffu, max(P[0].hi, P[1].hi));
+#endif
 
   const float rx0 = tx * GS_TILE + 0.5f, ry0 = ty * GS_TILE + 0.5f;
   const float rx1 = min(tx * GS_TILE + GS_TILE, a.width) - 0.5f;
@@ -349,7 +399,18 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
       s_idx[slot] = (uint32_t)(bend - 1 - tid);
     }
     __syncthreads();
-    for (int j = 0; j < m; j++) {
+    int j0 = 0;
+#if GS_BWD_WARP_HI
+    if (FULL) {  // the batch is in descending list order: first slot below whi
+      int lo = 0, up = m;
+      while (lo < up) {
+        const int mid = (lo + up) >> 1;
+        if (s_idx[mid] >= whi) lo = mid + 1; else up = mid;
+      }
+      j0 = lo;
+    }
+#endif
+    for (int j = j0; j < m; j++) {
       const uint32_t idx = s_idx[j];
       const float4 g0 = s0[j];
       const float4 g1 = s1[j];
@@ -362,7 +423,19 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
 #pragma unroll
       for (int h = 0; h < kBwdPix; h++)
         ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2.x, g2.y, amin, amax, short_exp, dx, dxxa, v);
-      if (__any_sync(0xffffffffu, ok)) {
+      const uint32_t hits = __ballot_sync(0xffffffffu, ok);
+#if GS_BWD_DIRECT > 0
+      if (hits && __popc(hits) <= GS_BWD_DIRECT) {
+        // few lanes hit: their partials go straight to the global sums
+        if (ok) {
+          float* dst = a.grad2d + (size_t)s_gid[j] * 9;
+#pragma unroll
+          for (int k = 0; k < 9; k++)
+            if (v[k] != 0.0f) atomicAdd(dst + k, v[k]);
+        }
+      } else
+#endif
+      if (hits) {
         float* red = s_red[tid >> 5];
 #pragma unroll
         for (int k = 0; k < 9; k++) red[k * 36 + lane] = v[k];

@@ -63,6 +63,14 @@ struct CompositeFwdArgs {
   uint32_t* last;
   unsigned long long* pge;  // if set: += pixel-Gaussian evaluations (tile-list entries visited)
   uint32_t* tile_work;         // if set: per tile, the largest per-pixel `last` (backward list length)
+  // Depth-sliced binning: the tile lists come in slices of the depth order and
+  // each launch composites one slice on top of the per-pixel state the
+  // previous one left (C in image, T in final_T, n_contrib, last). With
+  // tile_base (per tile: entries of the earlier slices, the list index of this
+  // slice's first entry) null there is one slice.
+  uint32_t* tile_base;
+  uint8_t* tile_done;  // per tile: every pixel stopped (set by a slice, read by the next)
+  int first_slice, last_slice;
 };
 
 struct CompositeBwdArgs {
@@ -137,8 +145,18 @@ int launch_emit_keys(const float* splats, int64_t n, const uint64_t* offsets, in
                      int tiles_y, uint64_t* keys, uint32_t* vals, cudaStream_t stream);
 int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint32_t* ranges,
                        cudaStream_t stream);
+// Depth-sliced binning (GSC_BIN_OCCLUDED): at most kMaxSlices slices of the depth order.
+constexpr int kMaxSlices = 4;
+// Pair count of each 256-position chunk of `order`. With tile_done, Gaussians
+// whose listed tiles are all done count 0 and get their bit in skip_bits.
 int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
-                             cudaStream_t stream);
+                             cudaStream_t stream, const uint8_t* tile_done = nullptr, int tiles_x = 0,
+                             uint32_t* skip_bits = nullptr);
+// Per tile, the first keep[t] entries of the slices' lists, concatenated;
+// *total (device) = their count.
+int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* const* slice_ranges, int nslices,
+                         const uint32_t* keep, int32_t num_tiles, uint32_t* out_vals, uint32_t* out_ranges,
+                         uint64_t* total, cudaStream_t stream);
 // hist (may be null): the tile sort's digit counts of the tile bits, digit d of
 // pass q at hist[(q * 256 + d) * kHistStride]; ranges (may be null): preset to
 // {0xFFFFFFFF, 0} for num_tiles tiles; grid_cap (> 0): at most that many blocks.
@@ -146,7 +164,7 @@ constexpr int kHistStride = 32;
 int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
                       int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist = nullptr,
                       int hist_passes = 0, uint32_t* ranges = nullptr, int32_t num_tiles = 0,
-                      int64_t grid_cap = 0);
+                      int64_t grid_cap = 0, const uint32_t* skip_bits = nullptr);
 // Tiles in decreasing order of their work (log-spaced buckets, 4 per
 // octave), so that the compositing's last wave holds the short tiles: work
 // = range length (ranges given) or tile_work[t].
@@ -177,7 +195,7 @@ size_t sort_scratch_bytes_packed(int64_t n, int begin_bit, int end_bit);
 // {0xFFFFFFFF, 0} per tile) the last pass also writes each tile's range.
 int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
                        uint32_t* lo_out, char* scratch, uint32_t lo_mask = 0xFFFFFFFFu, bool hist_ready = false,
-                       uint32_t* ranges = nullptr, uint32_t ntiles = 0);
+                       uint32_t* ranges = nullptr, uint32_t ntiles = 0, const uint64_t* n_dev = nullptr);
 uint32_t* sort_packed_hist(char* scratch, int64_t n, int begin_bit, int end_bit);  // wide digit counts
 int sort_packed_clear(gsc_ctx* ctx, int64_t n, int begin_bit, int end_bit, char* scratch);
 int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t n, int begin_bit,

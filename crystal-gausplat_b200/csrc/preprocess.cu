@@ -18,6 +18,18 @@
 namespace gs {
 
 constexpr int kPreThreads = 128;
+
+// The two halves of contributing-pairs binning's per-tile test for tile
+// column tx of a row (see row_extent): its pixel-centre span [rx0, rx1]
+// reaches right of xl, and starts left of xr.
+__device__ __forceinline__ bool row_tile_right_ok(const RowCull& rc, int tx, int width, float xl) {
+  const float rx1 = min(tx * GS_TILE + GS_TILE, width) - 0.5f;
+  return rx1 - rc.mx >= xl;
+}
+__device__ __forceinline__ bool row_tile_left_ok(const RowCull& rc, int tx, float xr) {
+  const float rx0 = tx * GS_TILE + 0.5f;
+  return rx0 - rc.mx <= xr;
+}
 constexpr int kShRow = 13;  // float4 per staged SH row (12 used + 1 pad)
 
 // One Gaussian per thread; a.nviews views per launch. The camera-independent
@@ -105,14 +117,30 @@ __global__ void __launch_bounds__(kPreThreads, GS_PRE_MIN_CTAS) preprocess_kerne
           const RowCull rc = row_cull_prepare(g0, pr.Cc, o_eff, cfg.alpha_min);
           if (rc.kind != 0) {
             mask = 0ull;
-            int bit = 0;
-            for (int ty = y0; ty <= y1; ty++) {
+            const int wx = x1 - x0 + 1;
+            for (int ty = y0, bit = 0; ty <= y1; ty++, bit += wx) {
               float ry0, ry1, xl = 0.0f, xr = -1.0f, rx0, rx1;
               tile_pixel_rect(x0, ty, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
-              const bool hit = rc.kind == 2 && row_extent(rc, ry0, ry1, &xl, &xr);
-              for (int tx = x0; tx <= x1; tx++, bit++) {
-                tile_pixel_rect(tx, ty, cam.width, cam.height, &rx0, &rx1, &ry0, &ry1);
-                if (hit && rx1 - rc.mx >= xl && rx0 - rc.mx <= xr) mask |= 1ull << bit;
+              if (!(rc.kind == 2 && row_extent(rc, ry0, ry1, &xl, &xr))) continue;
+              // A tile tx of the row survives iff rx1(tx) - mx >= xl and
+              // rx0(tx) - mx <= xr. Both sides are monotone in tx, so the
+              // survivors are one run [ta, tb]: estimate its ends, then move
+              // them with the exact per-tile tests (usually no step).
+              int ta = x0, tb = x1;
+              if (!row_tile_right_ok(rc, ta, cam.width, xl)) {
+                ta = min(max((int)ceilf((xl + rc.mx - 15.5f) * 0.0625f), x0), x1 + 1);
+                while (ta > x0 && row_tile_right_ok(rc, ta - 1, cam.width, xl)) ta--;
+                while (ta <= x1 && !row_tile_right_ok(rc, ta, cam.width, xl)) ta++;
+              }
+              if (!row_tile_left_ok(rc, tb, xr)) {
+                tb = max(min((int)floorf((xr + rc.mx - 0.5f) * 0.0625f), x1), x0 - 1);
+                while (tb < x1 && row_tile_left_ok(rc, tb + 1, xr)) tb++;
+                while (tb >= x0 && !row_tile_left_ok(rc, tb, xr)) tb--;
+              }
+              if (ta <= tb) {
+                const int len = tb - ta + 1;
+                const uint64_t run = len >= 64 ? ~0ull : (1ull << len) - 1ull;
+                mask |= run << (bit + (ta - x0));
               }
             }
           } else {

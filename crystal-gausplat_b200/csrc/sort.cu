@@ -19,6 +19,8 @@
 // high word and value in the low word, sorted by key bits only; scatter runs
 // are then twice as long and there is no value phase. The last pass writes
 // the two words to separate arrays.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -129,13 +131,14 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
 #ifndef GS_PAIR_MIN_CTAS
 #define GS_PAIR_MIN_CTAS 5
 #endif
-template <typename K, int MODE = 0>
-__global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PACKED_MIN_CTAS) onesweep_kernel(
+// One partition (4096 keys) of a onesweep pass; `part` is its ticket.
+template <typename K, int MODE>
+__device__ __forceinline__ void onesweep_tile(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
-    uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
-    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu,
-    uint32_t* __restrict__ ranges = nullptr, uint32_t ntiles = 0, int hstride = 1) {
+    uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t part,
+    uint32_t* err, uint32_t* __restrict__ keys_hi, uint32_t lo_mask,
+    uint32_t* __restrict__ ranges, uint32_t ntiles, int hstride) {
   __shared__ K s_keys[kTileKeys];  // reused for values
   // per-warp digit counters; in pair mode two 16-bit counters per word (a warp
   // ranks at most 512 keys per digit, a tile 4096), which saves the 4 KB that
@@ -146,13 +149,10 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   __shared__ uint32_t s_gbase[256];
   __shared__ uint8_t s_dig[MODE == 0 ? kTileKeys : 1];  // pair mode only
   __shared__ uint32_t s_warp[kWarps];
-  __shared__ uint32_t s_part;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  if (tid == 0) s_part = atomicAdd(ticket, 1u);
   for (int k = tid; k < kWarps * (kPack16 ? 128 : 256); k += kThreads) (&s_whw[0][0])[k] = 0;
   __syncthreads();
-  const uint32_t part = s_part;
   const int64_t tile_base = (int64_t)part * kTileKeys;
   const int64_t warp_base = tile_base + (int64_t)w * kWarpKeys;
   const uint32_t num_valid = (uint32_t)min((int64_t)kTileKeys, n - tile_base);
@@ -293,6 +293,57 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
   }
 }
 
+
+// One onesweep pass. The grid is at most what is resident at once; every CTA
+// takes partitions by atomic ticket until none is left, so the look-back only
+// ever waits on partitions that a running CTA holds. With n_dev the key count
+// is known on the device only (the host sizes buffers by an upper bound).
+template <typename K, int MODE = 0>
+__global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PACKED_MIN_CTAS) onesweep_kernel(
+    const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+    K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
+    uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
+    uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu,
+    uint32_t* __restrict__ ranges = nullptr, uint32_t ntiles = 0, int hstride = 1,
+    const uint64_t* __restrict__ n_dev = nullptr) {
+  __shared__ uint32_t s_part;
+  if (n_dev) n = (int64_t)*n_dev;
+  const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
+  for (;;) {
+    if (threadIdx.x == 0) s_part = atomicAdd(ticket, 1u);
+    __syncthreads();
+    const uint32_t part = s_part;
+    if ((int64_t)part >= parts) return;
+    onesweep_tile<K, MODE>(keys_in, vals_in, keys_out, vals_out, n, shift, digit_mask, hist, status, part, err,
+                           keys_hi, lo_mask, ranges, ntiles, hstride);
+    __syncthreads();  // shared memory is reused by the next partition
+  }
+}
+
+// Grid of a onesweep pass: the partitions, at most as many CTAs as fit on the
+// device at once (the CTAs loop over partitions).
+#ifndef GS_SORT_PERSISTENT
+#define GS_SORT_PERSISTENT 1
+#endif
+template <typename K, int MODE>
+static unsigned onesweep_grid(const gsc_ctx* ctx, int64_t parts) {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, onesweep_kernel<K, MODE>, kThreads, 0) != cudaSuccess ||
+        nb < 1) {
+      cudaGetLastError();
+      nb = 1;
+    }
+    per_sm = nb;
+  }
+#if GS_SORT_PERSISTENT
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(parts, (int64_t)per_sm * ctx->num_sms));
+#else
+  return (unsigned)std::max<int64_t>(1, parts);
+#endif
+}
+
 template <typename K>
 size_t sort_scratch_bytes_t(int64_t n, int begin_bit, int end_bit) {
   const int npass = (end_bit - begin_bit + 7) / 8;
@@ -337,7 +388,7 @@ static int sort_pairs_t(gsc_ctx* ctx, K* keys, uint32_t* vals, int64_t n, int be
   for (int p = 0; p < npass; p++) {
     const int shift = begin_bit + 8 * p;
     const int bits = min(8, end_bit - shift);
-    onesweep_kernel<K><<<(unsigned)parts, kThreads, 0, stream>>>(
+    onesweep_kernel<K><<<onesweep_grid<K, 0>(ctx, parts), kThreads, 0, stream>>>(
         src_k, src_v, dst_k, dst_v, n, shift, (1u << bits) - 1u, hist + p * 256,
         status + (size_t)p * parts * 256, tickets + p, ctx->err);
     GS_CK_LAUNCH("onesweep_kernel");
@@ -393,7 +444,7 @@ uint32_t* sort_packed_hist(char* scratch, int64_t n, int begin_bit, int end_bit)
 
 int sort_packed_clear(gsc_ctx* ctx, int64_t n, int begin_bit, int end_bit, char* scratch) {
   const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
-  if (n <= 1 || npass == 0) return GSC_OK;
+  if (n < 1 || npass == 0) return GSC_OK;
   // compact histograms, status words and tickets, through the wide histograms
   char* from = reinterpret_cast<char*>(compact_hist(scratch, n));
   char* to = reinterpret_cast<char*>(sort_packed_hist(scratch, n, begin_bit, end_bit)) +
@@ -404,11 +455,15 @@ int sort_packed_clear(gsc_ctx* ctx, int64_t n, int begin_bit, int end_bit, char*
 
 int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, int end_bit, uint32_t* hi_out,
                        uint32_t* lo_out, char* scratch, uint32_t lo_mask, bool hist_ready, uint32_t* ranges,
-                       uint32_t ntiles) {
+                       uint32_t ntiles, const uint64_t* n_dev) {
   cudaStream_t stream = ctx->stream;
   if (n <= 0) return GSC_OK;
   const int npass = end_bit > begin_bit ? (end_bit - begin_bit + 7) / 8 : 0;
-  if (n == 1 || npass == 0) {
+  if (n_dev && (!hist_ready || npass == 0)) {
+    set_error("launch_sort_packed: a device-side count needs producer-counted digits");
+    return GSC_ERR_INVALID;
+  }
+  if (!n_dev && (npass == 0 || (n == 1 && !ranges))) {
     split_words_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(pairs, n, hi_out, lo_out, lo_mask);
     GS_CK_LAUNCH("split_words_kernel");
     return GSC_OK;
@@ -435,13 +490,15 @@ int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, 
     const int shift = begin_bit + 8 * p;
     const int bits = min(8, end_bit - shift);
     if (p + 1 < npass) {
-      onesweep_kernel<uint64_t, 1><<<(unsigned)parts, kThreads, 0, stream>>>(
+      onesweep_kernel<uint64_t, 1><<<onesweep_grid<uint64_t, 1>(ctx, parts), kThreads, 0, stream>>>(
           src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err, nullptr, 0xFFFFFFFFu, nullptr, 0, hstride);
+          status + (size_t)p * parts * 256, tickets + p, ctx->err, nullptr, 0xFFFFFFFFu, nullptr, 0, hstride,
+          n_dev);
     } else {
-      onesweep_kernel<uint64_t, 2><<<(unsigned)parts, kThreads, 0, stream>>>(
+      onesweep_kernel<uint64_t, 2><<<onesweep_grid<uint64_t, 2>(ctx, parts), kThreads, 0, stream>>>(
           src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask, ranges, ntiles, hstride);
+          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask, ranges, ntiles, hstride,
+          n_dev);
     }
     GS_CK_LAUNCH("onesweep_kernel");
     std::swap(src, dst);

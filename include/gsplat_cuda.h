@@ -109,6 +109,15 @@ typedef struct gsc_raster_config {
  * point gsc_bin always builds the reference lists. */
 #define GSC_BIN_REFERENCE 0
 #define GSC_BIN_CONTRIBUTING 1
+/* OCCLUDED: the contributing lists binned and composited in slices of the
+ * depth order; a Gaussian all of whose tiles are already opaque (every pixel
+ * stopped at T <= t_stop in an earlier slice) is not binned. The frame's
+ * final lists are, per tile, the contributing list up to the largest `last`
+ * of the tile's pixels (the entries the backward reads). Images, n_contrib,
+ * final_T, last and gradients are bit-identical to CONTRIBUTING and
+ * REFERENCE; *num_rendered reports the contributing pairs before occlusion
+ * and gsc_frame_get's count the final lists. */
+#define GSC_BIN_OCCLUDED 2
 
 /* The trainable state of Gaussian3D (src/gaussian_splatting/gaussian.cr:19-37):
  * position [N,3], log_scale [N,3], rotation [N,4] (w,x,y,z),

@@ -310,6 +310,25 @@ def contributing_lists(W, H, skeys, svals, pre, alpha_min):
     return ok[:k].copy(), ov[:k].copy()
 
 
+def occluded_lists(W, H, skeys, svals, ranges, last):
+    """GSC_BIN_OCCLUDED's final lists: per tile, the first max(last) entries of
+    its (contributing) list -- every entry that a pixel of the tile composited
+    up to its stop, i.e. all that the backward reads."""
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    r = ranges.reshape(-1, 2).astype(np.int64)
+    lp = np.zeros((ty * 16, tx * 16), np.int64)
+    lp[:H, :W] = last
+    keep = lp.reshape(ty, 16, tx, 16).max(axis=(1, 3)).reshape(-1)
+    keep = np.minimum(keep, r[:, 1] - r[:, 0])
+    sel = np.concatenate([np.arange(a, a + k) for a, k in zip(r[:, 0], keep)]) if keep.sum() else \
+        np.zeros(0, np.int64)
+    out_r = np.zeros_like(r)
+    out_r[:, 1] = np.cumsum(keep)
+    out_r[:, 0] = out_r[:, 1] - keep
+    out_r[keep == 0] = 0  # the reference's empty range {0, 0}
+    return skeys[sel].copy(), svals[sel].copy(), out_r.astype(np.uint32).reshape(-1)
+
+
 def forward_pipeline(scene, cam, cfg):
     """All forward intermediates of one view (preprocess .. composite)."""
     W, H = cam.width, cam.height
@@ -318,10 +337,13 @@ def forward_pipeline(scene, cam, cfg):
     keys, vals = emit_keys(pre, tx, ty)
     end_bit = 32 + max(0, int(np.ceil(np.log2(tx * ty))) if tx * ty > 1 else 0)
     skeys, svals = sort_pairs(keys, vals, 0, end_bit)
-    if getattr(cfg, "binning", _abi.GSC_BIN_REFERENCE) == _abi.GSC_BIN_CONTRIBUTING:
+    binning = getattr(cfg, "binning", _abi.GSC_BIN_REFERENCE)
+    if binning in (_abi.GSC_BIN_CONTRIBUTING, _abi.GSC_BIN_OCCLUDED):
         skeys, svals = contributing_lists(W, H, skeys, svals, pre, cfg.alpha_min)
     ranges = tile_ranges(skeys, tx * ty)
     img, nc, fT, last = composite_forward(W, H, ranges, svals, pre, cfg)
+    if binning == _abi.GSC_BIN_OCCLUDED:
+        skeys, svals, ranges = occluded_lists(W, H, skeys, svals, ranges, last)
     return {"pre": pre, "keys": keys, "vals": vals, "sorted_keys": skeys, "sorted_vals": svals,
             "ranges": ranges, "image": img, "n_contrib": nc, "final_T": fT, "last": last}
 

@@ -16,12 +16,13 @@ elements no more numerous than fp32 summation itself produces (see `gate`).
   and all 59 parameter gradients, at both stops.
 - config 3 path: 3M Gaussians at 1920x1080, three views through the
   benchmark's own training path (DataParallelTrainer: one batched forward with
-  contributing-pairs lists and batched depth words, deferred compositing
+  depth-sliced occluded lists and batched depth words, deferred compositing
   backwards, one batched preprocess backward). Per view the lists equal the
-  oracle's contributing lists and are an order-preserving subset of the
-  reference's sorted lists; images, contributor counts and final
-  transmittance equal the oracle's over the reference lists; the summed
-  gradients of the three views are within 1e-4.
+  oracle's contributing lists cut after each tile's largest `last`, the
+  contributing lists are an order-preserving subset of the reference's sorted
+  lists, and images, contributor counts, final transmittance and `last` equal
+  the oracle's (images also over the reference lists); the summed gradients
+  of the three views pass the gradient gate.
 """
 import importlib
 import os
@@ -57,8 +58,8 @@ def target_of(seed, v, H, W):
     return np.random.default_rng(seed * 1000 + v).random((H, W, 3), dtype=np.float32)
 
 
-def check_forward(ctx, img, ref, W, H):
-    assert ctx.num_rendered == ref["sorted_keys"].size
+def check_forward(ctx, img, ref, W, H, rendered=None):
+    assert ctx.num_rendered == (ref["sorted_keys"].size if rendered is None else rendered)
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
@@ -145,8 +146,8 @@ def check_backward(o, sc, cs, cfg, ref, grads, loss, target, W, H):
 # ---- config 0 ------------------------------------------------------------------
 
 @pytest.mark.parametrize("t_stop", [1e-3, 1e-4], ids=["T1e-3", "T1e-4"])
-@pytest.mark.parametrize("binning", [_abi.GSC_BIN_REFERENCE, _abi.GSC_BIN_CONTRIBUTING],
-                         ids=["reference_lists", "contributing_lists"])
+@pytest.mark.parametrize("binning", [_abi.GSC_BIN_REFERENCE, _abi.GSC_BIN_CONTRIBUTING, _abi.GSC_BIN_OCCLUDED],
+                         ids=["reference_lists", "contributing_lists", "occluded_lists"])
 @pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF], ids=["full", "ref"])
 def test_c0_forward_backward(cuda, par_oracle, mode, binning, t_stop):
     W = H = 256
@@ -162,8 +163,14 @@ def test_c0_forward_backward(cuda, par_oracle, mode, binning, t_stop):
     sc = par_oracle.Scene(arrays)
     cs = cam.to_struct()
     ref = par_oracle.forward_pipeline(sc, cs, cfg)
-    assert ref["sorted_keys"].size > 100_000
-    check_forward(ctx, img, ref, W, H)
+    rendered = None
+    if binning == _abi.GSC_BIN_OCCLUDED:  # num_rendered: the contributing pairs before occlusion
+        c = gs.default_config(mode=mode, binning=_abi.GSC_BIN_CONTRIBUTING, t_stop=t_stop)
+        rendered = par_oracle.forward_pipeline(sc, cs, c)["sorted_keys"].size
+        assert ref["sorted_keys"].size < rendered
+    else:
+        assert ref["sorted_keys"].size > 100_000
+    check_forward(ctx, img, ref, W, H, rendered)
     check_backward(par_oracle, sc, cs, cfg, ref, grads, loss, target, W, H)
 
 
@@ -199,8 +206,7 @@ def test_c3_training_path_three_views(cuda, par_oracle):
     g = gs.Gaussian3D(arrays)
     eyes = gs.sphere_poses(64, 4.0, C3_SEED + 101)[:views]  # the benchmark's first three poses
     cams = [gs.make_camera(W, H, tuple(e)) for e in eyes]
-    cfg = gs.default_config()  # contributing-pairs lists, as the benchmark
-    assert cfg.binning == _abi.GSC_BIN_CONTRIBUTING
+    cfg = gs.default_config(binning=_abi.GSC_BIN_OCCLUDED)  # the benchmark's lists
     tr = trainer_mod.DataParallelTrainer(g, cams, cfg)
     targets = [target_of(C3_SEED, v, H, W) for v in range(views)]
     dev_t = [to_dev(t) for t in targets]
@@ -213,6 +219,8 @@ def test_c3_training_path_three_views(cuda, par_oracle):
                "vals": tr.ctxs[v].get(_abi.GSC_FRAME_VALUES, np.uint32),
                "ranges": tr.ctxs[v].get(_abi.GSC_FRAME_RANGES, np.uint32),
                "n_contrib": tr.ctxs[v].get(_abi.GSC_FRAME_N_CONTRIB, np.uint32).reshape(H, W),
+               "last": tr.ctxs[v].get(_abi.GSC_FRAME_LAST, np.uint32).reshape(H, W),
+               "rendered": tr.ctxs[v].num_rendered,
                "final_T": tr.ctxs[v].get(_abi.GSC_FRAME_FINAL_T, np.float32).reshape(H, W),
                "image": host(tr.images[v])} for v in range(views)}
     gpu_grads = host(tr.grads.arena).copy()
@@ -233,10 +241,18 @@ def test_c3_training_path_three_views(cuda, par_oracle):
         sk, sv = O.sort_pairs(keys, vals, 0, end_bit)
         del keys, vals
         ck, cv = O.contributing_lists(W, H, sk, sv, pre, ref_cfg.alpha_min)
-        # the GPU's lists are the oracle's contributing lists, bit for bit
-        np.testing.assert_array_equal(got[v]["keys"], ck)
-        np.testing.assert_array_equal(got[v]["vals"], cv)
-        np.testing.assert_array_equal(got[v]["ranges"], O.tile_ranges(ck, tx * ty))
+        assert got[v]["rendered"] == ck.size  # contributing pairs before occlusion
+        # compositing over the contributing lists gives every pixel's last
+        # contributor; the GPU's final lists are those lists cut after each
+        # tile's largest `last`, bit for bit
+        cr = O.tile_ranges(ck, tx * ty)
+        img_c, nc_c, fT_c, last_c = O.composite_forward(W, H, cr, cv, pre, ref_cfg)
+        np.testing.assert_array_equal(got[v]["last"], last_c)
+        ok, ov, orr = O.occluded_lists(W, H, ck, cv, cr, last_c)
+        np.testing.assert_array_equal(got[v]["keys"], ok)
+        np.testing.assert_array_equal(got[v]["vals"], ov)
+        np.testing.assert_array_equal(got[v]["ranges"], orr)
+        assert ok.size < ck.size
         # ... which are an order-preserving subset of the reference's sorted lists
         assert ck.size < sk.size
         # (tile, id) pairs are unique: locate each contributing pair in the
@@ -252,6 +268,7 @@ def test_c3_training_path_three_views(cuda, par_oracle):
         # the image over the reference lists equals the GPU's over the contributing lists
         ranges = O.tile_ranges(sk, tx * ty)
         img, nc, fT, last = O.composite_forward(W, H, ranges, sv, pre, ref_cfg)
+        np.testing.assert_array_equal(img_c, img)
         np.testing.assert_array_equal(got[v]["image"], img)
         np.testing.assert_array_equal(got[v]["n_contrib"], nc)
         np.testing.assert_array_equal(got[v]["final_T"], fT)

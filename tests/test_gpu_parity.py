@@ -140,10 +140,20 @@ def test_sort_c1_distribution_sorted(cuda, oracle):
     np.testing.assert_array_equal(v, vals[order])
 
 
-BINNINGS = [_abi.GSC_BIN_REFERENCE, _abi.GSC_BIN_CONTRIBUTING]
+BINNINGS = [_abi.GSC_BIN_REFERENCE, _abi.GSC_BIN_CONTRIBUTING, _abi.GSC_BIN_OCCLUDED]
+BIN_IDS = ["reference_lists", "contributing_lists", "occluded_lists"]
 
 
-@pytest.mark.parametrize("binning", BINNINGS, ids=["reference_lists", "contributing_lists"])
+def expected_rendered(oracle, arrays, cam, cfg, ref):
+    """num_rendered: the list length, or for OCCLUDED the contributing pairs before occlusion."""
+    if cfg.binning != _abi.GSC_BIN_OCCLUDED:
+        return ref["sorted_keys"].size
+    c = gs.default_config(mode=cfg.mode, binning=_abi.GSC_BIN_CONTRIBUTING)
+    c.t_stop, c.near_z, c.far_z = cfg.t_stop, cfg.near_z, cfg.far_z
+    return oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), c)["sorted_keys"].size
+
+
+@pytest.mark.parametrize("binning", BINNINGS, ids=BIN_IDS)
 @pytest.mark.parametrize("mode", [gs.GSC_MODE_FULL, gs.GSC_MODE_REF])
 @pytest.mark.parametrize("case", CASES)
 def test_rasterize_forward_matches_oracle(cuda, oracle, case, mode, binning):
@@ -155,7 +165,7 @@ def test_rasterize_forward_matches_oracle(cuda, oracle, case, mode, binning):
     fT = ctx.get(_abi.GSC_FRAME_FINAL_T, np.float32)
     last = ctx.get(_abi.GSC_FRAME_LAST, np.uint32)
     ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
-    assert ctx.num_rendered == ref["sorted_keys"].size
+    assert ctx.num_rendered == expected_rendered(oracle, arrays, cam, cfg, ref)
     if binning == _abi.GSC_BIN_REFERENCE:
         assert ctx.num_rendered == ref["keys"].size
     np.testing.assert_array_equal(ctx.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
@@ -229,6 +239,11 @@ def test_contributing_lists_change_nothing_but_the_lists(cuda, oracle, case):
     assert np.all(np.diff(pos) > 0)  # order preserved
     np.testing.assert_array_equal(r[3][pos], c[3])
     assert grad_close(c[5], r[5]) <= GRAD_RTOL
+    o = out[_abi.GSC_BIN_OCCLUDED]  # depth-sliced: same results, shorter lists
+    for k in range(3):
+        np.testing.assert_array_equal(o[k], r[k])
+    assert o[3].size <= c[3].size
+    assert grad_close(o[5], r[5]) <= GRAD_RTOL
 
 
 def test_backward_with_explicit_dl_dimage(cuda, oracle):
@@ -388,7 +403,7 @@ def test_backward_batch_equals_per_view_backwards(cuda, mode, k):
     assert grad_close(a, b) <= GRAD_RTOL
 
 
-@pytest.mark.parametrize("binning", BINNINGS, ids=["reference_lists", "contributing_lists"])
+@pytest.mark.parametrize("binning", BINNINGS, ids=BIN_IDS)
 def test_forward_batch_equals_single_view_forwards(cuda, binning):
     """gsc_rasterize_forward_batch == gsc_rasterize_forward per view, bit for bit."""
     n, W, H = 30000, 112, 72
@@ -410,19 +425,21 @@ def test_forward_batch_equals_single_view_forwards(cuda, binning):
 
 @pytest.mark.parametrize("near_far", [(0.01, 1000.0), (0.5, 6.0), (-1.0, 1000.0), (0.01, float("inf"))],
                          ids=["default", "narrow", "negative_near", "infinite_far"])
-def test_forward_batch_depth_words(cuda, oracle, near_far):
+@pytest.mark.parametrize("binning", [_abi.GSC_BIN_CONTRIBUTING, _abi.GSC_BIN_OCCLUDED],
+                         ids=["contributing_lists", "occluded_lists"])
+def test_forward_batch_depth_words(cuda, oracle, near_far, binning):
     """The batched depth sort (compact view/depth words where the near..far
     span allows, 36-bit words otherwise) gives the oracle's lists per view."""
     n, W, H = 6000, 80, 64
     arrays, g, _ = make(n, W, H, seed=12)
     cams = [gs.make_camera(W, H, tuple(e)) for e in gs.sphere_poses(3, 4.0, seed=5)]
-    cfg = gs.default_config()
+    cfg = gs.default_config(binning=binning)
     cfg.near_z, cfg.far_z = near_far
     ctxs = [gs.RasterizerContext() for _ in cams]
     imgs = gs.Rasterizer.forward_batch(g, cams, ctxs, config=cfg)
     for cam, c, im in zip(cams, ctxs, imgs):
         ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
-        assert c.num_rendered == ref["sorted_keys"].size
+        assert c.num_rendered == expected_rendered(oracle, arrays, cam, cfg, ref)
         np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
         np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
         np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
@@ -431,7 +448,9 @@ def test_forward_batch_depth_words(cuda, oracle, near_far):
 
 @pytest.mark.parametrize("n,W,H", [(300, 16, 16), (300, 13, 9), (1, 48, 48), (2, 48, 48)],
                          ids=["one_tile", "one_ragged_tile", "one_gaussian", "two_gaussians"])
-def test_forward_tiny_lists(cuda, oracle, n, W, H):
+@pytest.mark.parametrize("binning", [_abi.GSC_BIN_CONTRIBUTING, _abi.GSC_BIN_OCCLUDED],
+                         ids=["contributing_lists", "occluded_lists"])
+def test_forward_tiny_lists(cuda, oracle, n, W, H, binning):
     """One tile (no tile bits to sort) and lists of one or two pairs."""
     arrays = scene(n, 4)
     if n <= 2:
@@ -439,14 +458,14 @@ def test_forward_tiny_lists(cuda, oracle, n, W, H):
         arrays["log_scale"][:] = -5.0
     g = gs.Gaussian3D(arrays)
     cam = gs.make_camera(W, H, (0.0, 0.0, 4.0))
-    cfg = gs.default_config()
+    cfg = gs.default_config(binning=binning)
     for views in (1, 2):
         cams = [cam] * views
         ctxs = [gs.RasterizerContext() for _ in cams]
         imgs = gs.Rasterizer.forward_batch(g, cams, ctxs, config=cfg)
         ref = oracle.forward_pipeline(oracle.Scene(arrays), cam.to_struct(), cfg)
         for c, im in zip(ctxs, imgs):
-            assert c.num_rendered == ref["sorted_keys"].size
+            assert c.num_rendered == expected_rendered(oracle, arrays, cam, cfg, ref)
             np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_KEYS, np.uint64), ref["sorted_keys"])
             np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_VALUES, np.uint32), ref["sorted_vals"])
             np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_RANGES, np.uint32), ref["ranges"])
