@@ -217,7 +217,7 @@ def check(rc, what=""):
 
 def default_config(mode=GSC_MODE_FULL, sh_degree=3, background=(0.0, 0.0, 0.0), t_stop=None,
                    binning=None):
-    """gsc_raster_config_default with overrides (binning: GSC_BIN_*, default CONTRIBUTING)."""
+    """gsc_raster_config_default with overrides (binning: GSC_BIN_*, default OCCLUDED)."""
     cfg = RasterConfig()
     lib().gsc_raster_config_default(C.byref(cfg))
     if binning is not None:

@@ -105,7 +105,7 @@ GSC_API void gsc_raster_config_default(gsc_raster_config* cfg) {
   cfg->near_z = 0.01f;
   cfg->far_z = 1000.0f;
   cfg->background[0] = cfg->background[1] = cfg->background[2] = 0.0f;
-  cfg->binning = GSC_BIN_CONTRIBUTING;
+  cfg->binning = GSC_BIN_OCCLUDED;
 }
 
 GSC_API int gsc_init(int device, gsc_ctx** out) {
@@ -777,7 +777,8 @@ int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_u
     StageScope sc(ctx, GSC_STAGE_SCAN);
     sc.kernels(2);
     GS_TRY(launch_block_sums_gather(frame_bins(f), order, n_s, (uint32_t*)f->block_sums.ptr, ctx->stream,
-                                    (const uint8_t*)f->tile_done.ptr, tx, (uint32_t*)f->skip_bits.ptr));
+                                    (const unsigned long long*)f->tile_done.ptr, done_words_of(tx),
+                                    (uint32_t*)f->skip_bits.ptr));
     GS_TRY(launch_scan_block_sums((const uint32_t*)f->block_sums.ptr, (n_s + 255) / 256, (uint64_t*)f->offsets.ptr,
                                   (uint64_t*)f->total.ptr, ctx->stream));
     offsets = (const uint64_t*)f->offsets.ptr;
@@ -815,8 +816,9 @@ int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_u
 // builds the frame's final lists and the backward's tile order.
 int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, int s, int S) {
   const int32_t T = f->tiles_x * f->tiles_y;
+  const size_t done_bytes = (size_t)f->tiles_y * done_words_of(f->tiles_x) * 8;
   if (s == 0) {
-    GS_CK(cudaMemsetAsync(f->tile_done.ptr, 0, (size_t)T, ctx->stream));
+    GS_CK(cudaMemsetAsync(f->tile_done.ptr, 0, done_bytes, ctx->stream));
     GS_CK(cudaMemsetAsync(f->tile_base.ptr, 0, (size_t)T * 4, ctx->stream));
   }
   CompositeFwdArgs a;
@@ -827,7 +829,8 @@ int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, i
   a.last = (uint32_t*)f->last.ptr;
   a.n_contrib = (uint32_t*)f->n_contrib.ptr;
   a.tile_base = (uint32_t*)f->tile_base.ptr;
-  a.tile_done = (uint8_t*)f->tile_done.ptr;
+  a.tile_done = (unsigned long long*)f->tile_done.ptr;
+  a.done_words = done_words_of(f->tiles_x);
   a.first_slice = s == 0;
   a.last_slice = s == S - 1;
   const bool last = s == S - 1;
@@ -891,7 +894,7 @@ int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc
     const int32_t T = f->tiles_x * f->tiles_y;
     uint64_t mmax = 0;
     for (int s = 0; s < S[v]; s++) mmax = std::max(mmax, up[v][s]);
-    GS_TRY(ensure(ctx, &f->tile_done, (size_t)T + 16));
+    GS_TRY(ensure(ctx, &f->tile_done, (size_t)f->tiles_y * done_words_of(f->tiles_x) * 8 + 16));
     GS_TRY(ensure(ctx, &f->tile_base, (size_t)T * 4 + 4));
     GS_TRY(ensure(ctx, &f->skip_bits, (size_t)(f->n + 31) / 32 * 4 + 4));
     // the final lists hold at most every pair of the view

@@ -190,20 +190,26 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
 // `bins`: the 32-byte binning records of preprocess ({x0, y0, width, count},
 // {mask low, mask high, 0, 0}), gathered in depth order, one sector each.
 // True if every tile the Gaussian's binning record lists is marked done (all
-// its pixels stopped in an earlier depth slice). Rectangles of more than 64
-// tiles are never skipped.
-__device__ __forceinline__ bool all_tiles_done(uint4 b0, uint4 b1, const uint8_t* __restrict__ tile_done,
-                                               int tiles_x) {
+// its pixels stopped in an earlier depth slice). tile_done holds one bit per
+// tile, `words` 64-bit words per tile row. The record's tiles are, row by row
+// of its rectangle, a mask of at most 64 bits (all of them when the mask is
+// ~0); each row's part is compared with the done bits of the same tiles.
+// Rectangles of more than 64 tiles are never skipped.
+__device__ __forceinline__ bool all_tiles_done(uint4 b0, uint4 b1, const unsigned long long* __restrict__ tile_done,
+                                               int words) {
   const uint32_t cnt = b0.w, wx = b0.z;
-  if (cnt > 64) return false;
+  if (cnt > 64 || wx == 0 || wx > 64) return false;
   uint64_t mk = ((uint64_t)b1.y << 32) | b1.x;
   if (mk == ~0ull) mk = cnt == 64 ? ~0ull : (1ull << cnt) - 1ull;  // every tile of the rect
-  while (mk) {
-    const uint32_t pos = (uint32_t)(__ffsll((long long)mk) - 1);
-    mk &= mk - 1ull;
-    const uint32_t ry = pos / wx;
-    const int t = ((int)b0.y + (int)ry) * tiles_x + (int)b0.x + (int)(pos - ry * wx);
-    if (!tile_done[t]) return false;
+  const uint64_t row_bits = wx == 64 ? ~0ull : (1ull << wx) - 1ull;
+  const int lo = (int)b0.x >> 6, sh = (int)b0.x & 63;
+  const unsigned long long* row = tile_done + (size_t)b0.y * words;
+  for (; mk; mk = wx == 64 ? 0ull : mk >> wx, row += words) {
+    const uint64_t want = mk & row_bits;
+    if (!want) continue;
+    uint64_t d = row[lo] >> sh;
+    if (sh && lo + 1 < words) d |= row[lo + 1] << (64 - sh);
+    if (want & ~d) return false;
   }
   return true;
 }
@@ -213,8 +219,8 @@ __device__ __forceinline__ bool all_tiles_done(uint4 b0, uint4 b1, const uint8_t
 __global__ void __launch_bounds__(256) block_sums_gather_kernel(const uint4* __restrict__ bins,
                                                                 const uint32_t* __restrict__ order,
                                                                 int64_t n, uint32_t* __restrict__ sums,
-                                                                const uint8_t* __restrict__ tile_done,
-                                                                int tiles_x, uint32_t* __restrict__ skip_bits) {
+                                                                const unsigned long long* __restrict__ tile_done,
+                                                                int done_words, uint32_t* __restrict__ skip_bits) {
   __shared__ uint32_t s_warp[8];
   const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
   uint32_t t = 0;
@@ -224,7 +230,7 @@ __global__ void __launch_bounds__(256) block_sums_gather_kernel(const uint4* __r
     const uint4 b0 = bins[(size_t)gid * 2];
     t = b0.w;
     if (tile_done && t) {
-      skip = all_tiles_done(b0, bins[(size_t)gid * 2 + 1], tile_done, tiles_x);
+      skip = all_tiles_done(b0, bins[(size_t)gid * 2 + 1], tile_done, done_words);
       if (skip) t = 0;
     }
   }
@@ -424,10 +430,11 @@ __global__ void __launch_bounds__(256) tile_ranges_u32_kernel(const uint32_t* __
 }
 
 int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
-                             cudaStream_t stream, const uint8_t* tile_done, int tiles_x, uint32_t* skip_bits) {
+                             cudaStream_t stream, const unsigned long long* tile_done, int done_words,
+                             uint32_t* skip_bits) {
   if (n == 0) return GSC_OK;
   block_sums_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, sums, tile_done,
-                                                                            tiles_x, skip_bits);
+                                                                            done_words, skip_bits);
   GS_CK_LAUNCH("block_sums_gather_kernel");
   return GSC_OK;
 }

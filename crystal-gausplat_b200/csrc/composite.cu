@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
   float T = 1.0f, C0 = 0.0f, C1 = 0.0f, C2 = 0.0f;
   uint32_t cnt = 0, lst = 0;
   // a tile whose pixels all stopped in an earlier slice has nothing to add
-  const bool tile_skip = sliced && !first && a.tile_done[tile];
+  const bool tile_skip =
+      sliced && !first && ((a.tile_done[(size_t)ty * a.done_words + (tx >> 6)] >> (tx & 63)) & 1ull);
   if (!first && inside && (!tile_skip || last_slice)) {
     T = a.final_T[pix];
     C0 = a.image[pix * 3 + 0];
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     const bool all_done = __syncthreads_count(done) == 256;
     if (tid == 0) {
       a.tile_base[tile] = base + (end - start);
-      if (all_done) a.tile_done[tile] = 1;
+      if (all_done) atomicOr(&a.tile_done[(size_t)ty * a.done_words + (tx >> 6)], 1ull << (tx & 63));
     }
     if (!inside) return;
     a.final_T[pix] = T;

@@ -69,7 +69,10 @@ struct CompositeFwdArgs {
   // tile_base (per tile: entries of the earlier slices, the list index of this
   // slice's first entry) null there is one slice.
   uint32_t* tile_base;
-  uint8_t* tile_done;  // per tile: every pixel stopped (set by a slice, read by the next)
+  // one bit per tile (done_words 64-bit words per tile row): every pixel
+  // stopped (set by a slice, read by the next)
+  unsigned long long* tile_done;
+  int done_words;
   int first_slice, last_slice;
 };
 
@@ -147,11 +150,14 @@ int launch_tile_ranges(const uint64_t* keys, int64_t n, int32_t num_tiles, uint3
                        cudaStream_t stream);
 // Depth-sliced binning (GSC_BIN_OCCLUDED): at most kMaxSlices slices of the depth order.
 constexpr int kMaxSlices = 4;
-// Pair count of each 256-position chunk of `order`. With tile_done, Gaussians
-// whose listed tiles are all done count 0 and get their bit in skip_bits.
+// Pair count of each 256-position chunk of `order`. With tile_done (one bit
+// per tile, done_words 64-bit words per tile row), Gaussians whose listed
+// tiles are all done count 0 and get their bit in skip_bits.
 int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums,
-                             cudaStream_t stream, const uint8_t* tile_done = nullptr, int tiles_x = 0,
-                             uint32_t* skip_bits = nullptr);
+                             cudaStream_t stream, const unsigned long long* tile_done = nullptr,
+                             int done_words = 0, uint32_t* skip_bits = nullptr);
+// 64-bit words per tile row of a tile-done bit set
+inline int done_words_of(int tiles_x) { return (tiles_x + 63) / 64; }
 // Per tile, the first keep[t] entries of the slices' lists, concatenated;
 // *total (device) = their count.
 int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* const* slice_ranges, int nslices,

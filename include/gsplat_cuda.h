@@ -95,7 +95,7 @@ typedef struct gsc_raster_config {
   float near_z;      /* cull z <= near_z: 0.01 */
   float far_z;       /* cull z > far_z: 1000 */
   float background[3];
-  int32_t binning;   /* GSC_BIN_*: tile lists of the whole-view calls (default CONTRIBUTING) */
+  int32_t binning;   /* GSC_BIN_*: tile lists of the whole-view calls (default OCCLUDED) */
 } gsc_raster_config;
 
 /* Tile lists built by gsc_rasterize_forward. REFERENCE: every tile of each

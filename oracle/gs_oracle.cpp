@@ -280,7 +280,7 @@ void gso_raster_config_default(gsc_raster_config* cfg) {
   cfg->near_z = 0.01f;
   cfg->far_z = 1000.0f;
   cfg->background[0] = cfg->background[1] = cfg->background[2] = 0.0f;
-  cfg->binning = GSC_BIN_CONTRIBUTING;
+  cfg->binning = GSC_BIN_OCCLUDED;
 }
 
 float gso_expf(float x) {
