@@ -88,6 +88,8 @@ def gpu_rank(rank, world, port, out_dir, steps=2):
         tr = trainer.DataParallelTrainer(g, cams, cfg, process_group=dist.group.WORLD, exchange=mode)
         for _ in range(steps):
             tr.step(lambda v: targets[v])
+        if mode == "fused":
+            tr.check()  # no cross-rank wait gave up
         torch.cuda.synchronize()
         out[mode] = g.arena.detach().cpu().numpy().copy()
         out[mode + "_loss"] = float(tr.loss.item())
