@@ -261,10 +261,12 @@ def pge_count(gs, rctx):
 # ---------------------------------------------------------------------------
 # algorithmic work per stage (bytes, or FP32 ops for compositing)
 # ---------------------------------------------------------------------------
-# DRAM bytes per launch (per view for the sort) measured by ncu on config 3.
-TRAFFIC_C3 = {"composite_fwd": 49.0e6, "composite_bwd": 114.8e6,
-              # per view: batched depth sort (1/8 of histogram + 4 passes) + tile sort (2 passes)
-              "sort": 873e6}
+# DRAM bytes per launch of the dominant kernel on a config-3 view: ncu's
+# dram__bytes_read + write of composite_bwd on the config-2 scene (96.5 MB at
+# 148.5 M pixel-Gaussian evaluations), scaled by the evaluations of a
+# config-3 view (199.3 M); the backward's traffic is its list entries' splat
+# records and per-pixel state, which grow with them.
+TRAFFIC_C3 = {"composite_bwd": 130e6}
 
 PREPROCESS_B = 284      # read 236 (pos 12, log_scale 12, rot 16, logit 4, SH 192) + write 48 (splat record)
 PARAM_ROW_B = 236  # the 59 floats of one Gaussian
@@ -288,59 +290,77 @@ def packed_sort_bytes(bits, hist=True, hi=False):
     return (8 if hist else 0) + 16 * (passes - 1) + 8 + 4 + (4 if hi else 0)
 
 
-def stage_work(stats, n, keys_per_view, pge, tiles, end_bit, batch=1):
-    """Algorithmic work of each stage for ONE view: (bound, bytes or flops, stage calls per view).
+# First depth slice of occluded binning (GS_OCC_FRAC1 of the library): the
+# later slice's pair counting gathers the remaining positions again.
+OCC_FIRST_SLICE = 0.2
+
+
+def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False):
+    """Algorithmic work of each stage for ONE view: (bound, bytes or flops).
 
     Binning of a view = a stable depth sort of the N Gaussians (per view: 32 bits,
     4 passes; batched: one sort of view << 56 | (bits(depth) - bits(near)) << 28 |
     index words by 28 + ceil(log2(batch)) bits, 4 passes), a gather-scan and
     emission of packed (tile << 32 | id) words in depth order, which also counts
     the tile digits, and a stable sort of those words by the tile bits
-    (end_bit - 32 bits) whose last pass writes the ids and the tile ranges. The
-    preprocess and its backward run once per `batch` views: parameters read once,
+    (end_bit - 32 bits) whose last pass writes the ids and the tile ranges.
+    `binned`: pairs emitted and sorted per view (with occluded binning, those
+    of both depth slices); `kept`: pairs in the final lists. The preprocess
+    and its backward run once per `batch` views: parameters read once,
     gradient rows read and written once, one grad2d row per view."""
     tb = end_bit - 32
-    m = keys_per_view
     depth_bits = 28 + max(1, (batch - 1).bit_length()) if batch > 1 else 32
+    later = (1.0 - OCC_FIRST_SLICE) * n if occluded else 0.0
+    slices = 2 if occluded else 1
     return {
         # one launch per `batch` views: parameters read once, per view a 48 B splat
         # record + 32 B binning record + 8 B packed depth word
-        "preprocess": ("hbm", (PARAM_ROW_B / batch + 88) * n, 1.0 / batch),
-        "scan": ("hbm", 4 * n + 16 * n, 2),  # order + binning-record word gather, then the block-sum scan
-        "emit": ("hbm", (4 + 32) * n + 8 * m, 1),  # order + 32 B binning record; packed pairs
-        # depth sort (per view, or one per batch) + tile sort
-        "sort": ("hbm", packed_sort_bytes(depth_bits, hi=batch == 1) * n + packed_sort_bytes(tb, hist=False) * m,
-                 1 + (1.0 / batch if batch > 1 else 1)),
-        "ranges": ("hbm", 8 * tiles, 1),  # empty ranges {~0, 0} -> {0, 0}
-        "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge, 1),
-        "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge, 1),
-        "preprocess_bwd": ("hbm", (3 * PARAM_ROW_B / batch + GRAD2D_B) * n, 1.0 / batch),
-        "adam": ("hbm", ADAM_B * n, 1),
+        "preprocess": ("hbm", (PARAM_ROW_B / batch + 88) * n),
+        # order + binning-record word gather and the block-sum scan; the later
+        # slice gathers order + the 32 B record again (skip test)
+        "scan": ("hbm", 20 * n + 36 * later),
+        "emit": ("hbm", (4 + 32) * n + 8 * binned),  # order + 32 B binning record; packed pairs
+        # depth sort (per view, or one per batch) + tile sorts of the binned pairs
+        "sort": ("hbm", packed_sort_bytes(depth_bits, hi=batch == 1) * n + packed_sort_bytes(tb, hist=False) * binned),
+        # empty ranges {~0, 0} -> {0, 0} per slice; occluded: the kept ids copied
+        "ranges": ("hbm", 8 * tiles * slices + (8 * kept + 8 * tiles if occluded else 0)),
+        "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge),
+        "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge),
+        "preprocess_bwd": ("hbm", (3 * PARAM_ROW_B / batch + GRAD2D_B) * n),
+        "adam": ("hbm", ADAM_B * n),
     }
 
 
-def rooflines(stats, work, peaks):
+def rooflines(stats, work, peaks, views):
+    """Per stage: algorithmic work of one view / the stage's device time per
+    view (its CUDA-event milliseconds over the traced steps / views)."""
     out = {}
-    for name, (bound, amount, calls_per_unit) in work.items():
+    for name, (bound, amount) in work.items():
         s = stats.get(name)
         if not s or s["calls"] == 0 or s["ms"] <= 0:
             continue
-        per_launch_s = s["ms"] / 1e3 / (s["calls"] / calls_per_unit)
+        per_view_s = s["ms"] / 1e3 / views
         if bound == "hbm":
-            ach = amount / per_launch_s / 1e9
+            ach = amount / per_view_s / 1e9
             peak = peaks["hbm_gbs"]
             unit = "GB/s"
         else:
-            ach = amount / per_launch_s / 1e12
+            ach = amount / per_view_s / 1e12
             peak = FP32_NOMINAL_TFLOPS
             unit = "TFLOP/s"
         out[name] = {"bound": bound, "achieved": round(ach, 2), "peak": round(peak, 1), "unit": unit,
-                     "frac": round(ach / peak, 4), "ms_per_unit": round(per_launch_s * 1e3, 4),
+                     "frac": round(ach / peak, 4), "ms_per_view": round(per_view_s * 1e3, 4),
                      "stage_calls": s["calls"], "kernels": s["kernels"], "share": None}
     tot = sum(stats[k]["ms"] for k in stats)
     for k in out:
         out[k]["share"] = round(stats[k]["ms"] / tot, 4) if tot else None
     return out
+
+
+def profile_pairs(gs, ctx, reset=True):
+    v = (C.c_uint64 * 2)()
+    gs._abi.check(gs._abi.lib().gsc_profile_pairs(ctx, v, 1 if reset else 0))
+    return int(v[0]), int(v[1])
 
 
 # ---------------------------------------------------------------------------
@@ -435,6 +455,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     # (stage times, pixel-Gaussian evaluations): the roofline's kernel times
     profile_read(gs, ctx, reset=True)
     profile_pge(gs, ctx, reset=True)
+    profile_pairs(gs, ctx, reset=True)
     lib.gsc_profile_enable(ctx, 1)
     with Timer(torch, world) as tm_traced:
         for _ in range(args.steps):
@@ -448,8 +469,10 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     keys_per_view = keys_total / (args.steps * my_views)
     tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
-    work = stage_work(stats, cfg["n"], keys_per_view, pge, tiles, end_bit, batch=tr.batch)
-    roof = rooflines(stats, work, peaks)
+    binned, kept = (c / (args.steps * my_views) for c in profile_pairs(gs, ctx))
+    occluded = rcfg.binning == gs._abi.GSC_BIN_OCCLUDED
+    work = stage_work(cfg["n"], binned, kept, pge, tiles, end_bit, batch=tr.batch, occluded=occluded)
+    roof = rooflines(stats, work, peaks, args.steps * my_views)
 
     e2e = None
     if not args.no_e2e:
@@ -480,7 +503,9 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "data": "synthetic (seeded Gaussians, poses and U[0,1] targets per BASELINE.json)",
             "config": workload_config(args, cfg, world),
             "workload_stats": {"exchange": tr.exchange, "backward_batch_views": tr.batch,
-                               "keys_per_view": round(keys_per_view), "pge_per_view": round(pge),
+                               "contributing_pairs_per_view": round(keys_per_view),
+                               "binned_pairs_per_view": round(binned), "kept_pairs_per_view": round(kept),
+                               "pge_per_view": round(pge),
                                "traced_pass_ms_per_step": round(ms_traced / args.steps, 3),
                                "stage_times": "per-stage CUDA events of a second, traced pass of "
                                               "the same steps (the timed region runs untraced)"},
@@ -585,6 +610,7 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     # the same steps again with the library's per-stage events (stage times, PGE)
     profile_read(gs, ctx, reset=True)
     profile_pge(gs, ctx, reset=True)
+    profile_pairs(gs, ctx, reset=True)
     lib.gsc_profile_enable(ctx, 1)
     for _ in range(args.steps):
         render_all()
@@ -596,7 +622,10 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
     tiles = ((cfg["W"] + 15) // 16) * ((cfg["H"] + 15) // 16)
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
     kpv = keys_total / max(1, args.steps * (hi - lo))
-    roof = rooflines(stats, stage_work(stats, cfg["n"], kpv, pge, tiles, end_bit, batch=kb), peaks)
+    binned, kept = (c / max(1, args.steps * (hi - lo)) for c in profile_pairs(gs, ctx))
+    roof = rooflines(stats, stage_work(cfg["n"], binned, kept, pge, tiles, end_bit, batch=kb,
+                                       occluded=rcfg.binning == gs._abi.GSC_BIN_OCCLUDED),
+                     peaks, args.steps * (hi - lo))
     e2e = None
     if not args.no_e2e:
         host_imgs = [torch.empty(cfg["H"], cfg["W"], 3).pin_memory() for _ in range(kb)]
@@ -616,7 +645,8 @@ def run_render(args, cfg, rank, world, local, peaks, peak_kind):
            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "config": workload_config(args, cfg, world),
-           "workload_stats": {"keys_per_view": round(kpv), "pge_per_view": round(pge)},
+           "workload_stats": {"contributing_pairs_per_view": round(kpv), "binned_pairs_per_view": round(binned),
+                              "kept_pairs_per_view": round(kept), "pge_per_view": round(pge)},
            "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
            "roofline": dict(roof[dominant], kernel=dominant, traffic=None,
                             peak_kind="nominal FP32" if roof[dominant]["bound"] == "fp32" else peak_kind),

@@ -175,6 +175,7 @@ _SIGS = {
     "gsc_profile_read": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_int64),
                                    C.POINTER(C.c_int64), C.c_int]),
     "gsc_kernel_count": (C.c_int64, [P]),
+    "gsc_profile_pairs": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int]),
     "gsc_profile_pge": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int]),
 }
 

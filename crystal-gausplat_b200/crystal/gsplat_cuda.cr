@@ -277,4 +277,5 @@ lib GSCuda
                                       reset : Int32) : Int32
   fun kernel_count = gsc_kernel_count(ctx : Ctx) : Int64
   fun profile_pge = gsc_profile_pge(ctx : Ctx, out : UInt64*, reset : Int32) : Int32
+  fun profile_pairs = gsc_profile_pairs(ctx : Ctx, out : UInt64*, reset : Int32) : Int32
 end

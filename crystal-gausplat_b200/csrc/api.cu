@@ -126,8 +126,8 @@ GSC_API int gsc_init(int device, gsc_ctx** out) {
   gsc_ctx* ctx = new gsc_ctx();
   ctx->device = device;
   cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
-  e = cudaMalloc(&ctx->err, 16);
-  if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, 16);
+  e = cudaMalloc(&ctx->err, 64);
+  if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, 64);
   if (e == cudaSuccess) e = cudaMallocHost(&ctx->pinned, 4096);
   if (e != cudaSuccess) {
     int rc = cuda_fail(e, "gsc_init");
@@ -618,6 +618,10 @@ int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64
     return GSC_ERR_CAPACITY;
   }
   f->num_keys = (int64_t)m;
+  if (ctx->profiling) {
+    ctx->prof_binned += m;
+    ctx->prof_kept += m;
+  }
   const float* splats = (const float*)f->splats.ptr;
   GS_TRY(ensure(ctx, &f->tiles, (size_t)m * 4 + 4));
   GS_TRY(ensure(ctx, &f->vals, (size_t)m * 4 + 4));
@@ -784,6 +788,10 @@ int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_u
     offsets = (const uint64_t*)f->offsets.ptr;
     n_dev = (const uint64_t*)f->total.ptr;
     skip = (const uint32_t*)f->skip_bits.ptr;
+    if (ctx->profiling)
+      GS_TRY(launch_add_u64(n_dev, reinterpret_cast<unsigned long long*>(ctx->err + 4), ctx->stream));
+  } else if (s == 0 && ctx->profiling) {
+    ctx->prof_binned += m_up;
   }
   if (m_up == 0 || n_s == 0) {
     GS_CK(cudaMemsetAsync(ranges, 0, (size_t)T * 8, ctx->stream));
@@ -857,6 +865,9 @@ int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, i
     sc.kernels(2);
     GS_TRY(launch_concat_slices(sv, sr, S, a.tile_work, T, (uint32_t*)f->vals.ptr, (uint32_t*)f->ranges.ptr,
                                 (uint64_t*)f->total.ptr, ctx->stream));
+    if (ctx->profiling)
+      GS_TRY(launch_add_u64((const uint64_t*)f->total.ptr, reinterpret_cast<unsigned long long*>(ctx->err + 6),
+                            ctx->stream));
   }
   const bool full = cfg->mode == GSC_MODE_FULL;
   GS_TRY(ensure(ctx, &f->tile_order, (size_t)T * 4 + 4));
@@ -1319,6 +1330,22 @@ GSC_API int gsc_profile_read(gsc_ctx* ctx, double* ms, int64_t* calls, int64_t* 
 }
 
 GSC_API int64_t gsc_kernel_count(gsc_ctx* ctx) { return ctx ? ctx->kernels : 0; }
+
+GSC_API int gsc_profile_pairs(gsc_ctx* ctx, uint64_t* out, int reset) {
+  GS_REQUIRE(ctx && out, "gsc_profile_pairs: null argument");
+  GS_CK(cudaMemcpyAsync(ctx->pinned, ctx->err + 4, 16, cudaMemcpyDeviceToHost, ctx->stream));
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  uint64_t dev[2];
+  std::memcpy(dev, ctx->pinned, 16);
+  out[0] = ctx->prof_binned + dev[0];
+  out[1] = ctx->prof_kept + dev[1];
+  if (reset) {
+    GS_CK(cudaMemsetAsync(ctx->err + 4, 0, 16, ctx->stream));
+    GS_CK(cudaStreamSynchronize(ctx->stream));
+    ctx->prof_binned = ctx->prof_kept = 0;
+  }
+  return GSC_OK;
+}
 
 GSC_API int gsc_profile_pge(gsc_ctx* ctx, uint64_t* out, int reset) {
   GS_REQUIRE(ctx && out, "gsc_profile_pge: null argument");

@@ -504,6 +504,16 @@ __global__ void __launch_bounds__(256) concat_slices_kernel(SliceLists sl, const
   }
 }
 
+__global__ void add_u64_kernel(const uint64_t* __restrict__ src, unsigned long long* __restrict__ dst) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(dst, (unsigned long long)*src);
+}
+
+int launch_add_u64(const uint64_t* src, unsigned long long* dst, cudaStream_t stream) {
+  add_u64_kernel<<<1, 32, 0, stream>>>(src, dst);
+  GS_CK_LAUNCH("add_u64_kernel");
+  return GSC_OK;
+}
+
 int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* const* slice_ranges, int nslices,
                          const uint32_t* keep, int32_t num_tiles, uint32_t* out_vals, uint32_t* out_ranges,
                          uint64_t* total, cudaStream_t stream) {

@@ -174,11 +174,14 @@ struct gsc_ctx {
   // "slice composited" (side -> stream)
   cudaEvent_t bin_ev[GSC_MAX_BATCH_VIEWS] = {};
   cudaEvent_t comp_ev[GSC_MAX_BATCH_VIEWS] = {};
-  uint32_t* err = nullptr;    // device error word
+  uint32_t* err = nullptr;    // device error word (+2: PGE, +4 / +6: binned / kept pairs, u64)
   void* pinned = nullptr;     // 4 KB pinned host staging for small readbacks
   // tracing
   bool profiling = false;
   int64_t kernels = 0;
+  // pairs binned / kept in the final lists by whole-view forwards while
+  // profiling: host-known counts here, device-known ones at err + 4 / err + 6
+  uint64_t prof_binned = 0, prof_kept = 0;
   std::vector<cudaEvent_t> ev_pool;
   struct Mark { int stage; cudaEvent_t a, b; };
   std::vector<Mark> marks;

@@ -158,6 +158,8 @@ int launch_block_sums_gather(const uint4* bins, const uint32_t* order, int64_t n
                              int done_words = 0, uint32_t* skip_bits = nullptr);
 // 64-bit words per tile row of a tile-done bit set
 inline int done_words_of(int tiles_x) { return (tiles_x + 63) / 64; }
+// *dst += *src on the device (tracing counters).
+int launch_add_u64(const uint64_t* src, unsigned long long* dst, cudaStream_t stream);
 // Per tile, the first keep[t] entries of the slices' lists, concatenated;
 // *total (device) = their count.
 int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* const* slice_ranges, int nslices,

@@ -539,6 +539,10 @@ GSC_API int64_t gsc_kernel_count(gsc_ctx* ctx);
  * was enabled: per pixel, the tile-list entries up to the transmittance stop
  * (the whole list if the pixel never stopped). */
 GSC_API int gsc_profile_pge(gsc_ctx* ctx, uint64_t* out, int reset);
+/* (Tile, Gaussian) pairs of whole-view forwards while profiling was enabled:
+ * out[0] = pairs emitted and sorted (with GSC_BIN_OCCLUDED, what the depth
+ * slices binned), out[1] = pairs kept in the frames' final lists. */
+GSC_API int gsc_profile_pairs(gsc_ctx* ctx, uint64_t* out, int reset);
 
 #ifdef __cplusplus
 }

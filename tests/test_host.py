@@ -57,12 +57,22 @@ def test_bench_work_model():
     # histogram read, 16 B per pass, the last pass writing 4 B ids (+ 4 B keys)
     assert bench.packed_sort_bytes(32, hi=True) == 8 + 16 * 4
     assert bench.packed_sort_bytes(13, hist=False) == 16 + 12
-    w = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45)
-    assert w["adam"] == ("hbm", 1652 * 1000, 1)
+    w = bench.stage_work(1000, 5000, 5000, 10 ** 6, 8160, 45)
+    assert w["adam"] == ("hbm", 1652 * 1000)
     assert w["preprocess"][1] == (236 + 88) * 1000
-    w8 = bench.stage_work({}, 1000, 5000, 10 ** 6, 8160, 45, batch=8)
-    assert w8["preprocess"] == ("hbm", (236 / 8 + 88) * 1000, 1 / 8)
-    assert w8["preprocess_bwd"] == ("hbm", (3 * 236 / 8 + 36) * 1000, 1 / 8)
+    w8 = bench.stage_work(1000, 5000, 5000, 10 ** 6, 8160, 45, batch=8)
+    assert w8["preprocess"] == ("hbm", (236 / 8 + 88) * 1000)
+    assert w8["preprocess_bwd"] == ("hbm", (3 * 236 / 8 + 36) * 1000)
     # batched depth words: 28 + 3 bits (4 passes); tile sort: digits counted by emission
-    assert w8["sort"] == ("hbm", (8 + 16 * 3 + 12) * 1000 + (16 + 12) * 5000, 1 + 1 / 8)
-    assert w8["ranges"] == ("hbm", 8 * 8160, 1)
+    assert w8["sort"] == ("hbm", (8 + 16 * 3 + 12) * 1000 + (16 + 12) * 5000)
+    assert w8["ranges"] == ("hbm", 8 * 8160)
+    # occluded binning: the binned pairs are sorted, the later slice gathers again,
+    # two slices of ranges and the kept ids copied
+    wo = bench.stage_work(1000, 2000, 300, 10 ** 6, 8160, 45, batch=8, occluded=True)
+    assert wo["sort"][1] == (8 + 16 * 3 + 12) * 1000 + (16 + 12) * 2000
+    assert wo["emit"][1] == 36 * 1000 + 8 * 2000
+    assert wo["scan"][1] == 20 * 1000 + 36 * 800
+    assert wo["ranges"][1] == 8 * 8160 * 2 + 8 * 300 + 8 * 8160
+    r = bench.rooflines({"adam": {"ms": 2.0, "calls": 1, "kernels": 1}}, {"adam": ("hbm", 1e9)},
+                        {"hbm_gbs": 1000.0}, 2)
+    assert r["adam"]["achieved"] == 1000.0 and r["adam"]["ms_per_view"] == 1.0
