@@ -131,13 +131,14 @@ __device__ __forceinline__ uint32_t block_excl_scan_256(uint32_t v, uint32_t* s_
 #ifndef GS_PAIR_MIN_CTAS
 #define GS_PAIR_MIN_CTAS 5
 #endif
-// One partition (4096 keys) of a onesweep pass; `part` is its ticket.
+// One partition (4096 keys) of a onesweep pass: the CTA takes the next
+// ticket; false (nothing done) if it is past the last partition (`parts`).
 template <typename K, int MODE>
-__device__ __forceinline__ void onesweep_tile(
+__device__ __forceinline__ bool onesweep_tile(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
-    uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t part,
-    uint32_t* err, uint32_t* __restrict__ keys_hi, uint32_t lo_mask,
+    uint32_t digit_mask, const uint32_t* __restrict__ hist, uint32_t* status, uint32_t* ticket,
+    int64_t parts, uint32_t* err, uint32_t* __restrict__ keys_hi, uint32_t lo_mask,
     uint32_t* __restrict__ ranges, uint32_t ntiles, int hstride) {
   __shared__ K s_keys[kTileKeys];  // reused for values
   // per-warp digit counters; in pair mode two 16-bit counters per word (a warp
@@ -149,10 +150,14 @@ __device__ __forceinline__ void onesweep_tile(
   __shared__ uint32_t s_gbase[256];
   __shared__ uint8_t s_dig[MODE == 0 ? kTileKeys : 1];  // pair mode only
   __shared__ uint32_t s_warp[kWarps];
+  __shared__ uint32_t s_part;
 
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) s_part = atomicAdd(ticket, 1u);
   for (int k = tid; k < kWarps * (kPack16 ? 128 : 256); k += kThreads) (&s_whw[0][0])[k] = 0;
   __syncthreads();
+  const uint32_t part = s_part;
+  if ((int64_t)part >= parts) return false;
   const int64_t tile_base = (int64_t)part * kTileKeys;
   const int64_t warp_base = tile_base + (int64_t)w * kWarpKeys;
   const uint32_t num_valid = (uint32_t)min((int64_t)kTileKeys, n - tile_base);
@@ -278,7 +283,7 @@ __device__ __forceinline__ void onesweep_tile(
       keys_out[gpos] = key;
     }
   }
-  if (MODE != 0) return;
+  if (MODE != 0) return true;
   __syncthreads();
   uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys);
 #pragma unroll
@@ -291,14 +296,18 @@ __device__ __forceinline__ void onesweep_tile(
     const uint32_t gpos = s_gbase[s_dig[j]] + j;
     if ((int64_t)gpos < n) vals_out[gpos] = s_vals[j];
   }
+  return true;
 }
 
 
-// One onesweep pass. The grid is at most what is resident at once; every CTA
-// takes partitions by atomic ticket until none is left, so the look-back only
-// ever waits on partitions that a running CTA holds. With n_dev the key count
-// is known on the device only (the host sizes buffers by an upper bound).
-template <typename K, int MODE = 0>
+// One onesweep pass; every CTA takes partitions by atomic ticket, so the
+// look-back only ever waits on partitions that a running CTA holds. With
+// n_dev the key count is known on the device only (the host sizes buffers by
+// an upper bound) and PERSIST kernels run a grid of at most what is resident
+// at once, each CTA taking partitions until none is left; otherwise the grid
+// is the partitions, one per CTA (the loop's live state costs the one-shot
+// kernel registers: 15.8 vs 16.8 Gkey/s on the 30M-pair sort).
+template <typename K, int MODE = 0, bool PERSIST = false>
 __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PACKED_MIN_CTAS) onesweep_kernel(
     const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n, int shift,
@@ -306,42 +315,34 @@ __global__ void __launch_bounds__(kThreads, MODE == 0 ? GS_PAIR_MIN_CTAS : GS_PA
     uint32_t* err, uint32_t* __restrict__ keys_hi = nullptr, uint32_t lo_mask = 0xFFFFFFFFu,
     uint32_t* __restrict__ ranges = nullptr, uint32_t ntiles = 0, int hstride = 1,
     const uint64_t* __restrict__ n_dev = nullptr) {
-  __shared__ uint32_t s_part;
+  if (!PERSIST) {  // one partition per CTA (grid = partitions; the last ticket is past them)
+    onesweep_tile<K, MODE>(keys_in, vals_in, keys_out, vals_out, n, shift, digit_mask, hist, status, ticket,
+                           INT64_MAX, err, keys_hi, lo_mask, ranges, ntiles, hstride);
+    return;
+  }
   if (n_dev) n = (int64_t)*n_dev;
   const int64_t parts = (n + kTileKeys - 1) / kTileKeys;
-  for (;;) {
-    if (threadIdx.x == 0) s_part = atomicAdd(ticket, 1u);
-    __syncthreads();
-    const uint32_t part = s_part;
-    if ((int64_t)part >= parts) return;
-    onesweep_tile<K, MODE>(keys_in, vals_in, keys_out, vals_out, n, shift, digit_mask, hist, status, part, err,
-                           keys_hi, lo_mask, ranges, ntiles, hstride);
+  while (onesweep_tile<K, MODE>(keys_in, vals_in, keys_out, vals_out, n, shift, digit_mask, hist, status, ticket,
+                                parts, err, keys_hi, lo_mask, ranges, ntiles, hstride))
     __syncthreads();  // shared memory is reused by the next partition
-  }
 }
 
-// Grid of a onesweep pass: the partitions, at most as many CTAs as fit on the
-// device at once (the CTAs loop over partitions).
-#ifndef GS_SORT_PERSISTENT
-#define GS_SORT_PERSISTENT 1
-#endif
+// Grid of a persistent onesweep pass: the partitions, at most as many CTAs as
+// fit on the device at once (the CTAs loop over partitions).
 template <typename K, int MODE>
 static unsigned onesweep_grid(const gsc_ctx* ctx, int64_t parts) {
   static int per_sm = 0;
   if (per_sm == 0) {
     int nb = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, onesweep_kernel<K, MODE>, kThreads, 0) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, onesweep_kernel<K, MODE, true>, kThreads, 0) !=
+            cudaSuccess ||
         nb < 1) {
       cudaGetLastError();
       nb = 1;
     }
     per_sm = nb;
   }
-#if GS_SORT_PERSISTENT
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>(parts, (int64_t)per_sm * ctx->num_sms));
-#else
-  return (unsigned)std::max<int64_t>(1, parts);
-#endif
 }
 
 template <typename K>
@@ -388,7 +389,7 @@ static int sort_pairs_t(gsc_ctx* ctx, K* keys, uint32_t* vals, int64_t n, int be
   for (int p = 0; p < npass; p++) {
     const int shift = begin_bit + 8 * p;
     const int bits = min(8, end_bit - shift);
-    onesweep_kernel<K><<<onesweep_grid<K, 0>(ctx, parts), kThreads, 0, stream>>>(
+    onesweep_kernel<K><<<(unsigned)parts, kThreads, 0, stream>>>(
         src_k, src_v, dst_k, dst_v, n, shift, (1u << bits) - 1u, hist + p * 256,
         status + (size_t)p * parts * 256, tickets + p, ctx->err);
     GS_CK_LAUNCH("onesweep_kernel");
@@ -490,15 +491,25 @@ int launch_sort_packed(gsc_ctx* ctx, uint64_t* pairs, int64_t n, int begin_bit, 
     const int shift = begin_bit + 8 * p;
     const int bits = min(8, end_bit - shift);
     if (p + 1 < npass) {
-      onesweep_kernel<uint64_t, 1><<<onesweep_grid<uint64_t, 1>(ctx, parts), kThreads, 0, stream>>>(
-          src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err, nullptr, 0xFFFFFFFFu, nullptr, 0, hstride,
-          n_dev);
+      if (n_dev)
+        onesweep_kernel<uint64_t, 1, true><<<onesweep_grid<uint64_t, 1>(ctx, parts), kThreads, 0, stream>>>(
+            src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
+            status + (size_t)p * parts * 256, tickets + p, ctx->err, nullptr, 0xFFFFFFFFu, nullptr, 0, hstride,
+            n_dev);
+      else
+        onesweep_kernel<uint64_t, 1><<<(unsigned)parts, kThreads, 0, stream>>>(
+            src, nullptr, dst, nullptr, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
+            status + (size_t)p * parts * 256, tickets + p, ctx->err, nullptr, 0xFFFFFFFFu, nullptr, 0, hstride);
     } else {
-      onesweep_kernel<uint64_t, 2><<<onesweep_grid<uint64_t, 2>(ctx, parts), kThreads, 0, stream>>>(
-          src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
-          status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask, ranges, ntiles, hstride,
-          n_dev);
+      if (n_dev)
+        onesweep_kernel<uint64_t, 2, true><<<onesweep_grid<uint64_t, 2>(ctx, parts), kThreads, 0, stream>>>(
+            src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
+            status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask, ranges, ntiles, hstride,
+            n_dev);
+      else
+        onesweep_kernel<uint64_t, 2><<<(unsigned)parts, kThreads, 0, stream>>>(
+            src, nullptr, nullptr, lo_out, n, shift, (1u << bits) - 1u, hist + (size_t)p * 256 * hstride,
+            status + (size_t)p * parts * 256, tickets + p, ctx->err, hi_out, lo_mask, ranges, ntiles, hstride);
     }
     GS_CK_LAUNCH("onesweep_kernel");
     std::swap(src, dst);
