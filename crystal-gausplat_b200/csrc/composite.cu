@@ -58,6 +58,19 @@ __device__ __forceinline__ int compact_slot(bool keep, uint32_t* s_cnt, int* tot
 // contributors; send the partials of a Gaussian that at most GS_BWD_DIRECT
 // lanes of a warp hit straight to global memory instead of through the
 // warp's transpose reduction.
+// Forward: the next batch's splat records are fetched into shared memory with
+// cp.async while the current batch is composited.
+#ifndef GS_FWD_CPASYNC
+#define GS_FWD_CPASYNC 1
+#endif
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
 #ifndef GS_BWD_WARP_HI
 #define GS_BWD_WARP_HI 1
 #endif
@@ -108,17 +121,43 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     lst = a.last[pix];
   }
   bool done = !inside || !(T > t_stop);
+#if GS_FWD_CPASYNC
+  // Each thread stages the 48-byte record of its own entry of the next batch
+  // (s_raw[3 tid .. 3 tid + 2]) and reads it back itself after waiting for
+  // its own copies; the entry's id is loaded one batch earlier still.
+  __shared__ float4 s_raw[3 * 256];
+  uint32_t gid_next = 0;
+  if (!tile_skip && start < end) {
+    if (start + tid < end) {
+      const float4* src = splats + (size_t)a.vals[start + tid] * 3;
+      cp_async16(&s_raw[3 * tid], src);
+      cp_async16(&s_raw[3 * tid + 1], src + 1);
+      cp_async16(&s_raw[3 * tid + 2], src + 2);
+    }
+    cp_async_commit();
+    if (start + 256 + tid < end) gid_next = a.vals[start + 256 + tid];
+  }
+#endif
   for (uint32_t b = start; b < end && !tile_skip; b += 256) {
     if (__syncthreads_count(done) == 256) break;
     const uint32_t idx = b + tid;
     float4 g0, g1;
     float g2 = 0.0f, pcut = cut;
     bool keep = false;
+#if GS_FWD_CPASYNC
+    cp_async_wait_all();
+#endif
     if (idx < end) {
+#if GS_FWD_CPASYNC
+      g0 = s_raw[3 * tid];
+      g1 = s_raw[3 * tid + 1];
+      g2 = s_raw[3 * tid + 2].x;
+#else
       const uint32_t gid = a.vals[idx];
       g0 = splats[(size_t)gid * 3];
       g1 = splats[(size_t)gid * 3 + 1];
       g2 = splats[(size_t)gid * 3 + 2].x;
+#endif
       const CullGauss cg = cull_prepare(g0, g1.x, g1.y, amin);
       keep = !cull_tile(cg, rx0, rx1, ry0, ry1);
       pcut = pixel_power_cut(cg, cut);
@@ -133,6 +172,18 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
       s2[slot] = make_float4(g1.z, g1.w, g2, 0.0f);
       s_idx[slot] = idx - start;
     }
+#if GS_FWD_CPASYNC
+    if (b + 256 < end) {  // the next batch's records, while this one is composited
+      if (b + 256 + tid < end) {
+        const float4* src = splats + (size_t)gid_next * 3;
+        cp_async16(&s_raw[3 * tid], src);
+        cp_async16(&s_raw[3 * tid + 1], src + 1);
+        cp_async16(&s_raw[3 * tid + 2], src + 2);
+      }
+      cp_async_commit();
+      gid_next = b + 512 + tid < end ? a.vals[b + 512 + tid] : 0u;
+    }
+#endif
     __syncthreads();
     if (!done) {
       int jl = -1;  // slot of the last accepted entry of this batch
@@ -161,6 +212,9 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
       if (jl >= 0) lst = base + s_idx[jl] + 1;
     }
   }
+#if GS_FWD_CPASYNC
+  cp_async_wait_all();  // no copy outlives the loop (an early stop leaves one in flight)
+#endif
   if (!last_slice) {
     // hand the state to the next slice; mark the tile if every pixel stopped
     if (tile_skip) {
