@@ -1175,6 +1175,12 @@ GSC_API int gsc_rasterize_backward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussia
   return do_preprocess_bwd(ctx, g, cam, cfg, grad2d, grads, g2d);
 }
 
+// The batched preprocess backward runs over the Gaussians that received a
+// screen-space gradient only (preprocess_bwd.cu).
+#ifndef GS_PBWD_COMPACT
+#define GS_PBWD_COMPACT 1
+#endif
+
 GSC_API int gsc_rasterize_backward_batch(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera* cams,
                                          int32_t nviews, const gsc_gaussians* g,
                                          const gsc_raster_config* cfg, const gsc_gaussian_grads* grads) {
@@ -1209,9 +1215,16 @@ GSC_API int gsc_rasterize_backward_batch(gsc_ctx* ctx, gsc_frame* const* frames,
   }
   a.g_pos = grads->position; a.g_log_scale = grads->log_scale; a.g_rot = grads->rotation;
   a.g_logit_opacity = grads->logit_opacity; a.g_sh = grads->sh;
+#if GS_PBWD_COMPACT
+  GS_TRY(scratch_reserve(ctx, preprocess_bwd_compact_scratch(g->count)));
+  StageScope sc(ctx, GSC_STAGE_PREPROCESS_BWD);
+  sc.kernels(g->count ? 2 : 0);
+  return launch_preprocess_bwd_compact(a, scratch_base(ctx), ctx->num_sms, ctx->stream);
+#else
   StageScope sc(ctx, GSC_STAGE_PREPROCESS_BWD);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess_bwd(a, true, ctx->stream);
+#endif
 }
 
 GSC_API int gsc_frame_get(gsc_frame* f, int which, void** ptr, int64_t* count) {

@@ -211,6 +211,10 @@ int launch_sort_pairs_u32(gsc_ctx* ctx, uint32_t* keys, uint32_t* vals, int64_t 
 int launch_composite_fwd(const CompositeFwdArgs& a, cudaStream_t stream);
 int launch_composite_bwd(const CompositeBwdArgs& a, bool full, cudaStream_t stream);
 int launch_preprocess_bwd(const PreprocessBwdArgs& a, bool full, cudaStream_t stream);
+// FULL mode over the Gaussians with a screen-space gradient in some view only
+// (scratch: preprocess_bwd_compact_scratch(n) bytes).
+int launch_preprocess_bwd_compact(const PreprocessBwdArgs& a, char* scratch, int num_sms, cudaStream_t stream);
+size_t preprocess_bwd_compact_scratch(int64_t n);
 int launch_adam(const AdamArgs& a, cudaStream_t stream);
 int launch_l1(const float* pred, const float* target, int64_t numel, float scale, float* grad,
               float* loss_sum, int num_sms, cudaStream_t stream);

@@ -10,6 +10,8 @@
 // -> position, colour -> SH coefficients and position through the view
 // direction, opacity -> logit. Gradients ACCUMULATE into the caller's buffers
 // so several views can be summed before the optimiser step.
+#include <algorithm>
+
 #include "geometry.cuh"
 #include "kernels.cuh"
 
@@ -72,50 +74,13 @@ __device__ __forceinline__ void unstage_rows(const float4* s4, float* g, int64_t
   for (int k = threadIdx.x; k < cnt * 12; k += kPbThreads) dst[k] = s4[(k / 12) * kRowF4 + k % 12];
 }
 
-// One Gaussian per thread, `nviews` views (camera + grad2d each) per launch.
-// The camera-independent terms (scales, rotation, 3-D covariance) are formed
-// once; per view the position gradient and the symmetric covariance gradient
-// dSigma are summed (the scale and rotation gradients are linear in dSigma),
-// the SH gradient goes straight into the staged gradient row, and every
-// gradient row is read and written once per launch. Dynamic shared memory:
-// the SH rows and the SH-gradient rows of the block.
-// 4 CTAs per SM (its shared memory allows no more): at most 128 registers.
-// Reading the SH rows from global memory instead of staging them (half the
-// shared memory) measured slower at 4 and 5 CTAs per SM (0.297 / 0.295 vs
-// 0.279 ms per view), and at 6 CTAs the registers spill.
-__global__ void __launch_bounds__(kPbThreads, 4) preprocess_bwd_full_kernel(PreprocessBwdArgs a) {
-  extern __shared__ float4 s_dyn[];
-  float4* s_par = s_dyn;                         // SH rows
-  float4* s_grd = s_dyn + kPbThreads * kRowF4;   // SH-gradient rows
-  const int64_t base = (int64_t)blockIdx.x * kPbThreads;
-  const int64_t i = base + threadIdx.x;
-  const int cnt = (int)min((int64_t)kPbThreads, a.n - base);
-  const bool valid = i < a.n;
+// The FULL chain of Gaussian i over the views whose bit is set in view_mask
+// (their grad2d rows); `row` is its SH row, `grow` its SH-gradient row (in
+// shared or global memory), every other gradient goes to global memory.
+__device__ __forceinline__ void pbwd_full_gaussian(const PreprocessBwdArgs& a, int64_t i, const float* row,
+                                                   float* grow, uint32_t view_mask) {
   const gsc_raster_config& cfg = a.cfg;
   const int nv = a.nviews;
-  bool any = false;
-  for (int v = 0; v < nv; v++) {
-    if (!valid) break;
-    const float* gv = a.grad2d_v[v] + i * 9;
-#pragma unroll
-    for (int k = 0; k < 9; k++) any = any || gv[k] != 0.0f;
-  }
-  if (valid && nv == 1) {  // screen-space views of a single-view call
-    const float* gv = a.grad2d_v[0] + i * 9;
-    if (a.d_mean2d) { a.d_mean2d[i * 2] = gv[0]; a.d_mean2d[i * 2 + 1] = gv[1]; }
-    if (a.d_opacity) a.d_opacity[i] = gv[5];
-    if (a.d_colors) { a.d_colors[i * 3] = gv[6]; a.d_colors[i * 3 + 1] = gv[7]; a.d_colors[i * 3 + 2] = gv[8]; }
-    if (a.d_cov2d) { a.d_cov2d[i * 3] = 0.0f; a.d_cov2d[i * 3 + 1] = 0.0f; a.d_cov2d[i * 3 + 2] = 0.0f; }
-  }
-  // every term below is linear in grad2d: blocks without gradients are done
-  if (!__syncthreads_or(any)) return;
-  stage_rows(s_par, a.sh, base, cnt);
-  stage_rows(s_grd, a.g_sh, base, cnt);
-  __syncthreads();
-
-  if (any) {
-    const float* row = reinterpret_cast<const float*>(s_par + threadIdx.x * kRowF4);
-    float* grow = reinterpret_cast<float*>(s_grd + threadIdx.x * kRowF4);
     const float p[3] = {a.pos[i * 3], a.pos[i * 3 + 1], a.pos[i * 3 + 2]};
     const float o = gs_sigmoid(a.logit_opacity[i]);
     const float s[3] = {gs_expf(a.log_scale[i * 3]), gs_expf(a.log_scale[i * 3 + 1]),
@@ -133,6 +98,7 @@ __global__ void __launch_bounds__(kPbThreads, 4) preprocess_bwd_full_kernel(Prep
     float dS[3][3] = {{0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f}};
     bool visible_any = false;
     for (int v = 0; v < nv; v++) {
+      if (!((view_mask >> v) & 1u)) continue;
       const float* gv = a.grad2d_v[v] + i * 9;
       const float dmx = gv[0], dmy = gv[1], dA = gv[2], dB = gv[3], dC = gv[4];
       const float dcol[3] = {gv[6], gv[7], gv[8]};
@@ -280,9 +246,117 @@ __global__ void __launch_bounds__(kPbThreads, 4) preprocess_bwd_full_kernel(Prep
       }
     }
   }
+
+// One Gaussian per thread, `nviews` views (camera + grad2d each) per launch.
+// The camera-independent terms (scales, rotation, 3-D covariance) are formed
+// once; per view the position gradient and the symmetric covariance gradient
+// dSigma are summed (the scale and rotation gradients are linear in dSigma),
+// the SH gradient goes straight into the staged gradient row, and every
+// gradient row is read and written once per launch. Dynamic shared memory:
+// the SH rows and the SH-gradient rows of the block.
+// 4 CTAs per SM (its shared memory allows no more): at most 128 registers.
+// Reading the SH rows from global memory instead of staging them (half the
+// shared memory) measured slower at 4 and 5 CTAs per SM (0.297 / 0.295 vs
+// 0.279 ms per view), and at 6 CTAs the registers spill.
+__global__ void __launch_bounds__(kPbThreads, 4) preprocess_bwd_full_kernel(PreprocessBwdArgs a) {
+  extern __shared__ float4 s_dyn[];
+  float4* s_par = s_dyn;                         // SH rows
+  float4* s_grd = s_dyn + kPbThreads * kRowF4;   // SH-gradient rows
+  const int64_t base = (int64_t)blockIdx.x * kPbThreads;
+  const int64_t i = base + threadIdx.x;
+  const int cnt = (int)min((int64_t)kPbThreads, a.n - base);
+  const bool valid = i < a.n;
+  const gsc_raster_config& cfg = a.cfg;
+  const int nv = a.nviews;
+  bool any = false;
+  for (int v = 0; v < nv; v++) {
+    if (!valid) break;
+    const float* gv = a.grad2d_v[v] + i * 9;
+#pragma unroll
+    for (int k = 0; k < 9; k++) any = any || gv[k] != 0.0f;
+  }
+  if (valid && nv == 1) {  // screen-space views of a single-view call
+    const float* gv = a.grad2d_v[0] + i * 9;
+    if (a.d_mean2d) { a.d_mean2d[i * 2] = gv[0]; a.d_mean2d[i * 2 + 1] = gv[1]; }
+    if (a.d_opacity) a.d_opacity[i] = gv[5];
+    if (a.d_colors) { a.d_colors[i * 3] = gv[6]; a.d_colors[i * 3 + 1] = gv[7]; a.d_colors[i * 3 + 2] = gv[8]; }
+    if (a.d_cov2d) { a.d_cov2d[i * 3] = 0.0f; a.d_cov2d[i * 3 + 1] = 0.0f; a.d_cov2d[i * 3 + 2] = 0.0f; }
+  }
+  // every term below is linear in grad2d: blocks without gradients are done
+  if (!__syncthreads_or(any)) return;
+  stage_rows(s_par, a.sh, base, cnt);
+  stage_rows(s_grd, a.g_sh, base, cnt);
+  __syncthreads();
+
+  if (any) {
+    const float* row = reinterpret_cast<const float*>(s_par + threadIdx.x * kRowF4);
+    float* grow = reinterpret_cast<float*>(s_grd + threadIdx.x * kRowF4);
+    pbwd_full_gaussian(a, i, row, grow, 0xFFFFFFFFu);
+  }
   __syncthreads();
   unstage_rows(s_grd, a.g_sh, base, cnt);
 }
+
+// Batched backward over the active Gaussians only. A few per cent of the
+// Gaussians of a view receive a screen-space gradient (the rest are culled
+// or occluded), so one thread per Gaussian left most lanes of a warp idle
+// through each view's chain. pbwd_active_kernel lists every Gaussian with a
+// nonzero grad2d row in some view (id, mask of those views) in any order;
+// pbwd_compact_kernel runs the chain of the listed Gaussians over their
+// masked views, reading the SH and SH-gradient rows in place. Each Gaussian's
+// arithmetic is that of preprocess_bwd_full_kernel (a view whose grad2d row is
+// zero adds only zeros there).
+__global__ void __launch_bounds__(256) pbwd_active_kernel(PreprocessBwdArgs a, uint2* __restrict__ list,
+                                                          uint32_t* __restrict__ count) {
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  uint32_t mask = 0;
+  if (i < a.n) {
+    for (int v = 0; v < a.nviews; v++) {
+      const float* gv = a.grad2d_v[v] + i * 9;
+      bool nz = false;
+#pragma unroll
+      for (int k = 0; k < 9; k++) nz = nz || gv[k] != 0.0f;
+      mask |= (uint32_t)nz << v;
+    }
+  }
+  const uint32_t bal = __ballot_sync(0xffffffffu, mask != 0u);
+  if (!bal) return;
+  const int lane = threadIdx.x & 31;
+  uint32_t base = 0;
+  if (lane == 0) base = atomicAdd(count, (uint32_t)__popc(bal));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  if (mask) list[base + __popc(bal & ((1u << lane) - 1u))] = make_uint2((uint32_t)i, mask);
+}
+
+__global__ void __launch_bounds__(kPbThreads, 4) pbwd_compact_kernel(PreprocessBwdArgs a,
+                                                                     const uint2* __restrict__ list,
+                                                                     const uint32_t* __restrict__ count) {
+  const uint32_t cnt = *count;
+  for (uint32_t t = blockIdx.x * kPbThreads + threadIdx.x; t < cnt; t += gridDim.x * kPbThreads) {
+    const uint2 e = list[t];
+    const int64_t i = e.x;
+    pbwd_full_gaussian(a, i, a.sh + i * 48, a.g_sh + i * 48, e.y);
+  }
+}
+
+int launch_preprocess_bwd_compact(const PreprocessBwdArgs& a, char* scratch, int num_sms, cudaStream_t stream) {
+  if (a.n == 0) return GSC_OK;
+  if (a.n >= (1ll << 32) || a.nviews < 1 || a.nviews > kMaxBatchViews) {
+    set_error("preprocess_bwd_compact: bad size");
+    return GSC_ERR_INVALID;
+  }
+  uint32_t* count = reinterpret_cast<uint32_t*>(scratch);
+  uint2* list = reinterpret_cast<uint2*>(scratch + 256);
+  GS_CK(cudaMemsetAsync(count, 0, 4, stream));
+  pbwd_active_kernel<<<(unsigned)((a.n + 255) / 256), 256, 0, stream>>>(a, list, count);
+  GS_CK_LAUNCH("pbwd_active_kernel");
+  const int64_t grid = std::min<int64_t>((a.n + kPbThreads - 1) / kPbThreads, (int64_t)num_sms * 8);
+  pbwd_compact_kernel<<<(unsigned)grid, kPbThreads, 0, stream>>>(a, list, count);
+  GS_CK_LAUNCH("pbwd_compact_kernel");
+  return GSC_OK;
+}
+
+size_t preprocess_bwd_compact_scratch(int64_t n) { return 256 + (size_t)n * 8; }
 
 constexpr size_t kPbSmem = 2 * (size_t)kPbThreads * kRowF4 * sizeof(float4);
 
