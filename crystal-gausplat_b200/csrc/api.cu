@@ -76,7 +76,7 @@ struct gsc_frame {
   GsBuf splats, depth_pairs, depth_keys, order, pairs, block_sums, offsets, total, tiles, keys, vals, ranges, image, final_T,
       last, n_contrib, grad2d, bins, tile_order, tile_work;
   // depth-sliced binning (GSC_BIN_OCCLUDED)
-  GsBuf slice_vals[kMaxSlices], slice_ranges[kMaxSlices], skip_bits, tile_done, tile_base;
+  GsBuf slice_vals[kMaxSlices], slice_ranges[kMaxSlices], skip_bits, tile_done, tile_base, pair_total;
   bool count_pending = false;  // the lists' length is on the device (the final ranges' end)
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
@@ -524,7 +524,7 @@ GSC_API int gsc_frame_destroy(gsc_frame* f) {
   GsBuf* bufs[] = {&f->splats, &f->depth_pairs, &f->pairs, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
                    &f->n_contrib, &f->grad2d, &f->bins, &f->tile_order, &f->tile_work,
-                   &f->skip_bits, &f->tile_done, &f->tile_base};
+                   &f->skip_bits, &f->tile_done, &f->tile_base, &f->pair_total};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
   for (int k = 0; k < kMaxSlices; k++) {
@@ -583,7 +583,9 @@ int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gs
 
 const uint4* frame_bins(const gsc_frame* f) { return (const uint4*)f->bins.ptr; }
 
-int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true) {
+// count_n >= 0: the pair counts and offsets cover depth positions [0, count_n)
+// only (occluded binning counts its later slices itself).
+int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true, int64_t count_n = -1) {
   const int64_t n = f->n;
   // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and
   //    sink); packed (depth << 32 | index) words, split into keys and order
@@ -597,15 +599,17 @@ int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true) {
   }
   // 2. exact allocation in depth order: per-block pair counts and their scan
   if (n == 0) return GSC_OK;
+  const int64_t cn = count_n >= 0 ? std::min(count_n, n) : n;
+  if (cn == 0) return cudaMemsetAsync(f->total.ptr, 0, 8, ctx->stream) == cudaSuccess ? GSC_OK : GSC_ERR_CUDA;
   {
     StageScope sc(ctx, GSC_STAGE_SCAN);
     sc.kernels(1);
-    GS_TRY(launch_block_sums_gather(frame_bins(f), f->order_ptr, n,
+    GS_TRY(launch_block_sums_gather(frame_bins(f), f->order_ptr, cn,
                                     (uint32_t*)f->block_sums.ptr, ctx->stream));
   }
   StageScope sc(ctx, GSC_STAGE_SCAN);
   sc.kernels(1);
-  return launch_scan_block_sums((const uint32_t*)f->block_sums.ptr, (n + 255) / 256, (uint64_t*)f->offsets.ptr,
+  return launch_scan_block_sums((const uint32_t*)f->block_sums.ptr, (cn + 255) / 256, (uint64_t*)f->offsets.ptr,
                                 (uint64_t*)f->total.ptr, ctx->stream);
 }
 
@@ -758,6 +762,39 @@ int occlusion_slices(int64_t n, int64_t* p) {
   }
   p[++S] = n;
   return S;
+}
+
+// The depth positions the whole-view pair counting covers: every slice but
+// the last (which counts its own pairs), or everything with one slice.
+int64_t occlusion_count_end(int S, const int64_t* p) { return S >= 2 ? p[S - 1] : p[S]; }
+
+// One readback per batch: each view's pair total (from preprocess) and the
+// pair counts before its slice boundaries (from the whole-view scan), turned
+// into up[v][s], slice s's pair count before the skip test.
+int read_slice_counts(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const int* S,
+                      const int64_t (*p)[kMaxSlices + 1], uint64_t* m, uint64_t (*up)[kMaxSlices]) {
+  uint64_t* pin = (uint64_t*)ctx->pinned;  // [slot k][view], slot 0 = totals
+  for (int v = 0; v < nviews; v++) {
+    const gsc_frame* f = frames[v];
+    GS_CK(cudaMemcpyAsync(pin + v, f->pair_total.ptr, 8, cudaMemcpyDeviceToHost, ctx->stream));
+    for (int k = 1; k < S[v]; k++) {
+      // boundary k < S - 1 from the offsets; the last one is the scan's total
+      const uint64_t* src = k + 1 < S[v] ? (const uint64_t*)f->offsets.ptr + p[v][k] / 256
+                                         : (const uint64_t*)f->total.ptr;
+      GS_CK(cudaMemcpyAsync(pin + GSC_MAX_BATCH_VIEWS * k + v, src, 8, cudaMemcpyDeviceToHost, ctx->stream));
+    }
+  }
+  GS_CK(cudaStreamSynchronize(ctx->stream));
+  for (int v = 0; v < nviews; v++) {
+    m[v] = pin[v];
+    uint64_t prev = 0;
+    for (int k = 0; k < S[v]; k++) {
+      const uint64_t at = k + 1 < S[v] ? pin[GSC_MAX_BATCH_VIEWS * (k + 1) + v] : m[v];
+      up[v][k] = at - prev;
+      prev = at;
+    }
+  }
+  return GSC_OK;
 }
 
 // Binning of slice s of frame f on ctx->stream. Slice 0 uses the whole-view
@@ -977,6 +1014,12 @@ int forward_preprocess(gsc_ctx* ctx, gsc_frame* const* frames, const gsc_camera*
   a.view_key = batch_words != nullptr;
   a.depth_compact = a.view_key && depth_compact_base(cfg, &a.depth_base);
   a.contributing = cfg->binning != GSC_BIN_REFERENCE;
+  if (occlusion_binning(cfg, frames[0]))
+    for (int v = 0; v < k; v++) {
+      GS_TRY(ensure(ctx, &frames[v]->pair_total, 8));
+      GS_CK(cudaMemsetAsync(frames[v]->pair_total.ptr, 0, 8, ctx->stream));
+      a.pair_total_v[v] = (unsigned long long*)frames[v]->pair_total.ptr;
+    }
   StageScope sc(ctx, GSC_STAGE_PREPROCESS);
   sc.kernels(g->count ? 1 : 0);
   return launch_preprocess(a, ctx->stream);
@@ -993,24 +1036,13 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
   if (occlusion_binning(cfg, f) && g->count) {
     // the depth-sliced path of the batched call, with one view
     GS_TRY(forward_preprocess(ctx, &f, cam, 1, g, cfg));
-    GS_TRY(forward_sort_scan(ctx, f));
     int S[1];
     int64_t bounds[1][kMaxSlices + 1];
-    uint64_t up[1][kMaxSlices];
+    uint64_t up[1][kMaxSlices], m = 0;
     S[0] = occlusion_slices(f->n, bounds[0]);
-    uint64_t* pin = (uint64_t*)ctx->pinned;
-    GS_CK(cudaMemcpyAsync(pin, f->total.ptr, 8, cudaMemcpyDeviceToHost, ctx->stream));
-    for (int k = 1; k < S[0]; k++)
-      GS_CK(cudaMemcpyAsync(pin + k, (const uint64_t*)f->offsets.ptr + bounds[0][k] / 256, 8,
-                            cudaMemcpyDeviceToHost, ctx->stream));
-    GS_CK(cudaStreamSynchronize(ctx->stream));
-    uint64_t prev = 0;
-    for (int k = 0; k < S[0]; k++) {
-      const uint64_t at = k + 1 < S[0] ? pin[k + 1] : pin[0];
-      up[0][k] = at - prev;
-      prev = at;
-    }
-    if (num_rendered) *num_rendered = (int64_t)pin[0];
+    GS_TRY(forward_sort_scan(ctx, f, true, occlusion_count_end(S[0], bounds[0])));
+    GS_TRY(read_slice_counts(ctx, &f, 1, S, bounds, &m, up));
+    if (num_rendered) *num_rendered = (int64_t)m;
     GS_TRY(forward_sliced(ctx, &f, 1, cfg, bounds, S, up));
     if (n_contrib)
       GS_CK(cudaMemcpyAsync(n_contrib, f->n_contrib.ptr, (size_t)f->width * f->height * 4, cudaMemcpyDeviceToDevice,
@@ -1042,7 +1074,10 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
     GS_TRY(forward_prepare(ctx, frames[v], g, &cams[v], cfg, images ? images[v] : nullptr));
   }
   const int64_t n = g->count;
-  if (nviews > 1 && n > 1 && n < (1ll << 28)) {
+  const bool batched_depth = nviews > 1 && n > 1 && n < (1ll << 28);
+  uint32_t* order = nullptr;
+  if (!batched_depth) GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg));
+  if (batched_depth) {
     // One depth sort for the whole batch: view << 60 | bits(depth) << 28 |
     // index words sorted by bits [28, 64), i.e. by view, then depth; view v's
     // order is the v-th run of n indices. With the compact depth keys the
@@ -1052,7 +1087,7 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
     GS_TRY(ensure(ctx, &ctx->batch_pairs, (size_t)total * 8));
     GS_TRY(ensure(ctx, &ctx->batch_order, (size_t)total * 4));
     uint64_t* words = (uint64_t*)ctx->batch_pairs.ptr;
-    uint32_t* order = (uint32_t*)ctx->batch_order.ptr;
+    order = (uint32_t*)ctx->batch_order.ptr;
     GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg, words));
     {
       uint32_t base;
@@ -1067,43 +1102,34 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
       sc.kernels(1 + (end_bit - 28 + 7) / 8);
       GS_TRY(launch_sort_packed(ctx, words, total, 28, end_bit, nullptr, order, scratch_base(ctx), 0x0FFFFFFFu));
     }
+  }
+  // depth-sliced binning counts the pairs of its first slices here (the last
+  // slice counts its own), the view's total comes from preprocess
+  const bool occl = occlusion_binning(cfg, frames[0]);
+  int S[GSC_MAX_BATCH_VIEWS] = {};
+  int64_t bounds[GSC_MAX_BATCH_VIEWS][kMaxSlices + 1] = {};
+  for (int v = 0; v < nviews && occl; v++) S[v] = occlusion_slices(frames[v]->n, bounds[v]);
+  if (batched_depth) {
     for (int v = 0; v < nviews; v++) {
       frames[v]->order_ptr = order + (size_t)v * n;
-      GS_TRY(forward_sort_scan(ctx, frames[v], false));
+      GS_TRY(forward_sort_scan(ctx, frames[v], false, occl ? occlusion_count_end(S[v], bounds[v]) : -1));
     }
   } else {
-    GS_TRY(forward_preprocess(ctx, frames, cams, nviews, g, cfg));
-    for (int v = 0; v < nviews; v++) GS_TRY(forward_sort_scan(ctx, frames[v]));
+    for (int v = 0; v < nviews; v++)
+      GS_TRY(forward_sort_scan(ctx, frames[v], true, occl ? occlusion_count_end(S[v], bounds[v]) : -1));
   }
   // one readback of every view's pair count (and, for depth-sliced binning,
   // of the pair counts before each slice boundary)
   uint64_t m[GSC_MAX_BATCH_VIEWS] = {};
-  const bool occl = occlusion_binning(cfg, frames[0]);
-  int S[GSC_MAX_BATCH_VIEWS] = {};
-  int64_t bounds[GSC_MAX_BATCH_VIEWS][kMaxSlices + 1] = {};
   uint64_t up[GSC_MAX_BATCH_VIEWS][kMaxSlices] = {};
-  if (g->count) {
+  if (g->count && occl) {
+    GS_TRY(read_slice_counts(ctx, frames, nviews, S, bounds, m, up));
+  } else if (g->count) {
     uint64_t* pin = (uint64_t*)ctx->pinned;
-    for (int v = 0; v < nviews; v++) {
+    for (int v = 0; v < nviews; v++)
       GS_CK(cudaMemcpyAsync(pin + v, frames[v]->total.ptr, 8, cudaMemcpyDeviceToHost, ctx->stream));
-      if (occl) {
-        S[v] = occlusion_slices(frames[v]->n, bounds[v]);
-        for (int k = 1; k < S[v]; k++)
-          GS_CK(cudaMemcpyAsync(pin + GSC_MAX_BATCH_VIEWS * k + v,
-                                (const uint64_t*)frames[v]->offsets.ptr + bounds[v][k] / 256, 8,
-                                cudaMemcpyDeviceToHost, ctx->stream));
-      }
-    }
     GS_CK(cudaStreamSynchronize(ctx->stream));
     std::memcpy(m, ctx->pinned, 8 * (size_t)nviews);
-    for (int v = 0; v < nviews && occl; v++) {
-      uint64_t prev = 0;
-      for (int k = 0; k < S[v]; k++) {
-        const uint64_t at = k + 1 < S[v] ? pin[GSC_MAX_BATCH_VIEWS * (k + 1) + v] : m[v];
-        up[v][k] = at - prev;
-        prev = at;
-      }
-    }
   }
   if (occl && g->count) {
     for (int v = 0; v < nviews; v++)

@@ -39,6 +39,8 @@ struct PreprocessArgs {
   // depth-ordered gathers of the pair counting and the emission read:
   // {x0, y0, rect width, pair count}, {mask low, mask high, 0, 0}
   uint4* bin_v[kMaxBatchViews];
+  // if set: per view, += the pairs every Gaussian emits (zeroed by the host)
+  unsigned long long* pair_total_v[kMaxBatchViews];
   float* mean2d;
   float* cov2d;
   float* conic;

@@ -174,6 +174,10 @@ __global__ void __launch_bounds__(kPreThreads, GS_PRE_MIN_CTAS) preprocess_kerne
     }
 
     const uint32_t emit = a.contributing ? nt : tiles;
+    if (a.pair_total_v[v]) {  // the view's pair count (occluded binning counts only its first slices)
+      const uint32_t ws = __reduce_add_sync(0xffffffffu, i < n ? emit : 0u);
+      if ((threadIdx.x & 31) == 0 && ws) atomicAdd(a.pair_total_v[v], (unsigned long long)ws);
+    }
     if (i < n) {
       reinterpret_cast<float4*>(a.splats_v[v])[i * 3 + 2] =
           make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
