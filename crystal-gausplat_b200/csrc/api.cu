@@ -45,7 +45,9 @@ int ensure(gsc_ctx* ctx, GsBuf* b, size_t bytes) {
   return GSC_OK;
 }
 
-int scratch_reserve(gsc_ctx* ctx, size_t bytes) { return ensure(ctx, &ctx->scratch, bytes); }
+int scratch_reserve(gsc_ctx* ctx, size_t bytes) {
+  return ensure(ctx, ctx->cur_scratch ? ctx->cur_scratch : &ctx->scratch, bytes);
+}
 
 static float power_cut_of(float alpha_min) {
   if (!(alpha_min > 0.0f)) return -INFINITY;
@@ -144,6 +146,13 @@ GSC_API int gsc_destroy(gsc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch.ptr) cudaFree(ctx->scratch.ptr);
+  if (ctx->scratch_alt.ptr) cudaFree(ctx->scratch_alt.ptr);
+  if (ctx->bin2) {
+    cudaStreamSynchronize(ctx->bin2);
+    for (auto& e : ctx->bin2_ev)
+      if (e) cudaEventDestroy(e);
+    cudaStreamDestroy(ctx->bin2);
+  }
   if (ctx->batch_pairs.ptr) cudaFree(ctx->batch_pairs.ptr);
   if (ctx->batch_order.ptr) cudaFree(ctx->batch_order.ptr);
   if (ctx->side) {
@@ -926,6 +935,9 @@ int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, i
 // on the caller's stream, compositing on the side stream, slice by slice
 // across the views, so that view v's compositing overlaps the binning of the
 // next views and slice s + 1 of a view waits only for its own slice s.
+#ifndef GS_BIN_STREAMS
+#define GS_BIN_STREAMS 2
+#endif
 int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc_raster_config* cfg,
                    const int64_t (*p)[kMaxSlices + 1], const int* S, const uint64_t (*up)[kMaxSlices]) {
   if (!ctx->side) {
@@ -953,6 +965,19 @@ int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc
     f->num_keys = (int64_t)total;
   }
   cudaStream_t main_stream = ctx->stream;
+  // views alternate between two binning streams (each with its own sort
+  // scratch), so the latency-bound sorts of two views overlap
+  const int nbin = GS_BIN_STREAMS > 1 && nviews > 1 ? 2 : 1;
+  cudaStream_t bin_stream[2] = {main_stream, main_stream};
+  if (nbin == 2) {
+    if (!ctx->bin2) {
+      GS_CK(cudaStreamCreateWithFlags(&ctx->bin2, cudaStreamNonBlocking));
+      for (auto& e : ctx->bin2_ev) GS_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    bin_stream[1] = ctx->bin2;
+    GS_CK(cudaEventRecord(ctx->bin2_ev[0], main_stream));  // bin2 follows the caller's earlier work
+    GS_CK(cudaStreamWaitEvent(ctx->bin2, ctx->bin2_ev[0], 0));
+  }
   int Smax = 0;
   for (int v = 0; v < nviews; v++) Smax = std::max(Smax, S[v]);
   int rc = GSC_OK;
@@ -960,21 +985,30 @@ int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc
     for (int v = 0; v < nviews && rc == GSC_OK; v++) {
       if (s >= S[v]) continue;
       gsc_frame* f = frames[v];
-      if (s > 0) GS_CK(cudaStreamWaitEvent(main_stream, ctx->comp_ev[v], 0));
+      const int lane = v % nbin;
+      cudaStream_t bs = bin_stream[lane];
+      ctx->stream = bs;
+      ctx->cur_scratch = lane ? &ctx->scratch_alt : &ctx->scratch;
+      if (s > 0) GS_CK(cudaStreamWaitEvent(bs, ctx->comp_ev[v], 0));
       rc = sliced_bin(ctx, f, s, p[v], up[v][s]);
       if (rc) break;
-      GS_CK(cudaEventRecord(ctx->bin_ev[v], main_stream));
+      GS_CK(cudaEventRecord(ctx->bin_ev[v], bs));
       GS_CK(cudaStreamWaitEvent(ctx->side, ctx->bin_ev[v], 0));
       ctx->stream = ctx->side;
+      ctx->cur_scratch = nullptr;
       rc = sliced_composite(ctx, f, cfg, s, S[v]);
-      ctx->stream = main_stream;
       GS_CK(cudaEventRecord(ctx->comp_ev[v], ctx->side));
     }
   }
   ctx->stream = main_stream;
-  // the caller's stream waits for every compositing
+  ctx->cur_scratch = nullptr;
+  // the caller's stream waits for every compositing and the second binning stream
   GS_CK(cudaEventRecord(ctx->side_ev[GSC_MAX_BATCH_VIEWS], ctx->side));
   GS_CK(cudaStreamWaitEvent(main_stream, ctx->side_ev[GSC_MAX_BATCH_VIEWS], 0));
+  if (nbin == 2) {
+    GS_CK(cudaEventRecord(ctx->bin2_ev[1], ctx->bin2));
+    GS_CK(cudaStreamWaitEvent(main_stream, ctx->bin2_ev[1], 0));
+  }
   return rc;
 }
 

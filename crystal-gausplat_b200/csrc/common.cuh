@@ -164,6 +164,12 @@ struct gsc_ctx {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   GsBuf scratch;              // per-call temporary storage (sort double buffer, ...)
+  // depth-sliced binning bins two views at once, on `stream` and on `bin2`,
+  // each with its own scratch (cur_scratch: the one of the stream in use)
+  GsBuf scratch_alt;
+  GsBuf* cur_scratch = nullptr;
+  cudaStream_t bin2 = nullptr;
+  cudaEvent_t bin2_ev[2] = {};
   GsBuf batch_pairs;          // batched forward: every view's packed depth words
   GsBuf batch_order;          // batched forward: every view's depth order
   // batched forward: compositing of view v on `side` overlaps the binning of
@@ -211,7 +217,9 @@ int ensure(gsc_ctx* ctx, GsBuf* b, size_t bytes);
 // Scratch carve-out: returns a 256-byte-aligned pointer inside ctx->scratch,
 // growing it (which invalidates earlier carve-outs of the same call) first.
 int scratch_reserve(gsc_ctx* ctx, size_t bytes);
-inline char* scratch_base(gsc_ctx* ctx) { return (char*)ctx->scratch.ptr; }
+inline char* scratch_base(gsc_ctx* ctx) {
+  return (char*)(ctx->cur_scratch ? ctx->cur_scratch->ptr : ctx->scratch.ptr);
+}
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace gs
