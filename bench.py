@@ -295,7 +295,7 @@ def packed_sort_bytes(bits, hist=True, hi=False):
 OCC_FIRST_SLICE = 0.2
 
 
-def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False):
+def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False, views_per_step=1):
     """Algorithmic work of each stage for ONE view: (bound, bytes or flops).
 
     Binning of a view = a stable depth sort of the N Gaussians (per view: 32 bits,
@@ -307,7 +307,9 @@ def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False):
     `binned`: pairs emitted and sorted per view (with occluded binning, those
     of both depth slices); `kept`: pairs in the final lists. The preprocess
     and its backward run once per `batch` views: parameters read once,
-    gradient rows read and written once, one grad2d row per view."""
+    gradient rows read and written once, one grad2d row per view. Adam runs
+    once per step over every parameter: its share of one view is the step's
+    bytes over the `views_per_step` this rank renders."""
     tb = end_bit - 32
     depth_bits = 28 + max(1, (batch - 1).bit_length()) if batch > 1 else 32
     later = (1.0 - OCC_FIRST_SLICE) * n if occluded else 0.0
@@ -327,7 +329,7 @@ def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False):
         "composite_fwd": ("fp32", FWD_FLOP_PER_PGE * pge),
         "composite_bwd": ("fp32", BWD_FLOP_PER_PGE * pge),
         "preprocess_bwd": ("hbm", (3 * PARAM_ROW_B / batch + GRAD2D_B) * n),
-        "adam": ("hbm", ADAM_B * n),
+        "adam": ("hbm", ADAM_B * n / views_per_step),
     }
 
 
@@ -471,7 +473,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     end_bit = 32 + int(math.ceil(math.log2(tiles)))
     binned, kept = (c / (args.steps * my_views) for c in profile_pairs(gs, ctx))
     occluded = rcfg.binning == gs._abi.GSC_BIN_OCCLUDED
-    work = stage_work(cfg["n"], binned, kept, pge, tiles, end_bit, batch=tr.batch, occluded=occluded)
+    work = stage_work(cfg["n"], binned, kept, pge, tiles, end_bit, batch=tr.batch, occluded=occluded,
+                      views_per_step=my_views)
     roof = rooflines(stats, work, peaks, args.steps * my_views)
 
     e2e = None

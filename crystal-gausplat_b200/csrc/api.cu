@@ -967,7 +967,10 @@ int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc
   cudaStream_t main_stream = ctx->stream;
   // views alternate between two binning streams (each with its own sort
   // scratch), so the latency-bound sorts of two views overlap
-  const int nbin = GS_BIN_STREAMS > 1 && nviews > 1 ? 2 : 1;
+  // Under per-stage tracing everything runs in order on the caller's stream,
+  // so that each stage's events time that stage alone.
+  const bool serial = ctx->profiling;
+  const int nbin = GS_BIN_STREAMS > 1 && nviews > 1 && !serial ? 2 : 1;
   cudaStream_t bin_stream[2] = {main_stream, main_stream};
   if (nbin == 2) {
     if (!ctx->bin2) {
@@ -994,10 +997,11 @@ int forward_sliced(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const gsc
       if (rc) break;
       GS_CK(cudaEventRecord(ctx->bin_ev[v], bs));
       GS_CK(cudaStreamWaitEvent(ctx->side, ctx->bin_ev[v], 0));
-      ctx->stream = ctx->side;
+      cudaStream_t cs = serial ? bs : ctx->side;
+      ctx->stream = cs;
       ctx->cur_scratch = nullptr;
       rc = sliced_composite(ctx, f, cfg, s, S[v]);
-      GS_CK(cudaEventRecord(ctx->comp_ev[v], ctx->side));
+      GS_CK(cudaEventRecord(ctx->comp_ev[v], cs));
     }
   }
   ctx->stream = main_stream;

@@ -66,6 +66,8 @@ def test_bench_work_model():
     # batched depth words: 28 + 3 bits (4 passes); tile sort: digits counted by emission
     assert w8["sort"] == ("hbm", (8 + 16 * 3 + 12) * 1000 + (16 + 12) * 5000)
     assert w8["ranges"] == ("hbm", 8 * 8160)
+    # Adam: once per step over every parameter, shared by the step's views
+    assert bench.stage_work(1000, 1, 1, 1, 8160, 45, views_per_step=4)["adam"] == ("hbm", 1652 * 1000 / 4)
     # occluded binning: the binned pairs are sorted, the later slice gathers again,
     # two slices of ranges and the kept ids copied
     wo = bench.stage_work(1000, 2000, 300, 10 ** 6, 8160, 45, batch=8, occluded=True)
