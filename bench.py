@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1 gradient exchange: fused NVLink reduce+Adam+broadcast kernel, or NCCL all-reduce")
+    ap.add_argument("--multicast", default="auto", choices=["auto", "on", "off"],
+                    help="fused exchange through the NVSwitch multicast object (auto: from 4 ranks on) or "
+                         "over plain peer loads/stores")
     ap.add_argument("--views", type=int, default=None,
                     help="profiling knob: override the number of views of --config (small ncu cases)")
     ap.add_argument("--binning", default="occluded", choices=["occluded", "contributing", "reference"],
@@ -420,7 +423,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     g = gs.Gaussian3D(arrays, device=dev)
     cams = make_cameras(gs, cfg)
     rcfg = gs.default_config(binning=binning_of(gs, args), t_stop=args.t_stop)
-    tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg, exchange=args.exchange)
+    tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg, exchange=args.exchange,
+                                         multicast={"auto": "auto", "on": True, "off": False}[args.multicast])
     host_t = make_targets(cfg, tr.lo, tr.hi)
     dev_t = host_t.to(dev)
     ctx = gs.context(dev)
@@ -505,7 +509,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Gaussians, poses and U[0,1] targets per BASELINE.json)",
             "config": workload_config(args, cfg, world),
-            "workload_stats": {"exchange": tr.exchange, "backward_batch_views": tr.batch,
+            "workload_stats": {"exchange": tr.exchange, "exchange_path": tr.exchange_path,
+                               "backward_batch_views": tr.batch,
                                "contributing_pairs_per_view": round(keys_per_view),
                                "binned_pairs_per_view": round(binned), "kept_pairs_per_view": round(kept),
                                "pge_per_view": round(pge),

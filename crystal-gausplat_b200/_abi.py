@@ -100,7 +100,7 @@ class DpAdamArgs(C.Structure):
                 ("ngroups", C.c_int32), ("offset", C.c_int64 * 8), ("numel", C.c_int64 * 8),
                 ("lr", C.c_float * 8), ("weight_decay", C.c_float * 8),
                 ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float), ("step", C.c_int32),
-                ("grad_scale", C.c_float)]
+                ("grad_scale", C.c_float), ("mc_grads", P), ("mc_params", P)]
 
 
 class DpBarrierArgs(C.Structure):

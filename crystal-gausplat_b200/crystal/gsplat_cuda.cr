@@ -143,6 +143,8 @@ lib GSCuda
     eps : Float32
     step : Int32
     grad_scale : Float32
+    mc_grads : Float32*
+    mc_params : Float32*
   end
 
   struct DpBarrierArgs

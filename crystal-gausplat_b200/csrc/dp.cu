@@ -9,6 +9,13 @@
 // from each peer and its parameters out once to each peer -- the bytes of a
 // reduce-scatter plus an all-gather -- with the optimiser arithmetic done once
 // per element instead of on every replica.
+//
+// With NVLink multicast addresses of the two arenas (an NVSwitch multicast
+// object bound to every rank's arena) the same kernel sums a gradient chunk
+// with one multimem.ld_reduce (the switch reads the ranks' copies and adds
+// them) and writes the new parameter chunk with one multimem.st (the switch
+// writes it into every replica): per NVLink direction a rank then moves
+// (1 + 1/P) arenas instead of 2 (P - 1)/P.
 #include <cmath>
 #include <cstring>
 
@@ -38,7 +45,30 @@ struct DpArgsDev {
   float beta1, beta2, eps, bc1, bc2, grad_scale;
   int64_t chunk_lo, chunk_hi;  // this rank's shard
   const uint32_t* err;         // the context's error word: skip all work after a failed barrier
+  float* mc_grads;             // multicast addresses (both or neither)
+  float* mc_params;
 };
+
+// Sum over every rank's copy, added by the NVSwitch (fp32).
+__device__ __forceinline__ float4 mc_sum4(const float* addr) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(addr) : "memory");
+  return r;
+}
+__device__ __forceinline__ float mc_sum1(const float* addr) {
+  float r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(r) : "l"(addr) : "memory");
+  return r;
+}
+// One store that lands in every rank's copy.
+__device__ __forceinline__ void mc_store4(float* addr, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+               ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+__device__ __forceinline__ void mc_store1(float* addr, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
 
 __device__ __forceinline__ float dp_adam(float p, float g, float& m, float& v, const DpArgsDev& a, int gi) {
   if (a.weight_decay[gi] > 0.0f) p = p * a.decay[gi];
@@ -50,6 +80,7 @@ __device__ __forceinline__ float dp_adam(float p, float g, float& m, float& v, c
   return p - a.lr[gi] * mh / (sqrtf(vh) + a.eps);
 }
 
+template <bool MC>
 __global__ void __launch_bounds__(256) dp_adam_kernel(DpArgsDev a) {
   const int64_t chunk = a.chunk_lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (chunk >= a.chunk_hi) return;
@@ -62,10 +93,15 @@ __global__ void __launch_bounds__(256) dp_adam_kernel(DpArgsDev a) {
   const int64_t cnt = min((int64_t)4, a.numel[gi] - first);
   const int64_t off = a.offset[gi] + first;  // float index in every arena
   if (cnt == 4) {
-    float4 g = *reinterpret_cast<const float4*>(a.peer_grads[0] + off);
-    for (int p = 1; p < a.nranks; p++) {
-      const float4 h = *reinterpret_cast<const float4*>(a.peer_grads[p] + off);
-      g.x += h.x; g.y += h.y; g.z += h.z; g.w += h.w;
+    float4 g;
+    if (MC) {
+      g = mc_sum4(a.mc_grads + off);
+    } else {
+      g = *reinterpret_cast<const float4*>(a.peer_grads[0] + off);
+      for (int p = 1; p < a.nranks; p++) {
+        const float4 h = *reinterpret_cast<const float4*>(a.peer_grads[p] + off);
+        g.x += h.x; g.y += h.y; g.z += h.z; g.w += h.w;
+      }
     }
     float4 pr = *reinterpret_cast<const float4*>(a.peer_params[a.rank] + off);  // local replica
     float4 m = *reinterpret_cast<float4*>(a.m + off);
@@ -76,16 +112,25 @@ __global__ void __launch_bounds__(256) dp_adam_kernel(DpArgsDev a) {
     pr.w = dp_adam(pr.w, g.w, m.w, v.w, a, gi);
     *reinterpret_cast<float4*>(a.m + off) = m;
     *reinterpret_cast<float4*>(a.v + off) = v;
-    for (int p = 0; p < a.nranks; p++) *reinterpret_cast<float4*>(a.peer_params[p] + off) = pr;
+    if (MC) mc_store4(a.mc_params + off, pr);
+    else
+      for (int p = 0; p < a.nranks; p++) *reinterpret_cast<float4*>(a.peer_params[p] + off) = pr;
   } else {
     for (int64_t k = 0; k < cnt; k++) {
-      float g = a.peer_grads[0][off + k];
-      for (int p = 1; p < a.nranks; p++) g += a.peer_grads[p][off + k];
+      float g;
+      if (MC) {
+        g = mc_sum1(a.mc_grads + off + k);
+      } else {
+        g = a.peer_grads[0][off + k];
+        for (int p = 1; p < a.nranks; p++) g += a.peer_grads[p][off + k];
+      }
       float m = a.m[off + k], v = a.v[off + k];
       const float pr = dp_adam(a.peer_params[a.rank][off + k], g, m, v, a, gi);
       a.m[off + k] = m;
       a.v[off + k] = v;
-      for (int p = 0; p < a.nranks; p++) a.peer_params[p][off + k] = pr;
+      if (MC) mc_store1(a.mc_params + off + k, pr);
+      else
+        for (int p = 0; p < a.nranks; p++) a.peer_params[p][off + k] = pr;
     }
   }
 }
@@ -169,6 +214,11 @@ extern "C" GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* in
              "gsc_dp_adam_step: moments must be 16-byte aligned");
   a.m = in->m;
   a.v = in->v;
+  GS_REQUIRE(!in->mc_grads == !in->mc_params, "gsc_dp_adam_step: give both multicast addresses or neither");
+  GS_REQUIRE(((uintptr_t)in->mc_grads & 15u) == 0 && ((uintptr_t)in->mc_params & 15u) == 0,
+             "gsc_dp_adam_step: multicast addresses must be 16-byte aligned");
+  a.mc_grads = in->mc_grads;
+  a.mc_params = in->mc_params;
   a.ngroups = in->ngroups;
   int64_t run = 0;
   for (int i = 0; i < in->ngroups; i++) {
@@ -192,7 +242,9 @@ extern "C" GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* in
   if (n <= 0) return GSC_OK;
   StageScope sc(ctx, GSC_STAGE_ADAM);
   sc.kernels(1);
-  dp_adam_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(a);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (a.mc_grads) dp_adam_kernel<true><<<blocks, 256, 0, ctx->stream>>>(a);
+  else dp_adam_kernel<false><<<blocks, 256, 0, ctx->stream>>>(a);
   GS_CK_LAUNCH("dp_adam_kernel");
   return GSC_OK;
 }

@@ -42,11 +42,33 @@ def _peer_ptrs(t, hdl):
     return [p + off for p in hdl.buffer_ptrs]
 
 
+# smallest world size at which multicast="auto" uses the NVSwitch multicast form
+MULTICAST_MIN_RANKS = 4
+
+
+def _multicast_ptr(t, hdl):
+    """NVLink multicast address of tensor t inside a symmetric-memory
+    buffer, or 0 when the buffer has no multicast object."""
+    try:
+        mc = int(hdl.multicast_ptr)
+    except (AttributeError, RuntimeError, TypeError):
+        return 0
+    if not mc:
+        return 0
+    return mc + (t.data_ptr() - hdl.buffer_ptrs[hdl.rank])
+
+
 class DataParallelTrainer:
     """exchange="nccl": all-reduce of the gradient arena, then Adam on every
     replica. exchange="fused": gsc_dp_adam_step -- each rank sums its shard of
     the peers' gradients over NVLink, applies Adam once and stores the new
-    parameters into every replica (arenas in torch symmetric memory).
+    parameters into every replica (arenas in torch symmetric memory);
+    multicast=True does the sum and the stores through the NVSwitch's
+    multicast object where the box has one (exchange_path "multimem", else
+    "peer"). Per NVLink direction the multicast form moves (1 + 1/P) arenas
+    and the peer form 2 (P - 1)/P: multicast="auto" takes the multicast form
+    from P = MULTICAST_MIN_RANKS ranks on (at P = 2 it measured 1.85 against
+    1.05 ms per 3M-Gaussian exchange).
 
     loss="l1": the L1 gradient fused into the backward compositing (the
     benchmark configurations). loss="combined": Trainer#train_step's
@@ -55,7 +77,7 @@ class DataParallelTrainer:
 
     def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl",
                  loss="l1", lambda_ssim=0.2, batch_views=_abi.GSC_MAX_BATCH_VIEWS,
-                 barrier_timeout_s=60.0):
+                 barrier_timeout_s=60.0, multicast="auto"):
         self.g = gaussians
         self.cameras = cameras
         self.cfg = config
@@ -72,6 +94,8 @@ class DataParallelTrainer:
         self.grads = RasterizerGradients(gaussians, arena=grad_arena, screen=False)
         self.opt = Adam.for_gaussians(gaussians, self.grads, lrs)
         self.barrier_timeout_s = barrier_timeout_s
+        self.multicast = multicast
+        self.exchange_path = None
         if self.exchange == "fused":
             self._setup_fused()
         # batch_views > 1: compositing backward per view, then one preprocess
@@ -169,6 +193,17 @@ class DataParallelTrainer:
             a.weight_decay[i] = self.opt.groups[i]["weight_decay"]
         a.beta1, a.beta2, a.eps = self.opt.beta1, self.opt.beta2, self.opt.eps
         a.grad_scale = 1.0 / len(self.cameras)
+        # NVSwitch multicast (multimem loads with in-switch sums, multimem
+        # stores into every replica) where the arenas are bound to a multicast
+        # object; otherwise plain peer loads and stores
+        use_mc = self.world >= MULTICAST_MIN_RANKS if self.multicast == "auto" else bool(self.multicast)
+        mc_g = _multicast_ptr(self.grads.arena, self.hdl_grads) if use_mc else 0
+        mc_p = _multicast_ptr(g.arena, self.hdl_params) if use_mc else 0
+        if mc_g and mc_p:
+            a.mc_grads, a.mc_params = mc_g, mc_p
+            self.exchange_path = "multimem"
+        else:
+            self.exchange_path = "peer"
         self.dp_args = a
         # bounded cross-rank barrier (gsc_dp_barrier) over one flag word per
         # rank in symmetric memory; every barrier call uses the next epoch

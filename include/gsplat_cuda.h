@@ -318,7 +318,15 @@ GSC_API int gsc_adam_step(gsc_ctx* ctx, const gsc_adam_group* groups, int32_t ng
  * complete before the call and the peers must not read parameters until every
  * rank's call has finished (the caller fences both with a cross-rank
  * barrier). Groups are [offset, offset + numel) float ranges of the arenas;
- * offsets must be multiples of 4. */
+ * offsets must be multiples of 4.
+ * mc_grads / mc_params (optional, both or neither): NVLink multicast
+ * addresses of the gradient and parameter arenas (an NVSwitch multicast
+ * object bound to every rank's arena, e.g. torch symmetric memory's
+ * multicast_ptr), 16-byte aligned. With them the shard's gradient sum is one
+ * multimem.ld_reduce per float4 (the switch adds the ranks' values in fp32,
+ * in an order of its own) and each new parameter float4 is one multimem.st
+ * that lands in every replica: per NVLink direction a rank moves
+ * (1 + 1/nranks) arenas instead of 2 (nranks - 1)/nranks. */
 #define GSC_DP_MAX_RANKS 8
 typedef struct gsc_dp_adam_args {
   int32_t nranks;
@@ -335,6 +343,8 @@ typedef struct gsc_dp_adam_args {
   float beta1, beta2, eps;
   int32_t step;
   float grad_scale;
+  float* mc_grads;
+  float* mc_params;
 } gsc_dp_adam_args;
 GSC_API int gsc_dp_adam_step(gsc_ctx* ctx, const gsc_dp_adam_args* args);
 

@@ -82,20 +82,22 @@ def gpu_rank(rank, world, port, out_dir, steps=2):
     targets = [torch.from_numpy(np.random.default_rng(200 + v).uniform(0, 1, (96, 128, 3))
                                 .astype(np.float32)).to(dev) for v in range(len(cams))]
     cfg = gs.default_config()
-    out = {}
-    for mode in ("nccl", "fused"):
+    paths = {}
+    # "fused": peer loads and stores; "multicast": the NVSwitch multicast
+    # object where the box has one (else the same peer path)
+    for mode, exchange, mc in (("nccl", "nccl", False), ("fused", "fused", False),
+                               ("multicast", "fused", True)):
         g = gs.Gaussian3D(arrays, device=dev)
-        tr = trainer.DataParallelTrainer(g, cams, cfg, process_group=dist.group.WORLD, exchange=mode)
+        tr = trainer.DataParallelTrainer(g, cams, cfg, process_group=dist.group.WORLD, exchange=exchange,
+                                         multicast=mc)
         for _ in range(steps):
             tr.step(lambda v: targets[v])
-        if mode == "fused":
+        if exchange == "fused":
             tr.check()  # no cross-rank wait gave up
         torch.cuda.synchronize()
-        out[mode] = g.arena.detach().cpu().numpy().copy()
-        out[mode + "_loss"] = float(tr.loss.item())
-    np.save(os.path.join(out_dir, f"gpu_rank{rank}_nccl.npy"), out["nccl"])
-    np.save(os.path.join(out_dir, f"gpu_rank{rank}_fused.npy"), out["fused"])
+        np.save(os.path.join(out_dir, f"gpu_rank{rank}_{mode}.npy"), g.arena.detach().cpu().numpy().copy())
+        paths[mode] = tr.exchange_path
     with open(os.path.join(out_dir, f"gpu_rank{rank}.status"), "w") as f:
-        f.write("ok")
+        f.write("ok " + str(paths.get("multicast")))
     dist.barrier()
     dist.destroy_process_group()

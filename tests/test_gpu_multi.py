@@ -1,6 +1,7 @@
 """Two-GPU test of the fused data-parallel exchange (gsc_dp_adam_step): after
-two training steps the fused path leaves every replica with identical
-parameters, equal (fp32 summation order aside) to all-reduce + Adam."""
+two training steps the fused path -- over peer loads and stores, and over the
+NVSwitch multicast object where the box has one -- leaves every replica with
+identical parameters, equal (fp32 summation order aside) to all-reduce + Adam."""
 import multiprocessing as mp
 import os
 import socket
@@ -36,9 +37,14 @@ def test_fused_exchange_matches_allreduce(tmp_path):
             p.kill()
             p.join()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    n0, f0 = np.load(tmp_path / "gpu_rank0_nccl.npy"), np.load(tmp_path / "gpu_rank0_fused.npy")
-    n1, f1 = np.load(tmp_path / "gpu_rank1_nccl.npy"), np.load(tmp_path / "gpu_rank1_fused.npy")
-    np.testing.assert_array_equal(f0, f1)           # one writer per element: replicas identical
+    n0, n1 = (np.load(tmp_path / f"gpu_rank{r}_nccl.npy") for r in range(2))
     np.testing.assert_array_equal(n0, n1)
-    init = np.asarray(n0)  # params moved: compare the update with a relative bar
-    assert np.max(np.abs(f0 - n0)) <= 1e-5 * max(1.0, float(np.abs(init).max()))
+    scale = max(1.0, float(np.abs(n0).max()))
+    for mode in ("fused", "multicast"):
+        f0, f1 = (np.load(tmp_path / f"gpu_rank{r}_{mode}.npy") for r in range(2))
+        np.testing.assert_array_equal(f0, f1)  # one writer per element: replicas identical
+        # equal to all-reduce + Adam up to the fp32 order of the two-rank sum
+        assert np.max(np.abs(f0 - n0)) <= 1e-5 * scale, mode
+    path = (tmp_path / "gpu_rank0.status").read_text().split()[1]
+    assert path in ("multimem", "peer")
+    print("multicast exchange path:", path)
