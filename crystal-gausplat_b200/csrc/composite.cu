@@ -74,6 +74,19 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 #ifndef GS_BWD_WARP_HI
 #define GS_BWD_WARP_HI 1
 #endif
+#ifndef GS_BWD_FAST_EXP
+#define GS_BWD_FAST_EXP 1
+#endif
+#ifndef GS_BWD_FAST_OMAX  // opacity bound of the hardware exponential (below alpha_max)
+#define GS_BWD_FAST_OMAX 0.98f
+#endif
+// e^x as 2^(x log2 e) on the hardware's approximate base-2 exponential
+// (subnormal results flushed to zero; they lie far below any accepted alpha).
+__device__ __forceinline__ float exp_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.44269504088896341f));
+  return y;
+}
 #ifndef GS_BWD_DIRECT
 #define GS_BWD_DIRECT 2
 #endif
@@ -287,18 +300,38 @@ struct BwdPixel {
 // adds the conic gradient, the alpha clamp and the corrected running colour).
 template <bool FULL>
 __device__ __forceinline__ bool bwd_pixel(BwdPixel& P, uint32_t idx, float4 g0, float4 g1, float g2,
-                                          float cut, float amin, float amax, bool short_exp, float dx, float dxxa,
-                                          float v[9]) {
+                                          float cut, float amin, float amax, float amin_lo, float amin_hi,
+                                          bool short_exp, bool fast, float dx, float dxxa, float v[9]) {
   if (!(P.inside && idx < P.hi)) return false;
   // dx and dx dx (-A/2) are shared by the thread's pixels (one column)
   const float dy = P.pyf - g0.y;
   const float power = fmaf(dy * dy, g1.x, fmaf(dx * dy, g0.w, dxxa));  // == forward's power
   if (power > 0.0f || power < cut) return false;
-  // Same exponential and tests as the forward, so the accepted set matches it.
-  const float G = short_exp ? gs_expf_pixel(power) : gs_expf(power);
-  const float alpha = fminf(amax, g1.y * G);
-  if (alpha < amin) return false;
   const float o = g1.y;
+  float G, alpha;
+#if GS_BWD_FAST_EXP
+  if (fast) {
+    // o < GS_BWD_FAST_OMAX < alpha_max: o G never reaches the clamp, and G
+    // is the hardware exponential (ex2.approx of power * log2 e, about 2e-7
+    // relative): the gradients only need to be within tolerance. Where o G
+    // falls within 1e-5 of alpha_min the forward's exponential decides
+    // instead, so that the accepted set is exactly the forward's.
+    G = exp_approx(power);
+    alpha = o * G;
+    if (alpha < amin_hi) {
+      if (alpha < amin_lo) return false;
+      G = short_exp ? gs_expf_pixel(power) : gs_expf(power);
+      alpha = o * G;
+      if (alpha < amin) return false;
+    }
+  } else
+#endif
+  {
+    // Same exponential and tests as the forward, so the accepted set matches it.
+    G = short_exp ? gs_expf_pixel(power) : gs_expf(power);
+    alpha = fminf(amax, o * G);
+    if (alpha < amin) return false;
+  }
   // From here on the gradients only need to be within tolerance, so products
   // and sums are fused (explicit fmaf; the file is built without contraction).
   // T_before = T / (1 - alpha) and dL/dalpha = T_before c.g - (acc / (1 - alpha)).g,
@@ -365,6 +398,8 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
   const float4* __restrict__ splats = reinterpret_cast<const float4*>(a.splats);
   const float amin = a.alpha_min, amax = a.alpha_max, cut = a.power_cut;
   const bool short_exp = cut >= -87.0f;
+  const float amin_lo = amin * (1.0f - 1e-5f), amin_hi = amin * (1.0f + 1e-5f);  // exact-decision band
+  const float fast_omax = fminf(GS_BWD_FAST_OMAX, amax * (1.0f - 1e-5f));
 
   BwdPixel P[kBwdPix];
   const float pxf = (float)(tx * GS_TILE + (tid & 15)) + 0.5f;  // the thread's pixel column
@@ -475,9 +510,11 @@ __global__ void __launch_bounds__(kBwdThreads, GS_BWD_MIN_CTAS) composite_bwd_ke
       for (int k = 0; k < 9; k++) v[k] = 0.0f;
       bool ok = false;
       const float dx = pxf - g0.x, dxxa = dx * dx * g0.z;
+      const bool fast = g1.y < fast_omax;  // the same for every lane
 #pragma unroll
       for (int h = 0; h < kBwdPix; h++)
-        ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2.x, g2.y, amin, amax, short_exp, dx, dxxa, v);
+        ok |= bwd_pixel<FULL>(P[h], idx, g0, g1, g2.x, g2.y, amin, amax, amin_lo, amin_hi, short_exp, fast, dx,
+                              dxxa, v);
       const uint32_t hits = __ballot_sync(0xffffffffu, ok);
 #if GS_BWD_DIRECT > 0
       if (hits && __popc(hits) <= GS_BWD_DIRECT) {
