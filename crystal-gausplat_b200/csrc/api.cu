@@ -635,7 +635,6 @@ int forward_bin(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, uint64
     ctx->prof_binned += m;
     ctx->prof_kept += m;
   }
-  const float* splats = (const float*)f->splats.ptr;
   GS_TRY(ensure(ctx, &f->tiles, (size_t)m * 4 + 4));
   GS_TRY(ensure(ctx, &f->vals, (size_t)m * 4 + 4));
   uint32_t* tiles = (uint32_t*)f->tiles.ptr;

@@ -266,7 +266,6 @@ __global__ void __launch_bounds__(kPbThreads, 4) preprocess_bwd_full_kernel(Prep
   const int64_t i = base + threadIdx.x;
   const int cnt = (int)min((int64_t)kPbThreads, a.n - base);
   const bool valid = i < a.n;
-  const gsc_raster_config& cfg = a.cfg;
   const int nv = a.nviews;
   bool any = false;
   for (int v = 0; v < nv; v++) {
