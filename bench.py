@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1 gradient exchange: fused NVLink reduce+Adam+broadcast kernel, or NCCL all-reduce")
+    ap.add_argument("--no-tile-hints", action="store_true",
+                    help="occluded binning without each view's per-tile depth cut from its previous forward")
     ap.add_argument("--multicast", default="auto", choices=["auto", "on", "off"],
                     help="fused exchange through the NVSwitch multicast object (auto: from 4 ranks on) or "
                          "over plain peer loads/stores")
@@ -424,7 +426,8 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     cams = make_cameras(gs, cfg)
     rcfg = gs.default_config(binning=binning_of(gs, args), t_stop=args.t_stop)
     tr = trainer_mod.DataParallelTrainer(g, cams, rcfg, process_group=pg, exchange=args.exchange,
-                                         multicast={"auto": "auto", "on": True, "off": False}[args.multicast])
+                                         multicast={"auto": "auto", "on": True, "off": False}[args.multicast],
+                                         tile_hints=not args.no_tile_hints)
     host_t = make_targets(cfg, tr.lo, tr.hi)
     dev_t = host_t.to(dev)
     ctx = gs.context(dev)
@@ -510,6 +513,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
             "data": "synthetic (seeded Gaussians, poses and U[0,1] targets per BASELINE.json)",
             "config": workload_config(args, cfg, world),
             "workload_stats": {"exchange": tr.exchange, "exchange_path": tr.exchange_path,
+                               "tile_hints": bool(tr.tile_hints),
                                "backward_batch_views": tr.batch,
                                "contributing_pairs_per_view": round(keys_per_view),
                                "binned_pairs_per_view": round(binned), "kept_pairs_per_view": round(kept),

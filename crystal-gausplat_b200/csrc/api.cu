@@ -79,6 +79,11 @@ struct gsc_frame {
       last, n_contrib, grad2d, bins, tile_order, tile_work;
   // depth-sliced binning (GSC_BIN_OCCLUDED)
   GsBuf slice_vals[kMaxSlices], slice_ranges[kMaxSlices], skip_bits, tile_done, tile_base, pair_total;
+  // per-tile depth cut of the slices (gsc_frame_set_tile_hint): the caller's
+  // array of tiles floats, read when valid, rewritten by every occluded forward
+  float* tile_hint = nullptr;
+  bool tile_hint_valid = false;
+  GsBuf cut_sub, cut_cnt, open_flag;
   bool count_pending = false;  // the lists' length is on the device (the final ranges' end)
   bool keys_valid = false;  // `keys` rebuilt from (tiles, vals) on request
   int64_t n = 0, num_keys = 0;
@@ -527,13 +532,22 @@ GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out) {
   return GSC_OK;
 }
 
+GSC_API int gsc_frame_set_tile_hint(gsc_frame* f, float* cut, int32_t valid) {
+  GS_REQUIRE(f, "gsc_frame_set_tile_hint: null frame");
+  GS_REQUIRE(((uintptr_t)cut & 3u) == 0, "gsc_frame_set_tile_hint: misaligned cut array");
+  f->tile_hint = cut;
+  f->tile_hint_valid = cut && valid;
+  return GSC_OK;
+}
+
 GSC_API int gsc_frame_destroy(gsc_frame* f) {
   if (!f) return GSC_OK;
   cudaStreamSynchronize(f->ctx->stream);
   GsBuf* bufs[] = {&f->splats, &f->depth_pairs, &f->pairs, &f->depth_keys, &f->order, &f->block_sums, &f->offsets, &f->total,
                    &f->tiles, &f->keys, &f->vals, &f->ranges, &f->image, &f->final_T, &f->last,
                    &f->n_contrib, &f->grad2d, &f->bins, &f->tile_order, &f->tile_work,
-                   &f->skip_bits, &f->tile_done, &f->tile_base, &f->pair_total};
+                   &f->skip_bits, &f->tile_done, &f->tile_base, &f->pair_total, &f->cut_sub, &f->cut_cnt,
+                   &f->open_flag};
   for (GsBuf* b : bufs)
     if (b->ptr) cudaFree(b->ptr);
   for (int k = 0; k < kMaxSlices; k++) {
@@ -594,7 +608,8 @@ const uint4* frame_bins(const gsc_frame* f) { return (const uint4*)f->bins.ptr; 
 
 // count_n >= 0: the pair counts and offsets cover depth positions [0, count_n)
 // only (occluded binning counts its later slices itself).
-int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true, int64_t count_n = -1) {
+int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true, int64_t count_n = -1,
+                      const TileCut* tc = nullptr) {
   const int64_t n = f->n;
   // 1. stable sort of the Gaussians by depth (non-emitting ones carry ~0 and
   //    sink); packed (depth << 32 | index) words, split into keys and order
@@ -612,9 +627,11 @@ int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true, int64_
   if (cn == 0) return cudaMemsetAsync(f->total.ptr, 0, 8, ctx->stream) == cudaSuccess ? GSC_OK : GSC_ERR_CUDA;
   {
     StageScope sc(ctx, GSC_STAGE_SCAN);
-    sc.kernels(1);
-    GS_TRY(launch_block_sums_gather(frame_bins(f), f->order_ptr, cn,
-                                    (uint32_t*)f->block_sums.ptr, ctx->stream));
+    sc.kernels(tc ? 2 : 1);
+    if (tc)
+      GS_TRY(launch_block_sums_cut(frame_bins(f), f->order_ptr, cn, (uint32_t*)f->block_sums.ptr, *tc, ctx->stream));
+    else
+      GS_TRY(launch_block_sums_gather(frame_bins(f), f->order_ptr, cn, (uint32_t*)f->block_sums.ptr, ctx->stream));
   }
   StageScope sc(ctx, GSC_STAGE_SCAN);
   sc.kernels(1);
@@ -776,6 +793,39 @@ int occlusion_slices(int64_t n, int64_t* p) {
 // the last (which counts its own pairs), or everything with one slice.
 int64_t occlusion_count_end(int S, const int64_t* p) { return S >= 2 ? p[S - 1] : p[S]; }
 
+// Per-tile cut (a valid tile hint): two slices that both span every depth
+// position, the first holding each tile's pairs in front of its cut, the
+// second the rest of the tiles whose pixels did not all stop.
+#ifndef GS_TILE_HINT_MARGIN
+#define GS_TILE_HINT_MARGIN 0.005f
+#endif
+bool tile_cut_mode(const gsc_frame* f) { return f->tile_hint && f->tile_hint_valid && f->n > 0; }
+
+int tile_cut_slices(int64_t n, int64_t* p) {
+  p[0] = 0;
+  p[1] = n;
+  p[2] = n;
+  return 2;
+}
+
+// The cut of slice `mode` (0 or 1) of frame f, with its per-position buffers.
+int tile_cut_of(gsc_ctx* ctx, gsc_frame* f, int mode, TileCut* tc) {
+  GS_TRY(ensure(ctx, &f->cut_sub, (size_t)f->n * 8 + 8));
+  GS_TRY(ensure(ctx, &f->cut_cnt, (size_t)f->n * 4 + 4));
+  GS_TRY(ensure(ctx, &f->open_flag, 16));
+  tc->cut = f->tile_hint;
+  tc->mode = mode;
+  tc->tiles_x = f->tiles_x;
+  tc->sub = (uint64_t*)f->cut_sub.ptr;
+  tc->cnt = (uint32_t*)f->cut_cnt.ptr;
+  if (mode == 1) {
+    tc->done = (const unsigned long long*)f->tile_done.ptr;
+    tc->done_words = done_words_of(f->tiles_x);
+    tc->open = (const unsigned int*)f->open_flag.ptr;
+  }
+  return GSC_OK;
+}
+
 // One readback per batch: each view's pair total (from preprocess) and the
 // pair counts before its slice boundaries (from the whole-view scan), turned
 // into up[v][s], slice s's pair count before the skip test.
@@ -810,29 +860,35 @@ int read_slice_counts(gsc_ctx* ctx, gsc_frame* const* frames, int nviews, const 
 // counts again with the skip test and sorts with a device-side count, its
 // buffers sized by the upper bound `m_up`.
 int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_up) {
-  const int64_t n_s = p[s + 1] - p[s];
+  const bool cutm = tile_cut_mode(f);
+  const int64_t n_s = cutm ? f->n : p[s + 1] - p[s];
   const int tx = f->tiles_x, ty = f->tiles_y;
   const int32_t T = tx * ty;
   const int tb = tile_bits_of(T);
-  const uint32_t* order = f->order_ptr + p[s];
+  const uint32_t* order = cutm ? f->order_ptr : f->order_ptr + p[s];
+  TileCut tc;
+  if (cutm) GS_TRY(tile_cut_of(ctx, f, s, &tc));
   GS_TRY(ensure(ctx, &f->slice_vals[s], (size_t)m_up * 4 + 4));
   GS_TRY(ensure(ctx, &f->slice_ranges[s], (size_t)T * 8));
   uint32_t* vals = (uint32_t*)f->slice_vals[s].ptr;
   uint32_t* ranges = (uint32_t*)f->slice_ranges[s].ptr;
-  const uint64_t* offsets = (const uint64_t*)f->offsets.ptr + p[s] / 256;
+  const uint64_t* offsets = (const uint64_t*)f->offsets.ptr + (cutm ? 0 : p[s] / 256);
   const uint64_t* n_dev = nullptr;
   const uint32_t* skip = nullptr;
   if (s > 0 && n_s > 0) {
     StageScope sc(ctx, GSC_STAGE_SCAN);
-    sc.kernels(2);
-    GS_TRY(launch_block_sums_gather(frame_bins(f), order, n_s, (uint32_t*)f->block_sums.ptr, ctx->stream,
-                                    (const unsigned long long*)f->tile_done.ptr, done_words_of(tx),
-                                    (uint32_t*)f->skip_bits.ptr));
+    sc.kernels(cutm ? 3 : 2);
+    if (cutm)
+      GS_TRY(launch_block_sums_cut(frame_bins(f), order, n_s, (uint32_t*)f->block_sums.ptr, tc, ctx->stream));
+    else
+      GS_TRY(launch_block_sums_gather(frame_bins(f), order, n_s, (uint32_t*)f->block_sums.ptr, ctx->stream,
+                                      (const unsigned long long*)f->tile_done.ptr, done_words_of(tx),
+                                      (uint32_t*)f->skip_bits.ptr));
     GS_TRY(launch_scan_block_sums((const uint32_t*)f->block_sums.ptr, (n_s + 255) / 256, (uint64_t*)f->offsets.ptr,
                                   (uint64_t*)f->total.ptr, ctx->stream));
     offsets = (const uint64_t*)f->offsets.ptr;
     n_dev = (const uint64_t*)f->total.ptr;
-    skip = (const uint32_t*)f->skip_bits.ptr;
+    if (!cutm) skip = (const uint32_t*)f->skip_bits.ptr;
     if (ctx->profiling)
       GS_TRY(launch_add_u64(n_dev, reinterpret_cast<unsigned long long*>(ctx->err + 4), ctx->stream));
   } else if (s == 0 && ctx->profiling) {
@@ -852,7 +908,7 @@ int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_u
     GS_TRY(sort_packed_clear(ctx, (int64_t)m_up, 32, 32 + tb, scratch));
     GS_TRY(launch_emit_tiles(frame_bins(f), order, n_s, offsets, tx, pairs, ctx->stream,
                              sort_packed_hist(scratch, (int64_t)m_up, 32, 32 + tb), (tb + 7) / 8, ranges, T,
-                             (int64_t)ctx->num_sms * 32, skip));
+                             (int64_t)ctx->num_sms * 32, skip, cutm ? &tc : nullptr));
   }
   {
     StageScope sc(ctx, GSC_STAGE_SORT);
@@ -870,9 +926,11 @@ int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_u
 int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, int s, int S) {
   const int32_t T = f->tiles_x * f->tiles_y;
   const size_t done_bytes = (size_t)f->tiles_y * done_words_of(f->tiles_x) * 8;
+  const bool cutm = tile_cut_mode(f);
   if (s == 0) {
     GS_CK(cudaMemsetAsync(f->tile_done.ptr, 0, done_bytes, ctx->stream));
     GS_CK(cudaMemsetAsync(f->tile_base.ptr, 0, (size_t)T * 4, ctx->stream));
+    if (cutm) GS_CK(cudaMemsetAsync(f->open_flag.ptr, 0, 4, ctx->stream));
   }
   CompositeFwdArgs a;
   fill_fwd(&a, (const float*)f->splats.ptr, (const uint32_t*)f->slice_vals[s].ptr,
@@ -887,6 +945,11 @@ int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, i
   a.first_slice = s == 0;
   a.last_slice = s == S - 1;
   const bool last = s == S - 1;
+  if (cutm && !last) {
+    a.tile_cut = f->tile_hint;
+    a.open_flag = (unsigned int*)f->open_flag.ptr;
+  }
+  a.mark_done = last && f->tile_hint != nullptr;  // the next cut needs the stopped tiles
   if (last) {
     if (ctx->profiling) a.pge = reinterpret_cast<unsigned long long*>(ctx->err + 2);
     GS_TRY(ensure(ctx, &f->tile_work, (size_t)T * 4 + 4));
@@ -907,12 +970,17 @@ int sliced_composite(gsc_ctx* ctx, gsc_frame* f, const gsc_raster_config* cfg, i
       sr[k] = (const uint32_t*)f->slice_ranges[k].ptr;
     }
     StageScope sc(ctx, GSC_STAGE_RANGES);
-    sc.kernels(2);
+    sc.kernels(f->tile_hint ? 3 : 2);
     GS_TRY(launch_concat_slices(sv, sr, S, a.tile_work, T, (uint32_t*)f->vals.ptr, (uint32_t*)f->ranges.ptr,
                                 (uint64_t*)f->total.ptr, ctx->stream));
     if (ctx->profiling)
       GS_TRY(launch_add_u64((const uint64_t*)f->total.ptr, reinterpret_cast<unsigned long long*>(ctx->err + 6),
                             ctx->stream));
+    if (f->tile_hint)  // the cut of this view's next forward
+      GS_TRY(launch_tile_cut_update((const uint32_t*)f->ranges.ptr, (const uint32_t*)f->vals.ptr, a.tile_work,
+                                    (const unsigned long long*)f->tile_done.ptr, done_words_of(f->tiles_x),
+                                    f->tiles_x, T, (const float*)f->splats.ptr, GS_TILE_HINT_MARGIN, f->tile_hint,
+                                    ctx->stream));
   }
   const bool full = cfg->mode == GSC_MODE_FULL;
   GS_TRY(ensure(ctx, &f->tile_order, (size_t)T * 4 + 4));
@@ -1076,8 +1144,11 @@ GSC_API int gsc_rasterize_forward(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussian
     int S[1];
     int64_t bounds[1][kMaxSlices + 1];
     uint64_t up[1][kMaxSlices], m = 0;
-    S[0] = occlusion_slices(f->n, bounds[0]);
-    GS_TRY(forward_sort_scan(ctx, f, true, occlusion_count_end(S[0], bounds[0])));
+    TileCut tc0;
+    const bool cutm = tile_cut_mode(f);
+    if (cutm) GS_TRY(tile_cut_of(ctx, f, 0, &tc0));
+    S[0] = cutm ? tile_cut_slices(f->n, bounds[0]) : occlusion_slices(f->n, bounds[0]);
+    GS_TRY(forward_sort_scan(ctx, f, true, occlusion_count_end(S[0], bounds[0]), cutm ? &tc0 : nullptr));
     GS_TRY(read_slice_counts(ctx, &f, 1, S, bounds, &m, up));
     if (num_rendered) *num_rendered = (int64_t)m;
     GS_TRY(forward_sliced(ctx, &f, 1, cfg, bounds, S, up));
@@ -1145,15 +1216,17 @@ GSC_API int gsc_rasterize_forward_batch(gsc_ctx* ctx, gsc_frame* const* frames, 
   const bool occl = occlusion_binning(cfg, frames[0]);
   int S[GSC_MAX_BATCH_VIEWS] = {};
   int64_t bounds[GSC_MAX_BATCH_VIEWS][kMaxSlices + 1] = {};
-  for (int v = 0; v < nviews && occl; v++) S[v] = occlusion_slices(frames[v]->n, bounds[v]);
-  if (batched_depth) {
-    for (int v = 0; v < nviews; v++) {
-      frames[v]->order_ptr = order + (size_t)v * n;
-      GS_TRY(forward_sort_scan(ctx, frames[v], false, occl ? occlusion_count_end(S[v], bounds[v]) : -1));
-    }
-  } else {
-    for (int v = 0; v < nviews; v++)
-      GS_TRY(forward_sort_scan(ctx, frames[v], true, occl ? occlusion_count_end(S[v], bounds[v]) : -1));
+  TileCut tc0[GSC_MAX_BATCH_VIEWS];
+  bool cutm[GSC_MAX_BATCH_VIEWS] = {};
+  for (int v = 0; v < nviews && occl; v++) {
+    cutm[v] = tile_cut_mode(frames[v]);
+    if (cutm[v]) GS_TRY(tile_cut_of(ctx, frames[v], 0, &tc0[v]));
+    S[v] = cutm[v] ? tile_cut_slices(frames[v]->n, bounds[v]) : occlusion_slices(frames[v]->n, bounds[v]);
+  }
+  for (int v = 0; v < nviews; v++) {
+    if (batched_depth) frames[v]->order_ptr = order + (size_t)v * n;
+    GS_TRY(forward_sort_scan(ctx, frames[v], !batched_depth, occl ? occlusion_count_end(S[v], bounds[v]) : -1,
+                             cutm[v] ? &tc0[v] : nullptr));
   }
   // one readback of every view's pair count (and, for depth-sliced binning,
   // of the pair counts before each slice boundary)

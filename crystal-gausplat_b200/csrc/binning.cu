@@ -242,12 +242,105 @@ __global__ void __launch_bounds__(256) block_sums_gather_kernel(const uint4* __r
   if (threadIdx.x == 255) sums[blockIdx.x] = incl;
 }
 
+// ---- per-tile depth cut (tile hint) -----------------------------------------
+__device__ __forceinline__ bool tile_is_done(const unsigned long long* __restrict__ done, int words, int tx, int ty) {
+  return (done[(size_t)ty * words + (tx >> 6)] >> (tx & 63)) & 1ull;
+}
+// Whether pair (Gaussian at depth d, tile (tx, ty)) belongs to the cut's slice.
+// A NaN cut puts every pair in the first slice.
+__device__ __forceinline__ bool cut_passes(const TileCut& c, float d, int tx, int ty) {
+  const float ct = __ldg(c.cut + (size_t)ty * c.tiles_x + tx);
+  if (c.mode == 0) return !(d >= ct);
+  return d >= ct && !tile_is_done(c.done, c.done_words, tx, ty);
+}
+// Passing tiles of a binning record of at most 64 tiles: the sub-mask of its
+// mask (bit i = tile i of the rect, row-major) and its population count.
+__device__ __forceinline__ uint32_t cut_small_record(const TileCut& c, uint4 b0, uint4 b1, uint64_t* sub) {
+  const uint32_t cnt = b0.w, wx = b0.z;
+  const float d = __uint_as_float(b1.z);
+  uint64_t mk = ((uint64_t)b1.y << 32) | b1.x;
+  if (mk == ~0ull) mk = cnt == 64 ? ~0ull : (1ull << cnt) - 1ull;  // every tile of the rect
+  const uint32_t inv = (65535u + wx) / wx;  // row of a position < 64 by multiply and shift
+  uint64_t out = 0;
+  for (uint64_t m = mk; m; m &= m - 1ull) {
+    const uint32_t i = (uint32_t)(__ffsll((long long)m) - 1);
+    const uint32_t ry = (i * inv) >> 16;
+    if (cut_passes(c, d, (int)b0.x + (int)(i - ry * wx), (int)b0.y + (int)ry)) out |= 1ull << i;
+  }
+  *sub = out;
+  return (uint32_t)__popcll(out);
+}
+// Passing tiles of a record of more than 64 tiles (every tile of its rect),
+// counted by the whole warp: lane `who`'s record, tiles 32 at a time.
+__device__ __forceinline__ uint32_t cut_big_count(const TileCut& c, uint4 b0, float d, int lane) {
+  const uint32_t nr = b0.w, wx = b0.z;
+  uint32_t k = 0;
+  for (uint32_t r0 = 0; r0 < nr; r0 += 32) {
+    const uint32_t r = r0 + (uint32_t)lane;
+    bool ok = false;
+    if (r < nr) {
+      const uint32_t ry = r / wx;
+      ok = cut_passes(c, d, (int)b0.x + (int)(r - ry * wx), (int)b0.y + (int)ry);
+    }
+    k += (uint32_t)__popc(__ballot_sync(0xffffffffu, ok));
+  }
+  return k;
+}
+
+// Passing-tile count and (records of <= 64 tiles) sub-mask of every
+// Gaussian under a tile cut, in Gaussian order: the records are read
+// sequentially, and the 12 bytes per Gaussian written stay in L2 for the
+// depth-order passes that gather them.
+__global__ void __launch_bounds__(256) cut_count_kernel(const uint4* __restrict__ bins, int64_t n, TileCut tc) {
+  if (tc.open && *(volatile const unsigned int*)tc.open == 0u) return;  // no second-slice pair anywhere
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  uint32_t t = 0;
+  uint64_t sub = 0;
+  uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
+  if (i < n) {
+    b0 = bins[(size_t)i * 2];
+    if (b0.w) {
+      b1 = bins[(size_t)i * 2 + 1];
+      if (b0.w <= 64) t = cut_small_record(tc, b0, b1, &sub);
+    }
+  }
+  // records of more than 64 tiles: counted by the whole warp, one at a time
+  for (uint32_t big = __ballot_sync(0xffffffffu, b0.w > 64u); big; big &= big - 1u) {
+    const int who = __ffs(big) - 1;
+    uint4 w0;
+    w0.x = __shfl_sync(0xffffffffu, b0.x, who);
+    w0.y = __shfl_sync(0xffffffffu, b0.y, who);
+    w0.z = __shfl_sync(0xffffffffu, b0.z, who);
+    w0.w = __shfl_sync(0xffffffffu, b0.w, who);
+    const float d = __uint_as_float(__shfl_sync(0xffffffffu, b1.z, who));
+    const uint32_t k = cut_big_count(tc, w0, d, lane);
+    if (lane == who) t = k;
+  }
+  if (i < n) {
+    tc.sub[i] = sub;
+    tc.cnt[i] = t;
+  }
+}
+
+// Pair count of each 256-position chunk of `order` from the per-Gaussian
+// counts of cut_count_kernel.
+__global__ void __launch_bounds__(256) block_sums_cut_kernel(const uint32_t* __restrict__ order, int64_t n,
+                                                             uint32_t* __restrict__ sums, TileCut tc) {
+  __shared__ uint32_t s_warp[8];
+  if (tc.open && *(volatile const unsigned int*)tc.open == 0u) {
+    if (threadIdx.x == 0) sums[blockIdx.x] = 0u;
+    return;
+  }
+  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const uint32_t t = p < n ? tc.cnt[order[p]] : 0u;
+  const uint32_t incl = block_incl_scan_256(t, s_warp);
+  if (threadIdx.x == 255) sums[blockIdx.x] = incl;
+}
+
 constexpr int kEmitMaxPasses = 4;
 #ifndef GS_EMIT_FNS
 #define GS_EMIT_FNS 1
-#endif
-#ifndef GS_EMIT_OWNBUF
-#define GS_EMIT_OWNBUF 1
 #endif
 constexpr int kOwnWin = 1024;  // outputs per warp window (owner lane per output)
 
@@ -276,7 +369,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
                                                          int tiles_x, uint64_t* __restrict__ pair_out,
                                                          uint32_t* __restrict__ hist, int hist_passes,
                                                          uint32_t* __restrict__ ranges, int32_t num_tiles,
-                                                         const uint32_t* __restrict__ skip_bits) {
+                                                         const uint32_t* __restrict__ skip_bits, TileCut tc) {
   __shared__ uint32_t s_hist[kEmitMaxPasses][256];
   __shared__ uint32_t s_incl[256];
   __shared__ int s_x0[256], s_y0[256], s_wx[256];
@@ -284,9 +377,12 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
   __shared__ uint32_t s_id[256];
   __shared__ uint64_t s_mask[256];
   __shared__ uint32_t s_warp[8];
-#if GS_EMIT_OWNBUF
+  // tile cut: records of more than 64 tiles are emitted warp-cooperatively
+  __shared__ uint32_t s_big[256];  // tile count of such a record, else 0
+  __shared__ float s_depth[256];
+  const bool cut = tc.cut != nullptr;
+  const bool live = !(cut && tc.open && *(volatile const unsigned int*)tc.open == 0u);
   __shared__ uint8_t s_own[8][kOwnWin];
-#endif
   if (ranges)
     for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < num_tiles; r += (int64_t)gridDim.x * 256) {
       ranges[2 * r] = 0xFFFFFFFFu;
@@ -295,36 +391,52 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
   for (int k = threadIdx.x; k < hist_passes * 256; k += 256) (&s_hist[0][0])[k] = 0u;
   // A block takes chunks of 256 Gaussians (in depth order) in turn, so that
   // its digit counts reach global memory once per block, not per chunk.
-  const int64_t nchunks = (n + 255) / 256;
+  const int64_t nchunks = live ? (n + 255) / 256 : 0;
   for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
     const int64_t p = chunk * 256 + threadIdx.x;
     uint32_t t = 0;
+    s_big[threadIdx.x] = 0u;
     if (p < n) {
-      const uint32_t gid = order[p];
-      const uint4 b0 = bins[(size_t)gid * 2];
-      t = b0.w;
-      if (skip_bits && ((skip_bits[p >> 5] >> (p & 31)) & 1u)) t = 0;  // every tile already done
-      if (t) {
-        const uint4 b1 = bins[(size_t)gid * 2 + 1];
-        s_x0[threadIdx.x] = (int)b0.x;
-        s_y0[threadIdx.x] = (int)b0.y;
-        s_wx[threadIdx.x] = (int)b0.z;
-        s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
-        s_id[threadIdx.x] = gid;
-        s_mask[threadIdx.x] = ((uint64_t)b1.y << 32) | b1.x;
+      if (cut) {
+        const uint32_t gid = order[p];
+        t = tc.cnt[gid];  // passing tiles, counted by cut_count_kernel
+        if (t) {
+          const uint4 b0 = bins[(size_t)gid * 2];
+          s_x0[threadIdx.x] = (int)b0.x;
+          s_y0[threadIdx.x] = (int)b0.y;
+          s_wx[threadIdx.x] = (int)b0.z;
+          s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
+          s_id[threadIdx.x] = gid;
+          if (b0.w <= 64) {
+            s_mask[threadIdx.x] = tc.sub[gid];
+          } else {
+            s_big[threadIdx.x] = b0.w;
+            s_depth[threadIdx.x] = __uint_as_float(bins[(size_t)gid * 2 + 1].z);
+          }
+        }
+      } else {
+        const uint32_t gid = order[p];
+        const uint4 b0 = bins[(size_t)gid * 2];
+        t = b0.w;
+        if (skip_bits && ((skip_bits[p >> 5] >> (p & 31)) & 1u)) t = 0;  // every tile already done
+        if (t) {
+          const uint4 b1 = bins[(size_t)gid * 2 + 1];
+          s_x0[threadIdx.x] = (int)b0.x;
+          s_y0[threadIdx.x] = (int)b0.y;
+          s_wx[threadIdx.x] = (int)b0.z;
+          s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
+          s_id[threadIdx.x] = gid;
+          s_mask[threadIdx.x] = ((uint64_t)b1.y << 32) | b1.x;
+        }
       }
     }
     uint32_t incl = block_incl_scan_256(t, s_warp);
     s_incl[threadIdx.x] = incl;
     __syncthreads();
-    // Each warp writes the contiguous output range of its 32 Gaussians; a
-    // lane's output index grows by 32 per round, so the Gaussian that owns it
-    // is found by advancing a pointer instead of searching.
     const uint64_t out = offsets[chunk];
     const int wb = threadIdx.x & ~31;
     const uint32_t wend = s_incl[wb + 31];
     const uint32_t wbeg = wb ? s_incl[wb - 1] : 0u;
-#if GS_EMIT_OWNBUF
     // Each warp writes the contiguous output range of its 32 Gaussians, a
     // window of kOwnWin outputs at a time: every lane first marks its
     // Gaussian's outputs of the window with its lane number, then the lanes
@@ -338,10 +450,10 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
       __syncwarp();
       for (uint32_t k0 = w0; k0 < w1; k0 += 32) {
         const uint32_t k = k0 + lane;
-        const bool valid = k < w1;
+        const int own = k < w1 ? wb + own_of[k - w0] : wb;
+        const bool valid = k < w1 && !s_big[own];  // tile-cut records of > 64 tiles: below
         uint32_t tile = 0xFFFFFFFFu;
         if (valid) {
-          const int own = wb + own_of[k - w0];
           uint32_t local = k - (own ? s_incl[own - 1] : 0u);
           const uint64_t mk = s_mask[own];
           const uint32_t wx = (uint32_t)s_wx[own];
@@ -363,37 +475,33 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
       }
       __syncwarp();
     }
-#else
-    // Each warp writes the contiguous output range of its 32 Gaussians; a
-    // lane's output index grows by 32 per round, so the Gaussian that owns it
-    // is found by advancing a pointer instead of searching.
-    int own = wb;
-    for (uint32_t k0 = wbeg; k0 < wend; k0 += 32) {
-      const uint32_t k = k0 + (threadIdx.x & 31);
-      const bool valid = k < wend;
-      uint32_t tile = 0xFFFFFFFFu;
-      if (valid) {
-        while (s_incl[own] <= k) own++;
-        uint32_t local = k - (own ? s_incl[own - 1] : 0u);
-        const uint64_t mk = s_mask[own];
-        const uint32_t wx = (uint32_t)s_wx[own];
-        uint32_t ry;
-        if (mk != ~0ull) {
-          local = select_bit64(mk, local);  // local-th contributing tile of the rect (< 64)
-          ry = (local * s_inv[own]) >> 16;
-        } else {
-          ry = local / wx;
+    // tile-cut records of more than 64 tiles: the warp walks each one's rect,
+    // 32 tiles at a time, in the order block_sums_cut_kernel counted them
+    for (uint32_t big = __ballot_sync(0xffffffffu, s_big[threadIdx.x] != 0u); big; big &= big - 1u) {
+      const int g = wb + __ffs(big) - 1;
+      const uint32_t nr = s_big[g], wx = (uint32_t)s_wx[g];
+      const int x0 = s_x0[g], y0 = s_y0[g];
+      const float d = s_depth[g];
+      const uint64_t gbase = out + (g ? s_incl[g - 1] : 0u);
+      uint32_t run = 0;
+      for (uint32_t r0 = 0; r0 < nr; r0 += 32) {
+        const uint32_t r = r0 + (uint32_t)lane;
+        bool ok = false;
+        uint32_t tile = 0;
+        if (r < nr) {
+          const uint32_t ry = r / wx;
+          const int tx = x0 + (int)(r - ry * wx), ty = y0 + (int)ry;
+          ok = cut_passes(tc, d, tx, ty);
+          tile = (uint32_t)(ty * tiles_x + tx);
         }
-        const int ty = s_y0[own] + (int)ry;
-        const int tx = s_x0[own] + (int)(local - ry * wx);
-        tile = (uint32_t)(ty * tiles_x + tx);
-        pair_out[out + k] = ((uint64_t)tile << 32) | (uint64_t)s_id[own];
+        const uint32_t bal = __ballot_sync(0xffffffffu, ok);
+        if (ok) {
+          pair_out[gbase + run + (uint32_t)__popc(bal & ((1u << lane) - 1u))] = ((uint64_t)tile << 32) | (uint64_t)s_id[g];
+          for (int q = 0; q < hist_passes; q++) atomicAdd(&s_hist[q][(tile >> (8 * q)) & 255u], 1u);
+        }
+        run += (uint32_t)__popc(bal);
       }
-      // digit counts of the tile sort
-      if (valid)
-        for (int q = 0; q < hist_passes; q++) atomicAdd(&s_hist[q][(tile >> (8 * q)) & 255u], 1u);
     }
-#endif
     __syncthreads();  // the chunk's shared records are replaced next
   }
   if (hist_passes == 0) return;
@@ -540,17 +648,67 @@ int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* cons
 
 int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
                       int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist, int hist_passes,
-                      uint32_t* ranges, int32_t num_tiles, int64_t grid_cap, const uint32_t* skip_bits) {
+                      uint32_t* ranges, int32_t num_tiles, int64_t grid_cap, const uint32_t* skip_bits,
+                      const TileCut* tc) {
   if (n == 0) return GSC_OK;
   if (hist_passes < 0 || hist_passes > kEmitMaxPasses || (hist_passes > 0 && !hist)) {
     set_error("emit_tiles: bad histogram arguments");
     return GSC_ERR_INVALID;
   }
+  if (tc && (!tc->cut || !tc->sub || !tc->cnt || skip_bits)) {
+    set_error("emit_tiles: a tile cut needs its cut, sub-masks and counts (and no skip bits)");
+    return GSC_ERR_INVALID;
+  }
   const int64_t chunks = (n + 255) / 256;
   const int64_t grid = grid_cap > 0 ? std::min<int64_t>(chunks, grid_cap) : chunks;
   emit_tiles_kernel<<<(unsigned)grid, 256, 0, stream>>>(bins, order, n, offsets, tiles_x, pair_out, hist,
-                                                        hist_passes, ranges, num_tiles, skip_bits);
+                                                        hist_passes, ranges, num_tiles, skip_bits,
+                                                        tc ? *tc : TileCut());
   GS_CK_LAUNCH("emit_tiles_kernel");
+  return GSC_OK;
+}
+
+int launch_block_sums_cut(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums, const TileCut& tc,
+                          cudaStream_t stream) {
+  if (n == 0) return GSC_OK;
+  if (!tc.cut || !tc.sub || !tc.cnt || (tc.mode == 1 && !tc.done) || tc.tiles_x <= 0) {
+    set_error("block_sums_cut: incomplete tile cut");
+    return GSC_ERR_INVALID;
+  }
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  cut_count_kernel<<<blocks, 256, 0, stream>>>(bins, n, tc);
+  GS_CK_LAUNCH("cut_count_kernel");
+  block_sums_cut_kernel<<<blocks, 256, 0, stream>>>(order, n, sums, tc);
+  GS_CK_LAUNCH("block_sums_cut_kernel");
+  return GSC_OK;
+}
+
+__global__ void __launch_bounds__(256) tile_cut_update_kernel(const uint32_t* __restrict__ ranges,
+                                                              const uint32_t* __restrict__ vals,
+                                                              const uint32_t* __restrict__ keep,
+                                                              const unsigned long long* __restrict__ done,
+                                                              int done_words, int32_t tiles_x, int32_t num_tiles,
+                                                              const float4* __restrict__ splats, float margin,
+                                                              float* __restrict__ cut_out) {
+  const int32_t t = (int32_t)(blockIdx.x * 256 + threadIdx.x);
+  if (t >= num_tiles) return;
+  const uint32_t w = keep[t];
+  float c = __int_as_float(0x7f800000);  // +inf: the whole list stays in the first slice
+  if (w && tile_is_done(done, done_words, t % tiles_x, t / tiles_x)) {
+    const uint32_t gid = vals[ranges[2 * t] + w - 1];
+    c = splats[(size_t)gid * 3 + 2].y * (1.0f + margin);  // record word 9: depth
+  }
+  cut_out[t] = c;
+}
+
+int launch_tile_cut_update(const uint32_t* ranges, const uint32_t* vals, const uint32_t* keep,
+                           const unsigned long long* done, int done_words, int32_t tiles_x, int32_t num_tiles,
+                           const float* splats, float margin, float* cut_out, cudaStream_t stream) {
+  if (num_tiles <= 0) return GSC_OK;
+  tile_cut_update_kernel<<<(unsigned)((num_tiles + 255) / 256), 256, 0, stream>>>(
+      ranges, vals, keep, done, done_words, tiles_x, num_tiles, reinterpret_cast<const float4*>(splats), margin,
+      cut_out);
+  GS_CK_LAUNCH("tile_cut_update_kernel");
   return GSC_OK;
 }
 

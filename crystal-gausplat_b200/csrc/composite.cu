@@ -238,6 +238,8 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     if (tid == 0) {
       a.tile_base[tile] = base + (end - start);
       if (all_done) atomicOr(&a.tile_done[(size_t)ty * a.done_words + (tx >> 6)], 1ull << (tx & 63));
+      // a tile still open with a finite cut may have second-slice pairs
+      else if (a.open_flag && a.tile_cut[tile] < __int_as_float(0x7f800000)) atomicOr(a.open_flag, 1u);
     }
     if (!inside) return;
     a.final_T[pix] = T;
@@ -247,6 +249,11 @@ __global__ void __launch_bounds__(256, GS_FWD_MIN_CTAS) composite_fwd_kernel(Com
     a.n_contrib[pix] = cnt;
     a.last[pix] = lst;
     return;
+  }
+  if (a.mark_done && !tile_skip) {  // the next tile cut needs to know which tiles stopped
+    const bool all_done = __syncthreads_count(done) == 256;
+    if (tid == 0 && all_done)
+      atomicOr(&a.tile_done[(size_t)ty * a.done_words + (tx >> 6)], 1ull << (tx & 63));
   }
   const uint32_t list_len = base + (end - start);  // the whole tile list, every slice
   if (a.pge) {  // tracing: entries visited before the stop (whole list if never stopped)

@@ -76,6 +76,12 @@ struct CompositeFwdArgs {
   unsigned long long* tile_done;
   int done_words;
   int first_slice, last_slice;
+  // per-tile cut of the slices (tile hint): a first slice sets *open_flag when
+  // a tile whose pixels did not all stop has a finite cut (it may have
+  // second-slice pairs); mark_done: the last slice also marks its done tiles
+  const float* tile_cut;
+  unsigned int* open_flag;
+  int mark_done;
 };
 
 struct CompositeBwdArgs {
@@ -167,6 +173,32 @@ int launch_add_u64(const uint64_t* src, unsigned long long* dst, cudaStream_t st
 int launch_concat_slices(const uint32_t* const* slice_vals, const uint32_t* const* slice_ranges, int nslices,
                          const uint32_t* keep, int32_t num_tiles, uint32_t* out_vals, uint32_t* out_ranges,
                          uint64_t* total, cudaStream_t stream);
+// Per-tile depth cut of occluded binning (a tile hint): the pairs of a view
+// are split into the pairs (g, t) with !(depth(g) >= cut[t]) (mode 0: the
+// first slice, a depth prefix of every tile's list) and those with
+// depth(g) >= cut[t] whose tile is not done (mode 1: the second slice). The
+// binning record's third word of its second half holds bits(depth).
+struct TileCut {
+  const float* cut = nullptr;                  // per tile; null: no cut
+  const unsigned long long* done = nullptr;    // mode 1: tile-done bits
+  int done_words = 0;
+  int mode = 0;
+  int tiles_x = 0;
+  uint64_t* sub = nullptr;  // per Gaussian: the record's passing tiles (records of <= 64 tiles)
+  uint32_t* cnt = nullptr;  // per Gaussian: number of passing tiles
+  const unsigned int* open = nullptr;  // mode 1: 0 if no tile can have a second-slice pair
+};
+// Pair count of each 256-position chunk of `order` under a tile cut (two
+// kernels: the per-Gaussian counts and sub-masks tc.cnt / tc.sub, read in
+// Gaussian order, then the chunk sums in depth order).
+int launch_block_sums_cut(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums, const TileCut& tc,
+                          cudaStream_t stream);
+// Next cut of every tile after a view's last slice: done tiles (every pixel
+// stopped) get (1 + margin) x the depth of the last entry any pixel used
+// (entry keep[t] - 1 of the final list), the others +inf.
+int launch_tile_cut_update(const uint32_t* ranges, const uint32_t* vals, const uint32_t* keep,
+                           const unsigned long long* done, int done_words, int32_t tiles_x, int32_t num_tiles,
+                           const float* splats, float margin, float* cut_out, cudaStream_t stream);
 // hist (may be null): the tile sort's digit counts of the tile bits, digit d of
 // pass q at hist[(q * 256 + d) * kHistStride]; ranges (may be null): preset to
 // {0xFFFFFFFF, 0} for num_tiles tiles; grid_cap (> 0): at most that many blocks.
@@ -174,7 +206,7 @@ constexpr int kHistStride = 32;
 int launch_emit_tiles(const uint4* bins, const uint32_t* order, int64_t n, const uint64_t* offsets,
                       int tiles_x, uint64_t* pair_out, cudaStream_t stream, uint32_t* hist = nullptr,
                       int hist_passes = 0, uint32_t* ranges = nullptr, int32_t num_tiles = 0,
-                      int64_t grid_cap = 0, const uint32_t* skip_bits = nullptr);
+                      int64_t grid_cap = 0, const uint32_t* skip_bits = nullptr, const TileCut* tc = nullptr);
 // Tiles in decreasing order of their work (log-spaced buckets, 4 per
 // octave), so that the compositing's last wave holds the short tiles: work
 // = range length (ranges given) or tile_work[t].

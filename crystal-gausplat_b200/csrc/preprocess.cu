@@ -7,6 +7,9 @@
 // staged through shared memory with coalesced float4 loads, into rows padded
 // to 13 float4 so that the per-thread float4 reads are free of bank conflicts.
 //
+// Binning record (32 bytes per Gaussian and view): {x0, y0, rect width, pair
+// count}, {tile mask low, high, bits(depth), 0}.
+//
 // Packed splat record (12 floats, private to this library):
 //   s0 = {mean.x, mean.y, conic.xx, conic.xy}
 //   s1 = {conic.yy, opacity (0 if culled or det <= 0), r, g}
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(kPreThreads, GS_PRE_MIN_CTAS) preprocess_kerne
           make_float4(col_b, depth_o, radius_o, __uint_as_float(emit));
       if (a.bin_v[v]) {
         a.bin_v[v][2 * i] = make_uint4((uint32_t)rx_o, (uint32_t)ry_o, (uint32_t)rw_o, emit);
-        a.bin_v[v][2 * i + 1] = make_uint4((uint32_t)mask_o, (uint32_t)(mask_o >> 32), 0u, 0u);
+        a.bin_v[v][2 * i + 1] = make_uint4((uint32_t)mask_o, (uint32_t)(mask_o >> 32), __float_as_uint(depth_o), 0u);
       }
       if (a.depth_pairs_v[v]) {
         uint64_t word;

@@ -128,6 +128,17 @@ class RasterizerContext:
                   "gsc_memcpy_d2h")
         return out
 
+    def set_tile_hint(self, cut, valid):
+        """Bind a view's per-tile depth cut (a float32 device tensor of
+        tiles_x * tiles_y entries, or None) for the next occluded forwards on
+        this context (gsc_frame_set_tile_hint): valid=True reads it, and every
+        such forward rewrites it for the view's next one. Results do not
+        depend on its contents."""
+        if cut is not None:
+            assert cut.dtype == torch.float32 and cut.is_cuda and cut.is_contiguous()
+        check(lib().gsc_frame_set_tile_hint(self.frame, ptr(cut), 1 if (cut is not None and valid) else 0),
+              "gsc_frame_set_tile_hint")
+
     @property
     def tiles_x(self):
         return (self.width + 15) // 16

@@ -77,7 +77,7 @@ class DataParallelTrainer:
 
     def __init__(self, gaussians, cameras, config, lrs=None, process_group=None, exchange="nccl",
                  loss="l1", lambda_ssim=0.2, batch_views=_abi.GSC_MAX_BATCH_VIEWS,
-                 barrier_timeout_s=60.0, multicast="auto"):
+                 barrier_timeout_s=60.0, multicast="auto", tile_hints=True):
         self.g = gaussians
         self.cameras = cameras
         self.cfg = config
@@ -110,6 +110,14 @@ class DataParallelTrainer:
             self.images = [torch.empty(H, W, 3, device=gaussians.arena.device) for _ in range(self.batch)]
         self.loss = torch.zeros(1, device=gaussians.arena.device)
         self.cam_structs = [c.to_struct() for c in cameras]
+        # occluded binning: one per-tile depth cut per view of this rank, made
+        # by the view's forward and read by its next one (gsc_frame_set_tile_hint)
+        self.tile_hints = {}
+        if tile_hints and self.batch > 1 and config.binning == _abi.GSC_BIN_OCCLUDED:
+            for v in self.my_views:
+                c = cameras[v]
+                T = ((c.width + 15) // 16) * ((c.height + 15) // 16)
+                self.tile_hints[v] = [torch.empty(T, dtype=torch.float32, device=gaussians.arena.device), False]
         if loss not in ("l1", "combined"):
             raise ValueError(f"unknown loss {loss!r}")
         self.loss_kind, self.lambda_ssim = loss, lambda_ssim
@@ -141,6 +149,12 @@ class DataParallelTrainer:
                 self.flush()
                 views = list(range(v, min(v + self.batch, max(self.hi, v + 1))))
                 self._slot = {u: k for k, u in enumerate(views)}
+                for k, u in enumerate(views):
+                    if u in self.tile_hints:
+                        self.ctxs[k].set_tile_hint(*self.tile_hints[u])
+                        self.tile_hints[u][1] = True  # this forward writes it
+                    elif self.tile_hints:
+                        self.ctxs[k].set_tile_hint(None, False)
                 Rasterizer.forward_batch(self.g, [self.cameras[u] for u in views], self.ctxs,
                                          config=self.cfg, images=self.images[:len(views)])
             k = self._slot[v]

@@ -468,6 +468,23 @@ GSC_API int gsc_reset_opacity(gsc_ctx* ctx, float* logit_opacity, int64_t n, flo
 GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out);
 GSC_API int gsc_frame_destroy(gsc_frame* frame);
 
+/* Per-tile depth cut for occluded binning (GSC_BIN_OCCLUDED), no reference
+ * counterpart: `cut` is a DEVICE array of tiles_x * tiles_y floats owned by
+ * the caller, one per view (pass NULL to unbind). Every occluded forward on
+ * this frame while it is bound rewrites it with the view's next cut: for
+ * each tile whose pixels all stopped, 1.005 x the depth of the last list
+ * entry any of its pixels used, else +inf. With `valid` nonzero the forward
+ * reads it: the first slice holds, per tile, the pairs of Gaussians in front
+ * of the tile's cut, and the second slice the remaining pairs of the tiles
+ * whose pixels did not all stop. Each tile's list is then still its depth
+ * order cut at its saturation point, so images, per-pixel outputs, lists and
+ * gradients are the same bit for bit whatever the cut holds. Only the work
+ * changes: a cut from the same view's previous forward (training revisits
+ * its views) leaves the first slice close to the pairs that are kept. The
+ * binding is per frame; a caller that renders several views on one frame
+ * binds each view's array before its forward. */
+GSC_API int gsc_frame_set_tile_hint(gsc_frame* frame, float* cut, int32_t valid);
+
 /* preprocess -> bin -> sort -> ranges -> composite. `image` [H,W,3] may be
  * NULL (the frame's own buffer is used); n_contrib / final_T may be NULL.
  * *num_rendered (host, may be NULL) = number of keys (ctx.num_rendered). */

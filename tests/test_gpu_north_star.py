@@ -22,7 +22,8 @@ elements no more numerous than fp32 summation itself produces (see `gate`).
   contributing lists are an order-preserving subset of the reference's sorted
   lists, and images, contributor counts, final transmittance and `last` equal
   the oracle's (images also over the reference lists); the summed gradients
-  of the three views pass the gradient gate.
+  of the three views pass the gradient gate. A second pass, whose forwards
+  read each view's per-tile depth cut from the first, gives the same frames.
 """
 import importlib
 import os
@@ -225,6 +226,26 @@ def test_c3_training_path_three_views(cuda, par_oracle):
                "image": host(tr.images[v])} for v in range(views)}
     gpu_grads = host(tr.grads.arena).copy()
     gpu_loss = float(tr.loss.item())
+    # the same pass again: now each view's forward reads the per-tile depth
+    # cut its first forward wrote; lists, per-pixel outputs and images are
+    # the same bit for bit, gradients up to the order of the atomic adds
+    assert tr.tile_hints and all(h[1] for h in tr.tile_hints.values())
+    tr.zero()
+    for v in range(views):
+        tr.view_fwd_bwd(v, dev_t[v])
+    tr.flush()
+    R.sync()
+    for v in range(views):
+        c = tr.ctxs[v]
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_KEYS, np.uint64), got[v]["keys"])
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_VALUES, np.uint32), got[v]["vals"])
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_RANGES, np.uint32), got[v]["ranges"])
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_LAST, np.uint32).reshape(H, W), got[v]["last"])
+        np.testing.assert_array_equal(c.get(_abi.GSC_FRAME_FINAL_T, np.float32).reshape(H, W), got[v]["final_T"])
+        np.testing.assert_array_equal(host(tr.images[v]), got[v]["image"])
+        assert c.num_rendered == got[v]["rendered"]
+    g2 = host(tr.grads.arena)
+    assert np.linalg.norm(g2 - gpu_grads) <= 1e-5 * np.linalg.norm(gpu_grads)
     del tr
 
     sc = O.Scene(arrays)
