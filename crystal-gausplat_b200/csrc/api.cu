@@ -627,7 +627,7 @@ int forward_sort_scan(gsc_ctx* ctx, gsc_frame* f, bool sort_depth = true, int64_
   if (cn == 0) return cudaMemsetAsync(f->total.ptr, 0, 8, ctx->stream) == cudaSuccess ? GSC_OK : GSC_ERR_CUDA;
   {
     StageScope sc(ctx, GSC_STAGE_SCAN);
-    sc.kernels(tc ? 2 : 1);
+    sc.kernels(1);
     if (tc)
       GS_TRY(launch_block_sums_cut(frame_bins(f), f->order_ptr, cn, (uint32_t*)f->block_sums.ptr, *tc, ctx->stream));
     else
@@ -877,7 +877,7 @@ int sliced_bin(gsc_ctx* ctx, gsc_frame* f, int s, const int64_t* p, uint64_t m_u
   const uint32_t* skip = nullptr;
   if (s > 0 && n_s > 0) {
     StageScope sc(ctx, GSC_STAGE_SCAN);
-    sc.kernels(cutm ? 3 : 2);
+    sc.kernels(2);
     if (cutm)
       GS_TRY(launch_block_sums_cut(frame_bins(f), order, n_s, (uint32_t*)f->block_sums.ptr, tc, ctx->stream));
     else

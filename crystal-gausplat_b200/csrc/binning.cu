@@ -287,21 +287,29 @@ __device__ __forceinline__ uint32_t cut_big_count(const TileCut& c, uint4 b0, fl
   return k;
 }
 
-// Passing-tile count and (records of <= 64 tiles) sub-mask of every
-// Gaussian under a tile cut, in Gaussian order: the records are read
-// sequentially, and the 12 bytes per Gaussian written stay in L2 for the
-// depth-order passes that gather them.
-__global__ void __launch_bounds__(256) cut_count_kernel(const uint4* __restrict__ bins, int64_t n, TileCut tc) {
-  if (tc.open && *(volatile const unsigned int*)tc.open == 0u) return;  // no second-slice pair anywhere
-  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+// Pair count of each 256-position chunk under a tile cut, with every
+// position's passing-tile count and (records of <= 64 tiles) sub-mask. (A
+// count in Gaussian order -- records read sequentially, the counts gathered
+// in depth order from L2 by a second kernel -- measured slower, and so did
+// keeping the gathered records in depth order for the later passes.)
+__global__ void __launch_bounds__(256) block_sums_cut_kernel(const uint4* __restrict__ bins,
+                                                             const uint32_t* __restrict__ order, int64_t n,
+                                                             uint32_t* __restrict__ sums, TileCut tc) {
+  __shared__ uint32_t s_warp[8];
+  if (tc.open && *(volatile const unsigned int*)tc.open == 0u) {  // no second-slice pair anywhere
+    if (threadIdx.x == 0) sums[blockIdx.x] = 0u;
+    return;
+  }
+  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
   const int lane = threadIdx.x & 31;
   uint32_t t = 0;
   uint64_t sub = 0;
   uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
-  if (i < n) {
-    b0 = bins[(size_t)i * 2];
+  if (p < n) {
+    const uint32_t gid = order[p];
+    b0 = bins[(size_t)gid * 2];
     if (b0.w) {
-      b1 = bins[(size_t)i * 2 + 1];
+      b1 = bins[(size_t)gid * 2 + 1];
       if (b0.w <= 64) t = cut_small_record(tc, b0, b1, &sub);
     }
   }
@@ -317,23 +325,10 @@ __global__ void __launch_bounds__(256) cut_count_kernel(const uint4* __restrict_
     const uint32_t k = cut_big_count(tc, w0, d, lane);
     if (lane == who) t = k;
   }
-  if (i < n) {
-    tc.sub[i] = sub;
-    tc.cnt[i] = t;
+  if (p < n) {
+    tc.sub[p] = sub;
+    tc.cnt[p] = t;
   }
-}
-
-// Pair count of each 256-position chunk of `order` from the per-Gaussian
-// counts of cut_count_kernel.
-__global__ void __launch_bounds__(256) block_sums_cut_kernel(const uint32_t* __restrict__ order, int64_t n,
-                                                             uint32_t* __restrict__ sums, TileCut tc) {
-  __shared__ uint32_t s_warp[8];
-  if (tc.open && *(volatile const unsigned int*)tc.open == 0u) {
-    if (threadIdx.x == 0) sums[blockIdx.x] = 0u;
-    return;
-  }
-  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  const uint32_t t = p < n ? tc.cnt[order[p]] : 0u;
   const uint32_t incl = block_incl_scan_256(t, s_warp);
   if (threadIdx.x == 255) sums[blockIdx.x] = incl;
 }
@@ -398,9 +393,9 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
     s_big[threadIdx.x] = 0u;
     if (p < n) {
       if (cut) {
-        const uint32_t gid = order[p];
-        t = tc.cnt[gid];  // passing tiles, counted by cut_count_kernel
+        t = tc.cnt[p];  // passing tiles, counted by block_sums_cut_kernel
         if (t) {
+          const uint32_t gid = order[p];
           const uint4 b0 = bins[(size_t)gid * 2];
           s_x0[threadIdx.x] = (int)b0.x;
           s_y0[threadIdx.x] = (int)b0.y;
@@ -408,7 +403,7 @@ __global__ void __launch_bounds__(256) emit_tiles_kernel(const uint4* __restrict
           s_inv[threadIdx.x] = (65535u + b0.z) / b0.z;
           s_id[threadIdx.x] = gid;
           if (b0.w <= 64) {
-            s_mask[threadIdx.x] = tc.sub[gid];
+            s_mask[threadIdx.x] = tc.sub[p];
           } else {
             s_big[threadIdx.x] = b0.w;
             s_depth[threadIdx.x] = __uint_as_float(bins[(size_t)gid * 2 + 1].z);
@@ -675,10 +670,7 @@ int launch_block_sums_cut(const uint4* bins, const uint32_t* order, int64_t n, u
     set_error("block_sums_cut: incomplete tile cut");
     return GSC_ERR_INVALID;
   }
-  const unsigned blocks = (unsigned)((n + 255) / 256);
-  cut_count_kernel<<<blocks, 256, 0, stream>>>(bins, n, tc);
-  GS_CK_LAUNCH("cut_count_kernel");
-  block_sums_cut_kernel<<<blocks, 256, 0, stream>>>(order, n, sums, tc);
+  block_sums_cut_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(bins, order, n, sums, tc);
   GS_CK_LAUNCH("block_sums_cut_kernel");
   return GSC_OK;
 }

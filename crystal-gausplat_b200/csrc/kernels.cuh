@@ -184,13 +184,12 @@ struct TileCut {
   int done_words = 0;
   int mode = 0;
   int tiles_x = 0;
-  uint64_t* sub = nullptr;  // per Gaussian: the record's passing tiles (records of <= 64 tiles)
-  uint32_t* cnt = nullptr;  // per Gaussian: number of passing tiles
+  uint64_t* sub = nullptr;  // per position: the record's passing tiles (records of <= 64 tiles)
+  uint32_t* cnt = nullptr;  // per position: number of passing tiles
   const unsigned int* open = nullptr;  // mode 1: 0 if no tile can have a second-slice pair
 };
-// Pair count of each 256-position chunk of `order` under a tile cut (two
-// kernels: the per-Gaussian counts and sub-masks tc.cnt / tc.sub, read in
-// Gaussian order, then the chunk sums in depth order).
+// Pair count of each 256-position chunk of `order` under a tile cut, with
+// every position's count and sub-mask (tc.cnt, tc.sub).
 int launch_block_sums_cut(const uint4* bins, const uint32_t* order, int64_t n, uint32_t* sums, const TileCut& tc,
                           cudaStream_t stream);
 // Next cut of every tile after a view's last slice: done tiles (every pixel
