@@ -300,7 +300,7 @@ def packed_sort_bytes(bits, hist=True, hi=False):
 OCC_FIRST_SLICE = 0.2
 
 
-def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False, views_per_step=1):
+def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False, views_per_step=1, tile_cut=False):
     """Algorithmic work of each stage for ONE view: (bound, bytes or flops).
 
     Binning of a view = a stable depth sort of the N Gaussians (per view: 32 bits,
@@ -314,19 +314,27 @@ def stage_work(n, binned, kept, pge, tiles, end_bit, batch=1, occluded=False, vi
     and its backward run once per `batch` views: parameters read once,
     gradient rows read and written once, one grad2d row per view. Adam runs
     once per step over every parameter: its share of one view is the step's
-    bytes over the `views_per_step` this rank renders."""
+    bytes over the `views_per_step` this rank renders. tile_cut: occluded
+    binning with each view's per-tile depth cut, whose two slices both walk
+    every depth position (order + 32 B record read, count and sub-mask
+    written) and whose emissions read the counts back."""
     tb = end_bit - 32
     depth_bits = 28 + max(1, (batch - 1).bit_length()) if batch > 1 else 32
     later = (1.0 - OCC_FIRST_SLICE) * n if occluded else 0.0
     slices = 2 if occluded else 1
+    scan_b = 20 * n + 36 * later
+    emit_b = (4 + 32) * n + 8 * binned
+    if occluded and tile_cut:
+        scan_b = 2 * (4 + 32 + 4 + 8) * n
+        emit_b = 2 * 4 * n + 8 * binned
     return {
         # one launch per `batch` views: parameters read once, per view a 48 B splat
         # record + 32 B binning record + 8 B packed depth word
         "preprocess": ("hbm", (PARAM_ROW_B / batch + 88) * n),
         # order + binning-record word gather and the block-sum scan; the later
         # slice gathers order + the 32 B record again (skip test)
-        "scan": ("hbm", 20 * n + 36 * later),
-        "emit": ("hbm", (4 + 32) * n + 8 * binned),  # order + 32 B binning record; packed pairs
+        "scan": ("hbm", scan_b),
+        "emit": ("hbm", emit_b),  # order + 32 B binning record (or the cut's counts); packed pairs
         # depth sort (per view, or one per batch) + tile sorts of the binned pairs
         "sort": ("hbm", packed_sort_bytes(depth_bits, hi=batch == 1) * n + packed_sort_bytes(tb, hist=False) * binned),
         # empty ranges {~0, 0} -> {0, 0} per slice; occluded: the kept ids copied
@@ -481,7 +489,7 @@ def run_train(args, cfg, rank, world, local, peaks, peak_kind):
     binned, kept = (c / (args.steps * my_views) for c in profile_pairs(gs, ctx))
     occluded = rcfg.binning == gs._abi.GSC_BIN_OCCLUDED
     work = stage_work(cfg["n"], binned, kept, pge, tiles, end_bit, batch=tr.batch, occluded=occluded,
-                      views_per_step=my_views)
+                      views_per_step=my_views, tile_cut=bool(tr.tile_hints))
     roof = rooflines(stats, work, peaks, args.steps * my_views)
 
     e2e = None

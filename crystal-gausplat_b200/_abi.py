@@ -159,7 +159,7 @@ _SIGS = {
     "gsc_reset_opacity": (C.c_int, [P, P, C.c_int64, C.c_float]),
     "gsc_frame_create": (C.c_int, [P, C.POINTER(P)]),
     "gsc_frame_destroy": (C.c_int, [P]),
-    "gsc_frame_set_tile_hint": (C.c_int, [P, P, C.c_int32]),
+    "gsc_frame_set_tile_hint": (C.c_int, [P, P, C.c_int64, C.c_int32]),
     "gsc_rasterize_forward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),
                                         C.POINTER(RasterConfig), P, P, P, C.POINTER(C.c_int64)]),
     "gsc_rasterize_backward": (C.c_int, [P, P, C.POINTER(Gaussians), C.POINTER(Camera),

@@ -253,7 +253,7 @@ lib GSCuda
   # whole-view calls (Rasterizer.forward / .backward, rasterizer.cr:48-104)
   fun frame_create = gsc_frame_create(ctx : Ctx, out : Frame*) : Int32
   fun frame_destroy = gsc_frame_destroy(frame : Frame) : Int32
-  fun frame_set_tile_hint = gsc_frame_set_tile_hint(frame : Frame, cut : Float32*, valid : Int32) : Int32
+  fun frame_set_tile_hint = gsc_frame_set_tile_hint(frame : Frame, cut : Float32*, count : Int64, valid : Int32) : Int32
   fun rasterize_forward = gsc_rasterize_forward(ctx : Ctx, frame : Frame, g : Gaussians*,
                                                 cam : Camera*, cfg : RasterConfig*, image : Float32*,
                                                 n_contrib : UInt32*, final_t : Float32*,

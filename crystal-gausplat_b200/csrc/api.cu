@@ -82,6 +82,7 @@ struct gsc_frame {
   // per-tile depth cut of the slices (gsc_frame_set_tile_hint): the caller's
   // array of tiles floats, read when valid, rewritten by every occluded forward
   float* tile_hint = nullptr;
+  int64_t tile_hint_count = 0;
   bool tile_hint_valid = false;
   GsBuf cut_sub, cut_cnt, open_flag;
   bool count_pending = false;  // the lists' length is on the device (the final ranges' end)
@@ -532,10 +533,12 @@ GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out) {
   return GSC_OK;
 }
 
-GSC_API int gsc_frame_set_tile_hint(gsc_frame* f, float* cut, int32_t valid) {
+GSC_API int gsc_frame_set_tile_hint(gsc_frame* f, float* cut, int64_t count, int32_t valid) {
   GS_REQUIRE(f, "gsc_frame_set_tile_hint: null frame");
   GS_REQUIRE(((uintptr_t)cut & 3u) == 0, "gsc_frame_set_tile_hint: misaligned cut array");
+  GS_REQUIRE(!cut || count > 0, "gsc_frame_set_tile_hint: empty cut array");
   f->tile_hint = cut;
+  f->tile_hint_count = cut ? count : 0;
   f->tile_hint_valid = cut && valid;
   return GSC_OK;
 }
@@ -580,6 +583,8 @@ int forward_prepare(gsc_ctx* ctx, gsc_frame* f, const gsc_gaussians* g, const gs
   const size_t npix = (size_t)W * H;
   f->has_forward = false;
   f->has_grad2d = false;
+  GS_REQUIRE(!f->tile_hint || (int64_t)tx * ty <= f->tile_hint_count,
+             "gsc_rasterize_forward: the frame's tile cut array is shorter than the view's tiles");
   f->n = n; f->width = W; f->height = H; f->tiles_x = tx; f->tiles_y = ty;
   GS_TRY(ensure(ctx, &f->splats, (size_t)n * 48 + 48));
   GS_TRY(ensure(ctx, &f->depth_pairs, (size_t)n * 8 + 8));

@@ -136,8 +136,8 @@ class RasterizerContext:
         depend on its contents."""
         if cut is not None:
             assert cut.dtype == torch.float32 and cut.is_cuda and cut.is_contiguous()
-        check(lib().gsc_frame_set_tile_hint(self.frame, ptr(cut), 1 if (cut is not None and valid) else 0),
-              "gsc_frame_set_tile_hint")
+        check(lib().gsc_frame_set_tile_hint(self.frame, ptr(cut), cut.numel() if cut is not None else 0,
+                                            1 if (cut is not None and valid) else 0), "gsc_frame_set_tile_hint")
 
     @property
     def tiles_x(self):

@@ -469,8 +469,10 @@ GSC_API int gsc_frame_create(gsc_ctx* ctx, gsc_frame** out);
 GSC_API int gsc_frame_destroy(gsc_frame* frame);
 
 /* Per-tile depth cut for occluded binning (GSC_BIN_OCCLUDED), no reference
- * counterpart: `cut` is a DEVICE array of tiles_x * tiles_y floats owned by
- * the caller, one per view (pass NULL to unbind). Every occluded forward on
+ * counterpart: `cut` is a DEVICE array of `count` floats owned by the caller,
+ * one per view (pass NULL to unbind); it must stay allocated while bound, and
+ * a forward whose tiles_x * tiles_y exceeds `count` fails with
+ * GSC_ERR_INVALID before any work. Every occluded forward on
  * this frame while it is bound rewrites it with the view's next cut: for
  * each tile whose pixels all stopped, 1.005 x the depth of the last list
  * entry any of its pixels used, else +inf. With `valid` nonzero the forward
@@ -483,7 +485,7 @@ GSC_API int gsc_frame_destroy(gsc_frame* frame);
  * its views) leaves the first slice close to the pairs that are kept. The
  * binding is per frame; a caller that renders several views on one frame
  * binds each view's array before its forward. */
-GSC_API int gsc_frame_set_tile_hint(gsc_frame* frame, float* cut, int32_t valid);
+GSC_API int gsc_frame_set_tile_hint(gsc_frame* frame, float* cut, int64_t count, int32_t valid);
 
 /* preprocess -> bin -> sort -> ranges -> composite. `image` [H,W,3] may be
  * NULL (the frame's own buffer is used); n_contrib / final_T may be NULL.

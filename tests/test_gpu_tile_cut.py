@@ -134,3 +134,17 @@ def test_batched_views_with_per_view_cuts_and_backward(cuda):
     # same lists, so the gradients differ only by the order of the atomic adds
     assert abs(l1 - l0) <= 1e-6 * abs(l0)
     assert np.linalg.norm(g1 - g0) <= 1e-5 * np.linalg.norm(g0)
+
+
+def test_short_cut_array_is_refused(cuda):
+    g = gs.Gaussian3D(gs.synthetic_arrays(2_000, 0x7C0300))
+    cam = gs.make_camera(W, H, (0.0, 0.0, 4.0))
+    cfg = gs.default_config(binning=_abi.GSC_BIN_OCCLUDED)
+    ctx = R.RasterizerContext()
+    ctx.set_tile_hint(cuda.full((T - 1,), float("inf"), device="cuda"), True)
+    with pytest.raises(_abi.GscError, match="shorter than the view's tiles"):
+        gs.Rasterizer.forward(g, cam, context=ctx, config=cfg)
+    ctx.set_tile_hint(None, False)
+    img, _ = gs.Rasterizer.forward(g, cam, context=ctx, config=cfg)  # the frame still works
+    R.sync()
+    assert np.isfinite(host(img)).all()

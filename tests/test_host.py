@@ -75,6 +75,9 @@ def test_bench_work_model():
     assert wo["emit"][1] == 36 * 1000 + 8 * 2000
     assert wo["scan"][1] == 20 * 1000 + 36 * 800
     assert wo["ranges"][1] == 8 * 8160 * 2 + 8 * 300 + 8 * 8160
+    # with the per-tile cut both slices count over every position
+    wc = bench.stage_work(1000, 2000, 300, 10 ** 6, 8160, 45, batch=8, occluded=True, tile_cut=True)
+    assert wc["scan"][1] == 2 * 48 * 1000 and wc["emit"][1] == 8 * 1000 + 8 * 2000
     r = bench.rooflines({"adam": {"ms": 2.0, "calls": 1, "kernels": 1}}, {"adam": ("hbm", 1e9)},
                         {"hbm_gbs": 1000.0}, 2)
     assert r["adam"]["achieved"] == 1000.0 and r["adam"]["ms_per_view"] == 1.0
