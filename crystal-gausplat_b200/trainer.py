@@ -138,8 +138,10 @@ class DataParallelTrainer:
                                self.grads.arena.numel() * 4), "gsc_memset")
         check(lib().gsc_memset(ctx, C.c_void_p(self.loss.data_ptr()), 0, 4), "gsc_memset")
 
-    def view_fwd_bwd(self, v, target):
-        """Forward + backward of view v against a device target [H,W,3]."""
+    def view_fwd_bwd(self, v, target, ready=None):
+        """Forward + backward of view v against a device target [H,W,3]; with
+        `ready` (a CUDA event), the target is only waited for right before the
+        backward that reads it (the forward does not need it)."""
         cam = self.cameras[v]
         defer = self.batch > 1
         if defer:
@@ -164,6 +166,8 @@ class DataParallelTrainer:
             ctx = self.last_ctx = self.ctxs[0]
             image = self.image if self.loss_kind == "combined" else None
             Rasterizer.forward(self.g, cam, context=ctx, config=self.cfg, out=image)
+        if ready is not None:
+            torch.cuda.current_stream(self.g.arena.device).wait_event(ready)
         if self.loss_kind == "combined":
             combined_with_grad(image, target, self.lambda_ssim, out=self.loss_terms, grad=self.dimage)
             self.loss += self.loss_terms[0]
@@ -263,7 +267,7 @@ class DataParallelTrainer:
         """One training step with targets streamed from pinned host memory
         (feeder: HostTargetFeeder over this rank's views, indexed from 0)."""
         self.zero()
-        feeder.run(range(self.hi - self.lo), lambda k, t: self.view_fwd_bwd(self.lo + k, t))
+        feeder.run(range(self.hi - self.lo), lambda k, t, ready: self.view_fwd_bwd(self.lo + k, t, ready))
         self.reduce_and_step()
         return self.loss
 
@@ -278,15 +282,17 @@ class DataParallelTrainer:
 
 class HostTargetFeeder:
     """Streams per-view targets from pinned host memory to the device on a
-    side stream, double-buffered, so that the copy of view v+1 overlaps the
-    forward/backward of view v. `host` is a pinned [V, H, W, 3] tensor."""
+    side stream, `depth` views ahead (default: one forward batch), so that the
+    copies run under the batched forward and the earlier backwards. `host` is
+    a pinned [V, H, W, 3] tensor."""
 
-    def __init__(self, host, device):
+    def __init__(self, host, device, depth=_abi.GSC_MAX_BATCH_VIEWS):
         self.host = host
         self.copy_stream = torch.cuda.Stream(device=device)
-        self.bufs = [torch.empty_like(host[0], device=device) for _ in range(2)]
-        self.ready = [torch.cuda.Event() for _ in range(2)]
-        self.free = [torch.cuda.Event() for _ in range(2)]
+        depth = max(1, min(int(depth), host.shape[0]))
+        self.bufs = [torch.empty_like(host[0], device=device) for _ in range(depth)]
+        self.ready = [torch.cuda.Event() for _ in range(depth)]
+        self.free = [torch.cuda.Event() for _ in range(depth)]
         for e in self.free:
             e.record(torch.cuda.current_stream(device))
 
@@ -297,19 +303,21 @@ class HostTargetFeeder:
             self.ready[slot].record(self.copy_stream)
 
     def run(self, views, fn):
-        """Calls fn(v, device_target) for each view, prefetching the next."""
+        """Calls fn(v, device_target, ready_event) for each view; fn makes the
+        current stream wait for ready_event before it reads the target."""
         views = list(views)
         if not views:
             return
         cur = torch.cuda.current_stream(self.bufs[0].device)
-        self._issue(0, views[0])
+        D = len(self.bufs)
+        for k in range(min(D, len(views))):
+            self._issue(k, views[k])
         for k, v in enumerate(views):
-            slot = k % 2
-            if k + 1 < len(views):
-                self._issue((k + 1) % 2, views[k + 1])
-            cur.wait_event(self.ready[slot])
-            fn(v, self.bufs[slot])
+            slot = k % D
+            fn(v, self.bufs[slot], self.ready[slot])
             self.free[slot].record(cur)
+            if k + D < len(views):
+                self._issue(slot, views[k + D])
 
 
 # ---- the reference's single-view training loop ------------------------------
