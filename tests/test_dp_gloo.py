@@ -52,3 +52,34 @@ def test_rank_failure_is_reported_not_hung(tmp_path):
     assert procs[1].exitcode == 3
     status = (tmp_path / "rank0.status").read_text()
     assert status.startswith("error"), status
+
+
+def test_multicast_address_of_a_tensor_in_a_symmetric_buffer():
+    """The fused exchange's multicast form: the tensor's offset inside its
+    symmetric-memory buffer carried onto the buffer's multicast address, and
+    0 (the peer form) when the buffer has no multicast object."""
+    import importlib
+    trainer = importlib.import_module("crystal-gausplat_b200.trainer")
+
+    class Tensor:
+        def __init__(self, p):
+            self.p = p
+
+        def data_ptr(self):
+            return self.p
+
+    class Handle:
+        def __init__(self, mc, rank=1):
+            self._mc, self.rank = mc, rank
+            self.buffer_ptrs = [0x1000, 0x20000]
+
+        @property
+        def multicast_ptr(self):
+            if isinstance(self._mc, Exception):
+                raise self._mc
+            return self._mc
+
+    assert trainer._multicast_ptr(Tensor(0x20000 + 256), Handle(0x7000000)) == 0x7000000 + 256
+    assert trainer._multicast_ptr(Tensor(0x20000), Handle(0)) == 0
+    assert trainer._multicast_ptr(Tensor(0x20000), Handle(RuntimeError("no multicast"))) == 0
+    assert trainer.MULTICAST_MIN_RANKS == 4
